@@ -1,0 +1,254 @@
+/*
+ * vkb200.h — C ABI of the B200 (sm_100a) quantized-Whisper hot path.
+ *
+ * A drop-in for the seams of ayutaz/vokra that a Rust backend crate would bind
+ * with `extern "C"` (see INTEGRATION.md for the binding stubs). Every function
+ * takes plain pointers and sizes; no C++ or torch type crosses this boundary
+ * and no C++ exception escapes it (each entry point catches and converts, like
+ * the reference's panic firewall crates/vokra-capi/src/ffi_guard.rs:27).
+ *
+ * Conventions
+ *  - Functions return vkb_status; on error vkb_last_error() holds a message
+ *    for the calling thread (vokra_last_error, include/vokra.h).
+ *  - "_dev" pointers are device pointers on the context's GPU; "_host"
+ *    pointers are host memory. Device-pointer calls are asynchronous on the
+ *    context's stream; host-pointer calls are synchronous.
+ *  - There is no CPU fallback: an unsupported dtype, shape or mode returns
+ *    VKB_ERROR_UNSUPPORTED_OP or VKB_ERROR_INVALID_ARGUMENT, as the reference's
+ *    Compute seam does (crates/vokra-models/src/compute.rs:589-600).
+ *  - A context is used by one thread at a time (CudaContext is thread-affine,
+ *    crates/vokra-backend-cuda/src/context.rs:1071-1076).
+ */
+#ifndef VKB200_H
+#define VKB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VKB_API __attribute__((visibility("default")))
+#else
+#define VKB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes: the numbering of vokra_status_t (include/vokra.h:58-78),
+ * plus KV_CACHE_EXHAUSTED for VokraError::KvCacheExhausted
+ * (crates/vokra-core/src/error.rs:170), which vokra's C ABI folds into OTHER. */
+typedef enum vkb_status {
+    VKB_OK = 0,
+    VKB_ERROR_IO = 1,
+    VKB_ERROR_MODEL_LOAD = 2,
+    VKB_ERROR_UNSUPPORTED_OP = 3,
+    VKB_ERROR_BACKEND_UNAVAILABLE = 4,
+    VKB_ERROR_INVALID_ARGUMENT = 5,
+    VKB_ERROR_GRAPH_VALIDATION = 6,
+    VKB_ERROR_NOT_IMPLEMENTED = 7,
+    VKB_ERROR_PANIC = 8,
+    VKB_ERROR_OTHER = 9,
+    VKB_ERROR_KV_CACHE_EXHAUSTED = 10
+} vkb_status;
+
+/* GGUF dtype tags (GgmlType, crates/vokra-core/src/gguf/tensor.rs:59-97) plus
+ * the loader extension of this library: Q4_0 (2) and Q8_0 (8) in the public
+ * ggml block layout. */
+enum vkb_ggml_type {
+    VKB_GGML_F32 = 0,
+    VKB_GGML_F16 = 1,
+    VKB_GGML_Q4_0 = 2,
+    VKB_GGML_Q8_0 = 8,
+    VKB_GGML_Q4_K = 12,
+    VKB_GGML_Q5_K = 13,
+    VKB_GGML_Q6_K = 14,
+    VKB_GGML_BF16 = 30
+};
+
+/* KV quantization modes, numbered like KvQuant (crates/vokra-core/src/kv_quant/mod.rs:88). */
+enum vkb_kv_quant { VKB_KV_FP32 = 0, VKB_KV_Q4_0 = 1, VKB_KV_Q5_0 = 2, VKB_KV_Q8_0 = 3 };
+
+/* Activation / output element types of the device-pointer entry points. */
+enum vkb_dtype { VKB_DT_F32 = 0, VKB_DT_F16 = 1 };
+
+/* Fused epilogues of vkb_linear. */
+enum vkb_epilogue {
+    VKB_EPI_NONE = 0,       /* out = a.W^T + bias                      */
+    VKB_EPI_GELU = 1,       /* out = gelu(a.W^T + bias)  (erf form)    */
+    VKB_EPI_RESIDUAL = 2,   /* out = residual + a.W^T + bias (f32 out) */
+    VKB_EPI_SCALE = 3       /* out = (a.W^T + bias) * scale            */
+};
+
+typedef struct vkb_context vkb_context;
+typedef struct vkb_weight vkb_weight;
+typedef struct vkb_kv_pool vkb_kv_pool;
+typedef struct vkb_whisper vkb_whisper;
+typedef struct vkb_session vkb_session;
+
+/* ---- library / context --------------------------------------------------- */
+
+/* Thread-local message of the last failed call (vokra_last_error). */
+VKB_API const char* vkb_last_error(void);
+/* ABI version, bumped on incompatible change. */
+VKB_API int vkb_abi_version(void);
+
+/* Creates a context on `device` (one per GPU). Fails with
+ * VKB_ERROR_BACKEND_UNAVAILABLE when the device is absent or not sm_100. */
+VKB_API vkb_status vkb_context_create(int device, vkb_context** out);
+VKB_API vkb_status vkb_context_destroy(vkb_context* ctx);
+/* Launch subsequent device-pointer work on `stream` (a cudaStream_t of the
+ * same device; NULL = the context's own stream). */
+VKB_API vkb_status vkb_context_set_stream(vkb_context* ctx, void* stream);
+VKB_API vkb_status vkb_context_synchronize(vkb_context* ctx);
+/* Number of kernels this context has launched (CudaContext::submission_count,
+ * crates/vokra-backend-cuda/src/context.rs:3152). */
+VKB_API uint64_t vkb_context_launch_count(const vkb_context* ctx);
+
+/* ---- quantized Linear: Compute::gemm_q_f32 (compute.rs:943) ---------------- */
+
+/* Uploads an untransposed [n][k] GGUF weight payload (`bytes`, `len` host
+ * bytes) and repacks it once into the device tile layout. Accepted tags:
+ * Q4_0, Q8_0, Q4_K (quantized) and F32/F16 (dense). Replaces the load-time
+ * binding of whisper::weights::linear_with (whisper/weights.rs:439). */
+VKB_API vkb_status vkb_weight_upload(vkb_context* ctx, uint32_t ggml_type, int64_t n, int64_t k,
+                             const void* bytes, size_t len, vkb_weight** out);
+VKB_API vkb_status vkb_weight_destroy(vkb_weight* w);
+/* Device bytes the repacked weight occupies. */
+VKB_API size_t vkb_weight_device_bytes(const vkb_weight* w);
+
+/* out[m][n] = epilogue(a[m][k] . dequant(W)[n][k]^T + bias[n]), all device
+ * pointers. a is F32 or F16; out is F32 or F16 (EPI_RESIDUAL requires F32 and
+ * may alias residual). bias_dev may be NULL (Whisper k_proj). `scale` is used
+ * by EPI_SCALE only. Small m runs the streaming GEMV kernel, larger m the
+ * tcgen05 tensor-core GEMM. */
+VKB_API vkb_status vkb_linear(vkb_context* ctx, const vkb_weight* w, int64_t m,
+                      const void* a_dev, int a_dtype, const float* bias_dev,
+                      void* out_dev, int out_dtype, int epilogue,
+                      const float* residual_dev, float scale);
+
+/* The exact gemm_q_f32 contract with host buffers: uploads `wq` ([n][k] GGUF
+ * bytes of `ggml_type`), a[m][k] and bias, runs the GPU kernel, downloads
+ * out[m][n]. Synchronous. The reference returns UnsupportedOp on every GPU
+ * arm (compute.rs:589-600); this is the B200 arm. */
+VKB_API vkb_status vkb_gemm_q_f32(vkb_context* ctx, int64_t m, int64_t n, int64_t k,
+                          const float* a_host, const void* wq_host, size_t wq_len,
+                          uint32_t ggml_type, const float* bias_host, float* out_host);
+
+/* ---- KvQuantDequantGemvOps::fused_dequant_gemv (kv_quant/gpu_ops.rs:70) ----- */
+
+/* y[n_rows] = dequant(blocks)[n_rows][nbpr*32] . x. Same rejection rules as
+ * validate_dequant_gemv (gpu_ops.rs:95): FP32 mode, x_len != nbpr*32 or
+ * n_bytes != n_rows*nbpr*block_bytes give VKB_ERROR_INVALID_ARGUMENT. */
+VKB_API vkb_status vkb_kv_dequant_gemv(vkb_context* ctx, int mode, const void* blocks_dev, size_t n_bytes,
+                               size_t n_rows, size_t nbpr, const float* x_dev, size_t x_len,
+                               float* y_dev);
+/* Host-buffer form of the same (the trait's exact signature). Synchronous. */
+VKB_API vkb_status vkb_kv_dequant_gemv_host(vkb_context* ctx, int mode, const void* blocks_host,
+                                    size_t n_bytes, size_t n_rows, size_t nbpr,
+                                    const float* x_host, size_t x_len, float* y_host);
+
+/* ---- paged quantized KV cache: QuantizedPagedKvCache (cache/paged_quant.rs)
+ *      and GpuPagedKvCacheOps (cache/paged.rs:956) --------------------------- */
+
+enum vkb_kv_layout {
+    /* The reference layout (paged_quant.rs:100-130): one page per
+     * (layer, time-block) holding every stream, page table indexed by
+     * layer * pages_per_layer + t / page_tokens, LIFO allocation.
+     * page_tokens 2 or 4 (BlockSize, cache/paged.rs:110) or 16. */
+    VKB_KV_LAYOUT_REFERENCE = 0,
+    /* Per-sequence pages: one page holds page_tokens tokens of one sequence;
+     * the table [n_stream][max_time/page_tokens] is shared by every layer
+     * (each layer has its own arena indexed by the same page id). Pages of a
+     * sequence are returned by vkb_kv_release_seq (continuous batching). */
+    VKB_KV_LAYOUT_SEQUENCE = 1
+};
+
+typedef struct vkb_kv_pool_desc {
+    int32_t n_layer;
+    int32_t n_head;
+    int32_t d_head;
+    int32_t n_stream;    /* concurrent sequences (KvDims::n_stream) */
+    int32_t n_codebook;  /* 1 for Whisper (KvDims::n_codebook) */
+    int32_t max_time;    /* KvDims::max_time */
+    int32_t page_tokens; /* 2, 4 or 16 */
+    int32_t mode;        /* vkb_kv_quant; Q8_0 is the device-kernel format */
+    int32_t layout;      /* vkb_kv_layout */
+    int32_t n_pages;     /* arena pages; 0 = enough for every stream at max_time */
+} vkb_kv_pool_desc;
+
+/* Allocates the whole arena up front (no allocation on the hot path,
+ * paged_quant.rs:30-36). */
+VKB_API vkb_status vkb_kv_pool_create(vkb_context* ctx, const vkb_kv_pool_desc* desc, vkb_kv_pool** out);
+VKB_API vkb_status vkb_kv_pool_destroy(vkb_kv_pool* pool);
+
+/* Declares the tokens of the next decode step: token i belongs to stream
+ * seq_ids[i] at absolute position positions[i] (host arrays). Acquires pages
+ * in the reference's order (layer-major, then token), uploads the table and
+ * the step's slot list. VKB_ERROR_KV_CACHE_EXHAUSTED when the free list runs
+ * out (QuantPageAllocator::acquire, paged_quant.rs:193). Tokens of one stream
+ * must be contiguous and in increasing position. */
+VKB_API vkb_status vkb_kv_begin_step(vkb_kv_pool* pool, int32_t n_tok, const int32_t* seq_ids_host,
+                             const int32_t* positions_host);
+/* Quantizes and stores the step's K and V rows ([n_tok][n_head*d_head] f32,
+ * device) for `layer`, bit-exact to BlockQ8_0::pack (kv_quant/q8_0.rs:40). */
+VKB_API vkb_status vkb_kv_append(vkb_kv_pool* pool, int32_t layer, const float* k_dev, const float* v_dev);
+/* Causal self-attention of the step's queries (q_dev [n_tok][n_head*d_head]
+ * f32, already scaled by d_head^-0.5) over their own stream's cached keys
+ * 0..position; ctx_out_dev [n_tok][n_head*d_head] in out_dtype. Online
+ * softmax in fp32 over the int8 pages gathered through the page table. */
+VKB_API vkb_status vkb_kv_attention(vkb_kv_pool* pool, int32_t layer, const float* q_dev,
+                            void* ctx_out_dev, int out_dtype);
+/* Frees every page of one stream (SEQUENCE layout). */
+VKB_API vkb_status vkb_kv_release_seq(vkb_kv_pool* pool, int32_t seq_id);
+/* release_layer (paged_quant.rs:500): REFERENCE layout only. */
+VKB_API vkb_status vkb_kv_release_layer(vkb_kv_pool* pool, int32_t layer);
+/* reset (paged_quant.rs:489): empties the table, zeroes pages, rebuilds the free list. */
+VKB_API vkb_status vkb_kv_reset(vkb_kv_pool* pool);
+/* GpuPagedKvCacheOps::upload_page_table: installs an explicit page table
+ * (SEQUENCE layout, [n_stream][pages_per_stream] int32, -1 = empty) and marks
+ * the listed pages in use. */
+VKB_API vkb_status vkb_kv_set_page_table(vkb_kv_pool* pool, const int32_t* table_host, size_t len);
+/* Introspection for parity tests (synchronous). */
+VKB_API size_t vkb_kv_table_len(const vkb_kv_pool* pool);
+VKB_API vkb_status vkb_kv_page_table(const vkb_kv_pool* pool, int64_t* out_host, size_t len);
+VKB_API int32_t vkb_kv_pages_in_use(const vkb_kv_pool* pool);
+VKB_API size_t vkb_kv_page_bytes(const vkb_kv_pool* pool);      /* on-wire bytes of one K (or V) page */
+VKB_API size_t vkb_kv_on_wire_bytes(const vkb_kv_pool* pool);   /* on_wire_storage_bytes, paged_quant.rs:382 */
+/* On-wire bytes (reference block order, 34-byte Q8_0 blocks) of one page of
+ * `layer` (SEQUENCE layout; the layer is ignored for REFERENCE layout). */
+VKB_API vkb_status vkb_kv_read_page(const vkb_kv_pool* pool, int32_t layer, int32_t page,
+                            void* k_host, void* v_host);
+/* read_step (paged_quant.rs:448): dequantized K and V rows; VKB_ERROR_INVALID_ARGUMENT
+ * when out of range, VKB_ERROR_OTHER when the slot was never written. */
+VKB_API vkb_status vkb_kv_read_step(const vkb_kv_pool* pool, int32_t layer, int32_t t, int32_t s,
+                            float* k_host, float* v_host);
+
+/* ---- dense attention (cross-attention and the encoder) ------------------- */
+
+/* ctx[i] = softmax(q[i] . K_s^T) V_s per head, for n_tok query rows where row
+ * i belongs to stream seq_of_tok_dev[i] (device int32). K_s / V_s are the
+ * stream's dense rows s*n_ctx .. s*n_ctx+n_ctx-1 of [*][n_head*d_head]:
+ *   kv_dtype VKB_DT_F16   : k_dev / v_dev are f16 rows, scales unused (NULL);
+ *   kv_dtype VKB_KV_Q8_0  : k_dev / v_dev are int8 quants, k_scale_dev /
+ *                           v_scale_dev the f16 scale per 32 channels
+ *                           (the layout vkb_quantize_rows_q8_0 writes).
+ * q is f32 and already scaled by d_head^-0.5; no mask (cross-attention,
+ * whisper/nn.rs:209 with causal=false). ctx_out is f32 or f16. */
+VKB_API vkb_status vkb_attention_dense(vkb_context* ctx, int32_t n_tok, int32_t n_head, int32_t d_head,
+                               const float* q_dev, const int32_t* seq_of_tok_dev,
+                               const void* k_dev, const void* v_dev,
+                               const void* k_scale_dev, const void* v_scale_dev,
+                               int32_t n_ctx, int32_t kv_dtype, void* ctx_out_dev, int32_t out_dtype);
+
+/* Quantizes f32 rows [n_rows][width] (width % 32 == 0) into int8 quants
+ * q_dev [n_rows][width] and f16 scales d_dev [n_rows][width/32] with the
+ * arithmetic of BlockQ8_0::pack (crates/vokra-core/src/kv_quant/q8_0.rs:40),
+ * bit-exact. Used for the cross-attention K/V store. */
+VKB_API vkb_status vkb_quantize_rows_q8_0(vkb_context* ctx, const float* x_dev, int64_t n_rows, int32_t width,
+                                  void* q_dev, void* d_dev);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VKB200_H */

@@ -1,0 +1,267 @@
+"""Paged quantized KV cache on the B200: bit-exact Q8_0 bytes and page tables
+against the oracle QuantizedPagedKvCache, and decode attention over the pages."""
+import numpy as np
+import pytest
+
+from oracle import py as o
+from vokra_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to("cuda:0")
+
+
+def _rows(rng, n, w):
+    x = rng.standard_normal((n, w)).astype(np.float32)
+    # edge blocks: all-zero, huge, tiny, one NaN, exact ties
+    x[0, :32] = 0.0
+    x[0, 32:64] = 1e30
+    if n > 1:
+        x[1, :32] = 1e-30
+        x[1, 40] = np.nan
+        x[1, 64:96] = np.float32(127.0) * np.arange(32, dtype=np.float32) / 64
+    return x
+
+
+def test_append_bytes_and_page_table_match_reference_layout(ctx):
+    from vokra_b200 import ops
+    n_layer, n_head, d_head, n_stream, max_time, bs = 2, 2, 32, 3, 12, 4
+    dims = ops.KvDims(n_layer, n_head, d_head, n_stream, 1, max_time)
+    dev = ops.QuantizedPagedKvCache(ctx, dims, bs, _lib.KV_Q8_0, _lib.KV_LAYOUT_REFERENCE)
+    ref = o.PagedKv(n_layer, n_head, d_head, n_stream, 1, max_time, bs, 3)
+    w = n_head * d_head
+    rng = np.random.default_rng(0)
+    steps = [([0, 0, 1], [0, 1, 0]), ([0, 1, 2], [2, 1, 0]), ([2], [1]), ([1, 1, 1, 1], [2, 3, 4, 5])]
+    for seqs, poss in steps:
+        dev.begin_step(seqs, poss)
+        for layer in range(n_layer):
+            k = _rows(rng, len(seqs), w)
+            v = _rows(rng, len(seqs), w)
+            dev.append(layer, _dev(k), _dev(v))
+            for i, (s, t) in enumerate(zip(seqs, poss)):
+                assert ref.append_step(layer, t, s, 0, k[i], v[i]) == 0
+        ctx.synchronize()
+        assert np.array_equal(dev.page_table(), ref.page_table())
+    assert dev.pages_in_use() == ref.pages_in_use()
+    assert dev.on_wire_storage_bytes() == ref.on_wire_storage_bytes()
+    for pid in range(ref.page_table().size):
+        dk, dv = dev.read_page(pid)
+        rk, rv = ref.page(pid)
+        assert np.array_equal(dk, rk), pid
+        assert np.array_equal(dv, rv), pid
+    kk, vv = dev.read_step(1, 3, 1)
+    rk, rv = ref.read_step(1, 3, 1)
+    assert np.array_equal(kk, rk) and np.array_equal(vv, rv)
+    dev.release_layer(0)
+    ref.release_layer(0)
+    assert np.array_equal(dev.page_table(), ref.page_table())
+    dev.reset()
+    ref.reset()
+    assert dev.pages_in_use() == 0 and dev.read_step(0, 0, 0) is None
+
+
+def test_reference_layout_exhaustion(ctx):
+    from vokra_b200 import ops
+    dims = ops.KvDims(1, 1, 32, 1, 1, 4)
+    c = ops.QuantizedPagedKvCache(ctx, dims, 4, _lib.KV_Q8_0, _lib.KV_LAYOUT_REFERENCE)
+    with pytest.raises(ops.VkbError) as e:
+        c.begin_step([0], [4])
+    assert e.value.code == _lib.ERROR_INVALID_ARGUMENT
+    with pytest.raises(ops.VkbError) as e:
+        ops.QuantizedPagedKvCache(ctx, dims, 4, _lib.KV_FP32)
+    assert e.value.code == _lib.ERROR_INVALID_ARGUMENT
+    with pytest.raises(ops.VkbError) as e:
+        ops.QuantizedPagedKvCache(ctx, ops.KvDims(1, 1, 33, 1, 1, 4), 4, _lib.KV_Q8_0)
+    assert e.value.code == _lib.ERROR_INVALID_ARGUMENT
+
+
+def test_sequence_pool_exhaustion_is_reported(ctx):
+    from vokra_b200 import ops
+    dims = ops.KvDims(2, 2, 32, 4, 1, 64)
+    c = ops.QuantizedPagedKvCache(ctx, dims, 16, _lib.KV_Q8_0, _lib.KV_LAYOUT_SEQUENCE, n_pages=2)
+    c.begin_step([0, 1], [0, 0])
+    with pytest.raises(ops.VkbError) as e:
+        c.begin_step([2], [0])
+    assert e.value.code == _lib.ERROR_KV_CACHE_EXHAUSTED
+    c.release_seq(0)
+    c.begin_step([2], [0])
+    assert c.pages_in_use() == 2
+
+
+def _oracle_attention(kv_rows_k, kv_rows_v, q, n_head, causal_pos):
+    # q: [n_q, w] with positions causal_pos[i]; keys 0..pos
+    out = np.zeros_like(q)
+    for i in range(q.shape[0]):
+        L = causal_pos[i] + 1
+        out[i] = o.attention(q[i:i + 1], kv_rows_k[:L], kv_rows_v[:L], n_head)[0]
+    return out
+
+
+@pytest.mark.parametrize("n_head,d_head", [(2, 64), (20, 64), (8, 64)])
+def test_paged_attention_sequence_layout(ctx, n_head, d_head):
+    import torch
+    from vokra_b200 import ops
+    rng = np.random.default_rng(n_head)
+    n_layer, n_seq, max_time, bs = 2, 5, 200, 16
+    w = n_head * d_head
+    dims = ops.KvDims(n_layer, n_head, d_head, n_seq, 1, max_time)
+    pool = ops.QuantizedPagedKvCache(ctx, dims, bs, _lib.KV_Q8_0, _lib.KV_LAYOUT_SEQUENCE)
+    # scatter pages by a seeded permutation (config 3)
+    pps = (max_time + bs - 1) // bs
+    perm = rng.permutation(n_seq * pps).astype(np.int32)
+    pool.set_page_table(perm)
+    lengths = [1, 17, 64, 130, 199]
+    Ks = [[rng.standard_normal((L, w)).astype(np.float32) for L in lengths] for _ in range(n_layer)]
+    Vs = [[rng.standard_normal((L, w)).astype(np.float32) for L in lengths] for _ in range(n_layer)]
+    # fill with a prefix step (4 tokens per stream) then one-token steps
+    maxlen = max(lengths)
+    t = 0
+    while t < maxlen:
+        seqs, poss = [], []
+        for s, L in enumerate(lengths):
+            take = 4 if t == 0 else 1
+            for j in range(t, min(L, t + take)):
+                seqs.append(s)
+                poss.append(j)
+        pool.begin_step(seqs, poss)
+        for layer in range(n_layer):
+            k = np.stack([Ks[layer][s][p] for s, p in zip(seqs, poss)])
+            v = np.stack([Vs[layer][s][p] for s, p in zip(seqs, poss)])
+            pool.append(layer, _dev(k), _dev(v))
+        t += 4 if t == 0 else 1
+    # final step: one query per stream at its last position (attends 0..L-1)
+    seqs = list(range(n_seq))
+    poss = [L - 1 for L in lengths]
+    # re-declare the last positions (the pages exist; appends overwrite identical bytes)
+    pool.begin_step(seqs, poss)
+    layer = 1
+    kl = np.stack([Ks[layer][s][p] for s, p in zip(seqs, poss)])
+    vl = np.stack([Vs[layer][s][p] for s, p in zip(seqs, poss)])
+    pool.append(layer, _dev(kl), _dev(vl))
+    q = rng.standard_normal((n_seq, w)).astype(np.float32) * np.float32(d_head ** -0.5)
+    out = torch.zeros((n_seq, w), dtype=torch.float32, device="cuda:0")
+    pool.attention(layer, _dev(q), out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for s, L in enumerate(lengths):
+        kd = o.kv_unpack(3, o.kv_pack(3, Ks[layer][s])).reshape(L, w)
+        vd = o.kv_unpack(3, o.kv_pack(3, Vs[layer][s])).reshape(L, w)
+        ref = o.attention(q[s:s + 1], kd, vd, n_head)[0]
+        assert np.max(np.abs(got[s] - ref)) <= 1e-4, (s, np.max(np.abs(got[s] - ref)))
+
+
+def test_paged_attention_prefix_causal(ctx):
+    import torch
+    from vokra_b200 import ops
+    rng = np.random.default_rng(9)
+    n_head, d_head = 4, 64
+    w = n_head * d_head
+    dims = ops.KvDims(1, n_head, d_head, 2, 1, 64)
+    pool = ops.QuantizedPagedKvCache(ctx, dims, 16, _lib.KV_Q8_0, _lib.KV_LAYOUT_SEQUENCE)
+    seqs = [0, 0, 0, 0, 1, 1, 1, 1, 1, 1]
+    poss = [0, 1, 2, 3, 0, 1, 2, 3, 4, 5]
+    k = rng.standard_normal((10, w)).astype(np.float32)
+    v = rng.standard_normal((10, w)).astype(np.float32)
+    q = rng.standard_normal((10, w)).astype(np.float32) * np.float32(0.125)
+    pool.begin_step(seqs, poss)
+    pool.append(0, _dev(k), _dev(v))
+    out = torch.zeros((10, w), dtype=torch.float32, device="cuda:0")
+    pool.attention(0, _dev(q), out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    kd = o.kv_unpack(3, o.kv_pack(3, k)).reshape(10, w)
+    vd = o.kv_unpack(3, o.kv_pack(3, v)).reshape(10, w)
+    for base, n in [(0, 4), (4, 6)]:
+        ref = o.attention(q[base:base + n], kd[base:base + n], vd[base:base + n], n_head, causal=True, q_off=0)
+        assert np.max(np.abs(got[base:base + n] - ref)) <= 1e-4
+
+
+def test_reference_layout_attention(ctx):
+    import torch
+    from vokra_b200 import ops
+    rng = np.random.default_rng(4)
+    n_head, d_head, n_stream = 2, 64, 3
+    w = n_head * d_head
+    dims = ops.KvDims(1, n_head, d_head, n_stream, 1, 40)
+    pool = ops.QuantizedPagedKvCache(ctx, dims, 4, _lib.KV_Q8_0, _lib.KV_LAYOUT_REFERENCE)
+    L = 23
+    K = rng.standard_normal((n_stream, L, w)).astype(np.float32)
+    V = rng.standard_normal((n_stream, L, w)).astype(np.float32)
+    for t in range(L):
+        pool.begin_step(list(range(n_stream)), [t] * n_stream)
+        pool.append(0, _dev(K[:, t]), _dev(V[:, t]))
+    q = rng.standard_normal((n_stream, w)).astype(np.float32) * np.float32(0.125)
+    pool.begin_step(list(range(n_stream)), [L - 1] * n_stream)
+    pool.append(0, _dev(K[:, L - 1]), _dev(V[:, L - 1]))
+    out = torch.zeros((n_stream, w), dtype=torch.float16, device="cuda:0")
+    pool.attention(0, _dev(q), out)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    for s in range(n_stream):
+        kd = o.kv_unpack(3, o.kv_pack(3, K[s])).reshape(L, w)
+        vd = o.kv_unpack(3, o.kv_pack(3, V[s])).reshape(L, w)
+        ref = o.attention(q[s:s + 1], kd, vd, n_head)[0]
+        assert np.max(np.abs(got[s] - ref)) <= 2e-3
+
+
+@pytest.mark.parametrize("kv", ["f16", "q8"])
+def test_dense_cross_attention(ctx, kv):
+    import torch
+    from vokra_b200 import ops
+    rng = np.random.default_rng(5)
+    n_head, d_head, n_ctx, n_seq = 20, 64, 1500, 3
+    w = n_head * d_head
+    K = rng.standard_normal((n_seq * n_ctx, w)).astype(np.float32)
+    V = rng.standard_normal((n_seq * n_ctx, w)).astype(np.float32)
+    q = rng.standard_normal((5, w)).astype(np.float32) * np.float32(0.125)
+    seq_of_tok = np.array([0, 2, 1, 2, 0], np.int32)
+    out = torch.zeros((5, w), dtype=torch.float32, device="cuda:0")
+    st = torch.from_numpy(seq_of_tok).to("cuda:0")
+    if kv == "f16":
+        kt, vt = _dev(K).half(), _dev(V).half()
+        ops.attention_dense(ctx, _dev(q), st, kt, vt, n_ctx, n_head, d_head, out)
+        Kr = K.astype(np.float16).astype(np.float32)
+        Vr = V.astype(np.float16).astype(np.float32)
+    else:
+        kq = torch.zeros((n_seq * n_ctx, w), dtype=torch.int8, device="cuda:0")
+        vq = torch.zeros_like(kq)
+        kd = torch.zeros((n_seq * n_ctx, w // 32), dtype=torch.float16, device="cuda:0")
+        vd = torch.zeros_like(kd)
+        ops.quantize_rows_q8_0(ctx, _dev(K), kq, kd)
+        ops.quantize_rows_q8_0(ctx, _dev(V), vq, vd)
+        torch.cuda.synchronize()
+        # bit-exact against BlockQ8_0::pack
+        blocks = o.kv_pack(3, K[:64]).reshape(-1, 34)
+        assert np.array_equal(kq[:64].cpu().numpy().reshape(-1, 32).view(np.uint8), blocks[:, 2:])
+        assert np.array_equal(kd[:64].cpu().numpy().reshape(-1).view(np.uint16),
+                              blocks[:, :2].copy().view(np.uint16).reshape(-1))
+        ops.attention_dense(ctx, _dev(q), st, kq, vq, n_ctx, n_head, d_head, out, k_scale=kd, v_scale=vd)
+        Kr = o.kv_unpack(3, o.kv_pack(3, K)).reshape(K.shape)
+        Vr = o.kv_unpack(3, o.kv_pack(3, V)).reshape(V.shape)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for i, s in enumerate(seq_of_tok):
+        ref = o.attention(q[i:i + 1], Kr[s * n_ctx:(s + 1) * n_ctx], Vr[s * n_ctx:(s + 1) * n_ctx], n_head)[0]
+        assert np.max(np.abs(got[i] - ref)) <= 1e-4
+
+
+@pytest.mark.parametrize("mode", [_lib.KV_Q4_0, _lib.KV_Q5_0, _lib.KV_Q8_0])
+def test_dequant_gemv_m3_04_shapes(ctx, kats, mode):
+    from vokra_b200 import ops
+    gemv = ops.KvQuantDequantGemvOps(ctx)
+    for n_rows, nbpr in kats["m3_04_shapes"]:
+        per = nbpr * 32
+        rng = np.random.default_rng(0xD3 ^ (n_rows * 131 + nbpr))
+        a = rng.uniform(-1, 1, (n_rows, per)).astype(np.float32)
+        x = rng.uniform(-1, 1, per).astype(np.float32)
+        blocks = o.kv_pack(mode, a)
+        rc, ref = o.dequant_gemv(mode, blocks, n_rows, nbpr, x)
+        assert rc == 0
+        got = gemv.fused_dequant_gemv(mode, blocks, n_rows, nbpr, x)
+        assert np.max(np.abs(got - ref)) <= kats["dequant_gemv_atol"]
+    with pytest.raises(ops.VkbError) as e:
+        gemv.fused_dequant_gemv(_lib.KV_FP32, b"", 0, 0, np.zeros(0, np.float32))
+    assert e.value.code == _lib.ERROR_INVALID_ARGUMENT

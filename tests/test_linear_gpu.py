@@ -1,0 +1,116 @@
+"""Quantized Linear on the B200 (GEMV and tcgen05 GEMM paths) against the CPU
+oracle's route R1 (dequantize, then the ascending-k FMA chain of gemm_f32)."""
+import numpy as np
+import pytest
+
+from oracle import py as o
+from vokra_b200 import _lib, synth
+
+pytestmark = pytest.mark.gpu
+
+TAGS = [synth.Q4_0, synth.Q8_0, synth.Q4_K]
+
+
+def _weights(tag, n, k, seed):
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal(n * k).astype(np.float32) * np.float32(0.02))
+    return synth.quantize(tag, w)
+
+
+def _rel_rms(a, b):
+    return float(np.sqrt(np.mean((a - b) ** 2)) / (np.sqrt(np.mean(b ** 2)) + 1e-30))
+
+
+def _run(ctx, tag, n, k, m, seed=0, bias=True, a_f16=False, out_f16=False, epi=_lib.EPI_NONE, scale=1.0):
+    import torch
+    from vokra_b200 import ops
+    wq = _weights(tag, n, k, seed)
+    rng = np.random.default_rng(seed + 1)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = (rng.standard_normal(n).astype(np.float32) * np.float32(0.1)) if bias else None
+    res = rng.standard_normal((m, n)).astype(np.float32)
+    w = ops.Weight(ctx, tag, n, k, wq)
+    dev = "cuda:0"
+    at = torch.from_numpy(a).to(dev)
+    if a_f16:
+        at = at.half()
+    bt = None if b is None else torch.from_numpy(b).to(dev)
+    out = torch.zeros((m, n), dtype=torch.float16 if out_f16 else torch.float32, device=dev)
+    rt = torch.from_numpy(res).to(dev) if epi == _lib.EPI_RESIDUAL else None
+    ops.linear(ctx, w, at, out, bias=bt, epilogue=epi, residual=rt, scale=scale)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    a_ref = at.float().cpu().numpy()
+    ref = o.linear_q(tag, a_ref, wq, n, k, b)
+    if epi == _lib.EPI_GELU:
+        ref = o.gelu(ref)
+    elif epi == _lib.EPI_SCALE:
+        ref = ref * np.float32(scale)
+    elif epi == _lib.EPI_RESIDUAL:
+        ref = res + ref
+    return got, ref
+
+
+@pytest.mark.parametrize("tag", TAGS)
+@pytest.mark.parametrize("m", [1, 2, 3, 4])
+def test_gemv_path_matches_oracle(ctx, tag, m):
+    for (k, n) in [(256, 128), (512, 300), (1280, 1280)]:
+        got, ref = _run(ctx, tag, n, k, m, seed=k + n)
+        assert np.max(np.abs(got - ref)) <= 1e-4 * max(1.0, np.max(np.abs(ref)))
+        assert _rel_rms(got, ref) <= 1e-5
+
+
+@pytest.mark.parametrize("tag", TAGS)
+@pytest.mark.parametrize("m", [5, 8, 33, 64, 100, 256, 300, 1500])
+def test_tensor_core_path_matches_oracle(ctx, tag, m):
+    # f16 operands on tcgen05 with fp32 accumulation: 1e-3 relative RMS, 1e-2 max-abs.
+    for (k, n) in [(256, 128), (1280, 384)]:
+        got, ref = _run(ctx, tag, n, k, m, seed=7 * k + n)
+        assert _rel_rms(got, ref) <= 1e-3, (k, n)
+        assert np.max(np.abs(got - ref)) <= 1e-2, (k, n)
+
+
+@pytest.mark.parametrize("tag", TAGS)
+def test_tensor_core_large_k_and_ragged_n(ctx, tag):
+    got, ref = _run(ctx, tag, 1300, 5120, 96, seed=11)
+    assert _rel_rms(got, ref) <= 1e-3
+    assert np.max(np.abs(got - ref)) <= 2e-2
+
+
+@pytest.mark.parametrize("m", [2, 64])
+@pytest.mark.parametrize("epi", [_lib.EPI_GELU, _lib.EPI_SCALE, _lib.EPI_RESIDUAL])
+def test_epilogues(ctx, m, epi):
+    got, ref = _run(ctx, synth.Q4_0, 256, 512, m, epi=epi, scale=0.125)
+    tol = 1e-3 if m > 4 else 1e-5
+    assert _rel_rms(got, ref) <= tol
+
+
+def test_f16_in_f16_out_no_bias(ctx):
+    got, ref = _run(ctx, synth.Q8_0, 384, 512, 128, bias=False, a_f16=True, out_f16=True)
+    assert _rel_rms(got, ref) <= 2e-3
+
+
+def test_host_gemm_q_f32_contract(ctx):
+    from vokra_b200 import ops
+    n, k, m = 256, 512, 3
+    wq = _weights(synth.Q4_K, n, k, 3)
+    rng = np.random.default_rng(4)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    out = np.zeros((m, n), np.float32)
+    ops.gemm_q_f32(ctx, m, n, k, a, wq, synth.Q4_K, b, out)
+    ref = o.linear_q(synth.Q4_K, a, wq, n, k, b)
+    assert np.max(np.abs(out - ref)) <= 1e-4
+
+
+def test_rejections(ctx):
+    from vokra_b200 import ops
+    with pytest.raises(ops.VkbError) as e:
+        ops.Weight(ctx, synth.Q4_0, 4, 96, synth.quantize(synth.Q4_0, np.zeros(4 * 96, np.float32)))
+    assert e.value.code == _lib.ERROR_UNSUPPORTED_OP
+    with pytest.raises(ops.VkbError) as e:
+        ops.Weight(ctx, synth.Q4_0, 4, 64, b"\0" * 10)
+    assert e.value.code == _lib.ERROR_INVALID_ARGUMENT
+    with pytest.raises(ops.VkbError) as e:
+        ops.Weight(ctx, 6, 4, 64, b"\0" * 10)
+    assert e.value.code == _lib.ERROR_UNSUPPORTED_OP

@@ -1,0 +1,248 @@
+// attn_core.cuh — decode attention over K/V rows fetched through a policy
+// (paged int8 pages, dense int8 or dense f16), fp32 online softmax.
+//
+// Work decomposition: one CTA per (query group, key split). A query group is
+// up to MAXQ consecutive query tokens of one stream (the decode step's token,
+// or a prefix). The CTA holds R row-groups of W/16 threads; a row-group owns
+// one key at a time and each of its threads owns 16 consecutive channels, so
+// the d_head/16 threads of a head reduce their partial q.k with two shuffles.
+// Row-groups walk keys j = j0 + g, j0 + g + R, ...; at the end the R partial
+// (max, sum, acc) triples are merged in shared memory. With one split the
+// CTA writes ctx = acc / sum, else the triple goes to a workspace and
+// attn_combine_kernel merges the splits.
+#pragma once
+#include "common.cuh"
+
+namespace vkb {
+
+constexpr int ATTN_MAX_THREADS = 512;
+
+// 16 int8 values of a 32-bit-word quadruple -> floats, exactly, without I2F:
+// the byte is placed in the low mantissa of 2^23 and the bias removed.
+__device__ __forceinline__ void i8x16_to_f32(uint4 q, float (&f)[16]) {
+    uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+            f[4 * i + b] = __uint_as_float(__byte_perm(w[i], 0x4B000000u, 0x7440u + b)) - 8388736.0f;
+    }
+}
+
+// ---- fetch policies: value of 16 channels [c0, c0+16) of key j ------------
+struct FetchPagedQ8 {
+    const int8_t* kq;
+    const __half* kd;
+    const int8_t* vq;
+    const __half* vd;
+    const int32_t* table;
+    int W;
+    int layout;      // 0 reference, 1 sequence
+    int table_base;  // reference: layer*ppl ; sequence: seq*ppseq
+    int bs;
+    int n_sc;        // slots per token row (reference: n_stream; sequence: 1)
+    int slot;        // reference: stream index ; sequence: 0
+    int64_t arena_row0;  // sequence: layer*n_pages*rpp ; reference: 0
+    __device__ __forceinline__ int64_t row(int j) const {
+        int pid = table[table_base + j / bs];
+        return arena_row0 + ((int64_t)pid * bs + (j % bs)) * n_sc + slot;
+    }
+    __device__ __forceinline__ void load(int64_t rw, int c0, bool is_v, float (&f)[16], float& scale) const {
+        const int8_t* q = (is_v ? vq : kq) + rw * W + c0;
+        const __half* d = (is_v ? vd : kd) + rw * (W / 32) + c0 / 32;
+        uint4 v = __ldg(reinterpret_cast<const uint4*>(q));
+        scale = __half2float(__ldg(d));
+        i8x16_to_f32(v, f);
+    }
+};
+
+struct FetchDenseQ8 {
+    const int8_t* kq;
+    const __half* kd;
+    const int8_t* vq;
+    const __half* vd;
+    int W;
+    int64_t seq_row0;  // seq * n_ctx
+    __device__ __forceinline__ int64_t row(int j) const { return seq_row0 + j; }
+    __device__ __forceinline__ void load(int64_t rw, int c0, bool is_v, float (&f)[16], float& scale) const {
+        const int8_t* q = (is_v ? vq : kq) + rw * W + c0;
+        const __half* d = (is_v ? vd : kd) + rw * (W / 32) + c0 / 32;
+        uint4 v = __ldg(reinterpret_cast<const uint4*>(q));
+        scale = __half2float(__ldg(d));
+        i8x16_to_f32(v, f);
+    }
+};
+
+struct FetchDenseF16 {
+    const __half* k;
+    const __half* v;
+    int W;
+    int64_t seq_row0;
+    __device__ __forceinline__ int64_t row(int j) const { return seq_row0 + j; }
+    __device__ __forceinline__ void load(int64_t rw, int c0, bool is_v, float (&f)[16], float& scale) const {
+        const __half* p = (is_v ? v : k) + rw * W + c0;
+        uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+        uint4 b = __ldg(reinterpret_cast<const uint4*>(p + 8));
+        uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float2 t = __half22float2(*reinterpret_cast<__half2*>(&w[i]));
+            f[2 * i] = t.x;
+            f[2 * i + 1] = t.y;
+        }
+        scale = 1.0f;
+    }
+};
+
+// Per-CTA query group descriptor.
+struct AttnGroup {
+    int first_tok;  // index of the first query row in q / ctx
+    int n_q;        // queries in the group (<= MAXQ)
+    int seq;        // stream
+    int pos0;       // absolute position of the first query; query i sees keys 0..pos0+i
+};
+
+// Partial layout in the workspace, per (group, split, query):
+//   acc[W] then m[H] then l[H]  (floats)
+template <class F, int MAXQ>
+__device__ __forceinline__ void attn_body(const F& fetch, const float* __restrict__ q, const AttnGroup& g, int n_head,
+                                          int d_head, int W, int key_begin, int key_end, int split, int n_splits,
+                                          void* ctx_out, int out_f16, float* ws) {
+    extern __shared__ float sm[];
+    const int tpr = W / 16;                // threads per key row
+    const int R = blockDim.x / tpr;        // row-groups
+    const int tid = threadIdx.x;
+    const int rg = tid / tpr, tr = tid % tpr;
+    const int c0 = tr * 16;
+    const int tph = d_head / 16;           // threads per head
+    const bool active = rg < R;
+
+    float qv[MAXQ][16];
+    float m[MAXQ], l[MAXQ], acc[MAXQ][16];
+#pragma unroll
+    for (int i = 0; i < MAXQ; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) acc[i][c] = 0.0f;
+        if (active && i < g.n_q) {
+            const float4* q4 = reinterpret_cast<const float4*>(q + (int64_t)(g.first_tok + i) * W + c0);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float4 t = q4[c];
+                qv[i][4 * c] = t.x; qv[i][4 * c + 1] = t.y; qv[i][4 * c + 2] = t.z; qv[i][4 * c + 3] = t.w;
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) qv[i][c] = 0.0f;
+        }
+    }
+
+    // Every row-group runs the same trip count so that the head shuffles
+    // always see full warps (a warp can hold threads of two row-groups).
+    const int n_iter = (key_end - key_begin + R - 1) / R;
+    if (active) {
+        for (int it = 0; it < n_iter; ++it) {
+            const int j = key_begin + rg + it * R;
+            const bool valid = j < key_end;
+            float kf[16], vf[16], ks = 0.0f, vs = 0.0f;
+            if (valid) {
+                int64_t rw = fetch.row(j);
+                fetch.load(rw, c0, false, kf, ks);
+                fetch.load(rw, c0, true, vf, vs);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 16; ++c) { kf[c] = 0.0f; vf[c] = 0.0f; }
+            }
+#pragma unroll
+            for (int i = 0; i < MAXQ; ++i) {
+                if (i >= g.n_q) break;
+                float part = 0.0f;
+#pragma unroll
+                for (int c = 0; c < 16; ++c) part = fmaf(qv[i][c], kf[c], part);
+                part *= ks;
+                // sum over the head's threads (consecutive, aligned to tph)
+                for (int o = 1; o < tph; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+                if (!valid || j > g.pos0 + i) continue;  // causal: key after this query
+                float mn = fmaxf(m[i], part);
+                float corr = __expf(m[i] - mn);
+                float p = __expf(part - mn);
+                l[i] = l[i] * corr + p;
+                float pv = p * vs;
+#pragma unroll
+                for (int c = 0; c < 16; ++c) acc[i][c] = fmaf(pv, vf[c], acc[i][c] * corr);
+                m[i] = mn;
+            }
+        }
+    }
+
+    // Merge the R row-groups: row-group 0 gathers (m, l, acc) of the others.
+    const int H = n_head;
+    float* s_acc = sm;                       // [R][MAXQ][W]
+    float* s_m = sm + (size_t)R * MAXQ * W;  // [R][MAXQ][H]
+    float* s_l = s_m + (size_t)R * MAXQ * H;
+    const int head = c0 / d_head;
+    if (active) {
+#pragma unroll
+        for (int i = 0; i < MAXQ; ++i) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) s_acc[((size_t)rg * MAXQ + i) * W + c0 + c] = acc[i][c];
+            if ((tr % tph) == 0) {
+                s_m[((size_t)rg * MAXQ + i) * H + head] = m[i];
+                s_l[((size_t)rg * MAXQ + i) * H + head] = l[i];
+            }
+        }
+    }
+    __syncthreads();
+    if (rg == 0) {
+#pragma unroll
+        for (int i = 0; i < MAXQ; ++i) {
+            if (i >= g.n_q) break;
+            float M = -INFINITY;
+            for (int r = 0; r < R; ++r) M = fmaxf(M, s_m[((size_t)r * MAXQ + i) * H + head]);
+            float L = 0.0f, o[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) o[c] = 0.0f;
+            for (int r = 0; r < R; ++r) {
+                float mr = s_m[((size_t)r * MAXQ + i) * H + head];
+                float w = (mr == -INFINITY) ? 0.0f : __expf(mr - M);
+                L += s_l[((size_t)r * MAXQ + i) * H + head] * w;
+#pragma unroll
+                for (int c = 0; c < 16; ++c) o[c] += s_acc[((size_t)r * MAXQ + i) * W + c0 + c] * w;
+            }
+            const int64_t tok = g.first_tok + i;
+            if (n_splits == 1) {
+                float inv = 1.0f / L;
+                if (out_f16) {
+                    __half* dst = reinterpret_cast<__half*>(ctx_out) + tok * W + c0;
+#pragma unroll
+                    for (int c = 0; c < 16; c += 2)
+                        *reinterpret_cast<__half2*>(dst + c) = __floats2half2_rn(o[c] * inv, o[c + 1] * inv);
+                } else {
+                    float* dst = reinterpret_cast<float*>(ctx_out) + tok * W + c0;
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) dst[c] = o[c] * inv;
+                }
+            } else {
+                // ws layout per (token, split): acc[W] m[H] l[H]
+                float* p = ws + ((size_t)tok * n_splits + split) * (W + 2 * H);
+#pragma unroll
+                for (int c = 0; c < 16; ++c) p[c0 + c] = o[c];
+                if ((tr % tph) == 0) {
+                    p[W + head] = M;
+                    p[W + H + head] = L;
+                }
+            }
+        }
+    }
+}
+
+// Merges split partials: one thread per (token, channel).
+__global__ void attn_combine_kernel(const float* __restrict__ ws, int n_tok, int n_splits, int n_head, int d_head,
+                                    void* ctx_out, int out_f16);
+
+inline size_t attn_smem_bytes(int R, int maxq, int W, int H) {
+    return (size_t)R * maxq * (W + 2 * H) * sizeof(float);
+}
+
+}  // namespace vkb

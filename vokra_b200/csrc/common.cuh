@@ -1,0 +1,179 @@
+// common.cuh — shared host/device helpers of libvkb200 (sm_100a only).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+#include <cstddef>
+#include <cstring>
+#include <string>
+#include <vector>
+#include <stdexcept>
+
+#include "../../include/vkb200.h"
+
+namespace vkb {
+
+// Error carried through the C++ layer and converted to vkb_status at the ABI.
+struct Error : std::runtime_error {
+    vkb_status code;
+    Error(vkb_status c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+[[noreturn]] inline void fail(vkb_status c, const std::string& m) { throw Error(c, m); }
+
+inline void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess)
+        fail(VKB_ERROR_BACKEND_UNAVAILABLE, std::string(what) + ": " + cudaGetErrorString(e));
+}
+#define VKB_CUDA(x) ::vkb::cuda_check((x), #x)
+
+void set_last_error(const std::string& m);
+
+// Runs `f` and converts every exception into a status (the ffi_guard firewall).
+template <class F>
+vkb_status guard(F&& f) {
+    try {
+        f();
+        return VKB_OK;
+    } catch (const Error& e) {
+        set_last_error(e.what());
+        return e.code;
+    } catch (const std::exception& e) {
+        set_last_error(std::string("internal error: ") + e.what());
+        return VKB_ERROR_PANIC;
+    } catch (...) {
+        set_last_error("internal error: unknown exception");
+        return VKB_ERROR_PANIC;
+    }
+}
+
+// Device-memory buffer owned by RAII (allocated only at set-up time).
+struct DevBuf {
+    void* p = nullptr;
+    size_t n = 0;
+    DevBuf() = default;
+    explicit DevBuf(size_t bytes) { alloc(bytes); }
+    void alloc(size_t bytes) {
+        release();
+        if (bytes) VKB_CUDA(cudaMalloc(&p, bytes));
+        n = bytes;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+    }
+    ~DevBuf() { release(); }
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    DevBuf(DevBuf&& o) noexcept : p(o.p), n(o.n) { o.p = nullptr; o.n = 0; }
+    DevBuf& operator=(DevBuf&& o) noexcept {
+        release();
+        p = o.p; n = o.n; o.p = nullptr; o.n = 0;
+        return *this;
+    }
+    template <class T> T* as() const { return reinterpret_cast<T*>(p); }
+};
+
+}  // namespace vkb
+
+// The context: one per GPU. Owns a stream and a grow-at-setup workspace that
+// kernels with split reductions use for their partial sums.
+struct vkb_context {
+    int device = 0;
+    int sm_count = 148;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    uint64_t launches = 0;
+    vkb::DevBuf workspace;
+    vkb::DevBuf err_flag;  // int set by a kernel whose bounded wait gave up
+    void ensure_workspace(size_t bytes) {
+        if (workspace.n < bytes) {
+            VKB_CUDA(cudaStreamSynchronize(stream));
+            workspace.alloc(bytes);
+        }
+    }
+    void count(int n = 1) { launches += (uint64_t)n; }
+};
+
+namespace vkb {
+
+// ---------------------------------------------------------------------------
+// Device helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// IEEE single -> half, round to nearest even; restates the reference encoder
+// f32_to_f16_bits (crates/vokra-core/src/kv_quant/half.rs:80-155) so that the
+// stored scale bits match it exactly, including NaN canonicalisation.
+__host__ __device__ __forceinline__ uint16_t f32_to_f16_bits(float x) {
+    uint32_t bits;
+#ifdef __CUDA_ARCH__
+    bits = __float_as_uint(x);
+#else
+    memcpy(&bits, &x, 4);
+#endif
+    uint32_t sign = (bits >> 31) & 1u;
+    int exp_f32 = (int)((bits >> 23) & 0xffu);
+    uint32_t mant = bits & 0x7fffffu;
+    if (exp_f32 == 0xff) {
+        if (mant == 0) return (uint16_t)((sign << 15) | (0x1fu << 10));
+        return (uint16_t)((sign << 15) | (0x1fu << 10) | 0x200u);
+    }
+    if (exp_f32 == 0 && mant == 0) return (uint16_t)(sign << 15);
+    int e16 = exp_f32 - 127 + 15;
+    if (e16 >= 0x1f) return (uint16_t)((sign << 15) | (0x1fu << 10));
+    if (e16 >= 1) {
+        uint32_t rb = (mant >> 12) & 1u;
+        bool sticky = (mant & 0xfffu) != 0;
+        uint32_t tr = mant >> 13;
+        uint32_t r = tr + ((rb && (sticky || (tr & 1u))) ? 1u : 0u);
+        uint32_t e = (uint32_t)e16;
+        if (r == 0x400u) {
+            r = 0;
+            e += 1;
+            if (e >= 0x1fu) return (uint16_t)((sign << 15) | (0x1fu << 10));
+        }
+        return (uint16_t)((sign << 15) | (e << 10) | (r & 0x3ffu));
+    }
+    if (e16 < -10) return (uint16_t)(sign << 15);
+    uint32_t mi = mant | 0x800000u;
+    uint32_t sh = (uint32_t)(1 - e16) + 13u;
+    uint32_t rb = (mi >> (sh - 1)) & 1u;
+    bool sticky = (mi & ((1u << (sh - 1)) - 1u)) != 0;
+    uint32_t tr = mi >> sh;
+    uint32_t r = tr + ((rb && (sticky || (tr & 1u))) ? 1u : 0u);
+    if (r >= 0x400u) return (uint16_t)((sign << 15) | (1u << 10));
+    return (uint16_t)((sign << 15) | (r & 0x3ffu));
+}
+
+// Abramowitz & Stegun 7.1.26 erf with the reference's constants
+// (crates/vokra-backend-cpu/src/kernels/scalar.rs:127-157) and exact GELU
+// (scalar.rs:166). expf is CUDA's own.
+__device__ __forceinline__ float gelu_as(float v) {
+    const float P = 0.3275911f, A1 = 0.254829592f, A2 = -0.284496736f, A3 = 1.421413741f,
+                A4 = -1.453152027f, A5 = 1.061405429f;
+    float x = v * 0.70710678118654752f;
+    float sign = x < 0.0f ? -1.0f : 1.0f;
+    x = fabsf(x);
+    float t = 1.0f / (1.0f + P * x);
+    float poly = ((((A5 * t + A4) * t + A3) * t + A2) * t + A1) * t;
+    float y = 1.0f - poly * expf(-x * x);
+    return 0.5f * v * (1.0f + sign * y);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+
+}  // namespace vkb

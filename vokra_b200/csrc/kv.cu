@@ -1,0 +1,835 @@
+// kv.cu — the paged quantized KV cache on the device, its host page allocator,
+// the bit-exact Q8_0 append kernel, decode attention over the pages, dense
+// (cross-) attention, and the KvQuantDequantGemvOps arm.
+//
+// Host allocator semantics follow QuantizedPagedKvCache
+// (crates/vokra-core/src/cache/paged_quant.rs:152-560): the arena is allocated
+// up front, the free list is LIFO and initially pops 0, 1, 2, ..., pages are
+// acquired on first touch in (layer, token) order, reset zeroes every page
+// and rebuilds the free list, release_layer zeroes and frees one layer.
+//
+// Device page storage keeps the quants and the f16 scales of each token row in
+// two planes ("split planes"): row r of an arena has W int8 quants at
+// q + r*W and W/32 scales at d + r*(W/32). A row is one (token, stream) slot:
+// REFERENCE layout rows are ((page*bs + offset)*n_stream + stream); SEQUENCE
+// layout rows are (layer*n_pages + page)*bs + offset. vkb_kv_read_page
+// reassembles the reference's 34-byte on-wire blocks from the two planes.
+#include "common.cuh"
+#include "attn_core.cuh"
+#include <algorithm>
+
+using namespace vkb;
+
+struct vkb_kv_pool {
+    vkb_context* ctx = nullptr;
+    vkb_kv_pool_desc d{};
+    int W = 0, row_blocks = 0, ppl = 0, ppseq = 0, rpp = 0, n_arena = 1;
+    int64_t n_pages = 0, table_len = 0;
+    std::vector<int32_t> table;      // host mirror (-1 = empty)
+    std::vector<int32_t> free_list;  // LIFO
+    // device
+    DevBuf kq, kd, vq, vd;           // arena planes
+    DevBuf table_dev;
+    DevBuf rows_dev;                 // int64 [n_layer][max_step]: row of each step token per layer
+    DevBuf groups_dev;               // AttnGroup [max_groups]
+    DevBuf part_dev;                 // split partials of the attention
+    int max_step = 0;
+    // pinned staging
+    int32_t* h_table = nullptr;
+    int64_t* h_rows = nullptr;
+    AttnGroup* h_groups = nullptr;
+    cudaEvent_t staged = nullptr;
+    bool staged_pending = false;
+    // current step
+    int n_tok = 0, n_groups = 0, maxq = 1, splits = 1, keys_per_split = 0, max_keys = 0;
+    std::vector<int32_t> step_seq, step_pos;
+    int64_t rows_in_arena() const { return n_pages * rpp; }
+};
+
+namespace vkb {
+
+// ---------------------------------------------------------------------------
+// Append: one warp per 32-element block; the arithmetic of BlockQ8_0::pack
+// (crates/vokra-core/src/kv_quant/q8_0.rs:40-66) in IEEE fp32 with Rust's
+// NaN rules (max ignores NaN, clamp keeps NaN, NaN casts to 0).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void q8_0_block_warp(float x, int lane, int8_t* q_out, __half* d_out) {
+    float a = fabsf(x);
+    a = warp_max(a);
+    float amax = fmaxf(0.0f, a);
+    float d = amax == 0.0f ? 0.0f : amax / 127.0f;
+    float inv = d == 0.0f ? 0.0f : 1.0f / d;
+    float s = x * inv;
+    float c = s < -127.0f ? -127.0f : (s > 127.0f ? 127.0f : s);
+    int8_t qv = isnan(c) ? (int8_t)0 : (int8_t)(int)roundf(c);
+    q_out[lane] = qv;
+    if (lane == 0) *reinterpret_cast<uint16_t*>(d_out) = f32_to_f16_bits(d);
+}
+
+__global__ void kv_append_kernel(const float* __restrict__ k, const float* __restrict__ v,
+                                 const int64_t* __restrict__ rows, int n_tok, int W, int8_t* kq, __half* kd,
+                                 int8_t* vq, __half* vd) {
+    const int nb = W / 32;
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (gw >= (int64_t)n_tok * nb * 2) return;
+    const int is_v = (int)(gw / ((int64_t)n_tok * nb));
+    const int64_t rem = gw % ((int64_t)n_tok * nb);
+    const int tok = (int)(rem / nb), b = (int)(rem % nb);
+    const float* src = (is_v ? v : k) + (int64_t)tok * W + b * 32;
+    const int64_t row = rows[tok];
+    int8_t* q = (is_v ? vq : kq) + row * W + b * 32;
+    __half* d = (is_v ? vd : kd) + row * nb + b;
+    q8_0_block_warp(src[lane], lane, q, d);
+}
+
+// Quantizes dense rows [n_rows][W] into the two planes (same arithmetic).
+__global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t n_rows, int W, int8_t* q, __half* d) {
+    const int nb = W / 32;
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (gw >= n_rows * nb) return;
+    const int64_t row = gw / nb;
+    const int b = (int)(gw % nb);
+    q8_0_block_warp(x[row * W + b * 32 + lane], lane, q + row * W + b * 32, d + row * nb + b);
+}
+
+// ---------------------------------------------------------------------------
+// Attention kernels
+// ---------------------------------------------------------------------------
+template <int MAXQ>
+__global__ void paged_attn_kernel(FetchPagedQ8 f, const float* __restrict__ q, const AttnGroup* __restrict__ groups,
+                                  int n_head, int d_head, int keys_per_split, int n_splits, void* ctx_out,
+                                  int out_f16, float* ws, int per_seq_base, int ppseq) {
+    const AttnGroup g = groups[blockIdx.x];
+    const int split = blockIdx.y;
+    const int n_keys = g.pos0 + g.n_q;  // keys 0 .. last query's position
+    const int kb = split * keys_per_split;
+    const int ke = min(n_keys, kb + keys_per_split);
+    FetchPagedQ8 ff = f;
+    if (per_seq_base) ff.table_base = g.seq * ppseq;
+    else ff.slot = g.seq;
+    attn_body<FetchPagedQ8, MAXQ>(ff, q, g, n_head, d_head, f.W, kb, max(kb, ke), split, n_splits, ctx_out, out_f16,
+                                  ws);
+}
+
+template <class F>
+__global__ void dense_attn_kernel(F f, const float* __restrict__ q, const int32_t* __restrict__ seq_of_tok, int n_ctx,
+                                  int n_head, int d_head, int keys_per_split, int n_splits, void* ctx_out,
+                                  int out_f16, float* ws) {
+    AttnGroup g;
+    g.first_tok = blockIdx.x;
+    g.n_q = 1;
+    g.seq = seq_of_tok[blockIdx.x];
+    g.pos0 = n_ctx;  // non-causal: every key is visible
+    const int split = blockIdx.y;
+    const int kb = split * keys_per_split;
+    const int ke = min(n_ctx, kb + keys_per_split);
+    F ff = f;
+    ff.seq_row0 = (int64_t)g.seq * n_ctx;
+    attn_body<F, 1>(ff, q, g, n_head, d_head, f.W, kb, max(kb, ke), split, n_splits, ctx_out, out_f16, ws);
+}
+
+__global__ void attn_combine_kernel(const float* __restrict__ ws, int n_tok, int n_splits, int n_head, int d_head,
+                                    void* ctx_out, int out_f16) {
+    const int W = n_head * d_head;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)n_tok * W) return;
+    const int tok = (int)(i / W), c = (int)(i % W), h = c / d_head;
+    const float* base = ws + (size_t)tok * n_splits * (W + 2 * n_head);
+    float M = -INFINITY;
+    for (int s = 0; s < n_splits; ++s) M = fmaxf(M, base[(size_t)s * (W + 2 * n_head) + W + h]);
+    float L = 0.0f, O = 0.0f;
+    for (int s = 0; s < n_splits; ++s) {
+        const float* p = base + (size_t)s * (W + 2 * n_head);
+        float ms = p[W + h];
+        float w = ms == -INFINITY ? 0.0f : __expf(ms - M);
+        L += p[W + n_head + h] * w;
+        O += p[c] * w;
+    }
+    float v = O / L;
+    if (out_f16) reinterpret_cast<__half*>(ctx_out)[i] = __float2half_rn(v);
+    else reinterpret_cast<float*>(ctx_out)[i] = v;
+}
+
+// Thread shape of the attention CTA: R row-groups of W/16 threads with
+// R*W/16 a multiple of 32 and at most ATTN_MAX_THREADS threads.
+static int attn_rowgroups(int W) {
+    int tpr = W / 16;
+    int best = 0;
+    for (int R = 1; R * tpr <= ATTN_MAX_THREADS; ++R)
+        if ((R * tpr) % 32 == 0) best = R;
+    if (!best) fail(VKB_ERROR_UNSUPPORTED_OP, "attention: n_head*d_head=" + std::to_string(W) + " has no thread shape");
+    return best;
+}
+
+static void check_heads(int n_head, int d_head) {
+    if (n_head <= 0 || d_head <= 0) fail(VKB_ERROR_INVALID_ARGUMENT, "attention: bad head shape");
+    if (d_head % 16 || d_head > 512 || (d_head / 16) & (d_head / 16 - 1))
+        fail(VKB_ERROR_UNSUPPORTED_OP, "attention: d_head must be 16 x a power of two (got " +
+                                           std::to_string(d_head) + ")");
+    if ((n_head * d_head) % 32) fail(VKB_ERROR_UNSUPPORTED_OP, "attention: n_head*d_head must be a multiple of 32");
+}
+
+// Dense attention (cross-attention): launch helper shared with the session.
+void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, const float* q, const int32_t* seq_of_tok,
+                         const void* k, const void* v, const void* k_scale, const void* v_scale, int n_ctx,
+                         int kv_fmt, void* out, int out_dtype, float* ws_override) {
+    check_heads(n_head, d_head);
+    const int W = n_head * d_head;
+    const int R = attn_rowgroups(W);
+    // Splits: about 4 CTAs per SM overall, at least 2*R keys per split.
+    int splits = std::max(1, std::min((4 * ctx->sm_count + n_tok - 1) / n_tok, n_ctx / (2 * R)));
+    int kps = (n_ctx + splits - 1) / splits;
+    splits = (n_ctx + kps - 1) / kps;
+    float* ws = nullptr;
+    if (splits > 1) {
+        if (ws_override) ws = ws_override;
+        else {
+            size_t bytes = (size_t)n_tok * splits * (W + 2 * n_head) * sizeof(float);
+            ctx->ensure_workspace(bytes);
+            ws = ctx->workspace.as<float>();
+        }
+    }
+    size_t sm = attn_smem_bytes(R, 1, W, n_head);
+    dim3 grid((unsigned)n_tok, (unsigned)splits);
+    const int threads = R * (W / 16);
+    if (kv_fmt == VKB_DT_F16) {
+        FetchDenseF16 f{reinterpret_cast<const __half*>(k), reinterpret_cast<const __half*>(v), W, 0};
+        static bool attr = false;
+        if (!attr) { VKB_CUDA(cudaFuncSetAttribute(dense_attn_kernel<FetchDenseF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
+        dense_attn_kernel<FetchDenseF16><<<grid, threads, sm, ctx->stream>>>(f, q, seq_of_tok, n_ctx, n_head, d_head, kps,
+                                                                            splits, out, out_dtype == VKB_DT_F16, ws);
+    } else {
+        FetchDenseQ8 f{reinterpret_cast<const int8_t*>(k), reinterpret_cast<const __half*>(k_scale),
+                       reinterpret_cast<const int8_t*>(v), reinterpret_cast<const __half*>(v_scale), W, 0};
+        static bool attr = false;
+        if (!attr) { VKB_CUDA(cudaFuncSetAttribute(dense_attn_kernel<FetchDenseQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
+        dense_attn_kernel<FetchDenseQ8><<<grid, threads, sm, ctx->stream>>>(f, q, seq_of_tok, n_ctx, n_head, d_head, kps,
+                                                                           splits, out, out_dtype == VKB_DT_F16, ws);
+    }
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
+    if (splits > 1) {
+        int64_t tot = (int64_t)n_tok * W;
+        attn_combine_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, ctx->stream>>>(ws, n_tok, splits, n_head, d_head,
+                                                                                   out, out_dtype == VKB_DT_F16);
+        VKB_CUDA(cudaGetLastError());
+        ctx->count();
+    }
+}
+
+void run_quantize_rows(vkb_context* ctx, const float* x, int64_t n_rows, int W, int8_t* q, __half* d) {
+    if (W % 32) fail(VKB_ERROR_INVALID_ARGUMENT, "quantize_rows: row width must be a multiple of 32");
+    int64_t warps = n_rows * (W / 32);
+    quantize_rows_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, ctx->stream>>>(x, n_rows, W, q, d);
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
+}
+
+// ---------------------------------------------------------------------------
+// Host side of the pool
+// ---------------------------------------------------------------------------
+static vkb_kv_pool* pool_create(vkb_context* ctx, const vkb_kv_pool_desc* desc) {
+    if (!ctx || !desc) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: null argument");
+    const vkb_kv_pool_desc& d = *desc;
+    if (d.mode == VKB_KV_FP32)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: mode=Fp32 — the paged quant cache needs a quantized mode");
+    if (d.mode != VKB_KV_Q8_0)
+        fail(VKB_ERROR_UNSUPPORTED_OP, "kv_pool_create: the device kernels implement Q8_0 pages only");
+    if (d.n_layer <= 0 || d.n_head <= 0 || d.d_head <= 0 || d.n_stream <= 0 || d.n_codebook <= 0 || d.max_time <= 0)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: every axis must be > 0");
+    if ((d.n_head * d.d_head) % 32) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: n_head*d_head not a multiple of 32");
+    if (d.n_codebook != 1) fail(VKB_ERROR_UNSUPPORTED_OP, "kv_pool_create: n_codebook must be 1 on the device");
+    if (d.page_tokens != 2 && d.page_tokens != 4 && d.page_tokens != 16)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: page_tokens must be 2, 4 or 16");
+    if (d.layout != VKB_KV_LAYOUT_REFERENCE && d.layout != VKB_KV_LAYOUT_SEQUENCE)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: bad layout");
+    check_heads(d.n_head, d.d_head);
+    auto* p = new vkb_kv_pool();
+    try {
+        p->ctx = ctx;
+        p->d = d;
+        p->W = d.n_head * d.d_head;
+        p->row_blocks = p->W / 32;
+        if (d.layout == VKB_KV_LAYOUT_REFERENCE) {
+            p->ppl = (d.max_time + d.page_tokens - 1) / d.page_tokens;
+            p->n_pages = (int64_t)p->ppl * d.n_layer;  // paged_quant.rs:300 total_pages
+            if (d.n_pages > 0 && d.n_pages != p->n_pages)
+                fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: the reference layout sizes its own arena");
+            p->rpp = d.page_tokens * d.n_stream;
+            p->table_len = p->n_pages;
+            p->n_arena = 1;
+        } else {
+            p->ppseq = (d.max_time + d.page_tokens - 1) / d.page_tokens;
+            p->n_pages = d.n_pages > 0 ? d.n_pages : (int64_t)p->ppseq * d.n_stream;
+            p->rpp = d.page_tokens;
+            p->table_len = (int64_t)p->ppseq * d.n_stream;
+            p->n_arena = d.n_layer;
+        }
+        p->table.assign(p->table_len, -1);
+        for (int64_t i = p->n_pages - 1; i >= 0; --i) p->free_list.push_back((int32_t)i);
+        const int64_t rows = (int64_t)p->n_arena * p->n_pages * p->rpp;
+        VKB_CUDA(cudaSetDevice(ctx->device));
+        p->kq.alloc((size_t)rows * p->W);
+        p->vq.alloc((size_t)rows * p->W);
+        p->kd.alloc((size_t)rows * p->row_blocks * 2);
+        p->vd.alloc((size_t)rows * p->row_blocks * 2);
+        VKB_CUDA(cudaMemsetAsync(p->kq.p, 0, p->kq.n, ctx->stream));
+        VKB_CUDA(cudaMemsetAsync(p->vq.p, 0, p->vq.n, ctx->stream));
+        VKB_CUDA(cudaMemsetAsync(p->kd.p, 0, p->kd.n, ctx->stream));
+        VKB_CUDA(cudaMemsetAsync(p->vd.p, 0, p->vd.n, ctx->stream));
+        p->table_dev.alloc((size_t)p->table_len * 4);
+        p->max_step = std::max(64, d.n_stream * 8);
+        p->rows_dev.alloc((size_t)d.n_layer * p->max_step * 8);
+        p->groups_dev.alloc((size_t)p->max_step * sizeof(AttnGroup));
+        // Partials: up to 4096 CTAs x 4 queries of (W + 2H) floats.
+        p->part_dev.alloc((size_t)4096 * 4 * (p->W + 2 * d.n_head) * sizeof(float));
+        VKB_CUDA(cudaMallocHost(&p->h_table, (size_t)p->table_len * 4));
+        VKB_CUDA(cudaMallocHost(&p->h_rows, (size_t)d.n_layer * p->max_step * 8));
+        VKB_CUDA(cudaMallocHost(&p->h_groups, (size_t)p->max_step * sizeof(AttnGroup)));
+        VKB_CUDA(cudaEventCreateWithFlags(&p->staged, cudaEventDisableTiming));
+        std::fill(p->h_table, p->h_table + p->table_len, -1);
+        VKB_CUDA(cudaMemcpyAsync(p->table_dev.p, p->h_table, p->table_dev.n, cudaMemcpyHostToDevice, ctx->stream));
+        VKB_CUDA(cudaStreamSynchronize(ctx->stream));
+    } catch (...) {
+        delete p;
+        throw;
+    }
+    return p;
+}
+
+static void pool_destroy(vkb_kv_pool* p) {
+    if (!p) return;
+    if (p->ctx) cudaStreamSynchronize(p->ctx->stream);
+    if (p->h_table) cudaFreeHost(p->h_table);
+    if (p->h_rows) cudaFreeHost(p->h_rows);
+    if (p->h_groups) cudaFreeHost(p->h_groups);
+    if (p->staged) cudaEventDestroy(p->staged);
+    delete p;
+}
+
+static int32_t acquire(vkb_kv_pool* p) {
+    if (p->free_list.empty())
+        fail(VKB_ERROR_KV_CACHE_EXHAUSTED, "paged KV cache exhausted: arena has " + std::to_string(p->n_pages) +
+                                               " pages, " + std::to_string(p->n_pages) + " in use");
+    int32_t id = p->free_list.back();
+    p->free_list.pop_back();
+    return id;
+}
+
+static int64_t row_of(const vkb_kv_pool* p, int layer, int t, int s) {
+    const int bs = p->d.page_tokens;
+    if (p->d.layout == VKB_KV_LAYOUT_REFERENCE) {
+        int32_t pid = p->table[(int64_t)layer * p->ppl + t / bs];
+        if (pid < 0) return -1;
+        return ((int64_t)pid * bs + t % bs) * p->d.n_stream + s;
+    }
+    int32_t pid = p->table[(int64_t)s * p->ppseq + t / bs];
+    if (pid < 0) return -1;
+    return ((int64_t)layer * p->n_pages + pid) * bs + t % bs;
+}
+
+static void wait_staging(vkb_kv_pool* p) {
+    if (p->staged_pending) {
+        VKB_CUDA(cudaEventSynchronize(p->staged));
+        p->staged_pending = false;
+    }
+}
+
+static void upload_table(vkb_kv_pool* p) {
+    wait_staging(p);
+    memcpy(p->h_table, p->table.data(), (size_t)p->table_len * 4);
+    VKB_CUDA(cudaMemcpyAsync(p->table_dev.p, p->h_table, (size_t)p->table_len * 4, cudaMemcpyHostToDevice,
+                             p->ctx->stream));
+    VKB_CUDA(cudaEventRecord(p->staged, p->ctx->stream));
+    p->staged_pending = true;
+}
+
+static void begin_step(vkb_kv_pool* p, int n_tok, const int32_t* seq, const int32_t* pos) {
+    const auto& d = p->d;
+    if (n_tok <= 0 || n_tok > p->max_step)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "kv_begin_step: n_tok must be in 1.." + std::to_string(p->max_step));
+    if (!seq || !pos) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_begin_step: null arrays");
+    for (int i = 0; i < n_tok; ++i) {
+        if (seq[i] < 0 || seq[i] >= d.n_stream)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "stream " + std::to_string(seq[i]) + " >= n_stream " + std::to_string(d.n_stream));
+        if (pos[i] < 0 || pos[i] >= d.max_time)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "t " + std::to_string(pos[i]) + " >= max_time " + std::to_string(d.max_time));
+        if (i > 0 && seq[i] == seq[i - 1] && pos[i] != pos[i - 1] + 1)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "kv_begin_step: tokens of one stream must be consecutive positions");
+    }
+    wait_staging(p);
+    // SEQUENCE layout: one page id serves every layer, acquired here in token
+    // order. REFERENCE layout: pages are acquired lazily per layer by
+    // vkb_kv_append, in the order the reference's append_step would
+    // (paged_quant.rs:396-420).
+    if (d.layout == VKB_KV_LAYOUT_SEQUENCE) {
+        for (int i = 0; i < n_tok; ++i) {
+            int64_t idx = (int64_t)seq[i] * p->ppseq + pos[i] / d.page_tokens;
+            if (p->table[idx] < 0) p->table[idx] = acquire(p);
+        }
+        memcpy(p->h_table, p->table.data(), (size_t)p->table_len * 4);
+        for (int layer = 0; layer < d.n_layer; ++layer)
+            for (int i = 0; i < n_tok; ++i) p->h_rows[(size_t)layer * n_tok + i] = row_of(p, layer, pos[i], seq[i]);
+    }
+    // Query groups: runs of one stream, at most 4 queries each.
+    int ng = 0, maxq = 1, max_keys = 0;
+    for (int i = 0; i < n_tok;) {
+        int j = i + 1;
+        while (j < n_tok && seq[j] == seq[i] && j - i < 4) ++j;
+        AttnGroup g{i, j - i, seq[i], pos[i]};
+        p->h_groups[ng++] = g;
+        maxq = std::max(maxq, j - i);
+        max_keys = std::max(max_keys, pos[j - 1] + 1);
+        i = j;
+    }
+    cudaStream_t st = p->ctx->stream;
+    if (d.layout == VKB_KV_LAYOUT_SEQUENCE) {
+        VKB_CUDA(cudaMemcpyAsync(p->table_dev.p, p->h_table, (size_t)p->table_len * 4, cudaMemcpyHostToDevice, st));
+        VKB_CUDA(cudaMemcpyAsync(p->rows_dev.p, p->h_rows, (size_t)d.n_layer * n_tok * 8, cudaMemcpyHostToDevice, st));
+    }
+    VKB_CUDA(cudaMemcpyAsync(p->groups_dev.p, p->h_groups, (size_t)ng * sizeof(AttnGroup), cudaMemcpyHostToDevice, st));
+    VKB_CUDA(cudaEventRecord(p->staged, st));
+    p->staged_pending = true;
+    p->n_tok = n_tok;
+    p->n_groups = ng;
+    p->maxq = maxq;
+    p->max_keys = max_keys;
+    p->step_seq.assign(seq, seq + n_tok);
+    p->step_pos.assign(pos, pos + n_tok);
+    // Key splits: about 4 CTAs per SM, at least 2*R keys per split, and the
+    // partials must fit the pool's buffer.
+    const int R = attn_rowgroups(p->W);
+    int splits = std::max(1, std::min((4 * p->ctx->sm_count + ng - 1) / ng, max_keys / (2 * R)));
+    while ((int64_t)ng * splits > 4096 && splits > 1) --splits;
+    int kps = (max_keys + splits - 1) / splits;
+    splits = (max_keys + kps - 1) / kps;
+    p->splits = splits;
+    p->keys_per_split = kps;
+}
+
+static void append(vkb_kv_pool* p, int layer, const float* k, const float* v) {
+    if (p->n_tok == 0) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_append: no step was begun");
+    if (layer < 0 || layer >= p->d.n_layer) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_append: layer out of range");
+    if (!k || !v) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_append: null k/v");
+    if (p->d.layout == VKB_KV_LAYOUT_REFERENCE) {
+        // Lazy per-layer acquisition, then upload this layer's table slice and
+        // row list (disjoint staging slots per layer within a step).
+        const int bs = p->d.page_tokens;
+        for (int i = 0; i < p->n_tok; ++i) {
+            int64_t idx = (int64_t)layer * p->ppl + p->step_pos[i] / bs;
+            if (p->table[idx] < 0) p->table[idx] = acquire(p);
+        }
+        int32_t* ht = p->h_table + (size_t)layer * p->ppl;
+        memcpy(ht, p->table.data() + (size_t)layer * p->ppl, (size_t)p->ppl * 4);
+        int64_t* hr = p->h_rows + (size_t)layer * p->n_tok;
+        for (int i = 0; i < p->n_tok; ++i) hr[i] = row_of(p, layer, p->step_pos[i], p->step_seq[i]);
+        cudaStream_t st = p->ctx->stream;
+        VKB_CUDA(cudaMemcpyAsync(p->table_dev.as<int32_t>() + (size_t)layer * p->ppl, ht, (size_t)p->ppl * 4,
+                                 cudaMemcpyHostToDevice, st));
+        VKB_CUDA(cudaMemcpyAsync(p->rows_dev.as<int64_t>() + (size_t)layer * p->n_tok, hr, (size_t)p->n_tok * 8,
+                                 cudaMemcpyHostToDevice, st));
+        VKB_CUDA(cudaEventRecord(p->staged, st));
+        p->staged_pending = true;
+    }
+    const int64_t warps = (int64_t)p->n_tok * p->row_blocks * 2;
+    const int64_t* rows = p->rows_dev.as<int64_t>() + (size_t)layer * p->n_tok;
+    kv_append_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, p->ctx->stream>>>(
+        k, v, rows, p->n_tok, p->W, p->kq.as<int8_t>(), p->kd.as<__half>(), p->vq.as<int8_t>(), p->vd.as<__half>());
+    VKB_CUDA(cudaGetLastError());
+    p->ctx->count();
+}
+
+static void attention(vkb_kv_pool* p, int layer, const float* q, void* out, int out_dtype) {
+    if (p->n_tok == 0) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: no step was begun");
+    if (layer < 0 || layer >= p->d.n_layer) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: layer out of range");
+    if (!q || !out) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: null q/out");
+    if (out_dtype != VKB_DT_F32 && out_dtype != VKB_DT_F16) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: bad out dtype");
+    const auto& d = p->d;
+    const int W = p->W;
+    const int R = attn_rowgroups(W);
+    FetchPagedQ8 f;
+    f.kq = p->kq.as<int8_t>();
+    f.kd = p->kd.as<__half>();
+    f.vq = p->vq.as<int8_t>();
+    f.vd = p->vd.as<__half>();
+    f.table = p->table_dev.as<int32_t>();
+    f.W = W;
+    f.layout = d.layout;
+    f.bs = d.page_tokens;
+    int per_seq_base;
+    if (d.layout == VKB_KV_LAYOUT_REFERENCE) {
+        f.table_base = layer * p->ppl;
+        f.n_sc = d.n_stream;
+        f.slot = 0;
+        f.arena_row0 = 0;
+        per_seq_base = 0;
+    } else {
+        f.table_base = 0;
+        f.n_sc = 1;
+        f.slot = 0;
+        f.arena_row0 = (int64_t)layer * p->n_pages * p->rpp;
+        per_seq_base = 1;
+    }
+    dim3 grid((unsigned)p->n_groups, (unsigned)p->splits);
+    const int threads = R * (W / 16);
+    float* ws = p->part_dev.as<float>();
+    const int of16 = out_dtype == VKB_DT_F16;
+    if (p->maxq == 1) {
+        static bool attr = false;
+        if (!attr) { VKB_CUDA(cudaFuncSetAttribute(paged_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
+        paged_attn_kernel<1><<<grid, threads, attn_smem_bytes(R, 1, W, d.n_head), p->ctx->stream>>>(
+            f, q, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->keys_per_split, p->splits, out, of16, ws,
+            per_seq_base, p->ppseq);
+    } else {
+        static bool attr = false;
+        if (!attr) { VKB_CUDA(cudaFuncSetAttribute(paged_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
+        paged_attn_kernel<4><<<grid, threads, attn_smem_bytes(R, 4, W, d.n_head), p->ctx->stream>>>(
+            f, q, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->keys_per_split, p->splits, out, of16, ws,
+            per_seq_base, p->ppseq);
+    }
+    VKB_CUDA(cudaGetLastError());
+    p->ctx->count();
+    if (p->splits > 1) {
+        int64_t tot = (int64_t)p->n_tok * W;
+        attn_combine_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, p->ctx->stream>>>(ws, p->n_tok, p->splits,
+                                                                                       d.n_head, d.d_head, out, of16);
+        VKB_CUDA(cudaGetLastError());
+        p->ctx->count();
+    }
+}
+
+// Zeroes the device rows of one page (all layers' arenas for SEQUENCE layout).
+static void zero_page(vkb_kv_pool* p, int32_t pid, int layer_for_seq) {
+    cudaStream_t st = p->ctx->stream;
+    auto z = [&](int64_t row0, int64_t nrows) {
+        VKB_CUDA(cudaMemsetAsync(p->kq.as<int8_t>() + row0 * p->W, 0, (size_t)nrows * p->W, st));
+        VKB_CUDA(cudaMemsetAsync(p->vq.as<int8_t>() + row0 * p->W, 0, (size_t)nrows * p->W, st));
+        VKB_CUDA(cudaMemsetAsync(p->kd.as<uint8_t>() + row0 * p->row_blocks * 2, 0, (size_t)nrows * p->row_blocks * 2, st));
+        VKB_CUDA(cudaMemsetAsync(p->vd.as<uint8_t>() + row0 * p->row_blocks * 2, 0, (size_t)nrows * p->row_blocks * 2, st));
+    };
+    if (p->d.layout == VKB_KV_LAYOUT_REFERENCE) z((int64_t)pid * p->rpp, p->rpp);
+    else z(((int64_t)layer_for_seq * p->n_pages + pid) * p->rpp, p->rpp);
+}
+
+// ---------------------------------------------------------------------------
+// dequant GEMV (KvQuantDequantGemvOps): one warp per row, lanes over blocks.
+// ---------------------------------------------------------------------------
+template <int MODE>
+__global__ void kv_dequant_gemv_kernel(const uint8_t* __restrict__ blocks, int64_t n_rows, int64_t nbpr,
+                                       const float* __restrict__ x, float* __restrict__ y) {
+    const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= n_rows) return;
+    constexpr int BB = MODE == VKB_KV_Q4_0 ? 18 : MODE == VKB_KV_Q5_0 ? 22 : 34;
+    float acc = 0.0f;
+    for (int64_t b = lane; b < nbpr; b += 32) {
+        const uint8_t* blk = blocks + (row * nbpr + b) * BB;
+        const float* xb = x + b * 32;
+        float d = __half2float(__ushort_as_half((uint16_t)(blk[0] | (blk[1] << 8))));
+        float part = 0.0f;
+        if (MODE == VKB_KV_Q8_0) {
+            for (int i = 0; i < 32; ++i) part = fmaf((float)(int8_t)blk[2 + i], xb[i], part);
+        } else if (MODE == VKB_KV_Q4_0) {
+            // vokra KV Q4_0: elements 2i / 2i+1 in the low / high nibble of byte i (kv_quant/q4_0.rs:73)
+            for (int i = 0; i < 16; ++i) {
+                uint8_t q = blk[2 + i];
+                part = fmaf((float)((int)(q & 0xf) - 8), xb[2 * i], part);
+                part = fmaf((float)((int)(q >> 4) - 8), xb[2 * i + 1], part);
+            }
+        } else {
+            // Q5_0 (kv_quant/q5_0.rs:84): low 4 bits pair-packed, 5th bit in qh
+            const uint8_t* qh = blk + 2;
+            const uint8_t* qs = blk + 6;
+            for (int i = 0; i < 32; ++i) {
+                uint8_t lo4 = (i & 1) ? (qs[i / 2] >> 4) : (qs[i / 2] & 0xf);
+                uint8_t hi1 = (qh[i / 8] >> (i % 8)) & 1;
+                part = fmaf((float)((int)((hi1 << 4) | lo4) - 16), xb[i], part);
+            }
+        }
+        acc = fmaf(part, d, acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) y[row] = acc;
+}
+
+static void validate_dequant_gemv(int mode, size_t n_bytes, size_t n_rows, size_t nbpr, size_t x_len) {
+    // validate_dequant_gemv (crates/vokra-core/src/kv_quant/gpu_ops.rs:95-130)
+    if (mode == VKB_KV_FP32)
+        fail(VKB_ERROR_INVALID_ARGUMENT,
+             "fused_dequant_gemv: mode=Fp32 has no on-wire block layout; use dense_gemv_f32 instead");
+    if (mode != VKB_KV_Q4_0 && mode != VKB_KV_Q5_0 && mode != VKB_KV_Q8_0)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "fused_dequant_gemv: unknown mode");
+    if (x_len != nbpr * 32)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "fused_dequant_gemv: x.len()=" + std::to_string(x_len) +
+                                             " != n_blocks_per_row*32 = " + std::to_string(nbpr * 32));
+    size_t bb = mode == VKB_KV_Q4_0 ? 18 : mode == VKB_KV_Q5_0 ? 22 : 34;
+    if (nbpr && n_rows > SIZE_MAX / nbpr / bb) fail(VKB_ERROR_INVALID_ARGUMENT, "fused_dequant_gemv: byte-length overflow");
+    if (n_bytes != n_rows * nbpr * bb)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "fused_dequant_gemv: blocks_bytes.len()=" + std::to_string(n_bytes) +
+                                             " != " + std::to_string(n_rows * nbpr * bb));
+}
+
+static void run_dequant_gemv(vkb_context* ctx, int mode, const void* blocks, size_t n_rows, size_t nbpr,
+                             const float* x, float* y) {
+    if (n_rows == 0) return;
+    unsigned grid = (unsigned)((n_rows * 32 + 255) / 256);
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(blocks);
+    if (mode == VKB_KV_Q8_0) kv_dequant_gemv_kernel<VKB_KV_Q8_0><<<grid, 256, 0, ctx->stream>>>(b, n_rows, nbpr, x, y);
+    else if (mode == VKB_KV_Q4_0) kv_dequant_gemv_kernel<VKB_KV_Q4_0><<<grid, 256, 0, ctx->stream>>>(b, n_rows, nbpr, x, y);
+    else kv_dequant_gemv_kernel<VKB_KV_Q5_0><<<grid, 256, 0, ctx->stream>>>(b, n_rows, nbpr, x, y);
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
+}
+
+}  // namespace vkb
+
+extern "C" {
+
+vkb_status vkb_kv_pool_create(vkb_context* ctx, const vkb_kv_pool_desc* desc, vkb_kv_pool** out) {
+    return guard([&] {
+        if (!out) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: null out");
+        *out = pool_create(ctx, desc);
+    });
+}
+
+vkb_status vkb_kv_pool_destroy(vkb_kv_pool* pool) {
+    return guard([&] { pool_destroy(pool); });
+}
+
+vkb_status vkb_kv_begin_step(vkb_kv_pool* pool, int32_t n_tok, const int32_t* seq_ids_host,
+                             const int32_t* positions_host) {
+    return guard([&] {
+        if (!pool) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_begin_step: null pool");
+        begin_step(pool, n_tok, seq_ids_host, positions_host);
+    });
+}
+
+vkb_status vkb_kv_append(vkb_kv_pool* pool, int32_t layer, const float* k_dev, const float* v_dev) {
+    return guard([&] {
+        if (!pool) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_append: null pool");
+        append(pool, layer, k_dev, v_dev);
+    });
+}
+
+vkb_status vkb_kv_attention(vkb_kv_pool* pool, int32_t layer, const float* q_dev, void* ctx_out_dev, int out_dtype) {
+    return guard([&] {
+        if (!pool) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: null pool");
+        attention(pool, layer, q_dev, ctx_out_dev, out_dtype);
+    });
+}
+
+vkb_status vkb_kv_release_seq(vkb_kv_pool* pool, int32_t seq_id) {
+    return guard([&] {
+        if (!pool) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_release_seq: null pool");
+        if (pool->d.layout != VKB_KV_LAYOUT_SEQUENCE)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "kv_release_seq: only the sequence layout frees per stream");
+        if (seq_id < 0 || seq_id >= pool->d.n_stream) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_release_seq: bad stream");
+        for (int i = 0; i < pool->ppseq; ++i) {
+            int32_t& e = pool->table[(int64_t)seq_id * pool->ppseq + i];
+            if (e >= 0) {
+                pool->free_list.push_back(e);
+                e = -1;
+            }
+        }
+        upload_table(pool);
+    });
+}
+
+vkb_status vkb_kv_release_layer(vkb_kv_pool* pool, int32_t layer) {
+    return guard([&] {
+        if (!pool) fail(VKB_ERROR_INVALID_ARGUMENT, "release_layer: null pool");
+        if (pool->d.layout != VKB_KV_LAYOUT_REFERENCE)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "release_layer: only the reference layout owns pages per layer");
+        if (layer < 0 || layer >= pool->d.n_layer)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "release_layer: layer " + std::to_string(layer) + " >= n_layer " +
+                                                 std::to_string(pool->d.n_layer));
+        for (int i = 0; i < pool->ppl; ++i) {
+            int32_t& e = pool->table[(int64_t)layer * pool->ppl + i];
+            if (e >= 0) {
+                zero_page(pool, e, 0);
+                pool->free_list.push_back(e);
+                e = -1;
+            }
+        }
+        upload_table(pool);
+    });
+}
+
+vkb_status vkb_kv_reset(vkb_kv_pool* pool) {
+    return guard([&] {
+        if (!pool) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_reset: null pool");
+        std::fill(pool->table.begin(), pool->table.end(), -1);
+        cudaStream_t st = pool->ctx->stream;
+        VKB_CUDA(cudaMemsetAsync(pool->kq.p, 0, pool->kq.n, st));
+        VKB_CUDA(cudaMemsetAsync(pool->vq.p, 0, pool->vq.n, st));
+        VKB_CUDA(cudaMemsetAsync(pool->kd.p, 0, pool->kd.n, st));
+        VKB_CUDA(cudaMemsetAsync(pool->vd.p, 0, pool->vd.n, st));
+        pool->free_list.clear();
+        for (int64_t i = pool->n_pages - 1; i >= 0; --i) pool->free_list.push_back((int32_t)i);
+        pool->n_tok = 0;
+        upload_table(pool);
+    });
+}
+
+vkb_status vkb_kv_set_page_table(vkb_kv_pool* pool, const int32_t* table_host, size_t len) {
+    return guard([&] {
+        if (!pool || !table_host) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_set_page_table: null argument");
+        if (pool->d.layout != VKB_KV_LAYOUT_SEQUENCE)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "kv_set_page_table: the reference layout allocates its own pages");
+        if ((int64_t)len != pool->table_len) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_set_page_table: wrong length");
+        std::vector<char> used(pool->n_pages, 0);
+        for (size_t i = 0; i < len; ++i) {
+            int32_t e = table_host[i];
+            if (e < -1 || e >= pool->n_pages) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_set_page_table: page id out of range");
+            if (e >= 0) {
+                if (used[e]) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_set_page_table: page listed twice");
+                used[e] = 1;
+            }
+        }
+        pool->table.assign(table_host, table_host + len);
+        pool->free_list.clear();
+        for (int64_t i = pool->n_pages - 1; i >= 0; --i)
+            if (!used[i]) pool->free_list.push_back((int32_t)i);
+        upload_table(pool);
+    });
+}
+
+size_t vkb_kv_table_len(const vkb_kv_pool* pool) { return pool ? (size_t)pool->table_len : 0; }
+
+vkb_status vkb_kv_page_table(const vkb_kv_pool* pool, int64_t* out_host, size_t len) {
+    return guard([&] {
+        if (!pool || !out_host) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_page_table: null argument");
+        if ((int64_t)len != pool->table_len) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_page_table: wrong length");
+        for (size_t i = 0; i < len; ++i) out_host[i] = pool->table[i];
+    });
+}
+
+int32_t vkb_kv_pages_in_use(const vkb_kv_pool* pool) {
+    return pool ? (int32_t)(pool->n_pages - (int64_t)pool->free_list.size()) : 0;
+}
+
+size_t vkb_kv_page_bytes(const vkb_kv_pool* pool) {
+    return pool ? (size_t)pool->rpp * pool->row_blocks * 34 : 0;
+}
+
+size_t vkb_kv_on_wire_bytes(const vkb_kv_pool* pool) {
+    return pool ? (size_t)pool->n_arena * pool->n_pages * 2 * vkb_kv_page_bytes(pool) : 0;
+}
+
+vkb_status vkb_kv_read_page(const vkb_kv_pool* pool, int32_t layer, int32_t page, void* k_host, void* v_host) {
+    return guard([&] {
+        if (!pool || !k_host || !v_host) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_read_page: null argument");
+        if (page < 0 || page >= pool->n_pages) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_read_page: page out of range");
+        int arena = pool->d.layout == VKB_KV_LAYOUT_SEQUENCE ? layer : 0;
+        if (arena < 0 || arena >= pool->n_arena) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_read_page: layer out of range");
+        const int64_t row0 = ((int64_t)arena * pool->n_pages + page) * pool->rpp;
+        const int W = pool->W, nb = pool->row_blocks;
+        std::vector<int8_t> q((size_t)pool->rpp * W);
+        std::vector<uint16_t> d((size_t)pool->rpp * nb);
+        cudaStream_t st = pool->ctx->stream;
+        for (int side = 0; side < 2; ++side) {
+            const DevBuf& qb = side ? pool->vq : pool->kq;
+            const DevBuf& db = side ? pool->vd : pool->kd;
+            VKB_CUDA(cudaMemcpyAsync(q.data(), qb.as<int8_t>() + row0 * W, q.size(), cudaMemcpyDeviceToHost, st));
+            VKB_CUDA(cudaMemcpyAsync(d.data(), db.as<uint16_t>() + row0 * nb, d.size() * 2, cudaMemcpyDeviceToHost, st));
+            VKB_CUDA(cudaStreamSynchronize(st));
+            uint8_t* o = reinterpret_cast<uint8_t*>(side ? v_host : k_host);
+            for (int64_t r = 0; r < pool->rpp; ++r)
+                for (int b = 0; b < nb; ++b) {
+                    uint8_t* blk = o + ((size_t)r * nb + b) * 34;
+                    uint16_t h = d[(size_t)r * nb + b];
+                    blk[0] = (uint8_t)(h & 0xff);
+                    blk[1] = (uint8_t)(h >> 8);
+                    memcpy(blk + 2, &q[(size_t)r * W + b * 32], 32);
+                }
+        }
+    });
+}
+
+vkb_status vkb_kv_read_step(const vkb_kv_pool* pool, int32_t layer, int32_t t, int32_t s, float* k_host,
+                            float* v_host) {
+    return guard([&] {
+        if (!pool || !k_host || !v_host) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_read_step: null argument");
+        const auto& d = pool->d;
+        if (layer < 0 || layer >= d.n_layer || t < 0 || t >= d.max_time || s < 0 || s >= d.n_stream)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "kv_read_step: out of range");
+        int64_t row = row_of(pool, layer, t, s);
+        if (row < 0) fail(VKB_ERROR_OTHER, "kv_read_step: slot was never written");
+        const int W = pool->W, nb = pool->row_blocks;
+        std::vector<int8_t> q(W);
+        std::vector<uint16_t> sc(nb);
+        cudaStream_t st = pool->ctx->stream;
+        for (int side = 0; side < 2; ++side) {
+            const DevBuf& qb = side ? pool->vq : pool->kq;
+            const DevBuf& db = side ? pool->vd : pool->kd;
+            VKB_CUDA(cudaMemcpyAsync(q.data(), qb.as<int8_t>() + row * W, W, cudaMemcpyDeviceToHost, st));
+            VKB_CUDA(cudaMemcpyAsync(sc.data(), db.as<uint16_t>() + row * nb, nb * 2, cudaMemcpyDeviceToHost, st));
+            VKB_CUDA(cudaStreamSynchronize(st));
+            float* o = side ? v_host : k_host;
+            for (int i = 0; i < W; ++i) {
+                // BlockQ8_0::unpack (q8_0.rs:69): q as f32 times the f16 scale
+                uint16_t h = sc[i / 32];
+                __half hh = __ushort_as_half(h);
+                o[i] = (float)q[i] * __half2float(hh);
+            }
+        }
+    });
+}
+
+vkb_status vkb_attention_dense(vkb_context* ctx, int32_t n_tok, int32_t n_head, int32_t d_head, const float* q_dev,
+                               const int32_t* seq_of_tok_dev, const void* k_dev, const void* v_dev,
+                               const void* k_scale_dev, const void* v_scale_dev, int32_t n_ctx, int32_t kv_dtype,
+                               void* ctx_out_dev, int32_t out_dtype) {
+    return guard([&] {
+        if (!ctx || !q_dev || !seq_of_tok_dev || !k_dev || !v_dev || !ctx_out_dev)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "attention_dense: null argument");
+        if (n_tok <= 0 || n_ctx <= 0) fail(VKB_ERROR_INVALID_ARGUMENT, "attention_dense: empty shape");
+        if (kv_dtype != VKB_DT_F16 && kv_dtype != VKB_KV_Q8_0)
+            fail(VKB_ERROR_UNSUPPORTED_OP, "attention_dense: kv dtype must be F16 or Q8_0");
+        if (kv_dtype == VKB_KV_Q8_0 && (!k_scale_dev || !v_scale_dev))
+            fail(VKB_ERROR_INVALID_ARGUMENT, "attention_dense: Q8_0 needs scale planes");
+        if (out_dtype != VKB_DT_F32 && out_dtype != VKB_DT_F16) fail(VKB_ERROR_INVALID_ARGUMENT, "attention_dense: bad out dtype");
+        run_dense_attention(ctx, n_tok, n_head, d_head, q_dev, seq_of_tok_dev, k_dev, v_dev, k_scale_dev, v_scale_dev,
+                            n_ctx, kv_dtype == VKB_DT_F16 ? VKB_DT_F16 : VKB_KV_Q8_0, ctx_out_dev, out_dtype, nullptr);
+    });
+}
+
+vkb_status vkb_quantize_rows_q8_0(vkb_context* ctx, const float* x_dev, int64_t n_rows, int32_t width, void* q_dev,
+                                  void* d_dev) {
+    return guard([&] {
+        if (!ctx || !x_dev || !q_dev || !d_dev) fail(VKB_ERROR_INVALID_ARGUMENT, "quantize_rows: null argument");
+        if (n_rows <= 0 || width <= 0) fail(VKB_ERROR_INVALID_ARGUMENT, "quantize_rows: empty shape");
+        run_quantize_rows(ctx, x_dev, n_rows, width, reinterpret_cast<int8_t*>(q_dev), reinterpret_cast<__half*>(d_dev));
+    });
+}
+
+vkb_status vkb_kv_dequant_gemv(vkb_context* ctx, int mode, const void* blocks_dev, size_t n_bytes, size_t n_rows,
+                               size_t nbpr, const float* x_dev, size_t x_len, float* y_dev) {
+    return guard([&] {
+        if (!ctx) fail(VKB_ERROR_INVALID_ARGUMENT, "dequant_gemv: null context");
+        validate_dequant_gemv(mode, n_bytes, n_rows, nbpr, x_len);
+        if (n_rows && (!blocks_dev || !x_dev || !y_dev)) fail(VKB_ERROR_INVALID_ARGUMENT, "dequant_gemv: null buffer");
+        run_dequant_gemv(ctx, mode, blocks_dev, n_rows, nbpr, x_dev, y_dev);
+    });
+}
+
+vkb_status vkb_kv_dequant_gemv_host(vkb_context* ctx, int mode, const void* blocks_host, size_t n_bytes, size_t n_rows,
+                                    size_t nbpr, const float* x_host, size_t x_len, float* y_host) {
+    return guard([&] {
+        if (!ctx) fail(VKB_ERROR_INVALID_ARGUMENT, "dequant_gemv: null context");
+        validate_dequant_gemv(mode, n_bytes, n_rows, nbpr, x_len);
+        if (n_rows == 0) return;
+        if (!blocks_host || !x_host || !y_host) fail(VKB_ERROR_INVALID_ARGUMENT, "dequant_gemv: null buffer");
+        DevBuf b(n_bytes), x(x_len * 4), y(n_rows * 4);
+        cudaStream_t st = ctx->stream;
+        VKB_CUDA(cudaMemcpyAsync(b.p, blocks_host, n_bytes, cudaMemcpyHostToDevice, st));
+        VKB_CUDA(cudaMemcpyAsync(x.p, x_host, x_len * 4, cudaMemcpyHostToDevice, st));
+        run_dequant_gemv(ctx, mode, b.p, n_rows, nbpr, x.as<float>(), y.as<float>());
+        VKB_CUDA(cudaMemcpyAsync(y_host, y.p, n_rows * 4, cudaMemcpyDeviceToHost, st));
+        VKB_CUDA(cudaStreamSynchronize(st));
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,665 @@
+// linear.cu — the quantized Linear of the Whisper hot path: weight upload and
+// repack, the small-m streaming GEMV, the tcgen05/TMEM GEMM, split-K reduce,
+// and the C ABI entry points vkb_weight_upload / vkb_linear / vkb_gemm_q_f32
+// (the B200 arm of Compute::gemm_q_f32, crates/vokra-models/src/compute.rs:943).
+#include "common.cuh"
+#include "weights.cuh"
+#include "tc_ptx.cuh"
+#include "linear.cuh"
+
+#include <cudaTypedefs.h>
+#include <mutex>
+#include <memory>
+#include <algorithm>
+
+namespace vkb {
+
+// ---------------------------------------------------------------------------
+// Host repack of GGUF block bytes [n][k] into the tile layout of weights.cuh.
+// ---------------------------------------------------------------------------
+static void repack_host(int fmt, const uint8_t* src, int64_t n, int64_t k, int64_t n_pad, std::vector<uint8_t>& qs,
+                        std::vector<uint8_t>& sc, uint32_t tag) {
+    int64_t T = n_pad / TILE_N;
+    if (fmt == W_Q4_0 || fmt == W_Q8_0) {
+        int bpb = fmt == W_Q4_0 ? 16 : 32, blk = fmt == W_Q4_0 ? 18 : 34;
+        int64_t KB = k / 32;
+        qs.assign((size_t)T * KB * TILE_N * bpb, 0);
+        sc.assign((size_t)T * KB * TILE_N * 2, 0);
+        for (int64_t row = 0; row < n; ++row) {
+            int64_t t = row / TILE_N, r = row % TILE_N;
+            const uint8_t* rb = src + (size_t)row * KB * blk;
+            for (int64_t b = 0; b < KB; ++b) {
+                size_t o = (size_t)((t * KB + b) * TILE_N + r);
+                memcpy(&sc[o * 2], rb + b * blk, 2);
+                memcpy(&qs[o * bpb], rb + b * blk + 2, bpb);
+            }
+        }
+    } else if (fmt == W_Q4_K) {
+        int64_t KC = k / 64, KSB = k / 256;
+        qs.assign((size_t)T * KC * TILE_N * 32, 0);
+        sc.assign((size_t)T * KSB * TILE_N * 16, 0);
+        for (int64_t row = 0; row < n; ++row) {
+            int64_t t = row / TILE_N, r = row % TILE_N;
+            const uint8_t* rb = src + (size_t)row * KSB * 144;
+            for (int64_t sb = 0; sb < KSB; ++sb) {
+                const uint8_t* blkp = rb + sb * 144;
+                memcpy(&sc[(size_t)((t * KSB + sb) * TILE_N + r) * 16], blkp, 16);
+                for (int c = 0; c < 4; ++c)
+                    memcpy(&qs[(size_t)((t * KC + sb * 4 + c) * TILE_N + r) * 32], blkp + 16 + 32 * c, 32);
+            }
+        }
+    } else {
+        int64_t KC = k / 64;
+        qs.assign((size_t)T * KC * TILE_N * 128, 0);
+        for (int64_t row = 0; row < n; ++row) {
+            int64_t t = row / TILE_N, r = row % TILE_N;
+            for (int64_t c = 0; c < KC; ++c) {
+                uint16_t* dst = reinterpret_cast<uint16_t*>(&qs[(size_t)((t * KC + c) * TILE_N + r) * 128]);
+                for (int e = 0; e < 64; ++e) {
+                    int64_t idx = row * k + c * 64 + e;
+                    if (tag == VKB_GGML_F16) {
+                        memcpy(&dst[e], src + idx * 2, 2);
+                    } else if (tag == VKB_GGML_BF16) {
+                        uint32_t b = (uint32_t)(src[idx * 2] | (src[idx * 2 + 1] << 8)) << 16;
+                        float f;
+                        memcpy(&f, &b, 4);
+                        dst[e] = f32_to_f16_bits(f);
+                    } else {
+                        float f;
+                        memcpy(&f, src + idx * 4, 4);
+                        dst[e] = f32_to_f16_bits(f);
+                    }
+                }
+            }
+        }
+    }
+}
+
+static int64_t payload_bytes(uint32_t tag, int64_t n, int64_t k) {
+    int64_t e = n * k;
+    switch (tag) {
+        case VKB_GGML_F32: return e * 4;
+        case VKB_GGML_F16: case VKB_GGML_BF16: return e * 2;
+        case VKB_GGML_Q4_0: return e / 32 * 18;
+        case VKB_GGML_Q8_0: return e / 32 * 34;
+        case VKB_GGML_Q4_K: return e / 256 * 144;
+        default: return -1;
+    }
+}
+
+vkb_weight* upload_weight(vkb_context* ctx, uint32_t tag, int64_t n, int64_t k, const void* bytes, size_t len) {
+    if (!ctx) fail(VKB_ERROR_INVALID_ARGUMENT, "weight_upload: null context");
+    if (!bytes) fail(VKB_ERROR_INVALID_ARGUMENT, "weight_upload: null bytes");
+    if (n <= 0 || k <= 0) fail(VKB_ERROR_INVALID_ARGUMENT, "weight_upload: n and k must be positive");
+    int fmt;
+    switch (tag) {
+        case VKB_GGML_Q4_0: fmt = W_Q4_0; break;
+        case VKB_GGML_Q8_0: fmt = W_Q8_0; break;
+        case VKB_GGML_Q4_K: fmt = W_Q4_K; break;
+        case VKB_GGML_F32: case VKB_GGML_F16: case VKB_GGML_BF16: fmt = W_F16; break;
+        default:
+            fail(VKB_ERROR_UNSUPPORTED_OP, "weight_upload: ggml type " + std::to_string(tag) +
+                                               " has no B200 kernel (supported: Q4_0, Q8_0, Q4_K, F16, BF16, F32)");
+    }
+    int64_t kmul = fmt == W_Q4_K ? 256 : 64;
+    if (k % kmul)
+        fail(VKB_ERROR_UNSUPPORTED_OP, "weight_upload: k=" + std::to_string(k) + " must be a multiple of " +
+                                           std::to_string(kmul) + " for this dtype");
+    int64_t want = payload_bytes(tag, n, k);
+    if ((int64_t)len != want)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "weight_upload: payload is " + std::to_string(len) + " bytes, want " +
+                                             std::to_string(want));
+    auto* w = new vkb_weight();
+    try {
+        w->ctx = ctx;
+        w->tag = tag;
+        w->fmt = fmt;
+        w->n = n;
+        w->k = k;
+        w->n_pad = (n + TILE_N - 1) / TILE_N * TILE_N;
+        std::vector<uint8_t> qs, sc;
+        repack_host(fmt, (const uint8_t*)bytes, n, k, w->n_pad, qs, sc, tag);
+        VKB_CUDA(cudaSetDevice(ctx->device));
+        w->qs.alloc(qs.size());
+        VKB_CUDA(cudaMemcpy(w->qs.p, qs.data(), qs.size(), cudaMemcpyHostToDevice));
+        if (!sc.empty()) {
+            w->sc.alloc(sc.size());
+            VKB_CUDA(cudaMemcpy(w->sc.p, sc.data(), sc.size(), cudaMemcpyHostToDevice));
+        }
+    } catch (...) {
+        delete w;
+        throw;
+    }
+    return w;
+}
+
+// ---------------------------------------------------------------------------
+// Epilogue shared by every Linear kernel.
+// ---------------------------------------------------------------------------
+struct Epi {
+    const float* bias;
+    const float* residual;
+    void* out;
+    int out_f16;
+    int kind;
+    float scale;
+    int64_t ldo;  // = n
+};
+
+__device__ __forceinline__ void epi_store(const Epi& e, int64_t m, int64_t n, float acc, float bias_n) {
+    float v = acc + bias_n;
+    int64_t idx = m * e.ldo + n;
+    if (e.kind == VKB_EPI_GELU) v = gelu_as(v);
+    else if (e.kind == VKB_EPI_SCALE) v = v * e.scale;
+    else if (e.kind == VKB_EPI_RESIDUAL) v = e.residual[idx] + v;
+    if (e.out_f16) reinterpret_cast<__half*>(e.out)[idx] = __float2half_rn(v);
+    else reinterpret_cast<float*>(e.out)[idx] = v;
+}
+
+// ---------------------------------------------------------------------------
+// Small-m streaming GEMV: one thread per weight row (128 per CTA), the CTA's
+// stage range of K, activations broadcast from shared memory, fp32 FMA.
+// grid = (n_pad/128 tiles, k splits). With one split the epilogue is applied
+// here, else fp32 partials go to ws[split][m][n].
+// ---------------------------------------------------------------------------
+template <int FMT, int MM>
+__global__ void __launch_bounds__(128) gemv_kernel(const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc,
+                                                   int64_t K, int64_t N, int64_t M, const void* __restrict__ a,
+                                                   int a_f16, int stages_per_split, int n_splits, float* ws, Epi e) {
+    extern __shared__ float xs[];  // [MM][stages_per_split*64]
+    const int tile = blockIdx.x, split = blockIdx.y, r = threadIdx.x;
+    const int64_t total_stages = K / STAGE_K;
+    const int64_t s0 = (int64_t)split * stages_per_split;
+    const int64_t s1 = min(total_stages, s0 + stages_per_split);
+    const int ks = (int)((s1 - s0) * STAGE_K);
+    // Stage the activations of this K range (rows >= M are zero).
+    for (int i = threadIdx.x; i < MM * ks; i += blockDim.x) {
+        int m = i / ks, kk = i % ks;
+        float v = 0.0f;
+        if (m < M) {
+            int64_t g = (int64_t)m * K + s0 * STAGE_K + kk;
+            v = a_f16 ? __half2float(reinterpret_cast<const __half*>(a)[g]) : reinterpret_cast<const float*>(a)[g];
+        }
+        xs[m * ks + kk] = v;
+    }
+    __syncthreads();
+    float acc[MM];
+#pragma unroll
+    for (int m = 0; m < MM; ++m) acc[m] = 0.0f;
+    for (int64_t s = s0; s < s1; ++s) {
+        StagePtrs p = stage_ptrs(FMT, qs, sc, K, tile, s);
+        float w[64];
+        dequant_row_stage<FMT>(p.qs, p.sc, r, (int)s, w);
+        const float* xb = xs + (s - s0) * STAGE_K;
+#pragma unroll
+        for (int m = 0; m < MM; ++m) {
+            const float4* x4 = reinterpret_cast<const float4*>(xb + m * ks);
+            float am = acc[m];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                float4 xv = x4[i];
+                am = fmaf(w[4 * i], xv.x, am);
+                am = fmaf(w[4 * i + 1], xv.y, am);
+                am = fmaf(w[4 * i + 2], xv.z, am);
+                am = fmaf(w[4 * i + 3], xv.w, am);
+            }
+            acc[m] = am;
+        }
+    }
+    const int64_t n = (int64_t)tile * TILE_N + r;
+    if (n >= N) return;
+    if (n_splits == 1) {
+        float b = e.bias ? e.bias[n] : 0.0f;
+#pragma unroll
+        for (int m = 0; m < MM; ++m)
+            if (m < M) epi_store(e, m, n, acc[m], b);
+    } else {
+#pragma unroll
+        for (int m = 0; m < MM; ++m)
+            if (m < M) ws[((int64_t)split * M + m) * N + n] = acc[m];
+    }
+}
+
+// Sums split-K partials ws[split][m][n] in split order and applies the epilogue.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int n_splits, int64_t M, int64_t N, Epi e) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= M * N) return;
+    int64_t m = i / N, n = i % N;
+    float acc = 0.0f;
+    for (int s = 0; s < n_splits; ++s) acc += ws[(int64_t)s * M * N + i];
+    epi_store(e, m, n, acc, e.bias ? e.bias[n] : 0.0f);
+}
+
+__global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, int64_t n) {
+    int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i + 3 < n) {
+        float4 v = *reinterpret_cast<const float4*>(x + i);
+        reinterpret_cast<__half2*>(y + i)[0] = __floats2half2_rn(v.x, v.y);
+        reinterpret_cast<__half2*>(y + i)[1] = __floats2half2_rn(v.z, v.w);
+    } else {
+        for (; i < n; ++i) y[i] = __float2half_rn(x[i]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 GEMM: D[n][m] = W[n][:] . X[m][:] with W dequantized into shared
+// memory (128 rows x 64 K per stage, f16, 128-byte swizzle) and X staged by
+// TMA (BN tokens x 64 K, f16, 128-byte swizzle). Accumulator in TMEM
+// (128 lanes x BN fp32 columns).
+//
+// Warp roles (192 threads):
+//   warp 0      : producer — TMA for X, bulk copies for the raw weight stage
+//   warp 1      : TMEM allocator; lane 0 issues tcgen05.mma and commits
+//   warps 2..5  : dequantize raw stage -> A tile; then the epilogue
+//                 (thread = one weight row = one TMEM lane)
+// Rings: S stages of (X tile + raw weights), 2 stages of A tiles.
+// Every mbarrier wait is bounded; on timeout the kernel records an error flag
+// and returns without hanging.
+// ---------------------------------------------------------------------------
+template <int FMT, int BN>
+struct TcCfg {
+    static constexpr int A_BYTES = TILE_N * 128;              // 16 KB
+    static constexpr int B_BYTES = BN * 128;                  // BN rows x 128 B
+    static constexpr int RAW_Q = stage_qs_bytes(FMT);
+    static constexpr int RAW_S = stage_sc_bytes(FMT);
+    static constexpr int RAW_BYTES = ((RAW_Q + RAW_S) + 1023) / 1024 * 1024;
+    static constexpr int STAGE_BYTES = B_BYTES + RAW_BYTES;
+    static constexpr int BUDGET = 225 * 1024 - 2 * A_BYTES - 2048;
+    static constexpr int S0 = BUDGET / STAGE_BYTES;
+    static constexpr int S = S0 > 6 ? 6 : S0;
+    static constexpr int SMEM = 1024 /*align slack*/ + 2 * A_BYTES + S * STAGE_BYTES + 1024 /*barriers*/;
+    static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+    static_assert(S >= 2, "pipeline needs at least two stages");
+};
+
+template <int FMT, int BN>
+__global__ void __launch_bounds__(192, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ qs,
+                   const uint8_t* __restrict__ sc, int64_t K, int64_t N, int64_t M, int n_tiles, int m_tiles,
+                   int stages_per_split, int n_splits, float* ws, Epi e, int* err) {
+    using C = TcCfg<FMT, BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* a_ring = smem;
+    uint8_t* st_ring = smem + 2 * C::A_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(st_ring + C::S * C::STAGE_BYTES);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + C::S;
+    uint64_t* a_full = bars + 2 * C::S;
+    uint64_t* a_empty = a_full + 2;
+    uint64_t* acc_full = a_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int bid = blockIdx.x;
+    const int n_tile = bid % n_tiles;
+    bid /= n_tiles;
+    const int m_tile = bid % m_tiles;
+    const int split = bid / m_tiles;
+    const int64_t total_stages = K / STAGE_K;
+    const int64_t s0 = (int64_t)split * stages_per_split;
+    const int64_t s1 = min(total_stages, s0 + stages_per_split);
+    const int nst = (int)(s1 - s0);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < C::S; ++i) {
+            ptx::mbar_init(&full[i], 1);
+            ptx::mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            ptx::mbar_init(&a_full[i], 128);
+            ptx::mbar_init(&a_empty[i], 1);
+        }
+        ptx::mbar_init(acc_full, 1);
+        ptx::fence_mbar_init();
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int i = 0; i < nst && ok; ++i) {
+                int s = i % C::S;
+                if (!ptx::mbar_wait(&empty[s], ((i / C::S) & 1) ^ 1)) { ok = false; break; }
+                uint8_t* b_dst = st_ring + s * C::STAGE_BYTES;
+                uint8_t* raw_dst = b_dst + C::B_BYTES;
+                int64_t stage = s0 + i;
+                StagePtrs p = stage_ptrs(FMT, qs, sc, K, n_tile, stage);
+                ptx::mbar_expect_tx(&full[s], C::B_BYTES + C::RAW_Q + C::RAW_S);
+                ptx::tma_load_2d(b_dst, &xmap, &full[s], (int32_t)(stage * STAGE_K), m_tile * BN);
+                ptx::bulk_load(raw_dst, p.qs, C::RAW_Q, &full[s]);
+                if (C::RAW_S) ptx::bulk_load(raw_dst + C::RAW_Q, p.sc, C::RAW_S, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = ptx::idesc_f16_f32(TILE_N, BN);
+            for (int i = 0; i < nst && ok; ++i) {
+                int s = i % C::S, a = i & 1;
+                if (!ptx::mbar_wait(&full[s], (i / C::S) & 1)) { ok = false; break; }
+                if (!ptx::mbar_wait(&a_full[a], (i >> 1) & 1)) { ok = false; break; }
+                ptx::tc_fence_after();
+                uint32_t a_addr = ptx::smem_u32(a_ring + a * C::A_BYTES);
+                uint32_t b_addr = ptx::smem_u32(st_ring + s * C::STAGE_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    uint64_t ad = ptx::sdesc_sw128(a_addr + kk * 32);
+                    uint64_t bd = ptx::sdesc_sw128(b_addr + kk * 32);
+                    ptx::mma_f16_ss(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                }
+                ptx::mma_commit(&empty[s]);
+                ptx::mma_commit(&a_empty[a]);
+            }
+            ptx::mma_commit(acc_full);
+        }
+    } else {
+        // Dequant + epilogue warps: row r of the 128-row tile = TMEM lane r.
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        for (int i = 0; i < nst && ok; ++i) {
+            int s = i % C::S, a = i & 1;
+            if (!ptx::mbar_wait(&full[s], (i / C::S) & 1)) { ok = false; break; }
+            if (!ptx::mbar_wait(&a_empty[a], ((i >> 1) & 1) ^ 1)) { ok = false; break; }
+            const uint8_t* raw = st_ring + s * C::STAGE_BYTES + C::B_BYTES;
+            float w[64];
+            dequant_row_stage<FMT>(raw, raw + C::RAW_Q, r, (int)(s0 + i), w);
+            uint8_t* arow = a_ring + a * C::A_BYTES + r * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                __half2 h0 = __floats2half2_rn(w[8 * c + 0], w[8 * c + 1]);
+                __half2 h1 = __floats2half2_rn(w[8 * c + 2], w[8 * c + 3]);
+                __half2 h2 = __floats2half2_rn(w[8 * c + 4], w[8 * c + 5]);
+                __half2 h3 = __floats2half2_rn(w[8 * c + 6], w[8 * c + 7]);
+                uint4 v;
+                v.x = *reinterpret_cast<uint32_t*>(&h0);
+                v.y = *reinterpret_cast<uint32_t*>(&h1);
+                v.z = *reinterpret_cast<uint32_t*>(&h2);
+                v.w = *reinterpret_cast<uint32_t*>(&h3);
+                *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = v;
+            }
+            ptx::fence_proxy_async_smem();
+            ptx::mbar_arrive(&a_full[a]);
+        }
+        // Epilogue.
+        if (ok && ptx::mbar_wait(acc_full, 0)) {
+            ptx::tc_fence_after();
+            const int64_t n = (int64_t)n_tile * TILE_N + r;
+            const float bias_n = (e.bias && n < N) ? e.bias[n] : 0.0f;
+            const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                uint32_t v[16];
+                ptx::tmem_ld16(lane_addr + c0, v);
+                ptx::tmem_ld_wait();
+                if (n < N) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        int64_t m = (int64_t)m_tile * BN + c0 + j;
+                        if (m < M) {
+                            float acc = __uint_as_float(v[j]);
+                            if (n_splits == 1) epi_store(e, m, n, acc, bias_n);
+                            else ws[((int64_t)split * M + m) * N + n] = acc;
+                        }
+                    }
+                }
+            }
+        } else {
+            ok = false;
+        }
+    }
+    if (!ok && err) atomicExch(err, 1);
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host dispatch
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, []() {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    if (!fn) fail(VKB_ERROR_BACKEND_UNAVAILABLE, "cuTensorMapEncodeTiled is unavailable from the driver");
+    return fn;
+}
+
+// 2-D tensor map over a row-major f16 matrix [rows][cols], box [box_rows][64], 128-byte swizzle.
+void make_tmap_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows) {
+    if (((uintptr_t)base & 15) || (cols * 2) % 16)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "activation rows must be 16-byte aligned (k % 8 == 0, aligned base)");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = get_encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(VKB_ERROR_BACKEND_UNAVAILABLE, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+}
+
+static int* device_err_flag(vkb_context* ctx) { return ctx->err_flag.as<int>(); }
+
+int gemv_max_m() { return 4; }
+
+template <int FMT>
+static void launch_gemv(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_f16, const Epi& e,
+                        float* ws, int stages_per_split, int splits) {
+    dim3 grid((unsigned)(w->n_pad / TILE_N), (unsigned)splits);
+    const uint8_t* qs = w->qs.as<uint8_t>();
+    const uint8_t* sc = w->sc.as<uint8_t>();
+#define VKB_GEMV(MMv)                                                                                           \
+    {                                                                                                           \
+        size_t sm = (size_t)(MMv)*stages_per_split * STAGE_K * sizeof(float);                                   \
+        static bool attr = false;                                                                               \
+        if (!attr) {                                                                                            \
+            VKB_CUDA(cudaFuncSetAttribute(gemv_kernel<FMT, MMv>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
+                                          200 * 1024));                                                         \
+            attr = true;                                                                                        \
+        }                                                                                                       \
+        gemv_kernel<FMT, MMv><<<grid, 128, sm, ctx->stream>>>(qs, sc, w->k, w->n, m, a, a_f16, stages_per_split, \
+                                                              splits, ws, e);                                   \
+    }
+    if (m <= 1) VKB_GEMV(1) else if (m <= 2) VKB_GEMV(2) else VKB_GEMV(4)
+#undef VKB_GEMV
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
+}
+
+template <int FMT, int BN>
+static void launch_tc(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const Epi& e, float* ws,
+                      int stages_per_split, int splits, int m_tiles) {
+    using C = TcCfg<FMT, BN>;
+    static bool attr = false;
+    if (!attr) {
+        VKB_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<FMT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr = true;
+    }
+    CUtensorMap map;
+    make_tmap_f16(&map, a16, m, w->k, BN);
+    int n_tiles = (int)(w->n_pad / TILE_N);
+    dim3 grid((unsigned)(n_tiles * m_tiles * splits));
+    tc_gemm_kernel<FMT, BN><<<grid, 192, C::SMEM, ctx->stream>>>(
+        map, w->qs.as<uint8_t>(), w->sc.as<uint8_t>(), w->k, w->n, m, n_tiles, m_tiles, stages_per_split, splits, ws,
+        e, device_err_flag(ctx));
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
+}
+
+template <int FMT>
+static void dispatch_tc(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const Epi& e, float* ws,
+                        int bn, int sps, int splits, int m_tiles) {
+    switch (bn) {
+        case 32: launch_tc<FMT, 32>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
+        case 64: launch_tc<FMT, 64>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
+        case 128: launch_tc<FMT, 128>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
+        default: launch_tc<FMT, 256>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
+    }
+}
+
+LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m) {
+    LinearPlan p;
+    const int64_t total = w->k / STAGE_K;
+    const int n_tiles = (int)(w->n_pad / TILE_N);
+    const int sms = ctx->sm_count;
+    if (m <= gemv_max_m()) {
+        p.tc = false;
+        // Enough CTAs to cover the SMs several times; at least 2 stages each.
+        int splits = std::max(1, std::min<int>((int)(total / 2), (4 * sms + n_tiles - 1) / n_tiles));
+        int sps = (int)((total + splits - 1) / splits);
+        sps = std::min(sps, 48);  // activation staging <= 48 KB per row of m
+        splits = (int)((total + sps - 1) / sps);
+        p.splits = splits;
+        p.sps = sps;
+    } else {
+        p.tc = true;
+        int bn = m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256;
+        int m_tiles = (int)((m + bn - 1) / bn);
+        if (bn == 256 && (int64_t)n_tiles * m_tiles < sms) {
+            bn = 128;
+            m_tiles = (int)((m + bn - 1) / bn);
+        }
+        int ctas = n_tiles * m_tiles;
+        int splits = 1;
+        if (ctas < sms) splits = std::max(1, std::min<int>((int)(total / 2), sms / ctas));
+        int sps = (int)((total + splits - 1) / splits);
+        splits = (int)((total + sps - 1) / sps);
+        p.bn = bn;
+        p.m_tiles = m_tiles;
+        p.splits = splits;
+        p.sps = sps;
+    }
+    p.ws_bytes = (p.splits > 1 ? (size_t)p.splits * m * w->n * sizeof(float) : 0);
+    p.a16_bytes = 0;
+    return p;
+}
+
+void run_linear(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_dtype, const float* bias,
+                void* out, int out_dtype, int epilogue, const float* residual, float scale, float* ws_override,
+                __half* a16_override) {
+    if (m <= 0) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: m must be positive");
+    if (!a || !out) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: null activation or output pointer");
+    if (a_dtype != VKB_DT_F32 && a_dtype != VKB_DT_F16) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: bad a_dtype");
+    if (out_dtype != VKB_DT_F32 && out_dtype != VKB_DT_F16) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: bad out_dtype");
+    if (epilogue < VKB_EPI_NONE || epilogue > VKB_EPI_SCALE) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: bad epilogue");
+    if (epilogue == VKB_EPI_RESIDUAL && (out_dtype != VKB_DT_F32 || !residual))
+        fail(VKB_ERROR_INVALID_ARGUMENT, "linear: the residual epilogue needs an f32 output and a residual pointer");
+    LinearPlan p = plan_linear(ctx, w, m);
+    Epi e{bias, residual, out, out_dtype == VKB_DT_F16, epilogue, scale, w->n};
+    // Workspace: [f16 copy of a (tc path with f32 input)] [split partials]
+    size_t a16_bytes = (p.tc && a_dtype == VKB_DT_F32 && !a16_override) ? ((size_t)m * w->k * 2 + 255) / 256 * 256 : 0;
+    size_t ws_bytes = ws_override ? 0 : p.ws_bytes;
+    if (a16_bytes + ws_bytes) ctx->ensure_workspace(a16_bytes + ws_bytes);
+    uint8_t* wsb = ctx->workspace.as<uint8_t>();
+    float* ws = ws_override ? ws_override : reinterpret_cast<float*>(wsb + a16_bytes);
+    if (!p.tc) {
+        switch (w->fmt) {
+            case W_Q4_0: launch_gemv<W_Q4_0>(ctx, w, m, a, a_dtype == VKB_DT_F16, e, ws, p.sps, p.splits); break;
+            case W_Q8_0: launch_gemv<W_Q8_0>(ctx, w, m, a, a_dtype == VKB_DT_F16, e, ws, p.sps, p.splits); break;
+            case W_Q4_K: launch_gemv<W_Q4_K>(ctx, w, m, a, a_dtype == VKB_DT_F16, e, ws, p.sps, p.splits); break;
+            default: launch_gemv<W_F16>(ctx, w, m, a, a_dtype == VKB_DT_F16, e, ws, p.sps, p.splits); break;
+        }
+    } else {
+        const __half* a16;
+        if (a_dtype == VKB_DT_F16) {
+            a16 = reinterpret_cast<const __half*>(a);
+        } else {
+            __half* dst = a16_override ? a16_override : reinterpret_cast<__half*>(wsb);
+            int64_t n = m * w->k;
+            int64_t thr = (n + 3) / 4;
+            f32_to_f16_kernel<<<(unsigned)((thr + 255) / 256), 256, 0, ctx->stream>>>(
+                reinterpret_cast<const float*>(a), dst, n);
+            VKB_CUDA(cudaGetLastError());
+            ctx->count();
+            a16 = dst;
+        }
+        switch (w->fmt) {
+            case W_Q4_0: dispatch_tc<W_Q4_0>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
+            case W_Q8_0: dispatch_tc<W_Q8_0>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
+            case W_Q4_K: dispatch_tc<W_Q4_K>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
+            default: dispatch_tc<W_F16>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
+        }
+    }
+    if (p.splits > 1) {
+        int64_t tot = m * w->n;
+        splitk_reduce_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, ctx->stream>>>(ws, p.splits, m, w->n, e);
+        VKB_CUDA(cudaGetLastError());
+        ctx->count();
+    }
+}
+
+int read_and_clear_err_flag(vkb_context* ctx) {
+    int* f = device_err_flag(ctx);
+    int h = 0;
+    VKB_CUDA(cudaMemcpyAsync(&h, f, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+    VKB_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (h) VKB_CUDA(cudaMemsetAsync(f, 0, sizeof(int), ctx->stream));
+    return h;
+}
+
+}  // namespace vkb
+
+using namespace vkb;
+
+extern "C" {
+
+vkb_status vkb_weight_upload(vkb_context* ctx, uint32_t ggml_type, int64_t n, int64_t k, const void* bytes,
+                             size_t len, vkb_weight** out) {
+    return guard([&] {
+        if (!out) fail(VKB_ERROR_INVALID_ARGUMENT, "weight_upload: null out");
+        *out = upload_weight(ctx, ggml_type, n, k, bytes, len);
+    });
+}
+
+vkb_status vkb_weight_destroy(vkb_weight* w) {
+    return guard([&] { delete w; });
+}
+
+size_t vkb_weight_device_bytes(const vkb_weight* w) { return w ? w->qs.n + w->sc.n : 0; }
+
+vkb_status vkb_linear(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a_dev, int a_dtype,
+                      const float* bias_dev, void* out_dev, int out_dtype, int epilogue, const float* residual_dev,
+                      float scale) {
+    return guard([&] {
+        if (!ctx || !w) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: null context or weight");
+        if (w->ctx != ctx) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: weight belongs to another context");
+        run_linear(ctx, w, m, a_dev, a_dtype, bias_dev, out_dev, out_dtype, epilogue, residual_dev, scale, nullptr,
+                   nullptr);
+    });
+}
+
+vkb_status vkb_gemm_q_f32(vkb_context* ctx, int64_t m, int64_t n, int64_t k, const float* a_host, const void* wq_host,
+                          size_t wq_len, uint32_t ggml_type, const float* bias_host, float* out_host) {
+    return guard([&] {
+        if (!ctx) fail(VKB_ERROR_INVALID_ARGUMENT, "gemm_q_f32: null context");
+        if (!a_host || !wq_host || !out_host) fail(VKB_ERROR_INVALID_ARGUMENT, "gemm_q_f32: null buffer");
+        if (m <= 0) fail(VKB_ERROR_INVALID_ARGUMENT, "gemm_q_f32: m must be positive");
+        std::unique_ptr<vkb_weight> w(upload_weight(ctx, ggml_type, n, k, wq_host, wq_len));
+        DevBuf a((size_t)m * k * 4), o((size_t)m * n * 4), b(bias_host ? (size_t)n * 4 : 0);
+        VKB_CUDA(cudaMemcpyAsync(a.p, a_host, a.n, cudaMemcpyHostToDevice, ctx->stream));
+        if (bias_host) VKB_CUDA(cudaMemcpyAsync(b.p, bias_host, b.n, cudaMemcpyHostToDevice, ctx->stream));
+        run_linear(ctx, w.get(), m, a.p, VKB_DT_F32, bias_host ? b.as<float>() : nullptr, o.p, VKB_DT_F32,
+                   VKB_EPI_NONE, nullptr, 1.0f, nullptr, nullptr);
+        VKB_CUDA(cudaMemcpyAsync(out_host, o.p, o.n, cudaMemcpyDeviceToHost, ctx->stream));
+        VKB_CUDA(cudaStreamSynchronize(ctx->stream));
+        if (read_and_clear_err_flag(ctx)) fail(VKB_ERROR_OTHER, "gemm_q_f32: a pipeline wait timed out on the device");
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,30 @@
+// linear.cuh — internal interface of the quantized Linear (linear.cu).
+#pragma once
+#include "common.cuh"
+#include "weights.cuh"
+#include <cuda.h>
+
+namespace vkb {
+
+struct LinearPlan {
+    bool tc = false;     // tcgen05 GEMM (else the streaming GEMV)
+    int bn = 0;          // token tile of the GEMM
+    int m_tiles = 0;
+    int splits = 1;      // K splits (partials reduced by splitk_reduce_kernel)
+    int sps = 0;         // stages per split
+    size_t ws_bytes = 0; // fp32 partials
+    size_t a16_bytes = 0;
+};
+
+vkb_weight* upload_weight(vkb_context* ctx, uint32_t tag, int64_t n, int64_t k, const void* bytes, size_t len);
+LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m);
+// Runs out = epilogue(a . W^T + bias). ws_override / a16_override let a caller
+// that pre-sized its own scratch avoid the context workspace.
+void run_linear(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_dtype, const float* bias,
+                void* out, int out_dtype, int epilogue, const float* residual, float scale, float* ws_override,
+                __half* a16_override);
+void make_tmap_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows);
+int read_and_clear_err_flag(vkb_context* ctx);
+int gemv_max_m();
+
+}  // namespace vkb
