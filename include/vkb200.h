@@ -248,6 +248,61 @@ VKB_API vkb_status vkb_attention_dense(vkb_context* ctx, int32_t n_tok, int32_t 
 VKB_API vkb_status vkb_quantize_rows_q8_0(vkb_context* ctx, const float* x_dev, int64_t n_rows, int32_t width,
                                   void* q_dev, void* d_dev);
 
+
+/* ---- Whisper model and decode session ------------------------------------ */
+
+/* Model hyper-parameters read from the GGUF metadata (vokra.whisper.*,
+ * crates/vokra-models/src/whisper/config.rs:19-50). */
+typedef struct vkb_whisper_dims {
+    int32_t n_mels, n_audio_ctx, d_model, n_audio_head, n_audio_layer;
+    int32_t n_text_ctx, n_text_head, n_text_layer, n_vocab, ffn_dim, eot;
+    int32_t n_start_ids;
+    int32_t start_ids[8];
+} vkb_whisper_dims;
+
+/* Loads a Whisper GGUF (tensor names of crates/vokra-models/src/whisper/weights.rs:302-360)
+ * and repacks every Linear once into the device tile layout. Linear weights
+ * may be Q4_0, Q8_0, Q4_K, F16 or F32; conv / positional / LayerNorm tensors
+ * F32, F16 or BF16. The file is read once and not kept. */
+VKB_API vkb_status vkb_whisper_load(vkb_context* ctx, const char* gguf_path, vkb_whisper** out);
+VKB_API vkb_status vkb_whisper_get_dims(const vkb_whisper* m, vkb_whisper_dims* out);
+VKB_API vkb_status vkb_whisper_destroy(vkb_whisper* m);
+
+typedef struct vkb_session_options {
+    int32_t max_streams;      /* concurrent utterances (KV streams, cross-store slots) */
+    int32_t max_step_tokens;  /* tokens per decode step (e.g. 4 * max_streams for prefixes) */
+    int32_t max_clips;        /* clips per vkb_session_encode call (0 = no encoder buffers) */
+    int32_t cross_kv_q8;      /* 1: cross K/V stored as Q8_0 int8 + f16 scales; 0: f16 */
+    int32_t kv_page_tokens;   /* self-attention page size (0 = 16) */
+} vkb_session_options;
+
+/* A batched decoding session (the DecoderStepSession / CudaDecodeSession seam,
+ * crates/vokra-models/src/compute.rs:2892-3140): owns the paged Q8_0
+ * self-attention cache (sequence layout), the cross-attention store and every
+ * device buffer; nothing is allocated per step. */
+VKB_API vkb_status vkb_session_create(vkb_whisper* m, const vkb_session_options* opt, vkb_session** out);
+VKB_API vkb_status vkb_session_destroy(vkb_session* s);
+/* Runs the encoder on n_clips log-mels ([n_clips][n_mels][2*n_audio_ctx] f32,
+ * device) and projects every decoder layer's cross K/V into the stream slots
+ * streams_host[i] (once per utterance, decoder.rs:205-216). */
+VKB_API vkb_status vkb_session_encode(vkb_session* s, int32_t n_clips, const float* logmel_dev,
+                                      const int32_t* streams_host);
+/* Device pointer to the last encoder output [n_clips][n_audio_ctx][d_model] f32 (after ln_post). */
+VKB_API const float* vkb_session_encoder_output(const vkb_session* s);
+/* One decoder step over n_tok tokens (token i of stream streams_host[i] at
+ * position positions_host[i]; tokens of one stream contiguous and
+ * consecutive): appends their self-attention K/V, writes logits
+ * [n_tok][n_vocab] f32 (logits_dev, or the session's buffer when NULL) and the
+ * greedy argmax ids (ids_dev, or the session's buffer when NULL). Asynchronous
+ * on the context stream. */
+VKB_API vkb_status vkb_session_step(vkb_session* s, int32_t n_tok, const int32_t* streams_host,
+                                    const int32_t* positions_host, const int32_t* tokens_host,
+                                    float* logits_dev, int32_t* ids_dev);
+VKB_API const float* vkb_session_logits(const vkb_session* s);
+VKB_API const int32_t* vkb_session_ids(const vkb_session* s);
+/* Returns a finished stream's KV pages to the pool (continuous batching). */
+VKB_API vkb_status vkb_session_release(vkb_session* s, int32_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -31,6 +31,7 @@ def lib():
             "orc_quantize": (C.c_int, [C.c_uint32, P, C.c_size_t, P]),
             "orc_set_threads": (None, [C.c_int]),
             "orc_linear_f32": (None, [C.c_int, C.c_int, C.c_int, P, P, P, P]),
+            "orc_gemm_f32": (None, [C.c_int, C.c_int, C.c_int, P, P, P, P]),
             "orc_linear_q": (C.c_int, [C.c_uint32, C.c_int, C.c_int, C.c_int, P, P, C.c_size_t, P, P]),
             "orc_kquant_gemm_i8": (C.c_int, [C.c_uint32, C.c_int, C.c_int, C.c_int, P, P, C.c_size_t, P, P]),
             "orc_int8_error_bound": (C.c_float, [C.c_uint32, P, C.c_int, P]),
@@ -142,6 +143,17 @@ def linear_f32(a, w, bias=None):
     m = a.size // k
     out = np.zeros((m, n), np.float32)
     lib().orc_linear_f32(m, n, k, _p(a), _p(w), _p(None if bias is None else f32(bias)), _p(out))
+    return out
+
+
+def gemm_kn(a, wt, bias=None):
+    """gemm_f32 with a pre-transposed [k][n] weight (the reference's load-time layout)."""
+    a = f32(a)
+    wt = f32(wt)
+    k, n = wt.shape
+    m = a.size // k
+    out = np.zeros((m, n), np.float32)
+    lib().orc_gemm_f32(m, n, k, _p(a), _p(wt), _p(None if bias is None else f32(bias)), _p(out))
     return out
 
 

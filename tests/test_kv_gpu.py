@@ -22,7 +22,8 @@ def _rows(rng, n, w):
     if n > 1:
         x[1, :32] = 1e-30
         x[1, 40] = np.nan
-        x[1, 64:96] = np.float32(127.0) * np.arange(32, dtype=np.float32) / 64
+        if w >= 96:
+            x[1, 64:96] = np.float32(127.0) * np.arange(32, dtype=np.float32) / 64
     return x
 
 

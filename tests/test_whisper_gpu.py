@@ -1,0 +1,86 @@
+"""End-to-end Whisper forward on the B200 against the oracle forward
+(route R1 with the self-attention cache in Q8_0 pages and the cross K/V in Q8_0)."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import whisper_ref
+from vokra_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel_rms(a, b):
+    return float(np.sqrt(np.mean((a - b) ** 2)) / (np.sqrt(np.mean(b ** 2)) + 1e-30))
+
+
+@pytest.fixture(scope="module", params=[synth.Q8_0, synth.Q4_0, synth.Q4_K])
+def tiny(request, tmp_path_factory):
+    path = str(tmp_path_factory.mktemp("w") / f"tiny_{request.param}.gguf")
+    synth.write_synthetic_whisper(path, synth.WHISPER_TINY_TEST, request.param, seed=1)
+    return path
+
+
+def _run(ctx, path, n_streams=3, n_steps=6, cross_q8=True, arch=synth.WHISPER_TINY_TEST, seed=2):
+    import torch
+    from vokra_b200 import whisper
+    rng = np.random.default_rng(seed)
+    a = arch
+    logmel = rng.uniform(-1.0, 1.5, (n_streams, a.n_mels, 2 * a.n_audio_ctx)).astype(np.float32)
+    model = whisper.WhisperModel(ctx, path)
+    sess = whisper.Session(model, max_streams=n_streams, max_clips=n_streams, cross_kv_q8=cross_q8)
+    sess.encode(torch.from_numpy(logmel).cuda(), list(range(n_streams)))
+    enc = sess.encoder_output(n_streams)
+    ref = whisper_ref.RefWhisper(path)
+    ref_enc = [ref.encode(logmel[i]) for i in range(n_streams)]
+    decs = [ref.decoder(ref_enc[i], kv_mode="q8", cross_mode="q8" if cross_q8 else "f16") for i in range(n_streams)]
+    toks = rng.integers(0, a.n_vocab, (n_streams, n_steps)).tolist()
+    V = a.n_vocab
+    results = []
+    # prefix step: the start ids for every stream in one step
+    prefix = list(a.start_ids)
+    streams = [s for s in range(n_streams) for _ in prefix]
+    positions = [p for _ in range(n_streams) for p in range(len(prefix))]
+    tokens = prefix * n_streams
+    out = torch.zeros((len(tokens), V), dtype=torch.float32, device="cuda:0")
+    sess.step(streams, positions, tokens, logits_dev=out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().reshape(n_streams, len(prefix), V)
+    for s in range(n_streams):
+        results.append((got[s], decs[s].step(prefix)))
+    pos = len(prefix)
+    for t in range(n_steps):
+        out = torch.zeros((n_streams, V), dtype=torch.float32, device="cuda:0")
+        sess.step(list(range(n_streams)), [pos] * n_streams, [toks[s][t] for s in range(n_streams)], logits_dev=out)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        for s in range(n_streams):
+            results.append((got[s:s + 1], decs[s].step([toks[s][t]])))
+        pos += 1
+    return enc, np.stack(ref_enc), results
+
+
+def test_tiny_whisper_matches_oracle(ctx, tiny):
+    enc, ref_enc, results = _run(ctx, tiny)
+    assert _rel_rms(enc, ref_enc) <= 2e-3
+    worst_abs, worst_rms = 0.0, 0.0
+    mism = 0
+    for got, ref in results:
+        worst_abs = max(worst_abs, float(np.max(np.abs(got - ref))))
+        worst_rms = max(worst_rms, _rel_rms(got, ref))
+        for r in range(ref.shape[0]):
+            top2 = np.sort(ref[r])[-2:]
+            if top2[1] - top2[0] > 1e-3 and int(np.argmax(got[r])) != int(np.argmax(ref[r])):
+                mism += 1
+    print(f"logits max-abs {worst_abs:.3e} rel-rms {worst_rms:.3e}")
+    assert worst_abs <= 1e-2
+    assert worst_rms <= 1e-3
+    assert mism == 0
+
+
+def test_tiny_whisper_f16_cross_store(ctx, tiny):
+    enc, ref_enc, results = _run(ctx, tiny, n_streams=2, n_steps=3, cross_q8=False)
+    for got, ref in results:
+        assert np.max(np.abs(got - ref)) <= 1e-2
+        assert _rel_rms(got, ref) <= 1e-3

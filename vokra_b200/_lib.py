@@ -58,6 +58,11 @@ class KvPoolDesc(C.Structure):
     ]
 
 
+class SessionOptions(C.Structure):
+    _fields_ = [("max_streams", C.c_int32), ("max_step_tokens", C.c_int32), ("max_clips", C.c_int32),
+                ("cross_kv_q8", C.c_int32), ("kv_page_tokens", C.c_int32)]
+
+
 class WhisperDims(C.Structure):
     _fields_ = [
         ("n_mels", C.c_int32), ("n_audio_ctx", C.c_int32), ("d_model", C.c_int32),
@@ -106,6 +111,17 @@ SIGNATURES = {
     "vkb_kv_read_step": (C.c_int, [P, I32, I32, I32, P, P]),
     "vkb_attention_dense": (C.c_int, [P, I32, I32, I32, P, P, P, P, P, P, I32, I32, P, I32]),
     "vkb_quantize_rows_q8_0": (C.c_int, [P, P, I64, I32, P, P]),
+    "vkb_whisper_load": (C.c_int, [P, C.c_char_p, PP]),
+    "vkb_whisper_get_dims": (C.c_int, [P, C.POINTER(WhisperDims)]),
+    "vkb_whisper_destroy": (C.c_int, [P]),
+    "vkb_session_create": (C.c_int, [P, C.POINTER(SessionOptions), PP]),
+    "vkb_session_destroy": (C.c_int, [P]),
+    "vkb_session_encode": (C.c_int, [P, I32, P, P]),
+    "vkb_session_encoder_output": (P, [P]),
+    "vkb_session_step": (C.c_int, [P, I32, P, P, P, P, P]),
+    "vkb_session_logits": (P, [P]),
+    "vkb_session_ids": (P, [P]),
+    "vkb_session_release": (C.c_int, [P, I32]),
 }
 
 _lib = None

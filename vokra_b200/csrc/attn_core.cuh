@@ -105,7 +105,8 @@ struct AttnGroup {
 // Partial layout in the workspace, per (group, split, query):
 //   acc[W] then m[H] then l[H]  (floats)
 template <class F, int MAXQ>
-__device__ __forceinline__ void attn_body(const F& fetch, const float* __restrict__ q, const AttnGroup& g, int n_head,
+__device__ __forceinline__ void attn_body(const F& fetch, const float* __restrict__ q, int64_t q_ld, const AttnGroup& g,
+                                          int n_head,
                                           int d_head, int W, int key_begin, int key_end, int split, int n_splits,
                                           void* ctx_out, int out_f16, float* ws) {
     extern __shared__ float sm[];
@@ -126,7 +127,7 @@ __device__ __forceinline__ void attn_body(const F& fetch, const float* __restric
 #pragma unroll
         for (int c = 0; c < 16; ++c) acc[i][c] = 0.0f;
         if (active && i < g.n_q) {
-            const float4* q4 = reinterpret_cast<const float4*>(q + (int64_t)(g.first_tok + i) * W + c0);
+            const float4* q4 = reinterpret_cast<const float4*>(q + (int64_t)(g.first_tok + i) * q_ld + c0);
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 float4 t = q4[c];

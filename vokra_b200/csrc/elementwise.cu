@@ -1,0 +1,200 @@
+// elementwise.cu — layer norm, token embedding, conv stem im2col, positional
+// add and argmax for the Whisper forward.
+#include "common.cuh"
+#include "weights.cuh"
+#include "elementwise.cuh"
+
+namespace vkb {
+
+// One warp per row; two passes over the row held in registers (cols <= 2048).
+template <int PER>
+__global__ void layer_norm_kernel(const float* __restrict__ x, int64_t rows, int cols, const float* __restrict__ g,
+                                  const float* __restrict__ b, float eps, void* out, int out_f16) {
+    const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* xr = x + row * cols;
+    float v[PER];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        int c = lane + 32 * i;
+        v[i] = c < cols ? xr[c] : 0.0f;
+        s += v[i];
+    }
+    s = warp_sum(s);
+    const float inv_cols = 1.0f / (float)cols;
+    const float mean = s * inv_cols;
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        int c = lane + 32 * i;
+        float d = c < cols ? v[i] - mean : 0.0f;
+        q += d * d;
+    }
+    q = warp_sum(q);
+    const float inv_std = 1.0f / sqrtf(q * inv_cols + eps);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        int c = lane + 32 * i;
+        if (c >= cols) break;
+        float y = (v[i] - mean) * inv_std * g[c] + b[c];
+        if (out_f16) reinterpret_cast<__half*>(out)[row * cols + c] = __float2half_rn(y);
+        else reinterpret_cast<float*>(out)[row * cols + c] = y;
+    }
+}
+
+void run_layer_norm(vkb_context* ctx, const float* x, int64_t rows, int cols, const float* g, const float* b, float eps,
+                    void* out, int out_f16) {
+    if (cols > 2048) fail(VKB_ERROR_UNSUPPORTED_OP, "layer_norm: row width above 2048");
+    unsigned grid = (unsigned)((rows * 32 + 255) / 256);
+    if (cols <= 512) layer_norm_kernel<16><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_f16);
+    else if (cols <= 1280) layer_norm_kernel<40><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_f16);
+    else layer_norm_kernel<64><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_f16);
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
+}
+
+// One thread per (token, 64-wide stage) of the embedding row.
+template <int FMT>
+__global__ void embed_kernel(const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc, int64_t K,
+                             const int32_t* __restrict__ tokens, const int32_t* __restrict__ positions, int n_tok,
+                             const float* __restrict__ pos, float* __restrict__ h) {
+    const int stages = (int)(K / STAGE_K);
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)n_tok * stages) return;
+    const int t = (int)(i / stages), s = (int)(i % stages);
+    const int64_t row = tokens[t];
+    StagePtrs p = stage_ptrs(FMT, qs, sc, K, row / TILE_N, s);
+    float w[64];
+    dequant_row_stage<FMT>(p.qs, p.sc, (int)(row % TILE_N), s, w);
+    const float* pe = pos + (int64_t)positions[t] * K + s * 64;
+    float* dst = h + (int64_t)t * K + s * 64;
+#pragma unroll
+    for (int e = 0; e < 64; ++e) dst[e] = w[e] + pe[e];
+}
+
+void run_embed(vkb_context* ctx, const vkb_weight* w, const int32_t* tokens, const int32_t* positions, int n_tok,
+               const float* pos, float* h) {
+    int64_t n = (int64_t)n_tok * (w->k / STAGE_K);
+    unsigned grid = (unsigned)((n + 127) / 128);
+    const uint8_t* qs = w->qs.as<uint8_t>();
+    const uint8_t* sc = w->sc.as<uint8_t>();
+    switch (w->fmt) {
+        case W_Q4_0: embed_kernel<W_Q4_0><<<grid, 128, 0, ctx->stream>>>(qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
+        case W_Q8_0: embed_kernel<W_Q8_0><<<grid, 128, 0, ctx->stream>>>(qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
+        case W_Q4_K: embed_kernel<W_Q4_K><<<grid, 128, 0, ctx->stream>>>(qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
+        default: embed_kernel<W_F16><<<grid, 128, 0, ctx->stream>>>(qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
+    }
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
+}
+
+// col[b*To + t][c*3 + kk] = x[b][c][t*stride + kk - 1]; columns C*3 .. ldc-1 are zero
+__global__ void im2col_ct_kernel(const float* __restrict__ x, int B, int C, int T, int To, int stride, int ldc,
+                                 __half* __restrict__ col) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t total = (int64_t)B * To * ldc;
+    if (i >= total) return;
+    const int64_t r = i / ldc;
+    const int cc = (int)(i % ldc);
+    if (cc >= C * 3) {
+        col[i] = __float2half_rn(0.0f);
+        return;
+    }
+    const int c = cc / 3, kk = cc % 3;
+    const int b = (int)(r / To), t = (int)(r % To);
+    const int p = t * stride + kk - 1;
+    float v = (p >= 0 && p < T) ? x[((int64_t)b * C + c) * T + p] : 0.0f;
+    col[i] = __float2half_rn(v);
+}
+
+// col[b*To + t][c*3 + kk] = x[b*T + t*stride + kk - 1][c]
+__global__ void im2col_tc_kernel(const __half* __restrict__ x, int B, int C, int T, int To, int stride,
+                                 __half* __restrict__ col) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t total = (int64_t)B * To * C * 3;
+    if (i >= total) return;
+    const int64_t r = i / (C * 3);
+    const int cc = (int)(i % (C * 3));
+    const int c = cc / 3, kk = cc % 3;
+    const int b = (int)(r / To), t = (int)(r % To);
+    const int p = t * stride + kk - 1;
+    col[i] = (p >= 0 && p < T) ? x[((int64_t)b * T + p) * C + c] : __float2half_rn(0.0f);
+}
+
+static int conv_out(int T, int stride) { return (T + 2 - 3) / stride + 1; }
+
+void run_im2col_ct(vkb_context* ctx, const float* x, int B, int C, int T, int stride, int ldc, __half* col) {
+    int To = conv_out(T, stride);
+    int64_t total = (int64_t)B * To * ldc;
+    im2col_ct_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(x, B, C, T, To, stride, ldc, col);
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
+}
+
+void run_im2col_tc(vkb_context* ctx, const __half* x, int B, int C, int T, int stride, __half* col) {
+    int To = conv_out(T, stride);
+    int64_t total = (int64_t)B * To * C * 3;
+    im2col_tc_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(x, B, C, T, To, stride, col);
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
+}
+
+__global__ void add_pos_kernel(const __half* __restrict__ y, const float* __restrict__ pos, int B, int T, int C,
+                               float* __restrict__ h) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t total = (int64_t)B * T * C;
+    if (i >= total) return;
+    const int64_t tc = i % ((int64_t)T * C);
+    h[i] = __half2float(y[i]) + pos[tc];
+}
+
+void run_add_pos(vkb_context* ctx, const __half* y, const float* pos, int B, int T, int C, float* h) {
+    int64_t total = (int64_t)B * T * C;
+    add_pos_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(y, pos, B, T, C, h);
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
+}
+
+// One CTA per row; first index of the maximum wins ties.
+__global__ void argmax_kernel(const float* __restrict__ logits, int n_cols, int32_t* __restrict__ ids) {
+    const float* r = logits + (int64_t)blockIdx.x * n_cols;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int j = threadIdx.x; j < n_cols; j += blockDim.x) {
+        float v = r[j];
+        if (v > best || (v == best && j < bi)) { best = v; bi = j; }
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) { sv[w] = best; si[w] = bi; }
+    __syncthreads();
+    if (w == 0) {
+        const int nw = blockDim.x >> 5;
+        best = l < nw ? sv[l] : -INFINITY;
+        bi = l < nw ? si[l] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+        }
+        if (l == 0) ids[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
+void run_argmax(vkb_context* ctx, const float* logits, int n_rows, int n_cols, int32_t* ids) {
+    argmax_kernel<<<n_rows, 512, 0, ctx->stream>>>(logits, n_cols, ids);
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
+}
+
+}  // namespace vkb

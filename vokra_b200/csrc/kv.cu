@@ -16,6 +16,7 @@
 // reassembles the reference's 34-byte on-wire blocks from the two planes.
 #include "common.cuh"
 #include "attn_core.cuh"
+#include "kv.cuh"
 #include <algorithm>
 
 using namespace vkb;
@@ -66,7 +67,7 @@ __device__ __forceinline__ void q8_0_block_warp(float x, int lane, int8_t* q_out
     if (lane == 0) *reinterpret_cast<uint16_t*>(d_out) = f32_to_f16_bits(d);
 }
 
-__global__ void kv_append_kernel(const float* __restrict__ k, const float* __restrict__ v,
+__global__ void kv_append_kernel(const float* __restrict__ k, const float* __restrict__ v, int64_t ld,
                                  const int64_t* __restrict__ rows, int n_tok, int W, int8_t* kq, __half* kd,
                                  int8_t* vq, __half* vd) {
     const int nb = W / 32;
@@ -76,29 +77,33 @@ __global__ void kv_append_kernel(const float* __restrict__ k, const float* __res
     const int is_v = (int)(gw / ((int64_t)n_tok * nb));
     const int64_t rem = gw % ((int64_t)n_tok * nb);
     const int tok = (int)(rem / nb), b = (int)(rem % nb);
-    const float* src = (is_v ? v : k) + (int64_t)tok * W + b * 32;
+    const float* src = (is_v ? v : k) + (int64_t)tok * ld + b * 32;
     const int64_t row = rows[tok];
     int8_t* q = (is_v ? vq : kq) + row * W + b * 32;
     __half* d = (is_v ? vd : kd) + row * nb + b;
     q8_0_block_warp(src[lane], lane, q, d);
 }
 
-// Quantizes dense rows [n_rows][W] into the two planes (same arithmetic).
-__global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t n_rows, int W, int8_t* q, __half* d) {
+// Quantizes dense rows [n_rows][W] (row stride ld) into the two planes (same
+// arithmetic). With a group map, source row r lands in destination row
+// map[r / group] * group + r % group.
+__global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t ld, int64_t n_rows, int W, int8_t* q,
+                                     __half* d, const int32_t* __restrict__ map, int group) {
     const int nb = W / 32;
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (gw >= n_rows * nb) return;
     const int64_t row = gw / nb;
     const int b = (int)(gw % nb);
-    q8_0_block_warp(x[row * W + b * 32 + lane], lane, q + row * W + b * 32, d + row * nb + b);
+    const int64_t dst = map ? (int64_t)map[row / group] * group + row % group : row;
+    q8_0_block_warp(x[row * ld + b * 32 + lane], lane, q + dst * W + b * 32, d + dst * nb + b);
 }
 
 // ---------------------------------------------------------------------------
 // Attention kernels
 // ---------------------------------------------------------------------------
 template <int MAXQ>
-__global__ void paged_attn_kernel(FetchPagedQ8 f, const float* __restrict__ q, const AttnGroup* __restrict__ groups,
+__global__ void __launch_bounds__(MAXQ > 1 ? ATTN_MAX_THREADS / 2 : ATTN_MAX_THREADS) paged_attn_kernel(FetchPagedQ8 f, const float* __restrict__ q, int64_t q_ld, const AttnGroup* __restrict__ groups,
                                   int n_head, int d_head, int keys_per_split, int n_splits, void* ctx_out,
                                   int out_f16, float* ws, int per_seq_base, int ppseq) {
     const AttnGroup g = groups[blockIdx.x];
@@ -109,12 +114,12 @@ __global__ void paged_attn_kernel(FetchPagedQ8 f, const float* __restrict__ q, c
     FetchPagedQ8 ff = f;
     if (per_seq_base) ff.table_base = g.seq * ppseq;
     else ff.slot = g.seq;
-    attn_body<FetchPagedQ8, MAXQ>(ff, q, g, n_head, d_head, f.W, kb, max(kb, ke), split, n_splits, ctx_out, out_f16,
-                                  ws);
+    attn_body<FetchPagedQ8, MAXQ>(ff, q, q_ld, g, n_head, d_head, f.W, kb, max(kb, ke), split, n_splits, ctx_out,
+                                  out_f16, ws);
 }
 
 template <class F>
-__global__ void dense_attn_kernel(F f, const float* __restrict__ q, const int32_t* __restrict__ seq_of_tok, int n_ctx,
+__global__ void __launch_bounds__(ATTN_MAX_THREADS) dense_attn_kernel(F f, const float* __restrict__ q, const int32_t* __restrict__ seq_of_tok, int n_ctx,
                                   int n_head, int d_head, int keys_per_split, int n_splits, void* ctx_out,
                                   int out_f16, float* ws) {
     AttnGroup g;
@@ -127,7 +132,8 @@ __global__ void dense_attn_kernel(F f, const float* __restrict__ q, const int32_
     const int ke = min(n_ctx, kb + keys_per_split);
     F ff = f;
     ff.seq_row0 = (int64_t)g.seq * n_ctx;
-    attn_body<F, 1>(ff, q, g, n_head, d_head, f.W, kb, max(kb, ke), split, n_splits, ctx_out, out_f16, ws);
+    attn_body<F, 1>(ff, q, (int64_t)f.W, g, n_head, d_head, f.W, kb, max(kb, ke), split, n_splits, ctx_out, out_f16,
+                    ws);
 }
 
 __global__ void attn_combine_kernel(const float* __restrict__ ws, int n_tok, int n_splits, int n_head, int d_head,
@@ -154,10 +160,11 @@ __global__ void attn_combine_kernel(const float* __restrict__ ws, int n_tok, int
 
 // Thread shape of the attention CTA: R row-groups of W/16 threads with
 // R*W/16 a multiple of 32 and at most ATTN_MAX_THREADS threads.
-static int attn_rowgroups(int W) {
+static int attn_rowgroups(int W, int maxq = 1) {
+    const int limit = maxq > 1 ? ATTN_MAX_THREADS / 2 : ATTN_MAX_THREADS;  // MAXQ=4 uses ~2x the registers
     int tpr = W / 16;
     int best = 0;
-    for (int R = 1; R * tpr <= ATTN_MAX_THREADS; ++R)
+    for (int R = 1; R * tpr <= limit; ++R)
         if ((R * tpr) % 32 == 0) best = R;
     if (!best) fail(VKB_ERROR_UNSUPPORTED_OP, "attention: n_head*d_head=" + std::to_string(W) + " has no thread shape");
     return best;
@@ -219,10 +226,12 @@ void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, co
     }
 }
 
-void run_quantize_rows(vkb_context* ctx, const float* x, int64_t n_rows, int W, int8_t* q, __half* d) {
+void run_quantize_rows(vkb_context* ctx, const float* x, int64_t ld, int64_t n_rows, int W, int8_t* q, __half* d,
+                       const int32_t* map, int group) {
     if (W % 32) fail(VKB_ERROR_INVALID_ARGUMENT, "quantize_rows: row width must be a multiple of 32");
     int64_t warps = n_rows * (W / 32);
-    quantize_rows_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, ctx->stream>>>(x, n_rows, W, q, d);
+    quantize_rows_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, ctx->stream>>>(x, ld, n_rows, W, q, d, map,
+                                                                                        group);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
@@ -230,7 +239,7 @@ void run_quantize_rows(vkb_context* ctx, const float* x, int64_t n_rows, int W, 
 // ---------------------------------------------------------------------------
 // Host side of the pool
 // ---------------------------------------------------------------------------
-static vkb_kv_pool* pool_create(vkb_context* ctx, const vkb_kv_pool_desc* desc) {
+vkb_kv_pool* kv_pool_create(vkb_context* ctx, const vkb_kv_pool_desc* desc) {
     if (!ctx || !desc) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: null argument");
     const vkb_kv_pool_desc& d = *desc;
     if (d.mode == VKB_KV_FP32)
@@ -299,7 +308,7 @@ static vkb_kv_pool* pool_create(vkb_context* ctx, const vkb_kv_pool_desc* desc) 
     return p;
 }
 
-static void pool_destroy(vkb_kv_pool* p) {
+void kv_pool_destroy(vkb_kv_pool* p) {
     if (!p) return;
     if (p->ctx) cudaStreamSynchronize(p->ctx->stream);
     if (p->h_table) cudaFreeHost(p->h_table);
@@ -346,7 +355,7 @@ static void upload_table(vkb_kv_pool* p) {
     p->staged_pending = true;
 }
 
-static void begin_step(vkb_kv_pool* p, int n_tok, const int32_t* seq, const int32_t* pos) {
+void kv_begin_step(vkb_kv_pool* p, int n_tok, const int32_t* seq, const int32_t* pos) {
     const auto& d = p->d;
     if (n_tok <= 0 || n_tok > p->max_step)
         fail(VKB_ERROR_INVALID_ARGUMENT, "kv_begin_step: n_tok must be in 1.." + std::to_string(p->max_step));
@@ -400,7 +409,7 @@ static void begin_step(vkb_kv_pool* p, int n_tok, const int32_t* seq, const int3
     p->step_pos.assign(pos, pos + n_tok);
     // Key splits: about 4 CTAs per SM, at least 2*R keys per split, and the
     // partials must fit the pool's buffer.
-    const int R = attn_rowgroups(p->W);
+    const int R = attn_rowgroups(p->W, maxq);
     int splits = std::max(1, std::min((4 * p->ctx->sm_count + ng - 1) / ng, max_keys / (2 * R)));
     while ((int64_t)ng * splits > 4096 && splits > 1) --splits;
     int kps = (max_keys + splits - 1) / splits;
@@ -409,7 +418,7 @@ static void begin_step(vkb_kv_pool* p, int n_tok, const int32_t* seq, const int3
     p->keys_per_split = kps;
 }
 
-static void append(vkb_kv_pool* p, int layer, const float* k, const float* v) {
+void kv_append_ex(vkb_kv_pool* p, int layer, const float* k, const float* v, int64_t ld) {
     if (p->n_tok == 0) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_append: no step was begun");
     if (layer < 0 || layer >= p->d.n_layer) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_append: layer out of range");
     if (!k || !v) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_append: null k/v");
@@ -436,19 +445,19 @@ static void append(vkb_kv_pool* p, int layer, const float* k, const float* v) {
     const int64_t warps = (int64_t)p->n_tok * p->row_blocks * 2;
     const int64_t* rows = p->rows_dev.as<int64_t>() + (size_t)layer * p->n_tok;
     kv_append_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, p->ctx->stream>>>(
-        k, v, rows, p->n_tok, p->W, p->kq.as<int8_t>(), p->kd.as<__half>(), p->vq.as<int8_t>(), p->vd.as<__half>());
+        k, v, ld, rows, p->n_tok, p->W, p->kq.as<int8_t>(), p->kd.as<__half>(), p->vq.as<int8_t>(), p->vd.as<__half>());
     VKB_CUDA(cudaGetLastError());
     p->ctx->count();
 }
 
-static void attention(vkb_kv_pool* p, int layer, const float* q, void* out, int out_dtype) {
+void kv_attention_ex(vkb_kv_pool* p, int layer, const float* q, int64_t q_ld, void* out, int out_dtype) {
     if (p->n_tok == 0) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: no step was begun");
     if (layer < 0 || layer >= p->d.n_layer) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: layer out of range");
     if (!q || !out) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: null q/out");
     if (out_dtype != VKB_DT_F32 && out_dtype != VKB_DT_F16) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: bad out dtype");
     const auto& d = p->d;
     const int W = p->W;
-    const int R = attn_rowgroups(W);
+    const int R = attn_rowgroups(W, p->maxq);
     FetchPagedQ8 f;
     f.kq = p->kq.as<int8_t>();
     f.kd = p->kd.as<__half>();
@@ -480,13 +489,13 @@ static void attention(vkb_kv_pool* p, int layer, const float* q, void* out, int 
         static bool attr = false;
         if (!attr) { VKB_CUDA(cudaFuncSetAttribute(paged_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
         paged_attn_kernel<1><<<grid, threads, attn_smem_bytes(R, 1, W, d.n_head), p->ctx->stream>>>(
-            f, q, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->keys_per_split, p->splits, out, of16, ws,
+            f, q, q_ld, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->keys_per_split, p->splits, out, of16, ws,
             per_seq_base, p->ppseq);
     } else {
         static bool attr = false;
         if (!attr) { VKB_CUDA(cudaFuncSetAttribute(paged_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
         paged_attn_kernel<4><<<grid, threads, attn_smem_bytes(R, 4, W, d.n_head), p->ctx->stream>>>(
-            f, q, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->keys_per_split, p->splits, out, of16, ws,
+            f, q, q_ld, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->keys_per_split, p->splits, out, of16, ws,
             per_seq_base, p->ppseq);
     }
     VKB_CUDA(cudaGetLastError());
@@ -590,33 +599,33 @@ extern "C" {
 vkb_status vkb_kv_pool_create(vkb_context* ctx, const vkb_kv_pool_desc* desc, vkb_kv_pool** out) {
     return guard([&] {
         if (!out) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: null out");
-        *out = pool_create(ctx, desc);
+        *out = kv_pool_create(ctx, desc);
     });
 }
 
 vkb_status vkb_kv_pool_destroy(vkb_kv_pool* pool) {
-    return guard([&] { pool_destroy(pool); });
+    return guard([&] { kv_pool_destroy(pool); });
 }
 
 vkb_status vkb_kv_begin_step(vkb_kv_pool* pool, int32_t n_tok, const int32_t* seq_ids_host,
                              const int32_t* positions_host) {
     return guard([&] {
         if (!pool) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_begin_step: null pool");
-        begin_step(pool, n_tok, seq_ids_host, positions_host);
+        kv_begin_step(pool, n_tok, seq_ids_host, positions_host);
     });
 }
 
 vkb_status vkb_kv_append(vkb_kv_pool* pool, int32_t layer, const float* k_dev, const float* v_dev) {
     return guard([&] {
         if (!pool) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_append: null pool");
-        append(pool, layer, k_dev, v_dev);
+        kv_append_ex(pool, layer, k_dev, v_dev, pool->W);
     });
 }
 
 vkb_status vkb_kv_attention(vkb_kv_pool* pool, int32_t layer, const float* q_dev, void* ctx_out_dev, int out_dtype) {
     return guard([&] {
         if (!pool) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: null pool");
-        attention(pool, layer, q_dev, ctx_out_dev, out_dtype);
+        kv_attention_ex(pool, layer, q_dev, pool->W, ctx_out_dev, out_dtype);
     });
 }
 
@@ -801,7 +810,8 @@ vkb_status vkb_quantize_rows_q8_0(vkb_context* ctx, const float* x_dev, int64_t 
     return guard([&] {
         if (!ctx || !x_dev || !q_dev || !d_dev) fail(VKB_ERROR_INVALID_ARGUMENT, "quantize_rows: null argument");
         if (n_rows <= 0 || width <= 0) fail(VKB_ERROR_INVALID_ARGUMENT, "quantize_rows: empty shape");
-        run_quantize_rows(ctx, x_dev, n_rows, width, reinterpret_cast<int8_t*>(q_dev), reinterpret_cast<__half*>(d_dev));
+        run_quantize_rows(ctx, x_dev, width, n_rows, width, reinterpret_cast<int8_t*>(q_dev),
+                          reinterpret_cast<__half*>(d_dev), nullptr, 1);
     });
 }
 

@@ -143,14 +143,21 @@ struct Epi {
     int out_f16;
     int kind;
     float scale;
-    int64_t ldo;  // = n
+    int64_t ldo;       // = n
+    int64_t n_scaled;  // EPI_SCALE scales columns [0, n_scaled) only
+    int64_t col_block; // > 0: column block c of width col_block is written as its own [rows][col_block] plane
+    int64_t out_rows;  // rows of each plane (col_block layout)
+    const int32_t* row_map;  // optional: row m lands in row_map[m / row_group] * row_group + m % row_group
+    int row_group;
 };
 
 __device__ __forceinline__ void epi_store(const Epi& e, int64_t m, int64_t n, float acc, float bias_n) {
     float v = acc + bias_n;
-    int64_t idx = m * e.ldo + n;
+    int64_t mr = e.row_map ? (int64_t)e.row_map[m / e.row_group] * e.row_group + m % e.row_group : m;
+    int64_t idx = e.col_block > 0 ? (n / e.col_block) * (e.out_rows * e.col_block) + mr * e.col_block + n % e.col_block
+                                  : mr * e.ldo + n;
     if (e.kind == VKB_EPI_GELU) v = gelu_as(v);
-    else if (e.kind == VKB_EPI_SCALE) v = v * e.scale;
+    else if (e.kind == VKB_EPI_SCALE) v = n < e.n_scaled ? v * e.scale : v;
     else if (e.kind == VKB_EPI_RESIDUAL) v = e.residual[idx] + v;
     if (e.out_f16) reinterpret_cast<__half*>(e.out)[idx] = __float2half_rn(v);
     else reinterpret_cast<float*>(e.out)[idx] = v;
@@ -553,6 +560,13 @@ LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m) {
 void run_linear(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_dtype, const float* bias,
                 void* out, int out_dtype, int epilogue, const float* residual, float scale, float* ws_override,
                 __half* a16_override) {
+    LinearExtra x;
+    run_linear_ex(ctx, w, m, a, a_dtype, bias, out, out_dtype, epilogue, residual, scale, ws_override, a16_override, x);
+}
+
+void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_dtype, const float* bias,
+                   void* out, int out_dtype, int epilogue, const float* residual, float scale, float* ws_override,
+                   __half* a16_override, const LinearExtra& x) {
     if (m <= 0) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: m must be positive");
     if (!a || !out) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: null activation or output pointer");
     if (a_dtype != VKB_DT_F32 && a_dtype != VKB_DT_F16) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: bad a_dtype");
@@ -561,7 +575,10 @@ void run_linear(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a,
     if (epilogue == VKB_EPI_RESIDUAL && (out_dtype != VKB_DT_F32 || !residual))
         fail(VKB_ERROR_INVALID_ARGUMENT, "linear: the residual epilogue needs an f32 output and a residual pointer");
     LinearPlan p = plan_linear(ctx, w, m);
-    Epi e{bias, residual, out, out_dtype == VKB_DT_F16, epilogue, scale, w->n};
+    Epi e{bias, residual, out, out_dtype == VKB_DT_F16, epilogue, scale, w->n,
+          x.n_scaled >= 0 ? x.n_scaled : w->n, x.col_block, x.out_rows > 0 ? x.out_rows : m, x.row_map,
+          x.row_group > 0 ? x.row_group : 1};
+    if (x.col_block > 0 && (w->n % x.col_block)) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: n not a multiple of col_block");
     // Workspace: [f16 copy of a (tc path with f32 input)] [split partials]
     size_t a16_bytes = (p.tc && a_dtype == VKB_DT_F32 && !a16_override) ? ((size_t)m * w->k * 2 + 255) / 256 * 256 : 0;
     size_t ws_bytes = ws_override ? 0 : p.ws_bytes;

@@ -16,6 +16,15 @@ struct LinearPlan {
     size_t a16_bytes = 0;
 };
 
+// Epilogue extensions used by the model runner (fused projections).
+struct LinearExtra {
+    int64_t n_scaled = -1;        // EPI_SCALE applies to columns [0, n_scaled); -1 = all
+    int64_t col_block = 0;        // write column blocks as separate [out_rows][col_block] planes
+    int64_t out_rows = 0;         // rows per plane (default m)
+    const int32_t* row_map = nullptr;  // device map of row groups to destination groups
+    int row_group = 1;
+};
+
 vkb_weight* upload_weight(vkb_context* ctx, uint32_t tag, int64_t n, int64_t k, const void* bytes, size_t len);
 LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m);
 // Runs out = epilogue(a . W^T + bias). ws_override / a16_override let a caller
@@ -23,6 +32,9 @@ LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m);
 void run_linear(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_dtype, const float* bias,
                 void* out, int out_dtype, int epilogue, const float* residual, float scale, float* ws_override,
                 __half* a16_override);
+void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_dtype, const float* bias,
+                   void* out, int out_dtype, int epilogue, const float* residual, float scale, float* ws_override,
+                   __half* a16_override, const LinearExtra& x);
 void make_tmap_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows);
 int read_and_clear_err_flag(vkb_context* ctx);
 int gemv_max_m();

@@ -274,7 +274,7 @@ WHISPER_BASE = WhisperArch(80, 1500, 512, 8, 6, 448, 8, 6, 51865, 2048, 50257, (
 WHISPER_LARGE_V3 = WhisperArch(128, 1500, 1280, 20, 32, 448, 20, 32, 51866, 5120, 50257,
                                (50258, 50259, 50360, 50364))
 # A small architecture for fast tests (same structure, tiny sizes).
-WHISPER_TINY_TEST = WhisperArch(16, 64, 128, 2, 2, 32, 2, 2, 500, 256, 499, (1, 2, 3, 4))
+WHISPER_TINY_TEST = WhisperArch(16, 64, 256, 4, 2, 32, 4, 2, 500, 512, 499, (1, 2, 3, 4))
 
 
 def whisper_tensor_decls(a: WhisperArch, qtag: int):

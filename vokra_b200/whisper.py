@@ -1,0 +1,92 @@
+"""Whisper on the B200 through the C ABI: model load and a batched decode session.
+
+Mirrors the reference's ASR flow (crates/vokra-models/src/whisper/asr.rs:113,
+decoder.rs:413, greedy.rs:32): encode once per utterance, then step the decoder
+one token per stream, teacher-forced or greedy.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+from ._lib import check
+from .ops import Context
+
+_L = _lib.load()
+
+
+class WhisperModel:
+    def __init__(self, ctx: Context, gguf_path: str):
+        h = C.c_void_p()
+        check(_L.vkb_whisper_load(ctx.h, gguf_path.encode(), C.byref(h)))
+        self.h, self.ctx = h, ctx
+        d = _lib.WhisperDims()
+        check(_L.vkb_whisper_get_dims(self.h, C.byref(d)))
+        self.dims = d
+        self.start_ids = [d.start_ids[i] for i in range(d.n_start_ids)]
+
+    def close(self):
+        if self.h:
+            check(_L.vkb_whisper_destroy(self.h))
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Session:
+    """A batched decoding session (paged Q8_0 self-attention KV + cross-attention store)."""
+
+    def __init__(self, model: WhisperModel, max_streams: int, max_step_tokens: int | None = None,
+                 max_clips: int = 0, cross_kv_q8: bool = True, kv_page_tokens: int = 16):
+        o = _lib.SessionOptions(max_streams, max_step_tokens or 4 * max_streams, max_clips, int(cross_kv_q8),
+                                kv_page_tokens)
+        h = C.c_void_p()
+        check(_L.vkb_session_create(model.h, C.byref(o), C.byref(h)))
+        self.h, self.model, self.ctx = h, model, model.ctx
+
+    def encode(self, logmel_dev, streams):
+        """logmel_dev: torch f32 [n_clips, n_mels, 2*n_audio_ctx] on the device."""
+        s = np.ascontiguousarray(streams, dtype=np.int32)
+        check(_L.vkb_session_encode(self.h, s.size, C.c_void_p(logmel_dev.data_ptr()), s.ctypes.data_as(C.c_void_p)))
+
+    def encoder_output(self, n_clips: int):
+        import torch
+        d = self.model.dims
+        ptr = _L.vkb_session_encoder_output(self.h)
+        n = n_clips * d.n_audio_ctx * d.d_model
+        self.ctx.synchronize()
+        host = np.empty(n, np.float32)
+        cudart = torch.cuda.cudart()
+        err = cudart.cudaMemcpy(host.ctypes.data, ptr, n * 4, 2)  # device -> host
+        if int(err) != 0:
+            raise RuntimeError(f"cudaMemcpy failed: {err}")
+        return host.reshape(n_clips, d.n_audio_ctx, d.d_model)
+
+    def step(self, streams, positions, tokens, logits_dev=None, ids_dev=None):
+        s = np.ascontiguousarray(streams, dtype=np.int32)
+        p = np.ascontiguousarray(positions, dtype=np.int32)
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        check(_L.vkb_session_step(self.h, s.size, s.ctypes.data_as(C.c_void_p), p.ctypes.data_as(C.c_void_p),
+                                  t.ctypes.data_as(C.c_void_p),
+                                  C.c_void_p(logits_dev.data_ptr() if logits_dev is not None else None),
+                                  C.c_void_p(ids_dev.data_ptr() if ids_dev is not None else None)))
+
+    def release(self, stream: int):
+        check(_L.vkb_session_release(self.h, stream))
+
+    def close(self):
+        if self.h:
+            check(_L.vkb_session_destroy(self.h))
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
