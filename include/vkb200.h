@@ -69,8 +69,18 @@ enum vkb_ggml_type {
 /* KV quantization modes, numbered like KvQuant (crates/vokra-core/src/kv_quant/mod.rs:88). */
 enum vkb_kv_quant { VKB_KV_FP32 = 0, VKB_KV_Q4_0 = 1, VKB_KV_Q5_0 = 2, VKB_KV_Q8_0 = 3 };
 
-/* Activation / output element types of the device-pointer entry points. */
-enum vkb_dtype { VKB_DT_F32 = 0, VKB_DT_F16 = 1 };
+/* Activation / output element types of the device-pointer entry points.
+ * F16X2 is a value stored as two f16 planes, hi = f16(x) then lo = f16(x - hi)
+ * (a buffer of 2 * rows * cols halves); the tensor-core GEMM consumes it at
+ * about fp32 accuracy. */
+enum vkb_dtype { VKB_DT_F32 = 0, VKB_DT_F16 = 1, VKB_DT_F16X2 = 2 };
+
+/* Tensor-core operand precision of a context.
+ * SPLIT (default): weights and activations enter the MMA as hi + lo f16
+ *   pairs (three MMAs per step), products accurate to about 2^-21 relative;
+ *   this is the mode the parity tolerances are stated for.
+ * F16: one f16 MMA per step (weights and activations rounded to f16). */
+enum vkb_precision { VKB_PREC_SPLIT = 0, VKB_PREC_F16 = 1 };
 
 /* Fused epilogues of vkb_linear. */
 enum vkb_epilogue {
@@ -101,6 +111,8 @@ VKB_API vkb_status vkb_context_destroy(vkb_context* ctx);
  * same device; NULL = the context's own stream). */
 VKB_API vkb_status vkb_context_set_stream(vkb_context* ctx, void* stream);
 VKB_API vkb_status vkb_context_synchronize(vkb_context* ctx);
+/* Selects the tensor-core operand precision (vkb_precision). */
+VKB_API vkb_status vkb_context_set_precision(vkb_context* ctx, int precision);
 /* Number of kernels this context has launched (CudaContext::submission_count,
  * crates/vokra-backend-cuda/src/context.rs:3152). */
 VKB_API uint64_t vkb_context_launch_count(const vkb_context* ctx);
@@ -289,6 +301,8 @@ VKB_API vkb_status vkb_session_encode(vkb_session* s, int32_t n_clips, const flo
                                       const int32_t* streams_host);
 /* Device pointer to the last encoder output [n_clips][n_audio_ctx][d_model] f32 (after ln_post). */
 VKB_API const float* vkb_session_encoder_output(const vkb_session* s);
+/* Synchronous copy of the first n_floats of that output to host memory. */
+VKB_API vkb_status vkb_session_read_encoder_output(const vkb_session* s, float* host, size_t n_floats);
 /* One decoder step over n_tok tokens (token i of stream streams_host[i] at
  * position positions_host[i]; tokens of one stream contiguous and
  * consecutive): appends their self-attention K/V, writes logits

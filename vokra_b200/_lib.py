@@ -35,7 +35,8 @@ STATUS_NAMES = {
 GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0, GGML_Q4_K, GGML_Q5_K, GGML_Q6_K, GGML_BF16 = 0, 1, 2, 8, 12, 13, 14, 30
 # KvQuant
 KV_FP32, KV_Q4_0, KV_Q5_0, KV_Q8_0 = 0, 1, 2, 3
-DT_F32, DT_F16 = 0, 1
+DT_F32, DT_F16, DT_F16X2 = 0, 1, 2
+PREC_SPLIT, PREC_F16 = 0, 1
 EPI_NONE, EPI_GELU, EPI_RESIDUAL, EPI_SCALE = 0, 1, 2, 3
 KV_LAYOUT_REFERENCE, KV_LAYOUT_SEQUENCE = 0, 1
 
@@ -86,6 +87,7 @@ SIGNATURES = {
     "vkb_context_set_stream": (C.c_int, [P, P]),
     "vkb_context_synchronize": (C.c_int, [P]),
     "vkb_context_launch_count": (U64, [P]),
+    "vkb_context_set_precision": (C.c_int, [P, C.c_int]),
     "vkb_weight_upload": (C.c_int, [P, U32, I64, I64, P, SZ, PP]),
     "vkb_weight_destroy": (C.c_int, [P]),
     "vkb_weight_device_bytes": (SZ, [P]),
@@ -118,6 +120,7 @@ SIGNATURES = {
     "vkb_session_destroy": (C.c_int, [P]),
     "vkb_session_encode": (C.c_int, [P, I32, P, P]),
     "vkb_session_encoder_output": (P, [P]),
+    "vkb_session_read_encoder_output": (C.c_int, [P, P, SZ]),
     "vkb_session_step": (C.c_int, [P, I32, P, P, P, P, P]),
     "vkb_session_logits": (P, [P]),
     "vkb_session_ids": (P, [P]),

@@ -108,7 +108,7 @@ template <class F, int MAXQ>
 __device__ __forceinline__ void attn_body(const F& fetch, const float* __restrict__ q, int64_t q_ld, const AttnGroup& g,
                                           int n_head,
                                           int d_head, int W, int key_begin, int key_end, int split, int n_splits,
-                                          void* ctx_out, int out_f16, float* ws) {
+                                          void* ctx_out, int out_fmt, int64_t out_plane, float* ws) {
     extern __shared__ float sm[];
     const int tpr = W / 16;                // threads per key row
     const int R = blockDim.x / tpr;        // row-groups
@@ -214,11 +214,18 @@ __device__ __forceinline__ void attn_body(const F& fetch, const float* __restric
             const int64_t tok = g.first_tok + i;
             if (n_splits == 1) {
                 float inv = 1.0f / L;
-                if (out_f16) {
+                if (out_fmt != 0) {
                     __half* dst = reinterpret_cast<__half*>(ctx_out) + tok * W + c0;
 #pragma unroll
-                    for (int c = 0; c < 16; c += 2)
-                        *reinterpret_cast<__half2*>(dst + c) = __floats2half2_rn(o[c] * inv, o[c + 1] * inv);
+                    for (int c = 0; c < 16; c += 2) {
+                        float v0 = o[c] * inv, v1 = o[c + 1] * inv;
+                        __half2 hi = __floats2half2_rn(v0, v1);
+                        *reinterpret_cast<__half2*>(dst + c) = hi;
+                        if (out_fmt == 2) {
+                            float2 hf = __half22float2(hi);
+                            *reinterpret_cast<__half2*>(dst + out_plane + c) = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
+                        }
+                    }
                 } else {
                     float* dst = reinterpret_cast<float*>(ctx_out) + tok * W + c0;
 #pragma unroll
@@ -240,7 +247,7 @@ __device__ __forceinline__ void attn_body(const F& fetch, const float* __restric
 
 // Merges split partials: one thread per (token, channel).
 __global__ void attn_combine_kernel(const float* __restrict__ ws, int n_tok, int n_splits, int n_head, int d_head,
-                                    void* ctx_out, int out_f16);
+                                    void* ctx_out, int out_fmt);
 
 inline size_t attn_smem_bytes(int R, int maxq, int W, int H) {
     return (size_t)R * maxq * (W + 2 * H) * sizeof(float);

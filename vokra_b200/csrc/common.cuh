@@ -86,6 +86,7 @@ struct vkb_context {
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
     uint64_t launches = 0;
+    int precision = VKB_PREC_SPLIT;  // tensor-core operand precision (vkb_context_set_precision)
     vkb::DevBuf workspace;
     vkb::DevBuf err_flag;  // int set by a kernel whose bounded wait gave up
     void ensure_workspace(size_t bytes) {

@@ -70,6 +70,15 @@ vkb_status vkb_context_synchronize(vkb_context* ctx) {
     });
 }
 
+vkb_status vkb_context_set_precision(vkb_context* ctx, int precision) {
+    return guard([&] {
+        if (!ctx) fail(VKB_ERROR_INVALID_ARGUMENT, "set_precision: null context");
+        if (precision != VKB_PREC_SPLIT && precision != VKB_PREC_F16)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "set_precision: unknown precision");
+        ctx->precision = precision;
+    });
+}
+
 uint64_t vkb_context_launch_count(const vkb_context* ctx) { return ctx ? ctx->launches : 0; }
 
 }  // extern "C"

@@ -9,7 +9,7 @@ namespace vkb {
 // One warp per row; two passes over the row held in registers (cols <= 2048).
 template <int PER>
 __global__ void layer_norm_kernel(const float* __restrict__ x, int64_t rows, int cols, const float* __restrict__ g,
-                                  const float* __restrict__ b, float eps, void* out, int out_f16) {
+                                  const float* __restrict__ b, float eps, void* out, int out_fmt) {
     const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -39,18 +39,23 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, int64_t rows, int
         int c = lane + 32 * i;
         if (c >= cols) break;
         float y = (v[i] - mean) * inv_std * g[c] + b[c];
-        if (out_f16) reinterpret_cast<__half*>(out)[row * cols + c] = __float2half_rn(y);
-        else reinterpret_cast<float*>(out)[row * cols + c] = y;
+        if (out_fmt == 0) {
+            reinterpret_cast<float*>(out)[row * cols + c] = y;
+        } else {
+            __half hi = __float2half_rn(y);
+            reinterpret_cast<__half*>(out)[row * cols + c] = hi;
+            if (out_fmt == 2) reinterpret_cast<__half*>(out)[rows * cols + row * cols + c] = __float2half_rn(y - __half2float(hi));
+        }
     }
 }
 
 void run_layer_norm(vkb_context* ctx, const float* x, int64_t rows, int cols, const float* g, const float* b, float eps,
-                    void* out, int out_f16) {
+                    void* out, int out_fmt) {
     if (cols > 2048) fail(VKB_ERROR_UNSUPPORTED_OP, "layer_norm: row width above 2048");
     unsigned grid = (unsigned)((rows * 32 + 255) / 256);
-    if (cols <= 512) layer_norm_kernel<16><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_f16);
-    else if (cols <= 1280) layer_norm_kernel<40><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_f16);
-    else layer_norm_kernel<64><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_f16);
+    if (cols <= 512) layer_norm_kernel<16><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_fmt);
+    else if (cols <= 1280) layer_norm_kernel<40><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_fmt);
+    else layer_norm_kernel<64><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_fmt);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
@@ -92,7 +97,7 @@ void run_embed(vkb_context* ctx, const vkb_weight* w, const int32_t* tokens, con
 
 // col[b*To + t][c*3 + kk] = x[b][c][t*stride + kk - 1]; columns C*3 .. ldc-1 are zero
 __global__ void im2col_ct_kernel(const float* __restrict__ x, int B, int C, int T, int To, int stride, int ldc,
-                                 __half* __restrict__ col) {
+                                 __half* __restrict__ col, int split) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t total = (int64_t)B * To * ldc;
     if (i >= total) return;
@@ -100,18 +105,21 @@ __global__ void im2col_ct_kernel(const float* __restrict__ x, int B, int C, int 
     const int cc = (int)(i % ldc);
     if (cc >= C * 3) {
         col[i] = __float2half_rn(0.0f);
+        if (split) col[total + i] = __float2half_rn(0.0f);
         return;
     }
     const int c = cc / 3, kk = cc % 3;
     const int b = (int)(r / To), t = (int)(r % To);
     const int p = t * stride + kk - 1;
     float v = (p >= 0 && p < T) ? x[((int64_t)b * C + c) * T + p] : 0.0f;
-    col[i] = __float2half_rn(v);
+    __half hi = __float2half_rn(v);
+    col[i] = hi;
+    if (split) col[total + i] = __float2half_rn(v - __half2float(hi));
 }
 
 // col[b*To + t][c*3 + kk] = x[b*T + t*stride + kk - 1][c]
 __global__ void im2col_tc_kernel(const __half* __restrict__ x, int B, int C, int T, int To, int stride,
-                                 __half* __restrict__ col) {
+                                 __half* __restrict__ col, int planes) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t total = (int64_t)B * To * C * 3;
     if (i >= total) return;
@@ -120,39 +128,45 @@ __global__ void im2col_tc_kernel(const __half* __restrict__ x, int B, int C, int
     const int c = cc / 3, kk = cc % 3;
     const int b = (int)(r / To), t = (int)(r % To);
     const int p = t * stride + kk - 1;
-    col[i] = (p >= 0 && p < T) ? x[((int64_t)b * T + p) * C + c] : __float2half_rn(0.0f);
+    const int64_t in_plane = (int64_t)B * T * C;
+    for (int pl = 0; pl < planes; ++pl)
+        col[pl * total + i] = (p >= 0 && p < T) ? x[pl * in_plane + ((int64_t)b * T + p) * C + c] : __float2half_rn(0.0f);
 }
 
 static int conv_out(int T, int stride) { return (T + 2 - 3) / stride + 1; }
 
-void run_im2col_ct(vkb_context* ctx, const float* x, int B, int C, int T, int stride, int ldc, __half* col) {
+void run_im2col_ct(vkb_context* ctx, const float* x, int B, int C, int T, int stride, int ldc, __half* col,
+                   bool split) {
     int To = conv_out(T, stride);
     int64_t total = (int64_t)B * To * ldc;
-    im2col_ct_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(x, B, C, T, To, stride, ldc, col);
+    im2col_ct_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(x, B, C, T, To, stride, ldc, col,
+                                                                              split ? 1 : 0);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
 
-void run_im2col_tc(vkb_context* ctx, const __half* x, int B, int C, int T, int stride, __half* col) {
+void run_im2col_tc(vkb_context* ctx, const __half* x, int B, int C, int T, int stride, __half* col, int planes) {
     int To = conv_out(T, stride);
     int64_t total = (int64_t)B * To * C * 3;
-    im2col_tc_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(x, B, C, T, To, stride, col);
+    im2col_tc_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(x, B, C, T, To, stride, col, planes);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
 
 __global__ void add_pos_kernel(const __half* __restrict__ y, const float* __restrict__ pos, int B, int T, int C,
-                               float* __restrict__ h) {
+                               float* __restrict__ h, int planes) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t total = (int64_t)B * T * C;
     if (i >= total) return;
     const int64_t tc = i % ((int64_t)T * C);
-    h[i] = __half2float(y[i]) + pos[tc];
+    float v = __half2float(y[i]);
+    if (planes == 2) v += __half2float(y[total + i]);
+    h[i] = v + pos[tc];
 }
 
-void run_add_pos(vkb_context* ctx, const __half* y, const float* pos, int B, int T, int C, float* h) {
+void run_add_pos(vkb_context* ctx, const __half* y, const float* pos, int B, int T, int C, float* h, int planes) {
     int64_t total = (int64_t)B * T * C;
-    add_pos_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(y, pos, B, T, C, h);
+    add_pos_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(y, pos, B, T, C, h, planes);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }

@@ -70,7 +70,8 @@ __device__ __forceinline__ void load_tile(__half* dst, const __half* base, int64
 }  // namespace
 
 __global__ void __launch_bounds__(128) enc_attn_kernel(const __half* __restrict__ qkv, int64_t ld, int kcol, int vcol,
-                                                       int T, int n_head, __half* __restrict__ ctx, int64_t ctx_ld) {
+                                                       int T, int n_head, __half* __restrict__ ctx, int64_t ctx_ld,
+                                                       __half* __restrict__ ctx_lo) {
     __shared__ __align__(128) __half sQ[BQ * LDS];
     __shared__ __align__(128) __half sK[2][BK * LDS];
     __shared__ __align__(128) __half sV[2][BK * LDS];
@@ -200,22 +201,28 @@ __global__ void __launch_bounds__(128) enc_attn_kernel(const __half* __restrict_
         int q = q0 + warp * 16 + (lane >> 2) + hr * 8;
         if (q >= T) continue;
         float inv = 1.0f / l_r[hr];
-        __half* dst = ctx + (row_base + q) * ctx_ld + h * HD;
+        const int64_t off = (row_base + q) * ctx_ld + h * HD;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             int d = j * 8 + (lane & 3) * 2;
-            *reinterpret_cast<__half2*>(dst + d) = __floats2half2_rn(o[j][2 * hr] * inv, o[j][2 * hr + 1] * inv);
+            float v0 = o[j][2 * hr] * inv, v1 = o[j][2 * hr + 1] * inv;
+            __half2 hi = __floats2half2_rn(v0, v1);
+            *reinterpret_cast<__half2*>(ctx + off + d) = hi;
+            if (ctx_lo) {
+                float2 hf = __half22float2(hi);
+                *reinterpret_cast<__half2*>(ctx_lo + off + d) = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
+            }
         }
     }
 }
 
 void run_encoder_attention(vkb_context* ctx, const __half* qkv, int64_t ld, int kcol, int vcol, int n_windows, int T,
-                           int n_head, int d_head, __half* out, int64_t out_ld) {
+                           int n_head, int d_head, __half* out, int64_t out_ld, __half* out_lo) {
     if (d_head != HD) fail(VKB_ERROR_UNSUPPORTED_OP, "encoder attention: d_head must be 64");
     if (ld % 8 || kcol % 8 || vcol % 8 || out_ld % 2)
         fail(VKB_ERROR_INVALID_ARGUMENT, "encoder attention: rows must be 16-byte aligned");
     dim3 grid((unsigned)((T + BQ - 1) / BQ), (unsigned)(n_windows * n_head));
-    enc_attn_kernel<<<grid, 128, 0, ctx->stream>>>(qkv, ld, kcol, vcol, T, n_head, out, out_ld);
+    enc_attn_kernel<<<grid, 128, 0, ctx->stream>>>(qkv, ld, kcol, vcol, T, n_head, out, out_ld, out_lo);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }

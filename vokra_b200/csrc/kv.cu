@@ -105,7 +105,7 @@ __global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t ld, in
 template <int MAXQ>
 __global__ void __launch_bounds__(MAXQ > 1 ? ATTN_MAX_THREADS / 2 : ATTN_MAX_THREADS) paged_attn_kernel(FetchPagedQ8 f, const float* __restrict__ q, int64_t q_ld, const AttnGroup* __restrict__ groups,
                                   int n_head, int d_head, int keys_per_split, int n_splits, void* ctx_out,
-                                  int out_f16, float* ws, int per_seq_base, int ppseq) {
+                                  int out_fmt, float* ws, int per_seq_base, int ppseq, int64_t out_plane) {
     const AttnGroup g = groups[blockIdx.x];
     const int split = blockIdx.y;
     const int n_keys = g.pos0 + g.n_q;  // keys 0 .. last query's position
@@ -115,13 +115,13 @@ __global__ void __launch_bounds__(MAXQ > 1 ? ATTN_MAX_THREADS / 2 : ATTN_MAX_THR
     if (per_seq_base) ff.table_base = g.seq * ppseq;
     else ff.slot = g.seq;
     attn_body<FetchPagedQ8, MAXQ>(ff, q, q_ld, g, n_head, d_head, f.W, kb, max(kb, ke), split, n_splits, ctx_out,
-                                  out_f16, ws);
+                                  out_fmt, out_plane, ws);
 }
 
 template <class F>
 __global__ void __launch_bounds__(ATTN_MAX_THREADS) dense_attn_kernel(F f, const float* __restrict__ q, const int32_t* __restrict__ seq_of_tok, int n_ctx,
                                   int n_head, int d_head, int keys_per_split, int n_splits, void* ctx_out,
-                                  int out_f16, float* ws) {
+                                  int out_fmt, float* ws, int64_t out_plane) {
     AttnGroup g;
     g.first_tok = blockIdx.x;
     g.n_q = 1;
@@ -132,12 +132,12 @@ __global__ void __launch_bounds__(ATTN_MAX_THREADS) dense_attn_kernel(F f, const
     const int ke = min(n_ctx, kb + keys_per_split);
     F ff = f;
     ff.seq_row0 = (int64_t)g.seq * n_ctx;
-    attn_body<F, 1>(ff, q, (int64_t)f.W, g, n_head, d_head, f.W, kb, max(kb, ke), split, n_splits, ctx_out, out_f16,
-                    ws);
+    attn_body<F, 1>(ff, q, (int64_t)f.W, g, n_head, d_head, f.W, kb, max(kb, ke), split, n_splits, ctx_out, out_fmt,
+                    out_plane, ws);
 }
 
 __global__ void attn_combine_kernel(const float* __restrict__ ws, int n_tok, int n_splits, int n_head, int d_head,
-                                    void* ctx_out, int out_f16) {
+                                    void* ctx_out, int out_fmt) {
     const int W = n_head * d_head;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)n_tok * W) return;
@@ -154,8 +154,13 @@ __global__ void attn_combine_kernel(const float* __restrict__ ws, int n_tok, int
         O += p[c] * w;
     }
     float v = O / L;
-    if (out_f16) reinterpret_cast<__half*>(ctx_out)[i] = __float2half_rn(v);
-    else reinterpret_cast<float*>(ctx_out)[i] = v;
+    if (out_fmt == 0) {
+        reinterpret_cast<float*>(ctx_out)[i] = v;
+    } else {
+        __half hi = __float2half_rn(v);
+        reinterpret_cast<__half*>(ctx_out)[i] = hi;
+        if (out_fmt == 2) reinterpret_cast<__half*>(ctx_out)[(int64_t)n_tok * W + i] = __float2half_rn(v - __half2float(hi));
+    }
 }
 
 // Thread shape of the attention CTA: R row-groups of W/16 threads with
@@ -206,21 +211,21 @@ void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, co
         static bool attr = false;
         if (!attr) { VKB_CUDA(cudaFuncSetAttribute(dense_attn_kernel<FetchDenseF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
         dense_attn_kernel<FetchDenseF16><<<grid, threads, sm, ctx->stream>>>(f, q, seq_of_tok, n_ctx, n_head, d_head, kps,
-                                                                            splits, out, out_dtype == VKB_DT_F16, ws);
+                                                                            splits, out, out_dtype, ws, (int64_t)n_tok * W);
     } else {
         FetchDenseQ8 f{reinterpret_cast<const int8_t*>(k), reinterpret_cast<const __half*>(k_scale),
                        reinterpret_cast<const int8_t*>(v), reinterpret_cast<const __half*>(v_scale), W, 0};
         static bool attr = false;
         if (!attr) { VKB_CUDA(cudaFuncSetAttribute(dense_attn_kernel<FetchDenseQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
         dense_attn_kernel<FetchDenseQ8><<<grid, threads, sm, ctx->stream>>>(f, q, seq_of_tok, n_ctx, n_head, d_head, kps,
-                                                                           splits, out, out_dtype == VKB_DT_F16, ws);
+                                                                           splits, out, out_dtype, ws, (int64_t)n_tok * W);
     }
     VKB_CUDA(cudaGetLastError());
     ctx->count();
     if (splits > 1) {
         int64_t tot = (int64_t)n_tok * W;
         attn_combine_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, ctx->stream>>>(ws, n_tok, splits, n_head, d_head,
-                                                                                   out, out_dtype == VKB_DT_F16);
+                                                                                   out, out_dtype);
         VKB_CUDA(cudaGetLastError());
         ctx->count();
     }
@@ -454,7 +459,8 @@ void kv_attention_ex(vkb_kv_pool* p, int layer, const float* q, int64_t q_ld, vo
     if (p->n_tok == 0) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: no step was begun");
     if (layer < 0 || layer >= p->d.n_layer) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: layer out of range");
     if (!q || !out) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: null q/out");
-    if (out_dtype != VKB_DT_F32 && out_dtype != VKB_DT_F16) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: bad out dtype");
+    if (out_dtype != VKB_DT_F32 && out_dtype != VKB_DT_F16 && out_dtype != VKB_DT_F16X2)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "kv_attention: bad out dtype");
     const auto& d = p->d;
     const int W = p->W;
     const int R = attn_rowgroups(W, p->maxq);
@@ -484,19 +490,20 @@ void kv_attention_ex(vkb_kv_pool* p, int layer, const float* q, int64_t q_ld, vo
     dim3 grid((unsigned)p->n_groups, (unsigned)p->splits);
     const int threads = R * (W / 16);
     float* ws = p->part_dev.as<float>();
-    const int of16 = out_dtype == VKB_DT_F16;
+    const int of16 = out_dtype;  // 0 f32, 1 f16, 2 f16 hi+lo planes
+    const int64_t oplane = (int64_t)p->n_tok * W;
     if (p->maxq == 1) {
         static bool attr = false;
         if (!attr) { VKB_CUDA(cudaFuncSetAttribute(paged_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
         paged_attn_kernel<1><<<grid, threads, attn_smem_bytes(R, 1, W, d.n_head), p->ctx->stream>>>(
             f, q, q_ld, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->keys_per_split, p->splits, out, of16, ws,
-            per_seq_base, p->ppseq);
+            per_seq_base, p->ppseq, oplane);
     } else {
         static bool attr = false;
         if (!attr) { VKB_CUDA(cudaFuncSetAttribute(paged_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
         paged_attn_kernel<4><<<grid, threads, attn_smem_bytes(R, 4, W, d.n_head), p->ctx->stream>>>(
             f, q, q_ld, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->keys_per_split, p->splits, out, of16, ws,
-            per_seq_base, p->ppseq);
+            per_seq_base, p->ppseq, oplane);
     }
     VKB_CUDA(cudaGetLastError());
     p->ctx->count();
@@ -799,7 +806,8 @@ vkb_status vkb_attention_dense(vkb_context* ctx, int32_t n_tok, int32_t n_head, 
             fail(VKB_ERROR_UNSUPPORTED_OP, "attention_dense: kv dtype must be F16 or Q8_0");
         if (kv_dtype == VKB_KV_Q8_0 && (!k_scale_dev || !v_scale_dev))
             fail(VKB_ERROR_INVALID_ARGUMENT, "attention_dense: Q8_0 needs scale planes");
-        if (out_dtype != VKB_DT_F32 && out_dtype != VKB_DT_F16) fail(VKB_ERROR_INVALID_ARGUMENT, "attention_dense: bad out dtype");
+        if (out_dtype != VKB_DT_F32 && out_dtype != VKB_DT_F16 && out_dtype != VKB_DT_F16X2)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "attention_dense: bad out dtype");
         run_dense_attention(ctx, n_tok, n_head, d_head, q_dev, seq_of_tok_dev, k_dev, v_dev, k_scale_dev, v_scale_dev,
                             n_ctx, kv_dtype == VKB_DT_F16 ? VKB_DT_F16 : VKB_KV_Q8_0, ctx_out_dev, out_dtype, nullptr);
     });

@@ -140,7 +140,7 @@ struct Epi {
     const float* bias;
     const float* residual;
     void* out;
-    int out_f16;
+    int out_fmt;       // VKB_DT_F32, VKB_DT_F16 or VKB_DT_F16X2 (hi plane, then lo plane)
     int kind;
     float scale;
     int64_t ldo;       // = n
@@ -149,6 +149,7 @@ struct Epi {
     int64_t out_rows;  // rows of each plane (col_block layout)
     const int32_t* row_map;  // optional: row m lands in row_map[m / row_group] * row_group + m % row_group
     int row_group;
+    int64_t plane;     // elements per plane of an F16X2 output
 };
 
 __device__ __forceinline__ void epi_store(const Epi& e, int64_t m, int64_t n, float acc, float bias_n) {
@@ -159,8 +160,13 @@ __device__ __forceinline__ void epi_store(const Epi& e, int64_t m, int64_t n, fl
     if (e.kind == VKB_EPI_GELU) v = gelu_as(v);
     else if (e.kind == VKB_EPI_SCALE) v = n < e.n_scaled ? v * e.scale : v;
     else if (e.kind == VKB_EPI_RESIDUAL) v = e.residual[idx] + v;
-    if (e.out_f16) reinterpret_cast<__half*>(e.out)[idx] = __float2half_rn(v);
-    else reinterpret_cast<float*>(e.out)[idx] = v;
+    if (e.out_fmt == VKB_DT_F32) {
+        reinterpret_cast<float*>(e.out)[idx] = v;
+    } else {
+        __half hi = __float2half_rn(v);
+        reinterpret_cast<__half*>(e.out)[idx] = hi;
+        if (e.out_fmt == VKB_DT_F16X2) reinterpret_cast<__half*>(e.out)[e.plane + idx] = __float2half_rn(v - __half2float(hi));
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -172,7 +178,7 @@ __device__ __forceinline__ void epi_store(const Epi& e, int64_t m, int64_t n, fl
 template <int FMT, int MM>
 __global__ void __launch_bounds__(128) gemv_kernel(const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc,
                                                    int64_t K, int64_t N, int64_t M, const void* __restrict__ a,
-                                                   int a_f16, int stages_per_split, int n_splits, float* ws, Epi e) {
+                                                   int a_fmt, int stages_per_split, int n_splits, float* ws, Epi e) {
     extern __shared__ float xs[];  // [MM][stages_per_split*64]
     const int tile = blockIdx.x, split = blockIdx.y, r = threadIdx.x;
     const int64_t total_stages = K / STAGE_K;
@@ -185,7 +191,13 @@ __global__ void __launch_bounds__(128) gemv_kernel(const uint8_t* __restrict__ q
         float v = 0.0f;
         if (m < M) {
             int64_t g = (int64_t)m * K + s0 * STAGE_K + kk;
-            v = a_f16 ? __half2float(reinterpret_cast<const __half*>(a)[g]) : reinterpret_cast<const float*>(a)[g];
+            if (a_fmt == VKB_DT_F32) {
+                v = reinterpret_cast<const float*>(a)[g];
+            } else {
+                const __half* ah = reinterpret_cast<const __half*>(a);
+                v = __half2float(ah[g]);
+                if (a_fmt == VKB_DT_F16X2) v += __half2float(ah[M * K + g]);
+            }
         }
         xs[m * ks + kk] = v;
     }
@@ -237,15 +249,20 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int n_splits,
     epi_store(e, m, n, acc, e.bias ? e.bias[n] : 0.0f);
 }
 
-__global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, int64_t n) {
-    int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
-    if (i + 3 < n) {
-        float4 v = *reinterpret_cast<const float4*>(x + i);
-        reinterpret_cast<__half2*>(y + i)[0] = __floats2half2_rn(v.x, v.y);
-        reinterpret_cast<__half2*>(y + i)[1] = __floats2half2_rn(v.z, v.w);
-    } else {
-        for (; i < n; ++i) y[i] = __float2half_rn(x[i]);
-    }
+// x (f32) -> f16 plane, or hi / lo f16 planes (x = hi + lo to ~2^-22) when split.
+__global__ void split_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, int64_t n, int split) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float v = x[i];
+    __half hi = __float2half_rn(v);
+    y[i] = hi;
+    if (split) y[n + i] = __float2half_rn(v - __half2float(hi));
+}
+
+void run_split_f16(vkb_context* ctx, const float* x, int64_t n, __half* y, bool split) {
+    split_f16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(x, y, n, split ? 1 : 0);
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
 }
 
 // ---------------------------------------------------------------------------
@@ -254,41 +271,51 @@ __global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restric
 // TMA (BN tokens x 64 K, f16, 128-byte swizzle). Accumulator in TMEM
 // (128 lanes x BN fp32 columns).
 //
+// SPLIT = true is the high-precision mode: the weight is dequantized to
+// W_hi = f16(w) and W_lo = f16(w - W_hi) and the activation arrives as two f16
+// planes X_hi, X_lo (x = X_hi + X_lo, written by the producing kernel); each
+// K=16 step issues W_hi.X_hi + W_hi.X_lo + W_lo.X_hi, which reproduces the
+// fp32 product to about 2^-21 relative (the W_lo.X_lo term is below that).
+//
 // Warp roles (192 threads):
 //   warp 0      : producer — TMA for X, bulk copies for the raw weight stage
 //   warp 1      : TMEM allocator; lane 0 issues tcgen05.mma and commits
-//   warps 2..5  : dequantize raw stage -> A tile; then the epilogue
+//   warps 2..5  : dequantize raw stage -> A tile(s); then the epilogue
 //                 (thread = one weight row = one TMEM lane)
-// Rings: S stages of (X tile + raw weights), 2 stages of A tiles.
+// Rings: S stages of (X tile(s) + raw weights), 2 stages of A tiles.
 // Every mbarrier wait is bounded; on timeout the kernel records an error flag
 // and returns without hanging.
 // ---------------------------------------------------------------------------
-template <int FMT, int BN>
+template <int FMT, int BN, bool SPLIT>
 struct TcCfg {
-    static constexpr int A_BYTES = TILE_N * 128;              // 16 KB
-    static constexpr int B_BYTES = BN * 128;                  // BN rows x 128 B
+    static constexpr int NP = SPLIT ? 2 : 1;                   // operand planes
+    static constexpr int A_BYTES = TILE_N * 128;               // 16 KB per plane
+    static constexpr int A_STAGE = NP * A_BYTES;
+    static constexpr int B_BYTES = BN * 128;                   // BN rows x 128 B per plane
     static constexpr int RAW_Q = stage_qs_bytes(FMT);
     static constexpr int RAW_S = stage_sc_bytes(FMT);
     static constexpr int RAW_BYTES = ((RAW_Q + RAW_S) + 1023) / 1024 * 1024;
-    static constexpr int STAGE_BYTES = B_BYTES + RAW_BYTES;
-    static constexpr int BUDGET = 225 * 1024 - 2 * A_BYTES - 2048;
+    static constexpr int STAGE_BYTES = NP * B_BYTES + RAW_BYTES;
+    static constexpr int BUDGET = 225 * 1024 - 2 * A_STAGE - 2048;
     static constexpr int S0 = BUDGET / STAGE_BYTES;
     static constexpr int S = S0 > 6 ? 6 : S0;
-    static constexpr int SMEM = 1024 /*align slack*/ + 2 * A_BYTES + S * STAGE_BYTES + 1024 /*barriers*/;
+    static constexpr int SMEM = 1024 /*align slack*/ + 2 * A_STAGE + S * STAGE_BYTES + 1024 /*barriers*/;
     static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
     static_assert(S >= 2, "pipeline needs at least two stages");
 };
 
-template <int FMT, int BN>
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+template <int FMT, int BN, bool SPLIT>
 __global__ void __launch_bounds__(192, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ qs,
-                   const uint8_t* __restrict__ sc, int64_t K, int64_t N, int64_t M, int n_tiles, int m_tiles,
-                   int stages_per_split, int n_splits, float* ws, Epi e, int* err) {
-    using C = TcCfg<FMT, BN>;
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_lo,
+                   const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc, int64_t K, int64_t N, int64_t M,
+                   int n_tiles, int m_tiles, int stages_per_split, int n_splits, float* ws, Epi e, int* err) {
+    using C = TcCfg<FMT, BN, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* a_ring = smem;
-    uint8_t* st_ring = smem + 2 * C::A_BYTES;
+    uint8_t* st_ring = smem + 2 * C::A_STAGE;
     uint64_t* bars = reinterpret_cast<uint64_t*>(st_ring + C::S * C::STAGE_BYTES);
     uint64_t* full = bars;
     uint64_t* empty = bars + C::S;
@@ -336,11 +363,13 @@ __global__ void __launch_bounds__(192, 1)
                 int s = i % C::S;
                 if (!ptx::mbar_wait(&empty[s], ((i / C::S) & 1) ^ 1)) { ok = false; break; }
                 uint8_t* b_dst = st_ring + s * C::STAGE_BYTES;
-                uint8_t* raw_dst = b_dst + C::B_BYTES;
+                uint8_t* raw_dst = b_dst + C::NP * C::B_BYTES;
                 int64_t stage = s0 + i;
                 StagePtrs p = stage_ptrs(FMT, qs, sc, K, n_tile, stage);
-                ptx::mbar_expect_tx(&full[s], C::B_BYTES + C::RAW_Q + C::RAW_S);
+                ptx::mbar_expect_tx(&full[s], C::NP * C::B_BYTES + C::RAW_Q + C::RAW_S);
                 ptx::tma_load_2d(b_dst, &xmap, &full[s], (int32_t)(stage * STAGE_K), m_tile * BN);
+                if (SPLIT)
+                    ptx::tma_load_2d(b_dst + C::B_BYTES, &xmap_lo, &full[s], (int32_t)(stage * STAGE_K), m_tile * BN);
                 ptx::bulk_load(raw_dst, p.qs, C::RAW_Q, &full[s]);
                 if (C::RAW_S) ptx::bulk_load(raw_dst + C::RAW_Q, p.sc, C::RAW_S, &full[s]);
             }
@@ -353,13 +382,19 @@ __global__ void __launch_bounds__(192, 1)
                 if (!ptx::mbar_wait(&full[s], (i / C::S) & 1)) { ok = false; break; }
                 if (!ptx::mbar_wait(&a_full[a], (i >> 1) & 1)) { ok = false; break; }
                 ptx::tc_fence_after();
-                uint32_t a_addr = ptx::smem_u32(a_ring + a * C::A_BYTES);
+                uint32_t a_addr = ptx::smem_u32(a_ring + a * C::A_STAGE);
                 uint32_t b_addr = ptx::smem_u32(st_ring + s * C::STAGE_BYTES);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     uint64_t ad = ptx::sdesc_sw128(a_addr + kk * 32);
                     uint64_t bd = ptx::sdesc_sw128(b_addr + kk * 32);
                     ptx::mma_f16_ss(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    if (SPLIT) {
+                        uint64_t bd_lo = ptx::sdesc_sw128(b_addr + C::B_BYTES + kk * 32);
+                        uint64_t ad_lo = ptx::sdesc_sw128(a_addr + C::A_BYTES + kk * 32);
+                        ptx::mma_f16_ss(tmem, ad, bd_lo, idesc, 1u);
+                        ptx::mma_f16_ss(tmem, ad_lo, bd, idesc, 1u);
+                    }
                 }
                 ptx::mma_commit(&empty[s]);
                 ptx::mma_commit(&a_empty[a]);
@@ -374,22 +409,29 @@ __global__ void __launch_bounds__(192, 1)
             int s = i % C::S, a = i & 1;
             if (!ptx::mbar_wait(&full[s], (i / C::S) & 1)) { ok = false; break; }
             if (!ptx::mbar_wait(&a_empty[a], ((i >> 1) & 1) ^ 1)) { ok = false; break; }
-            const uint8_t* raw = st_ring + s * C::STAGE_BYTES + C::B_BYTES;
+            const uint8_t* raw = st_ring + s * C::STAGE_BYTES + C::NP * C::B_BYTES;
             float w[64];
             dequant_row_stage<FMT>(raw, raw + C::RAW_Q, r, (int)(s0 + i), w);
-            uint8_t* arow = a_ring + a * C::A_BYTES + r * 128;
+            uint8_t* arow = a_ring + a * C::A_STAGE + r * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
-                __half2 h0 = __floats2half2_rn(w[8 * c + 0], w[8 * c + 1]);
-                __half2 h1 = __floats2half2_rn(w[8 * c + 2], w[8 * c + 3]);
-                __half2 h2 = __floats2half2_rn(w[8 * c + 4], w[8 * c + 5]);
-                __half2 h3 = __floats2half2_rn(w[8 * c + 6], w[8 * c + 7]);
                 uint4 v;
-                v.x = *reinterpret_cast<uint32_t*>(&h0);
-                v.y = *reinterpret_cast<uint32_t*>(&h1);
-                v.z = *reinterpret_cast<uint32_t*>(&h2);
-                v.w = *reinterpret_cast<uint32_t*>(&h3);
+                __half2 h[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) h[q] = __floats2half2_rn(w[8 * c + 2 * q], w[8 * c + 2 * q + 1]);
+                v.x = h2_bits(h[0]); v.y = h2_bits(h[1]); v.z = h2_bits(h[2]); v.w = h2_bits(h[3]);
                 *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = v;
+                if (SPLIT) {
+                    __half2 l[4];
+                    uint4 vl;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float2 hf = __half22float2(h[q]);
+                        l[q] = __floats2half2_rn(w[8 * c + 2 * q] - hf.x, w[8 * c + 2 * q + 1] - hf.y);
+                    }
+                    vl.x = h2_bits(l[0]); vl.y = h2_bits(l[1]); vl.z = h2_bits(l[2]); vl.w = h2_bits(l[3]);
+                    *reinterpret_cast<uint4*>(arow + C::A_BYTES + ((c ^ (r & 7)) << 4)) = vl;
+                }
             }
             ptx::fence_proxy_async_smem();
             ptx::mbar_arrive(&a_full[a]);
@@ -466,7 +508,7 @@ static int* device_err_flag(vkb_context* ctx) { return ctx->err_flag.as<int>(); 
 int gemv_max_m() { return 4; }
 
 template <int FMT>
-static void launch_gemv(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_f16, const Epi& e,
+static void launch_gemv(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_fmt, const Epi& e,
                         float* ws, int stages_per_split, int splits) {
     dim3 grid((unsigned)(w->n_pad / TILE_N), (unsigned)splits);
     const uint8_t* qs = w->qs.as<uint8_t>();
@@ -480,7 +522,7 @@ static void launch_gemv(vkb_context* ctx, const vkb_weight* w, int64_t m, const 
                                           200 * 1024));                                                         \
             attr = true;                                                                                        \
         }                                                                                                       \
-        gemv_kernel<FMT, MMv><<<grid, 128, sm, ctx->stream>>>(qs, sc, w->k, w->n, m, a, a_f16, stages_per_split, \
+        gemv_kernel<FMT, MMv><<<grid, 128, sm, ctx->stream>>>(qs, sc, w->k, w->n, m, a, a_fmt, stages_per_split, \
                                                               splits, ws, e);                                   \
     }
     if (m <= 1) VKB_GEMV(1) else if (m <= 2) VKB_GEMV(2) else VKB_GEMV(4)
@@ -489,38 +531,55 @@ static void launch_gemv(vkb_context* ctx, const vkb_weight* w, int64_t m, const 
     ctx->count();
 }
 
-template <int FMT, int BN>
+template <int FMT, int BN, bool SPLIT>
 static void launch_tc(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const Epi& e, float* ws,
                       int stages_per_split, int splits, int m_tiles) {
-    using C = TcCfg<FMT, BN>;
+    using C = TcCfg<FMT, BN, SPLIT>;
     static bool attr = false;
     if (!attr) {
-        VKB_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<FMT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        VKB_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<FMT, BN, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      C::SMEM));
         attr = true;
     }
-    CUtensorMap map;
+    CUtensorMap map, map_lo;
     make_tmap_f16(&map, a16, m, w->k, BN);
+    if (SPLIT) make_tmap_f16(&map_lo, a16 + m * w->k, m, w->k, BN);
+    else map_lo = map;
     int n_tiles = (int)(w->n_pad / TILE_N);
     dim3 grid((unsigned)(n_tiles * m_tiles * splits));
-    tc_gemm_kernel<FMT, BN><<<grid, 192, C::SMEM, ctx->stream>>>(
-        map, w->qs.as<uint8_t>(), w->sc.as<uint8_t>(), w->k, w->n, m, n_tiles, m_tiles, stages_per_split, splits, ws,
-        e, device_err_flag(ctx));
+    tc_gemm_kernel<FMT, BN, SPLIT><<<grid, 192, C::SMEM, ctx->stream>>>(
+        map, map_lo, w->qs.as<uint8_t>(), w->sc.as<uint8_t>(), w->k, w->n, m, n_tiles, m_tiles, stages_per_split,
+        splits, ws, e, device_err_flag(ctx));
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
 
-template <int FMT>
+template <int FMT, bool SPLIT>
 static void dispatch_tc(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const Epi& e, float* ws,
                         int bn, int sps, int splits, int m_tiles) {
     switch (bn) {
-        case 32: launch_tc<FMT, 32>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
-        case 64: launch_tc<FMT, 64>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
-        case 128: launch_tc<FMT, 128>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
-        default: launch_tc<FMT, 256>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
+        case 32: launch_tc<FMT, 32, SPLIT>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
+        case 64: launch_tc<FMT, 64, SPLIT>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
+        case 128: launch_tc<FMT, 128, SPLIT>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
+        default:
+            if constexpr (!SPLIT) launch_tc<FMT, 256, false>(ctx, w, m, a16, e, ws, sps, splits, m_tiles);
+            else fail(VKB_ERROR_OTHER, "linear: split precision uses token tiles up to 128");
+            break;
     }
 }
 
-LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m) {
+template <bool SPLIT>
+static void dispatch_fmt(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const Epi& e, float* ws,
+                         const LinearPlan& p) {
+    switch (w->fmt) {
+        case W_Q4_0: dispatch_tc<W_Q4_0, SPLIT>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
+        case W_Q8_0: dispatch_tc<W_Q8_0, SPLIT>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
+        case W_Q4_K: dispatch_tc<W_Q4_K, SPLIT>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
+        default: dispatch_tc<W_F16, SPLIT>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
+    }
+}
+
+LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m, bool split) {
     LinearPlan p;
     const int64_t total = w->k / STAGE_K;
     const int n_tiles = (int)(w->n_pad / TILE_N);
@@ -536,7 +595,9 @@ LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m) {
         p.sps = sps;
     } else {
         p.tc = true;
-        int bn = m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256;
+        p.split = split;
+        const int bn_max = split ? 128 : 256;
+        int bn = m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : bn_max;
         int m_tiles = (int)((m + bn - 1) / bn);
         if (bn == 256 && (int64_t)n_tiles * m_tiles < sms) {
             bn = 128;
@@ -553,8 +614,11 @@ LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m) {
         p.sps = sps;
     }
     p.ws_bytes = (p.splits > 1 ? (size_t)p.splits * m * w->n * sizeof(float) : 0);
-    p.a16_bytes = 0;
     return p;
+}
+
+LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m) {
+    return plan_linear(ctx, w, m, ctx->precision == VKB_PREC_SPLIT);
 }
 
 void run_linear(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_dtype, const float* bias,
@@ -569,49 +633,49 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
                    __half* a16_override, const LinearExtra& x) {
     if (m <= 0) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: m must be positive");
     if (!a || !out) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: null activation or output pointer");
-    if (a_dtype != VKB_DT_F32 && a_dtype != VKB_DT_F16) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: bad a_dtype");
-    if (out_dtype != VKB_DT_F32 && out_dtype != VKB_DT_F16) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: bad out_dtype");
+    if (a_dtype != VKB_DT_F32 && a_dtype != VKB_DT_F16 && a_dtype != VKB_DT_F16X2)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "linear: bad a_dtype");
+    if (out_dtype != VKB_DT_F32 && out_dtype != VKB_DT_F16 && out_dtype != VKB_DT_F16X2)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "linear: bad out_dtype");
     if (epilogue < VKB_EPI_NONE || epilogue > VKB_EPI_SCALE) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: bad epilogue");
     if (epilogue == VKB_EPI_RESIDUAL && (out_dtype != VKB_DT_F32 || !residual))
         fail(VKB_ERROR_INVALID_ARGUMENT, "linear: the residual epilogue needs an f32 output and a residual pointer");
-    LinearPlan p = plan_linear(ctx, w, m);
-    Epi e{bias, residual, out, out_dtype == VKB_DT_F16, epilogue, scale, w->n,
-          x.n_scaled >= 0 ? x.n_scaled : w->n, x.col_block, x.out_rows > 0 ? x.out_rows : m, x.row_map,
-          x.row_group > 0 ? x.row_group : 1};
+    if (x.col_block > 0 && out_dtype == VKB_DT_F16X2)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "linear: a column-block layout needs an f32 or f16 output");
+    // A single f16 activation plane carries no low part: the GEMM then runs unsplit.
+    const bool split = ctx->precision == VKB_PREC_SPLIT && a_dtype != VKB_DT_F16;
+    LinearPlan p = plan_linear(ctx, w, m, split);
+    const int64_t out_rows = x.out_rows > 0 ? x.out_rows : m;
+    Epi e{bias, residual, out, out_dtype, epilogue, scale, w->n,
+          x.n_scaled >= 0 ? x.n_scaled : w->n, x.col_block, out_rows, x.row_map,
+          x.row_group > 0 ? x.row_group : 1, out_rows * w->n};
     if (x.col_block > 0 && (w->n % x.col_block)) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: n not a multiple of col_block");
-    // Workspace: [f16 copy of a (tc path with f32 input)] [split partials]
-    size_t a16_bytes = (p.tc && a_dtype == VKB_DT_F32 && !a16_override) ? ((size_t)m * w->k * 2 + 255) / 256 * 256 : 0;
+    // Workspace: [f16 (or f16 hi+lo) copy of a: tc path with f32 input] [split-K partials]
+    size_t a16_bytes = (p.tc && a_dtype == VKB_DT_F32 && !a16_override)
+                           ? ((size_t)m * w->k * 2 * (split ? 2 : 1) + 255) / 256 * 256
+                           : 0;
     size_t ws_bytes = ws_override ? 0 : p.ws_bytes;
     if (a16_bytes + ws_bytes) ctx->ensure_workspace(a16_bytes + ws_bytes);
     uint8_t* wsb = ctx->workspace.as<uint8_t>();
     float* ws = ws_override ? ws_override : reinterpret_cast<float*>(wsb + a16_bytes);
     if (!p.tc) {
         switch (w->fmt) {
-            case W_Q4_0: launch_gemv<W_Q4_0>(ctx, w, m, a, a_dtype == VKB_DT_F16, e, ws, p.sps, p.splits); break;
-            case W_Q8_0: launch_gemv<W_Q8_0>(ctx, w, m, a, a_dtype == VKB_DT_F16, e, ws, p.sps, p.splits); break;
-            case W_Q4_K: launch_gemv<W_Q4_K>(ctx, w, m, a, a_dtype == VKB_DT_F16, e, ws, p.sps, p.splits); break;
-            default: launch_gemv<W_F16>(ctx, w, m, a, a_dtype == VKB_DT_F16, e, ws, p.sps, p.splits); break;
+            case W_Q4_0: launch_gemv<W_Q4_0>(ctx, w, m, a, a_dtype, e, ws, p.sps, p.splits); break;
+            case W_Q8_0: launch_gemv<W_Q8_0>(ctx, w, m, a, a_dtype, e, ws, p.sps, p.splits); break;
+            case W_Q4_K: launch_gemv<W_Q4_K>(ctx, w, m, a, a_dtype, e, ws, p.sps, p.splits); break;
+            default: launch_gemv<W_F16>(ctx, w, m, a, a_dtype, e, ws, p.sps, p.splits); break;
         }
     } else {
         const __half* a16;
-        if (a_dtype == VKB_DT_F16) {
+        if (a_dtype != VKB_DT_F32) {
             a16 = reinterpret_cast<const __half*>(a);
         } else {
             __half* dst = a16_override ? a16_override : reinterpret_cast<__half*>(wsb);
-            int64_t n = m * w->k;
-            int64_t thr = (n + 3) / 4;
-            f32_to_f16_kernel<<<(unsigned)((thr + 255) / 256), 256, 0, ctx->stream>>>(
-                reinterpret_cast<const float*>(a), dst, n);
-            VKB_CUDA(cudaGetLastError());
-            ctx->count();
+            run_split_f16(ctx, reinterpret_cast<const float*>(a), m * w->k, dst, split);
             a16 = dst;
         }
-        switch (w->fmt) {
-            case W_Q4_0: dispatch_tc<W_Q4_0>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
-            case W_Q8_0: dispatch_tc<W_Q8_0>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
-            case W_Q4_K: dispatch_tc<W_Q4_K>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
-            default: dispatch_tc<W_F16>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
-        }
+        if (p.split) dispatch_fmt<true>(ctx, w, m, a16, e, ws, p);
+        else dispatch_fmt<false>(ctx, w, m, a16, e, ws, p);
     }
     if (p.splits > 1) {
         int64_t tot = m * w->n;

@@ -12,8 +12,8 @@ struct LinearPlan {
     int m_tiles = 0;
     int splits = 1;      // K splits (partials reduced by splitk_reduce_kernel)
     int sps = 0;         // stages per split
+    bool split = false;  // high-precision (hi+lo) tensor-core mode
     size_t ws_bytes = 0; // fp32 partials
-    size_t a16_bytes = 0;
 };
 
 // Epilogue extensions used by the model runner (fused projections).
@@ -27,6 +27,9 @@ struct LinearExtra {
 
 vkb_weight* upload_weight(vkb_context* ctx, uint32_t tag, int64_t n, int64_t k, const void* bytes, size_t len);
 LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m);
+LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m, bool split);
+// x (f32, n elements) -> f16 plane (or hi then lo planes when split).
+void run_split_f16(vkb_context* ctx, const float* x, int64_t n, __half* y, bool split);
 // Runs out = epilogue(a . W^T + bias). ws_override / a16_override let a caller
 // that pre-sized its own scratch avoid the context workspace.
 void run_linear(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_dtype, const float* bias,

@@ -272,11 +272,12 @@ vkb_session* create_session(vkb_whisper* m, const vkb_session_options* o) {
     const int64_t mt = o->max_step_tokens;
     s->max_tok = (int)mt;
     s->h.alloc(mt * d * 4);
-    s->xln.alloc(mt * d * 2);
+    // activations that feed a GEMM are f16 hi + lo planes (VKB_DT_F16X2)
+    s->xln.alloc(mt * d * 4);
     s->qkv.alloc(mt * 3 * d * 4);
-    s->ctxb.alloc(mt * d * 2);
+    s->ctxb.alloc(mt * d * 4);
     s->qc.alloc(mt * d * 4);
-    s->ffn.alloc(mt * f * 2);
+    s->ffn.alloc(mt * f * 4);
     s->logits.alloc(mt * V * 4);
     s->ids.alloc(mt * 4);
     s->tok.alloc(mt * 4);
@@ -300,12 +301,14 @@ vkb_session* create_session(vkb_whisper* m, const vkb_session_options* o) {
     const int64_t C = o->max_clips;
     if (C > 0) {
         const int64_t Tin = 2 * T, M = C * T;
-        s->col1.alloc(C * Tin * m->k1p * 2);
-        s->bufA.alloc(std::max(M * f * 2, C * Tin * d * 2));
-        s->bufB.alloc(M * 3 * d * 2);
+        s->col1.alloc(C * Tin * m->k1p * 4);
+        // bufA holds the conv1 output [C*Tin][d], the MLP hidden [M][ffn] and the
+        // cross K/V projection [M][2d] f32 in turn.
+        s->bufA.alloc(std::max({M * f * 4, C * Tin * d * 4, M * 2 * d * 4}));
+        s->bufB.alloc(M * 3 * d * 4);
         s->eh.alloc(M * d * 4);
-        s->exln.alloc(M * d * 2);
-        s->ectx.alloc(M * d * 2);
+        s->exln.alloc(M * d * 4);
+        s->ectx.alloc(M * d * 4);
         s->eout.alloc(M * d * 4);
         s->emap.alloc(C * 4);
         VKB_CUDA(cudaMallocHost(&s->h_map, (size_t)C * 4));
@@ -344,33 +347,38 @@ void session_encode(vkb_session* s, int n, const float* logmel, const int32_t* s
     float* h = s->eh.as<float>();
     __half* xln = s->exln.as<__half>();
     __half* ectx = s->ectx.as<__half>();
+    // GEMM inputs are f16 hi + lo planes in the default (split) precision
+    const bool split = ctx->precision == VKB_PREC_SPLIT;
+    const int AF = split ? VKB_DT_F16X2 : VKB_DT_F16;
+    const int planes = split ? 2 : 1;
     // conv stem: conv1 (k3 s1 p1) + GELU, conv2 (k3 s2 p1) + GELU, + positions
-    run_im2col_ct(ctx, logmel, n, D.n_mels, (int)Tin, 1, m->k1p, s->col1.as<__half>());
-    run_linear(ctx, m->conv1.get(), n * Tin, s->col1.p, VKB_DT_F16, m->conv1_b.as<float>(), bufA, VKB_DT_F16,
-               VKB_EPI_GELU, nullptr, 1.0f, ws, nullptr);
-    run_im2col_tc(ctx, bufA, n, (int)d, (int)Tin, 2, bufB);
-    run_linear(ctx, m->conv2.get(), M, bufB, VKB_DT_F16, m->conv2_b.as<float>(), xln, VKB_DT_F16, VKB_EPI_GELU, nullptr,
+    run_im2col_ct(ctx, logmel, n, D.n_mels, (int)Tin, 1, m->k1p, s->col1.as<__half>(), split);
+    run_linear(ctx, m->conv1.get(), n * Tin, s->col1.p, AF, m->conv1_b.as<float>(), bufA, AF, VKB_EPI_GELU, nullptr,
                1.0f, ws, nullptr);
-    run_add_pos(ctx, xln, m->enc_pos.as<float>(), n, (int)T, (int)d, h);
+    run_im2col_tc(ctx, bufA, n, (int)d, (int)Tin, 2, bufB, planes);
+    run_linear(ctx, m->conv2.get(), M, bufB, AF, m->conv2_b.as<float>(), xln, AF, VKB_EPI_GELU, nullptr, 1.0f, ws,
+               nullptr);
+    run_add_pos(ctx, xln, m->enc_pos.as<float>(), n, (int)T, (int)d, h, planes);
     const float scale = 1.0f / sqrtf((float)(d / D.n_audio_head));
     for (const EncLayer& L : m->enc) {
-        run_layer_norm(ctx, h, M, (int)d, L.ln1g.as<float>(), L.ln1b.as<float>(), LN_EPS, xln, 1);
+        run_layer_norm(ctx, h, M, (int)d, L.ln1g.as<float>(), L.ln1b.as<float>(), LN_EPS, xln, AF);
         LinearExtra x;
         x.n_scaled = d;
-        run_linear_ex(ctx, L.qkv.get(), M, xln, VKB_DT_F16, L.qkv_b.as<float>(), bufB, VKB_DT_F16, VKB_EPI_SCALE,
-                      nullptr, scale, ws, nullptr, x);
-        run_encoder_attention(ctx, bufB, 3 * d, (int)d, (int)(2 * d), n, (int)T, D.n_audio_head, 64, ectx, d);
-        run_linear(ctx, L.o.get(), M, ectx, VKB_DT_F16, L.o_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h, 1.0f,
-                   ws, nullptr);
-        run_layer_norm(ctx, h, M, (int)d, L.ln2g.as<float>(), L.ln2b.as<float>(), LN_EPS, xln, 1);
-        run_linear(ctx, L.fc1.get(), M, xln, VKB_DT_F16, L.fc1_b.as<float>(), bufA, VKB_DT_F16, VKB_EPI_GELU, nullptr,
-                   1.0f, ws, nullptr);
-        run_linear(ctx, L.fc2.get(), M, bufA, VKB_DT_F16, L.fc2_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h, 1.0f,
-                   ws, nullptr);
+        run_linear_ex(ctx, L.qkv.get(), M, xln, AF, L.qkv_b.as<float>(), bufB, VKB_DT_F16, VKB_EPI_SCALE, nullptr,
+                      scale, ws, nullptr, x);
+        run_encoder_attention(ctx, bufB, 3 * d, (int)d, (int)(2 * d), n, (int)T, D.n_audio_head, 64, ectx, d,
+                              split ? ectx + M * d : nullptr);
+        run_linear(ctx, L.o.get(), M, ectx, AF, L.o_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h, 1.0f, ws,
+                   nullptr);
+        run_layer_norm(ctx, h, M, (int)d, L.ln2g.as<float>(), L.ln2b.as<float>(), LN_EPS, xln, AF);
+        run_linear(ctx, L.fc1.get(), M, xln, AF, L.fc1_b.as<float>(), bufA, AF, VKB_EPI_GELU, nullptr, 1.0f, ws,
+                   nullptr);
+        run_linear(ctx, L.fc2.get(), M, bufA, AF, L.fc2_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h, 1.0f, ws,
+                   nullptr);
     }
     (void)f;
     run_layer_norm(ctx, h, M, (int)d, m->enc_lng.as<float>(), m->enc_lnb.as<float>(), LN_EPS, s->eout.p, 0);
-    run_layer_norm(ctx, h, M, (int)d, m->enc_lng.as<float>(), m->enc_lnb.as<float>(), LN_EPS, xln, 1);
+    run_layer_norm(ctx, h, M, (int)d, m->enc_lng.as<float>(), m->enc_lnb.as<float>(), LN_EPS, xln, AF);
     // cross K/V for every decoder layer, rows remapped to the stream slots
     if (s->staged_pending) VKB_CUDA(cudaEventSynchronize(s->staged));
     memcpy(s->h_map, streams, (size_t)n * 4);
@@ -383,7 +391,7 @@ void session_encode(vkb_session* s, int n, const float* logmel, const int32_t* s
         const DecLayer& L = m->dec[l];
         if (s->opt.cross_kv_q8) {
             float* tmp = reinterpret_cast<float*>(bufA);  // [M][2d] f32
-            run_linear(ctx, L.ckv.get(), M, xln, VKB_DT_F16, L.ckv_b.as<float>(), tmp, VKB_DT_F32, VKB_EPI_NONE,
+            run_linear(ctx, L.ckv.get(), M, xln, AF, L.ckv_b.as<float>(), tmp, VKB_DT_F32, VKB_EPI_NONE,
                        nullptr, 1.0f, ws, nullptr);
             int8_t* kq = s->ck.as<int8_t>() + (size_t)l * rows * d;
             int8_t* vq = s->cv.as<int8_t>() + (size_t)l * rows * d;
@@ -393,7 +401,7 @@ void session_encode(vkb_session* s, int n, const float* logmel, const int32_t* s
             run_quantize_rows(ctx, tmp + d, 2 * d, M, (int)d, vq, vs, map, (int)T);
         } else {
             float* tmp = reinterpret_cast<float*>(bufA);  // [M][2d] f32
-            run_linear(ctx, L.ckv.get(), M, xln, VKB_DT_F16, L.ckv_b.as<float>(), tmp, VKB_DT_F32, VKB_EPI_NONE,
+            run_linear(ctx, L.ckv.get(), M, xln, AF, L.ckv_b.as<float>(), tmp, VKB_DT_F32, VKB_EPI_NONE,
                        nullptr, 1.0f, ws, nullptr);
             run_copy_rows_f16(ctx, tmp, 2 * d, M, (int)d, s->ck.as<__half>() + (size_t)l * rows * d, map, (int)T);
             run_copy_rows_f16(ctx, tmp + d, 2 * d, M, (int)d, s->cv.as<__half>() + (size_t)l * rows * d, map, (int)T);
@@ -436,45 +444,46 @@ void session_step(vkb_session* s, int n_tok, const int32_t* streams, const int32
     float* qc = s->qc.as<float>();
     __half* ffn = s->ffn.as<__half>();
     float* ws = s->ws.as<float>();
+    const int AF = ctx->precision == VKB_PREC_SPLIT ? VKB_DT_F16X2 : VKB_DT_F16;
     run_embed(ctx, m->tok_emb.get(), s->tok.as<int32_t>(), s->pos.as<int32_t>(), n_tok, m->dec_pos.as<float>(), h);
     const float scale = 1.0f / sqrtf((float)(d / D.n_text_head));
     const int64_t rows = (int64_t)s->opt.max_streams * T;
     for (int l = 0; l < D.n_text_layer; ++l) {
         const DecLayer& L = m->dec[l];
-        run_layer_norm(ctx, h, n_tok, (int)d, L.ln1g.as<float>(), L.ln1b.as<float>(), LN_EPS, xln, 1);
+        run_layer_norm(ctx, h, n_tok, (int)d, L.ln1g.as<float>(), L.ln1b.as<float>(), LN_EPS, xln, AF);
         LinearExtra x;
         x.n_scaled = d;
-        run_linear_ex(ctx, L.qkv.get(), n_tok, xln, VKB_DT_F16, L.qkv_b.as<float>(), qkv, VKB_DT_F32, VKB_EPI_SCALE,
+        run_linear_ex(ctx, L.qkv.get(), n_tok, xln, AF, L.qkv_b.as<float>(), qkv, VKB_DT_F32, VKB_EPI_SCALE,
                       nullptr, scale, ws, nullptr, x);
         kv_append_ex(s->pool, l, qkv + d, qkv + 2 * d, 3 * d);
-        kv_attention_ex(s->pool, l, qkv, 3 * d, ctxb, VKB_DT_F16);
-        run_linear(ctx, L.o.get(), n_tok, ctxb, VKB_DT_F16, L.o_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h, 1.0f,
+        kv_attention_ex(s->pool, l, qkv, 3 * d, ctxb, AF);
+        run_linear(ctx, L.o.get(), n_tok, ctxb, AF, L.o_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h, 1.0f,
                    ws, nullptr);
-        run_layer_norm(ctx, h, n_tok, (int)d, L.ln2g.as<float>(), L.ln2b.as<float>(), LN_EPS, xln, 1);
-        run_linear(ctx, L.cq.get(), n_tok, xln, VKB_DT_F16, L.cq_b.as<float>(), qc, VKB_DT_F32, VKB_EPI_SCALE, nullptr,
+        run_layer_norm(ctx, h, n_tok, (int)d, L.ln2g.as<float>(), L.ln2b.as<float>(), LN_EPS, xln, AF);
+        run_linear(ctx, L.cq.get(), n_tok, xln, AF, L.cq_b.as<float>(), qc, VKB_DT_F32, VKB_EPI_SCALE, nullptr,
                    scale, ws, nullptr);
         if (s->opt.cross_kv_q8) {
             run_dense_attention(ctx, n_tok, D.n_text_head, 64, qc, s->seq.as<int32_t>(),
                                 s->ck.as<int8_t>() + (size_t)l * rows * d, s->cv.as<int8_t>() + (size_t)l * rows * d,
                                 s->cks.as<__half>() + (size_t)l * rows * (d / 32),
                                 s->cvs.as<__half>() + (size_t)l * rows * (d / 32), (int)T, VKB_KV_Q8_0, ctxb,
-                                VKB_DT_F16, nullptr);
+                                AF, nullptr);
         } else {
             run_dense_attention(ctx, n_tok, D.n_text_head, 64, qc, s->seq.as<int32_t>(),
                                 s->ck.as<__half>() + (size_t)l * rows * d, s->cv.as<__half>() + (size_t)l * rows * d,
-                                nullptr, nullptr, (int)T, VKB_DT_F16, ctxb, VKB_DT_F16, nullptr);
+                                nullptr, nullptr, (int)T, VKB_DT_F16, ctxb, AF, nullptr);
         }
-        run_linear(ctx, L.co.get(), n_tok, ctxb, VKB_DT_F16, L.co_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h,
+        run_linear(ctx, L.co.get(), n_tok, ctxb, AF, L.co_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h,
                    1.0f, ws, nullptr);
-        run_layer_norm(ctx, h, n_tok, (int)d, L.ln3g.as<float>(), L.ln3b.as<float>(), LN_EPS, xln, 1);
-        run_linear(ctx, L.fc1.get(), n_tok, xln, VKB_DT_F16, L.fc1_b.as<float>(), ffn, VKB_DT_F16, VKB_EPI_GELU,
+        run_layer_norm(ctx, h, n_tok, (int)d, L.ln3g.as<float>(), L.ln3b.as<float>(), LN_EPS, xln, AF);
+        run_linear(ctx, L.fc1.get(), n_tok, xln, AF, L.fc1_b.as<float>(), ffn, AF, VKB_EPI_GELU,
                    nullptr, 1.0f, ws, nullptr);
-        run_linear(ctx, L.fc2.get(), n_tok, ffn, VKB_DT_F16, L.fc2_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h,
+        run_linear(ctx, L.fc2.get(), n_tok, ffn, AF, L.fc2_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h,
                    1.0f, ws, nullptr);
     }
-    run_layer_norm(ctx, h, n_tok, (int)d, m->dec_lng.as<float>(), m->dec_lnb.as<float>(), LN_EPS, xln, 1);
+    run_layer_norm(ctx, h, n_tok, (int)d, m->dec_lng.as<float>(), m->dec_lnb.as<float>(), LN_EPS, xln, AF);
     float* lg = logits_out ? logits_out : s->logits.as<float>();
-    run_linear(ctx, m->tok_emb.get(), n_tok, xln, VKB_DT_F16, nullptr, lg, VKB_DT_F32, VKB_EPI_NONE, nullptr, 1.0f, ws,
+    run_linear(ctx, m->tok_emb.get(), n_tok, xln, AF, nullptr, lg, VKB_DT_F32, VKB_EPI_NONE, nullptr, 1.0f, ws,
                nullptr);
     run_argmax(ctx, lg, n_tok, D.n_vocab, ids_out ? ids_out : s->ids.as<int32_t>());
 }
@@ -526,6 +535,15 @@ vkb_status vkb_session_encode(vkb_session* s, int32_t n_clips, const float* logm
 }
 
 const float* vkb_session_encoder_output(const vkb_session* s) { return s ? s->eout.as<float>() : nullptr; }
+
+vkb_status vkb_session_read_encoder_output(const vkb_session* s, float* host, size_t n_floats) {
+    return guard([&] {
+        if (!s || !host) fail(VKB_ERROR_INVALID_ARGUMENT, "read_encoder_output: null argument");
+        if (n_floats * 4 > s->eout.n) fail(VKB_ERROR_INVALID_ARGUMENT, "read_encoder_output: too many floats");
+        VKB_CUDA(cudaMemcpyAsync(host, s->eout.p, n_floats * 4, cudaMemcpyDeviceToHost, s->ctx->stream));
+        VKB_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    });
+}
 
 vkb_status vkb_session_step(vkb_session* s, int32_t n_tok, const int32_t* streams_host, const int32_t* positions_host,
                             const int32_t* tokens_host, float* logits_dev, int32_t* ids_dev) {

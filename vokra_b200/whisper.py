@@ -55,18 +55,12 @@ class Session:
         s = np.ascontiguousarray(streams, dtype=np.int32)
         check(_L.vkb_session_encode(self.h, s.size, C.c_void_p(logmel_dev.data_ptr()), s.ctypes.data_as(C.c_void_p)))
 
-    def encoder_output(self, n_clips: int):
-        import torch
+    def encoder_output(self, n_clips: int) -> np.ndarray:
+        """The last encoder output [n_clips, n_audio_ctx, d_model] (after ln_post), on the host."""
         d = self.model.dims
-        ptr = _L.vkb_session_encoder_output(self.h)
-        n = n_clips * d.n_audio_ctx * d.d_model
-        self.ctx.synchronize()
-        host = np.empty(n, np.float32)
-        cudart = torch.cuda.cudart()
-        err = cudart.cudaMemcpy(host.ctypes.data, ptr, n * 4, 2)  # device -> host
-        if int(err) != 0:
-            raise RuntimeError(f"cudaMemcpy failed: {err}")
-        return host.reshape(n_clips, d.n_audio_ctx, d.d_model)
+        host = np.empty((n_clips, d.n_audio_ctx, d.d_model), np.float32)
+        check(_L.vkb_session_read_encoder_output(self.h, host.ctypes.data_as(C.c_void_p), host.size))
+        return host
 
     def step(self, streams, positions, tokens, logits_dev=None, ids_dev=None):
         s = np.ascontiguousarray(streams, dtype=np.int32)
