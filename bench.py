@@ -1,0 +1,389 @@
+#!/usr/bin/env python3
+"""Benchmark: Whisper-large-v3 Q4_0 batched transcription on B200.
+
+Workload: 64 synthetic 30 s clips per GPU; encoder
+forward, then a 4-token prefix and a 128-token teacher-forced decode through
+the paged Q8_0 self-attention KV cache and the Q8_0 cross-attention store.
+One "step" = that whole pass for one batch of 64 utterances. With N GPUs
+(torchrun) every rank processes its own batch (utterances shard by request;
+weak scaling, no collective on the hot path).
+
+Prints one JSON line (rank 0). `value` = audio-seconds per second with the
+log-mels already in HBM; `e2e` = the same metric with the log-mels copied
+from pinned host memory and the greedy ids read back every step.
+
+`--impl reference` times the reference's CPU algorithm (the C++ restatement
+in oracle/, the Rust reference cannot be built here) on a bounded sample of
+the same workload and extrapolates to the metric's unit.
+"""
+from __future__ import annotations
+
+import argparse
+import dataclasses
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CLIP_SECONDS = 30.0
+PREFIX = 4
+METRIC = "audio-s/s + decode tok/s, Whisper-large-v3 Q4_0 @1/2/4/8 B200; % of roofline"
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], p.get("bf16_tflops_sustained", p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                for line in out.stdout.strip().splitlines():
+                    self.rows.append([c.strip() for c in line.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [v for v in (num(r[1]) for r in self.rows if len(r) > 2) if v is not None]
+        mx = [v for v in (num(r[2]) for r in self.rows if len(r) > 2) if v is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            for i, n in enumerate(names):
+                if len(r) > 5 + i and r[5 + i].lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+def model_path(name: str) -> str:
+    d = os.environ.get("VKB_BENCH_CACHE", "/tmp/vkb_bench")
+    os.makedirs(d, exist_ok=True)
+    return os.path.join(d, f"whisper_{name}_seed0.gguf")
+
+
+def ensure_model(path: str, arch, qtag: int):
+    from vokra_b200 import synth
+    if not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        synth.write_synthetic_whisper(tmp, arch, qtag, seed=0)
+        os.replace(tmp, path)
+    return path
+
+
+def synthetic_logmels(n: int, n_mels: int, n_frames: int, seed: int) -> np.ndarray:
+    """Seeded stand-in for the frontend output, in Whisper's normalised log-mel range."""
+    rng = np.random.default_rng(seed)
+    base = rng.uniform(-0.8, 0.2, (n, n_mels, 1)).astype(np.float32)
+    x = base + rng.standard_normal((n, n_mels, n_frames)).astype(np.float32) * np.float32(0.25)
+    return np.clip(x, -1.0, 1.5).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# CPU leg: the oracle (reference algorithm restated in C++) on a bounded sample
+# ---------------------------------------------------------------------------
+def cpu_sample(arch, qtag, qname, n_tokens: int, threads: int):
+    """Times 1 clip on a 2+2-layer model of the same dims; extrapolates to the full depth."""
+    from oracle import py as o, whisper_ref
+    o.lib().orc_set_threads(threads)
+    small = dataclasses.replace(arch, n_audio_layer=2, n_text_layer=2)
+    path = ensure_model(model_path(f"sample_{qname}_e2d2"), small, qtag)
+    ref = whisper_ref.RefWhisper(path)
+    lm = synthetic_logmels(1, arch.n_mels, 2 * arch.n_audio_ctx, 123)[0]
+    ref.n_audio_layer = 0
+    t0 = time.perf_counter()
+    ref.encode(lm)
+    t_conv = time.perf_counter() - t0
+    ref.n_audio_layer = 2
+    t0 = time.perf_counter()
+    enc = ref.encode(lm)
+    t_enc2 = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    dec = ref.decoder(enc, kv_mode="q8", cross_mode="q8")
+    t_cross2 = time.perf_counter() - t0
+    dec.step(list(arch.start_ids))
+    steps = 3
+    t0 = time.perf_counter()
+    for i in range(steps):
+        dec.step([100 + i])
+    t_step2 = (time.perf_counter() - t0) / steps
+    x = np.zeros((1, arch.d_model), np.float32)
+    t0 = time.perf_counter()
+    o.gemm_kn(x, ref.emb_t)
+    t_head = time.perf_counter() - t0
+    L_e, L_d = arch.n_audio_layer, arch.n_text_layer
+    t_enc = t_conv + (t_enc2 - t_conv) * L_e / 2
+    t_cross = t_cross2 * L_d / 2
+    t_step = t_head + max(0.0, t_step2 - t_head) * L_d / 2
+    t_clip = t_enc + t_cross + n_tokens * t_step
+    sample = (f"1 clip on a 2+2-layer {qname} model of the same dims (conv {t_conv:.2f}s, 2 enc layers "
+              f"{t_enc2 - t_conv:.2f}s, cross K/V {t_cross2:.2f}s, decode step {t_step2 * 1e3:.1f}ms), "
+              f"extrapolated linearly to {L_e}+{L_d} layers and {n_tokens} tokens; the reference CPU "
+              f"algorithm restated in C++ (oracle/)")
+    return {"audio_s_per_s": CLIP_SECONDS / t_clip, "tok_s": n_tokens / (t_cross + n_tokens * t_step),
+            "sample": sample}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    from vokra_b200 import synth
+    arch = synth.WHISPER_LARGE_V3
+    threads = os.cpu_count() or 1
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_sample(arch, synth.Q4_0, "q4_0", args.tokens, threads)
+        if i >= args.warmup:
+            vals.append(r)
+    v = float(np.median([r["audio_s_per_s"] for r in vals]))
+    tok = float(np.median([r["tok_s"] for r in vals]))
+    line = {
+        "metric": METRIC, "impl": "reference", "value": v, "unit": "audio-s/s", "decode_tok_s": tok,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * CLIP_SECONDS / v, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "configs[3]: whisper-large-v3 q4_0, encoder + 4-token prefix + 128 teacher-forced "
+                               "tokens; one utterance sampled per step on the host cores"},
+        "cpu_baseline": {"value": v, "unit": "audio-s/s", "cores": threads, "kind": "port",
+                         "sample": vals[-1]["sample"]},
+        "e2e": {"value": v, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="vkb", choices=["vkb", "reference"])
+    ap.add_argument("--clips", type=int, default=64)
+    ap.add_argument("--tokens", type=int, default=128)
+    ap.add_argument("--precision", default="split", choices=["split", "f16"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    from vokra_b200 import _lib, ops, synth, whisper
+    arch = synth.WHISPER_LARGE_V3
+    path = model_path("large_v3_q4_0")
+    if rank == 0:
+        ensure_model(path, arch, synth.Q4_0)
+    barrier()
+
+    ctx = ops.Context(local_rank)
+    if args.precision == "f16":
+        _lib.check(_lib.load().vkb_context_set_precision(ctx.h, _lib.PREC_F16))
+    model = whisper.WhisperModel(ctx, path)
+    B, NT = args.clips, args.tokens
+    sess = whisper.Session(model, max_streams=B, max_step_tokens=B * PREFIX, max_clips=B, cross_kv_q8=True)
+    dev = f"cuda:{local_rank}"
+    logmel_host = torch.from_numpy(synthetic_logmels(B, arch.n_mels, 2 * arch.n_audio_ctx, 1000 + rank)).pin_memory()
+    logmel_dev = logmel_host.to(dev)
+    rng = np.random.default_rng(2 + rank)
+    toks = rng.integers(0, arch.n_vocab, (NT, B)).astype(np.int32)
+    streams = np.arange(B, dtype=np.int32)
+    pre_streams = np.repeat(streams, PREFIX)
+    pre_pos = np.tile(np.arange(PREFIX, dtype=np.int32), B)
+    pre_tok = np.tile(np.array(arch.start_ids[:PREFIX], np.int32), B)
+    positions = [np.full(B, PREFIX + t, np.int32) for t in range(NT)]
+    ids_dev = torch.zeros((NT, B), dtype=torch.int32, device=dev)
+    ids_host = torch.zeros((NT, B), dtype=torch.int32).pin_memory()
+    stream = torch.cuda.current_stream()
+
+    def one_step(e2e: bool):
+        if e2e:
+            logmel_dev.copy_(logmel_host, non_blocking=True)
+        sess.encode(logmel_dev, streams)
+        sess.step(pre_streams, pre_pos, pre_tok)
+        for t in range(NT):
+            sess.step(streams, positions[t], toks[t], ids_dev=ids_dev[t])
+        if e2e:
+            ids_host.copy_(ids_dev, non_blocking=True)
+        for s in range(B):
+            sess.release(s)
+
+    for _ in range(args.warmup):
+        one_step(False)
+    torch.cuda.synchronize()
+
+    def timed(e2e: bool):
+        barrier()
+        torch.cuda.synchronize()
+        l0 = ctx.launch_count
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            one_step(e2e)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms = ev0.elapsed_time(ev1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms, ctx.launch_count - l0
+
+    phys = local_rank
+    cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if cvd:
+        try:
+            phys = int(cvd.split(",")[local_rank])
+        except Exception:
+            pass
+    with ClockSampler(phys) as clk:
+        ms, launches = timed(False)
+    ms_e2e, _ = timed(True)
+
+    audio = world * B * CLIP_SECONDS * args.steps
+    value = audio / (ms / 1e3)
+    tok_s = world * B * NT * args.steps / (ms / 1e3)
+    e2e_value = audio / (ms_e2e / 1e3)
+
+    # Dominant kernel: the encoder MLP fc1 GEMM (Q4_0, M = 64 x 1500 tokens, N = 5120, K = 1280,
+    # f16 hi+lo activations in the default precision), timed alone with CUDA events.
+    hbm, bf16, bf16_sus, peak_kind = _peaks()
+    M, N, K = B * arch.n_audio_ctx, arch.ffn_dim, arch.d_model
+    wq = synth.quantize(synth.Q4_0, np.random.default_rng(7).standard_normal(N * K).astype(np.float32) * 0.02)
+    w = ops.Weight(ctx, synth.Q4_0, N, K, wq)
+    planes = 2 if args.precision == "split" else 1
+    a = (torch.randn((planes * M, K), device=dev) * 0.5).half()
+    out = torch.empty((M, N), device=dev, dtype=torch.float16)
+    a_dt = _lib.DT_F16X2 if planes == 2 else _lib.DT_F16
+    L = _lib.load()
+    import ctypes as C
+
+    def fc1():
+        _lib.check(L.vkb_linear(ctx.h, w.h, M, C.c_void_p(a.data_ptr()), a_dt, None, C.c_void_p(out.data_ptr()),
+                                _lib.DT_F16, _lib.EPI_NONE, None, C.c_float(1.0)))
+    for _ in range(3):
+        fc1()
+    reps = 10
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        fc1()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    k_ms = e0.elapsed_time(e1) / reps
+    mma_factor = 3 if planes == 2 else 1
+    tflops = 2.0 * M * N * K / (k_ms / 1e3) / 1e12
+    roofline = {"bound": "tensor", "achieved": round(tflops, 1), "peak": bf16, "unit": "TFLOP/s",
+                "frac": round(tflops / bf16, 4), "traffic": None,
+                "kernel": f"tc_gemm_kernel Q4_0 encoder fc1 M={M} N={N} K={K}, "
+                          f"{'split f16 (3 MMAs per step)' if planes == 2 else 'f16'}",
+                "algorithmic_flops": 2 * M * N * K, "mma_flops_issued": 2 * M * N * K * mma_factor,
+                "ms_per_launch": round(k_ms, 4), "peak_kind": f"{peak_kind} bf16 dense burst"}
+    prof = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(prof):
+        try:
+            roofline["traffic"] = json.load(open(prof)).get("tc_gemm_fc1_bytes_per_launch")
+        except Exception:
+            pass
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            r = cpu_sample(arch, synth.Q4_0, "q4_0", NT, os.cpu_count() or 1)
+            cpu = {"value": r["audio_s_per_s"], "unit": "audio-s/s", "cores": os.cpu_count() or 1, "kind": "port",
+                   "sample": r["sample"], "decode_tok_s": r["tok_s"]}
+        except Exception as e:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "audio-s/s", "cores": os.cpu_count() or 1, "kind": "port",
+                   "sample": f"failed: {e}"}
+
+    if rank == 0:
+        h2d = int(logmel_host.numel() * 4 + (PREFIX * B * 3 + NT * B * 3) * 4)
+        d2h = int(ids_host.numel() * 4)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "audio-s/s", "decode_tok_s": round(tok_s, 1),
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16 hi+lo tensor-core operands, fp32 accumulate (Q4_0 weights, Q8_0 KV)"
+            if planes == 2 else "f16 (Q4_0 weights, Q8_0 KV)",
+            "data": "synthetic",
+            "config": {"workload": "configs[3]: whisper-large-v3 q4_0, 64 clips x 30 s per GPU, encoder + 4-token "
+                                   "prefix + 128 teacher-forced tokens through the paged Q8_0 KV",
+                       "global_batch": world * B, "seq_len": arch.n_audio_ctx, "decode_tokens": NT,
+                       "parallelism": f"dp{world} (utterances sharded by request)",
+                       "l2": "inputs larger than L2 (96000x1280 activations per layer)",
+                       "inputs": "seeded synthetic log-mels (the frontend is outside the timed path)"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "audio-s/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches),
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
