@@ -108,7 +108,8 @@ VKB_API int vkb_abi_version(void);
 VKB_API vkb_status vkb_context_create(int device, vkb_context** out);
 VKB_API vkb_status vkb_context_destroy(vkb_context* ctx);
 /* Launch subsequent device-pointer work on `stream` (a cudaStream_t of the
- * same device; NULL = the context's own stream). */
+ * same device, or cudaStreamLegacy = (void*)0x1 for the legacy default stream;
+ * NULL = the context's own stream). */
 VKB_API vkb_status vkb_context_set_stream(vkb_context* ctx, void* stream);
 VKB_API vkb_status vkb_context_synchronize(vkb_context* ctx);
 /* Selects the tensor-core operand precision (vkb_precision). */

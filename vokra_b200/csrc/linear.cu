@@ -268,8 +268,11 @@ void run_split_f16(vkb_context* ctx, const float* x, int64_t n, __half* y, bool 
 // ---------------------------------------------------------------------------
 // tcgen05 GEMM: D[n][m] = W[n][:] . X[m][:] with W dequantized into shared
 // memory (128 rows x 64 K per stage, f16, 128-byte swizzle) and X staged by
-// TMA (BN tokens x 64 K, f16, 128-byte swizzle). Accumulator in TMEM
-// (128 lanes x BN fp32 columns).
+// TMA (BN tokens x 64 K, f16, 128-byte swizzle). The dequantized weight tile
+// (the MMA's A operand, 128 rows x 64 K f16) is written straight into tensor
+// memory by the dequant warps (tcgen05.st, thread = row = TMEM lane), so the
+// MMAs read only B from shared memory. Accumulator in TMEM (128 lanes x BN
+// fp32 columns); A tiles in TMEM columns after it (2 stages x planes x 32).
 //
 // SPLIT = true is the high-precision mode: the weight is dequantized to
 // W_hi = f16(w) and W_lo = f16(w - W_hi) and the activation arrives as two f16
@@ -282,25 +285,29 @@ void run_split_f16(vkb_context* ctx, const float* x, int64_t n, __half* y, bool 
 //   warp 1      : TMEM allocator; lane 0 issues tcgen05.mma and commits
 //   warps 2..5  : dequantize raw stage -> A tile(s); then the epilogue
 //                 (thread = one weight row = one TMEM lane)
-// Rings: S stages of (X tile(s) + raw weights), 2 stages of A tiles.
+// Rings: S stages of (X tile(s) + raw weights) in shared memory, 2 stages of
+// A tiles in tensor memory.
 // Every mbarrier wait is bounded; on timeout the kernel records an error flag
 // and returns without hanging.
 // ---------------------------------------------------------------------------
 template <int FMT, int BN, bool SPLIT>
 struct TcCfg {
     static constexpr int NP = SPLIT ? 2 : 1;                   // operand planes
-    static constexpr int A_BYTES = TILE_N * 128;               // 16 KB per plane
-    static constexpr int A_STAGE = NP * A_BYTES;
     static constexpr int B_BYTES = BN * 128;                   // BN rows x 128 B per plane
     static constexpr int RAW_Q = stage_qs_bytes(FMT);
     static constexpr int RAW_S = stage_sc_bytes(FMT);
     static constexpr int RAW_BYTES = ((RAW_Q + RAW_S) + 1023) / 1024 * 1024;
     static constexpr int STAGE_BYTES = NP * B_BYTES + RAW_BYTES;
-    static constexpr int BUDGET = 225 * 1024 - 2 * A_STAGE - 2048;
+    static constexpr int BUDGET = 225 * 1024 - 2048;
     static constexpr int S0 = BUDGET / STAGE_BYTES;
     static constexpr int S = S0 > 6 ? 6 : S0;
-    static constexpr int SMEM = 1024 /*align slack*/ + 2 * A_STAGE + S * STAGE_BYTES + 1024 /*barriers*/;
-    static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+    static constexpr int SMEM = 1024 /*align slack*/ + S * STAGE_BYTES + 1024 /*barriers*/;
+    static constexpr int ACC_COLS = BN < 32 ? 32 : BN;
+    static constexpr int A_COL0 = ACC_COLS;                     // first A column
+    static constexpr int NEED_COLS = ACC_COLS + 2 * NP * 32;
+    static constexpr uint32_t TMEM_COLS = NEED_COLS <= 32 ? 32 : NEED_COLS <= 64 ? 64 : NEED_COLS <= 128 ? 128
+                                          : NEED_COLS <= 256 ? 256 : 512;
+    static_assert(NEED_COLS <= 512, "tensor memory budget");
     static_assert(S >= 2, "pipeline needs at least two stages");
 };
 
@@ -314,8 +321,7 @@ __global__ void __launch_bounds__(192, 1)
     using C = TcCfg<FMT, BN, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* a_ring = smem;
-    uint8_t* st_ring = smem + 2 * C::A_STAGE;
+    uint8_t* st_ring = smem;
     uint64_t* bars = reinterpret_cast<uint64_t*>(st_ring + C::S * C::STAGE_BYTES);
     uint64_t* full = bars;
     uint64_t* empty = bars + C::S;
@@ -382,18 +388,16 @@ __global__ void __launch_bounds__(192, 1)
                 if (!ptx::mbar_wait(&full[s], (i / C::S) & 1)) { ok = false; break; }
                 if (!ptx::mbar_wait(&a_full[a], (i >> 1) & 1)) { ok = false; break; }
                 ptx::tc_fence_after();
-                uint32_t a_addr = ptx::smem_u32(a_ring + a * C::A_STAGE);
+                const uint32_t a_t = tmem + C::A_COL0 + a * C::NP * 32;
                 uint32_t b_addr = ptx::smem_u32(st_ring + s * C::STAGE_BYTES);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    uint64_t ad = ptx::sdesc_sw128(a_addr + kk * 32);
                     uint64_t bd = ptx::sdesc_sw128(b_addr + kk * 32);
-                    ptx::mma_f16_ss(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    ptx::mma_f16_ts(tmem, a_t + kk * 8, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
                     if (SPLIT) {
                         uint64_t bd_lo = ptx::sdesc_sw128(b_addr + C::B_BYTES + kk * 32);
-                        uint64_t ad_lo = ptx::sdesc_sw128(a_addr + C::A_BYTES + kk * 32);
-                        ptx::mma_f16_ss(tmem, ad, bd_lo, idesc, 1u);
-                        ptx::mma_f16_ss(tmem, ad_lo, bd, idesc, 1u);
+                        ptx::mma_f16_ts(tmem, a_t + kk * 8, bd_lo, idesc, 1u);
+                        ptx::mma_f16_ts(tmem, a_t + 32 + kk * 8, bd, idesc, 1u);
                     }
                 }
                 ptx::mma_commit(&empty[s]);
@@ -412,28 +416,22 @@ __global__ void __launch_bounds__(192, 1)
             const uint8_t* raw = st_ring + s * C::STAGE_BYTES + C::NP * C::B_BYTES;
             float w[64];
             dequant_row_stage<FMT>(raw, raw + C::RAW_Q, r, (int)(s0 + i), w);
-            uint8_t* arow = a_ring + a * C::A_STAGE + r * 128;
+            ptx::tc_fence_after();
+            uint32_t hi[32], lo[32];
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                uint4 v;
-                __half2 h[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) h[q] = __floats2half2_rn(w[8 * c + 2 * q], w[8 * c + 2 * q + 1]);
-                v.x = h2_bits(h[0]); v.y = h2_bits(h[1]); v.z = h2_bits(h[2]); v.w = h2_bits(h[3]);
-                *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = v;
+            for (int q = 0; q < 32; ++q) {
+                __half2 h = __floats2half2_rn(w[2 * q], w[2 * q + 1]);
+                hi[q] = h2_bits(h);
                 if (SPLIT) {
-                    __half2 l[4];
-                    uint4 vl;
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        float2 hf = __half22float2(h[q]);
-                        l[q] = __floats2half2_rn(w[8 * c + 2 * q] - hf.x, w[8 * c + 2 * q + 1] - hf.y);
-                    }
-                    vl.x = h2_bits(l[0]); vl.y = h2_bits(l[1]); vl.z = h2_bits(l[2]); vl.w = h2_bits(l[3]);
-                    *reinterpret_cast<uint4*>(arow + C::A_BYTES + ((c ^ (r & 7)) << 4)) = vl;
+                    float2 hf = __half22float2(h);
+                    lo[q] = h2_bits(__floats2half2_rn(w[2 * q] - hf.x, w[2 * q + 1] - hf.y));
                 }
             }
-            ptx::fence_proxy_async_smem();
+            const uint32_t a_t = tmem + ((uint32_t)(quarter * 32) << 16) + C::A_COL0 + a * C::NP * 32;
+            ptx::tmem_st32(a_t, hi);
+            if (SPLIT) ptx::tmem_st32(a_t + 32, lo);
+            ptx::tmem_st_wait();
+            ptx::tc_fence_before();
             ptx::mbar_arrive(&a_full[a]);
         }
         // Epilogue.
@@ -561,10 +559,7 @@ static void dispatch_tc(vkb_context* ctx, const vkb_weight* w, int64_t m, const 
         case 32: launch_tc<FMT, 32, SPLIT>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
         case 64: launch_tc<FMT, 64, SPLIT>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
         case 128: launch_tc<FMT, 128, SPLIT>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
-        default:
-            if constexpr (!SPLIT) launch_tc<FMT, 256, false>(ctx, w, m, a16, e, ws, sps, splits, m_tiles);
-            else fail(VKB_ERROR_OTHER, "linear: split precision uses token tiles up to 128");
-            break;
+        default: launch_tc<FMT, 256, SPLIT>(ctx, w, m, a16, e, ws, sps, splits, m_tiles); break;
     }
 }
 
@@ -596,8 +591,7 @@ LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m, b
     } else {
         p.tc = true;
         p.split = split;
-        const int bn_max = split ? 128 : 256;
-        int bn = m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : bn_max;
+        int bn = m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256;
         int m_tiles = (int)((m + bn - 1) / bn);
         if (bn == 256 && (int64_t)n_tiles * m_tiles < sms) {
             bn = 128;

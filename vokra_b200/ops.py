@@ -42,7 +42,9 @@ class Context:
         if use_torch_stream:
             import torch
             s = torch.cuda.current_stream(device)
-            check(_L.vkb_context_set_stream(self.h, C.c_void_p(s.cuda_stream)))
+            # torch's default stream has handle 0, the legacy default stream; pass it
+            # as cudaStreamLegacy (0x1) because NULL selects the context's own stream.
+            check(_L.vkb_context_set_stream(self.h, C.c_void_p(s.cuda_stream or 1)))
 
     def set_stream(self, stream_handle: int | None):
         check(_L.vkb_context_set_stream(self.h, C.c_void_p(stream_handle) if stream_handle else None))
