@@ -414,19 +414,9 @@ __global__ void __launch_bounds__(192, 1)
             if (!ptx::mbar_wait(&full[s], (i / C::S) & 1)) { ok = false; break; }
             if (!ptx::mbar_wait(&a_empty[a], ((i >> 1) & 1) ^ 1)) { ok = false; break; }
             const uint8_t* raw = st_ring + s * C::STAGE_BYTES + C::NP * C::B_BYTES;
-            float w[64];
-            dequant_row_stage<FMT>(raw, raw + C::RAW_Q, r, (int)(s0 + i), w);
-            ptx::tc_fence_after();
             uint32_t hi[32], lo[32];
-#pragma unroll
-            for (int q = 0; q < 32; ++q) {
-                __half2 h = __floats2half2_rn(w[2 * q], w[2 * q + 1]);
-                hi[q] = h2_bits(h);
-                if (SPLIT) {
-                    float2 hf = __half22float2(h);
-                    lo[q] = h2_bits(__floats2half2_rn(w[2 * q] - hf.x, w[2 * q + 1] - hf.y));
-                }
-            }
+            dequant_row_stage_h<FMT, SPLIT>(raw, raw + C::RAW_Q, r, (int)(s0 + i), hi, lo);
+            ptx::tc_fence_after();
             const uint32_t a_t = tmem + ((uint32_t)(quarter * 32) << 16) + C::A_COL0 + a * C::NP * 32;
             ptx::tmem_st32(a_t, hi);
             if (SPLIT) ptx::tmem_st32(a_t + 32, lo);

@@ -26,6 +26,7 @@ __host__ __device__ constexpr int qs_bytes_per_row_stage(int fmt) {
     return fmt == W_Q4_0 ? 32 : fmt == W_Q8_0 ? 64 : fmt == W_Q4_K ? 32 : 128;
 }
 
+
 }  // namespace vkb
 
 struct vkb_weight {
@@ -142,6 +143,91 @@ __device__ __forceinline__ void dequant_row_stage(const uint8_t* qs, const uint8
                 float2 f = __half22float2(h2);
                 w[8 * i + 2 * e] = f.x;
                 w[8 * i + 2 * e + 1] = f.y;
+            }
+        }
+    }
+}
+
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// hi = f16(q*d) and lo = f16(q*d - hi) for a pair of small integers given as
+// the f16 bit patterns 0x6400|byte (= 1024 + byte, exact) minus `bias`. Both
+// are exact roundings: q*d has at most 19 significant bits (|q| <= 255, d f16),
+// so the residual q*d - hi fits an f16 and the fused multiply-add returns it.
+template <bool SPLIT>
+__device__ __forceinline__ void q_pair_to_f16(uint32_t biased_bits, __half2 bias, __half2 d2, uint32_t& hi,
+                                              uint32_t& lo) {
+    __half2 q = __hsub2(u2h(biased_bits), bias);
+    __half2 h = __hmul2(q, d2);
+    hi = h2u(h);
+    if (SPLIT) lo = h2u(__hfma2(q, d2, __hneg2(h)));
+}
+
+// Dequantizes the 64 weights of row r of one stage straight to f16 pairs
+// (hi[j] holds elements 2j, 2j+1; lo the residuals when SPLIT) without any
+// int/float conversion instruction. Values equal f16-rounding of the exact
+// reference dequantization (q-8)*d, q*d and d*sc*q - dmin*m.
+template <int FMT, bool SPLIT>
+__device__ __forceinline__ void dequant_row_stage_h(const uint8_t* qs, const uint8_t* sc, int r, int stage,
+                                                    uint32_t (&hi)[32], uint32_t (&lo)[32]) {
+    if constexpr (FMT == W_Q4_0) {
+        const __half2 bias = __float2half2_rn(1032.0f);  // 1024 + 8
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            uint4 q = *reinterpret_cast<const uint4*>(qs + j * (16 * TILE_N) + r * 16);
+            __half d = __ushort_as_half(*reinterpret_cast<const uint16_t*>(sc + j * (2 * TILE_N) + r * 2));
+            __half2 d2 = __half2half2(d);
+            uint32_t wds[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+                uint32_t lo4 = wds[wi] & 0x0F0F0F0Fu, hi4 = (wds[wi] >> 4) & 0x0F0F0F0Fu;
+                // low nibbles: elements 4wi..4wi+3 ; high nibbles: 16 + 4wi ..
+                q_pair_to_f16<SPLIT>(__byte_perm(lo4, 0x64u, 0x4140), bias, d2, hi[16 * j + 2 * wi], lo[16 * j + 2 * wi]);
+                q_pair_to_f16<SPLIT>(__byte_perm(lo4, 0x64u, 0x4342), bias, d2, hi[16 * j + 2 * wi + 1],
+                                     lo[16 * j + 2 * wi + 1]);
+                q_pair_to_f16<SPLIT>(__byte_perm(hi4, 0x64u, 0x4140), bias, d2, hi[16 * j + 8 + 2 * wi],
+                                     lo[16 * j + 8 + 2 * wi]);
+                q_pair_to_f16<SPLIT>(__byte_perm(hi4, 0x64u, 0x4342), bias, d2, hi[16 * j + 8 + 2 * wi + 1],
+                                     lo[16 * j + 8 + 2 * wi + 1]);
+            }
+        }
+    } else if constexpr (FMT == W_Q8_0) {
+        const __half2 bias = __float2half2_rn(1152.0f);  // 1024 + 128
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const uint4* p = reinterpret_cast<const uint4*>(qs + j * (32 * TILE_N) + r * 32);
+            uint4 q0 = p[0], q1 = p[1];
+            __half d = __ushort_as_half(*reinterpret_cast<const uint16_t*>(sc + j * (2 * TILE_N) + r * 2));
+            __half2 d2 = __half2half2(d);
+            uint32_t wds[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+            for (int wi = 0; wi < 8; ++wi) {
+                uint32_t u = wds[wi] ^ 0x80808080u;  // int8 -> byte + 128
+                q_pair_to_f16<SPLIT>(__byte_perm(u, 0x64u, 0x4140), bias, d2, hi[16 * j + 2 * wi], lo[16 * j + 2 * wi]);
+                q_pair_to_f16<SPLIT>(__byte_perm(u, 0x64u, 0x4342), bias, d2, hi[16 * j + 2 * wi + 1],
+                                     lo[16 * j + 2 * wi + 1]);
+            }
+        }
+    } else if constexpr (FMT == W_F16) {
+        const uint4* p = reinterpret_cast<const uint4*>(qs + r * 128);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            uint4 v = p[i];
+            hi[4 * i] = v.x; hi[4 * i + 1] = v.y; hi[4 * i + 2] = v.z; hi[4 * i + 3] = v.w;
+            if (SPLIT) { lo[4 * i] = 0; lo[4 * i + 1] = 0; lo[4 * i + 2] = 0; lo[4 * i + 3] = 0; }
+        }
+    } else {
+        float w[64];
+        dequant_row_stage<FMT>(qs, sc, r, stage, w);
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+            __half2 h = __floats2half2_rn(w[2 * q], w[2 * q + 1]);
+            hi[q] = h2u(h);
+            if (SPLIT) {
+                float2 hf = __half22float2(h);
+                lo[q] = h2u(__floats2half2_rn(w[2 * q] - hf.x, w[2 * q + 1] - hf.y));
             }
         }
     }
