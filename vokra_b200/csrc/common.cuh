@@ -86,7 +86,9 @@ struct vkb_context {
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
     uint64_t launches = 0;
-    int precision = VKB_PREC_SPLIT;  // tensor-core operand precision (vkb_context_set_precision)
+    int precision = VKB_PREC_SPLIT;
+    unsigned long long* trace = nullptr;
+    int debug = 0;  // debugging aid (VKB_DEBUG)  // debugging aid: GEMM block-0 timeline (VKB_TRACE)  // tensor-core operand precision (vkb_context_set_precision)
     vkb::DevBuf workspace;
     vkb::DevBuf err_flag;  // int set by a kernel whose bounded wait gave up
     void ensure_workspace(size_t bytes) {

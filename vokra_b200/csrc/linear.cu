@@ -317,8 +317,19 @@ template <int FMT, int BN, bool SPLIT>
 __global__ void __launch_bounds__(192, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_lo,
                    const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc, int64_t K, int64_t N, int64_t M,
-                   int n_tiles, int m_tiles, int stages_per_split, int n_splits, float* ws, Epi e, int* err) {
+                   int n_tiles, int m_tiles, int stages_per_split, int n_splits, float* ws, Epi e, int* err,
+                   unsigned long long* trace, const __grid_constant__ CUtensorMap omap,
+                   const __grid_constant__ CUtensorMap omap_lo, const __grid_constant__ CUtensorMap rmap,
+                   int tma_epi) {
     using C = TcCfg<FMT, BN, SPLIT>;
+    // Optional timeline of block 0 (debugging aid): [role][stage] globaltimer stamps.
+    auto stamp = [&](int role, int i) {
+        if (trace && blockIdx.x == 0 && i < 64) {
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            trace[role * 64 + i] = t;
+        }
+    };
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* st_ring = smem;
@@ -328,7 +339,8 @@ __global__ void __launch_bounds__(192, 1)
     uint64_t* a_full = bars + 2 * C::S;
     uint64_t* a_empty = a_full + 2;
     uint64_t* acc_full = a_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    uint64_t* res_full = acc_full + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int bid = blockIdx.x;
@@ -351,6 +363,7 @@ __global__ void __launch_bounds__(192, 1)
             ptx::mbar_init(&a_empty[i], 1);
         }
         ptx::mbar_init(acc_full, 1);
+        ptx::mbar_init(res_full, 1);
         ptx::fence_mbar_init();
     }
     if (warp == 1) {
@@ -372,6 +385,7 @@ __global__ void __launch_bounds__(192, 1)
                 uint8_t* raw_dst = b_dst + C::NP * C::B_BYTES;
                 int64_t stage = s0 + i;
                 StagePtrs p = stage_ptrs(FMT, qs, sc, K, n_tile, stage);
+                stamp(0, i);
                 ptx::mbar_expect_tx(&full[s], C::NP * C::B_BYTES + C::RAW_Q + C::RAW_S);
                 ptx::tma_load_2d(b_dst, &xmap, &full[s], (int32_t)(stage * STAGE_K), m_tile * BN);
                 if (SPLIT)
@@ -387,6 +401,7 @@ __global__ void __launch_bounds__(192, 1)
                 int s = i % C::S, a = i & 1;
                 if (!ptx::mbar_wait(&full[s], (i / C::S) & 1)) { ok = false; break; }
                 if (!ptx::mbar_wait(&a_full[a], (i >> 1) & 1)) { ok = false; break; }
+                stamp(1, i);
                 ptx::tc_fence_after();
                 const uint32_t a_t = tmem + C::A_COL0 + a * C::NP * 32;
                 uint32_t b_addr = ptx::smem_u32(st_ring + s * C::STAGE_BYTES);
@@ -413,6 +428,7 @@ __global__ void __launch_bounds__(192, 1)
             int s = i % C::S, a = i & 1;
             if (!ptx::mbar_wait(&full[s], (i / C::S) & 1)) { ok = false; break; }
             if (!ptx::mbar_wait(&a_empty[a], ((i >> 1) & 1) ^ 1)) { ok = false; break; }
+            if (threadIdx.x == 64) stamp(2, i);
             const uint8_t* raw = st_ring + s * C::STAGE_BYTES + C::NP * C::B_BYTES;
             uint32_t hi[32], lo[32];
             dequant_row_stage_h<FMT, SPLIT>(raw, raw + C::RAW_Q, r, (int)(s0 + i), hi, lo);
@@ -422,27 +438,72 @@ __global__ void __launch_bounds__(192, 1)
             if (SPLIT) ptx::tmem_st32(a_t + 32, lo);
             ptx::tmem_st_wait();
             ptx::tc_fence_before();
+            if (threadIdx.x == 64) stamp(3, i);
             ptx::mbar_arrive(&a_full[a]);
         }
         // Epilogue.
         if (ok && ptx::mbar_wait(acc_full, 0)) {
+            if (threadIdx.x == 64) stamp(4, 0);
             ptx::tc_fence_after();
             const int64_t n = (int64_t)n_tile * TILE_N + r;
             const float bias_n = (e.bias && n < N) ? e.bias[n] : 0.0f;
             const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+            if (tma_epi) {
+                // Stage the [BN tokens][128 features] tile in the idle ring, then one
+                // TMA tensor store per plane writes whole row segments.
+                float* sf = reinterpret_cast<float*>(st_ring);
+                __half* sh = reinterpret_cast<__half*>(st_ring);
+                if (e.kind == VKB_EPI_RESIDUAL) {
+                    if (threadIdx.x == 64) {
+                        ptx::mbar_expect_tx(res_full, BN * TILE_N * 4);
+                        ptx::tma_load_2d(st_ring, &rmap, res_full, n_tile * TILE_N, m_tile * BN);
+                    }
+                    if (!ptx::mbar_wait(res_full, 0)) ok = false;
+                }
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                uint32_t v[16];
-                ptx::tmem_ld16(lane_addr + c0, v);
-                ptx::tmem_ld_wait();
-                if (n < N) {
+                for (int c0 = 0; c0 < BN && ok; c0 += 16) {
+                    uint32_t v[16];
+                    ptx::tmem_ld16(lane_addr + c0, v);
+                    ptx::tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        int64_t m = (int64_t)m_tile * BN + c0 + j;
-                        if (m < M) {
-                            float acc = __uint_as_float(v[j]);
-                            if (n_splits == 1) epi_store(e, m, n, acc, bias_n);
-                            else ws[((int64_t)split * M + m) * N + n] = acc;
+                        const int row = c0 + j;
+                        float x = __uint_as_float(v[j]) + bias_n;
+                        if (e.kind == VKB_EPI_GELU) x = gelu_as(x);
+                        else if (e.kind == VKB_EPI_SCALE) x = n < e.n_scaled ? x * e.scale : x;
+                        else if (e.kind == VKB_EPI_RESIDUAL) x += sf[row * TILE_N + r];
+                        if (e.out_fmt == VKB_DT_F32) {
+                            sf[row * TILE_N + r] = x;
+                        } else {
+                            __half h = __float2half_rn(x);
+                            sh[row * TILE_N + r] = h;
+                            if (e.out_fmt == VKB_DT_F16X2) sh[BN * TILE_N + row * TILE_N + r] = __float2half_rn(x - __half2float(h));
+                        }
+                    }
+                }
+                ptx::fence_proxy_async_smem();
+                ptx::named_bar(1, 128);
+                if (threadIdx.x == 64 && ok) {
+                    ptx::tma_store_2d(&omap, st_ring, n_tile * TILE_N, m_tile * BN);
+                    if (e.out_fmt == VKB_DT_F16X2) ptx::tma_store_2d(&omap_lo, sh + BN * TILE_N, n_tile * TILE_N, m_tile * BN);
+                    ptx::bulk_commit();
+                    ptx::bulk_wait0();
+                }
+            } else {
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    uint32_t v[16];
+                    ptx::tmem_ld16(lane_addr + c0, v);
+                    ptx::tmem_ld_wait();
+                    if (n < N) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            int64_t m = (int64_t)m_tile * BN + c0 + j;
+                            if (m < M) {
+                                float acc = __uint_as_float(v[j]);
+                                if (n_splits == 1) epi_store(e, m, n, acc, bias_n);
+                                else ws[((int64_t)split * M + m) * N + n] = acc;
+                            }
                         }
                     }
                 }
@@ -451,6 +512,7 @@ __global__ void __launch_bounds__(192, 1)
             ok = false;
         }
     }
+    if (threadIdx.x == 64) stamp(4, 1);
     if (!ok && err) atomicExch(err, 1);
     ptx::tc_fence_before();
     __syncthreads();
@@ -491,6 +553,20 @@ void make_tmap_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t col
     if (r != CUDA_SUCCESS) fail(VKB_ERROR_BACKEND_UNAVAILABLE, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
 }
 
+// 2-D tensor map over a row-major matrix [rows][cols] of 2- or 4-byte elements,
+// box [box_rows][box_cols], no swizzle (the epilogue's staging layout).
+void make_tmap_2d(CUtensorMap* map, const void* base, int esz, int64_t rows, int64_t cols, int box_cols, int box_rows) {
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * esz)};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = get_encode_fn()(map, esz == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                                 const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(VKB_ERROR_BACKEND_UNAVAILABLE, "cuTensorMapEncodeTiled (epilogue) failed: " + std::to_string(r));
+}
+
 static int* device_err_flag(vkb_context* ctx) { return ctx->err_flag.as<int>(); }
 
 int gemv_max_m() { return 4; }
@@ -529,15 +605,29 @@ static void launch_tc(vkb_context* ctx, const vkb_weight* w, int64_t m, const __
                                       C::SMEM));
         attr = true;
     }
-    CUtensorMap map, map_lo;
+    CUtensorMap map, map_lo, omap, omap_lo, rmap;
     make_tmap_f16(&map, a16, m, w->k, BN);
     if (SPLIT) make_tmap_f16(&map_lo, a16 + m * w->k, m, w->k, BN);
     else map_lo = map;
+    // TMA epilogue: plain row-major output whose rows are 16-byte aligned.
+    const int esz = e.out_fmt == VKB_DT_F32 ? 4 : 2;
+    int tma_epi = splits == 1 && e.col_block == 0 && e.row_map == nullptr && ((uintptr_t)e.out % 16) == 0 &&
+                  (w->n * esz) % 16 == 0 && (e.kind != VKB_EPI_RESIDUAL || ((uintptr_t)e.residual % 16) == 0) &&
+                  (int64_t)BN * TILE_N * 4 * (e.out_fmt == VKB_DT_F16X2 ? 1 : 1) <= (int64_t)C::S * C::STAGE_BYTES;
+    if (tma_epi) {
+        make_tmap_2d(&omap, e.out, esz, m, w->n, TILE_N, BN);
+        if (e.out_fmt == VKB_DT_F16X2) make_tmap_2d(&omap_lo, reinterpret_cast<const __half*>(e.out) + e.plane, 2, m, w->n, TILE_N, BN);
+        else omap_lo = omap;
+        if (e.kind == VKB_EPI_RESIDUAL) make_tmap_2d(&rmap, e.residual, 4, m, w->n, TILE_N, BN);
+        else rmap = omap;
+    } else {
+        omap = omap_lo = rmap = map;
+    }
     int n_tiles = (int)(w->n_pad / TILE_N);
     dim3 grid((unsigned)(n_tiles * m_tiles * splits));
     tc_gemm_kernel<FMT, BN, SPLIT><<<grid, 192, C::SMEM, ctx->stream>>>(
         map, map_lo, w->qs.as<uint8_t>(), w->sc.as<uint8_t>(), w->k, w->n, m, n_tiles, m_tiles, stages_per_split,
-        splits, ws, e, device_err_flag(ctx));
+        splits, ws, e, device_err_flag(ctx), ctx->trace, omap, omap_lo, rmap, tma_epi);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
