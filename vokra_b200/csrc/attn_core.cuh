@@ -15,7 +15,7 @@
 
 namespace vkb {
 
-constexpr int ATTN_MAX_THREADS = 512;
+constexpr int ATTN_MAX_THREADS = 256;
 
 // 16 int8 values of a 32-bit-word quadruple -> floats, exactly, without I2F:
 // the byte is placed in the low mantissa of 2^23 and the bias removed.
@@ -28,6 +28,12 @@ __device__ __forceinline__ void i8x16_to_f32(uint4 q, float (&f)[16]) {
             f[4 * i + b] = __uint_as_float(__byte_perm(w[i], 0x4B000000u, 0x7440u + b)) - 8388736.0f;
     }
 }
+
+// Raw bytes of 16 channels of one K or V row, kept in registers until use.
+struct RawRow {
+    uint4 a, b;   // int8: a only; f16: a then b
+    float s;      // block scale (1 for f16)
+};
 
 // ---- fetch policies: value of 16 channels [c0, c0+16) of key j ------------
 struct FetchPagedQ8 {
@@ -47,13 +53,11 @@ struct FetchPagedQ8 {
         int pid = table[table_base + j / bs];
         return arena_row0 + ((int64_t)pid * bs + (j % bs)) * n_sc + slot;
     }
-    __device__ __forceinline__ void load(int64_t rw, int c0, bool is_v, float (&f)[16], float& scale) const {
-        const int8_t* q = (is_v ? vq : kq) + rw * W + c0;
-        const __half* d = (is_v ? vd : kd) + rw * (W / 32) + c0 / 32;
-        uint4 v = __ldg(reinterpret_cast<const uint4*>(q));
-        scale = __half2float(__ldg(d));
-        i8x16_to_f32(v, f);
+    __device__ __forceinline__ void load_raw(int64_t rw, int c0, bool is_v, RawRow& r) const {
+        r.a = __ldg(reinterpret_cast<const uint4*>((is_v ? vq : kq) + rw * W + c0));
+        r.s = __half2float(__ldg((is_v ? vd : kd) + rw * (W / 32) + c0 / 32));
     }
+    static __device__ __forceinline__ void convert(const RawRow& r, float (&f)[16]) { i8x16_to_f32(r.a, f); }
 };
 
 struct FetchDenseQ8 {
@@ -64,13 +68,11 @@ struct FetchDenseQ8 {
     int W;
     int64_t seq_row0;  // seq * n_ctx
     __device__ __forceinline__ int64_t row(int j) const { return seq_row0 + j; }
-    __device__ __forceinline__ void load(int64_t rw, int c0, bool is_v, float (&f)[16], float& scale) const {
-        const int8_t* q = (is_v ? vq : kq) + rw * W + c0;
-        const __half* d = (is_v ? vd : kd) + rw * (W / 32) + c0 / 32;
-        uint4 v = __ldg(reinterpret_cast<const uint4*>(q));
-        scale = __half2float(__ldg(d));
-        i8x16_to_f32(v, f);
+    __device__ __forceinline__ void load_raw(int64_t rw, int c0, bool is_v, RawRow& r) const {
+        r.a = __ldg(reinterpret_cast<const uint4*>((is_v ? vq : kq) + rw * W + c0));
+        r.s = __half2float(__ldg((is_v ? vd : kd) + rw * (W / 32) + c0 / 32));
     }
+    static __device__ __forceinline__ void convert(const RawRow& r, float (&f)[16]) { i8x16_to_f32(r.a, f); }
 };
 
 struct FetchDenseF16 {
@@ -79,18 +81,20 @@ struct FetchDenseF16 {
     int W;
     int64_t seq_row0;
     __device__ __forceinline__ int64_t row(int j) const { return seq_row0 + j; }
-    __device__ __forceinline__ void load(int64_t rw, int c0, bool is_v, float (&f)[16], float& scale) const {
+    __device__ __forceinline__ void load_raw(int64_t rw, int c0, bool is_v, RawRow& r) const {
         const __half* p = (is_v ? v : k) + rw * W + c0;
-        uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
-        uint4 b = __ldg(reinterpret_cast<const uint4*>(p + 8));
-        uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        r.a = __ldg(reinterpret_cast<const uint4*>(p));
+        r.b = __ldg(reinterpret_cast<const uint4*>(p + 8));
+        r.s = 1.0f;
+    }
+    static __device__ __forceinline__ void convert(const RawRow& r, float (&f)[16]) {
+        uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             float2 t = __half22float2(*reinterpret_cast<__half2*>(&w[i]));
             f[2 * i] = t.x;
             f[2 * i + 1] = t.y;
         }
-        scale = 1.0f;
     }
 };
 
@@ -141,37 +145,67 @@ __device__ __forceinline__ void attn_body(const F& fetch, const float* __restric
 
     // Every row-group runs the same trip count so that the head shuffles
     // always see full warps (a warp can hold threads of two row-groups).
-    const int n_iter = (key_end - key_begin + R - 1) / R;
+    // KU keys per row-group per iteration: their loads are issued together and
+    // the running softmax is rescaled once per iteration.
+    constexpr int KU = 2;
+    const int n_iter = (key_end - key_begin + R * KU - 1) / (R * KU);
     if (active) {
         for (int it = 0; it < n_iter; ++it) {
-            const int j = key_begin + rg + it * R;
-            const bool valid = j < key_end;
-            float kf[16], vf[16], ks = 0.0f, vs = 0.0f;
-            if (valid) {
-                int64_t rw = fetch.row(j);
-                fetch.load(rw, c0, false, kf, ks);
-                fetch.load(rw, c0, true, vf, vs);
-            } else {
+            int jj[KU];
+            bool valid[KU];
+            RawRow kr[KU], vr[KU];
 #pragma unroll
-                for (int c = 0; c < 16; ++c) { kf[c] = 0.0f; vf[c] = 0.0f; }
+            for (int u = 0; u < KU; ++u) {
+                jj[u] = key_begin + rg + (it * KU + u) * R;
+                valid[u] = jj[u] < key_end;
+                if (valid[u]) {
+                    int64_t rw = fetch.row(jj[u]);
+                    fetch.load_raw(rw, c0, false, kr[u]);
+                    fetch.load_raw(rw, c0, true, vr[u]);
+                } else {
+                    kr[u].a = make_uint4(0, 0, 0, 0);
+                    kr[u].b = kr[u].a;
+                    kr[u].s = 0.0f;
+                    vr[u] = kr[u];
+                }
             }
 #pragma unroll
             for (int i = 0; i < MAXQ; ++i) {
                 if (i >= g.n_q) break;
-                float part = 0.0f;
+                float part[KU];
 #pragma unroll
-                for (int c = 0; c < 16; ++c) part = fmaf(qv[i][c], kf[c], part);
-                part *= ks;
-                // sum over the head's threads (consecutive, aligned to tph)
-                for (int o = 1; o < tph; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-                if (!valid || j > g.pos0 + i) continue;  // causal: key after this query
-                float mn = fmaxf(m[i], part);
-                float corr = __expf(m[i] - mn);
-                float p = __expf(part - mn);
-                l[i] = l[i] * corr + p;
-                float pv = p * vs;
+                for (int u = 0; u < KU; ++u) {
+                    float kf[16];
+                    F::convert(kr[u], kf);
+                    float acc_d = 0.0f;
 #pragma unroll
-                for (int c = 0; c < 16; ++c) acc[i][c] = fmaf(pv, vf[c], acc[i][c] * corr);
+                    for (int c = 0; c < 16; ++c) acc_d = fmaf(qv[i][c], kf[c], acc_d);
+                    acc_d *= kr[u].s;
+                    // sum over the head's threads (consecutive, aligned to tph)
+                    for (int o = 1; o < tph; o <<= 1) acc_d += __shfl_xor_sync(0xffffffffu, acc_d, o);
+                    const bool use = valid[u] && jj[u] <= g.pos0 + i;  // causal: keys up to this query
+                    part[u] = use ? acc_d : -INFINITY;
+                }
+                float mx = part[0];
+#pragma unroll
+                for (int u = 1; u < KU; ++u) mx = fmaxf(mx, part[u]);
+                if (mx == -INFINITY) continue;
+                const float mn = fmaxf(m[i], mx);
+                const float corr = __expf(m[i] - mn);
+                float lsum = l[i] * corr;
+#pragma unroll
+                for (int c = 0; c < 16; ++c) acc[i][c] *= corr;
+#pragma unroll
+                for (int u = 0; u < KU; ++u) {
+                    const float p = __expf(part[u] - mn);  // 0 for unused keys
+                    lsum += p;
+                    float vf[16];
+                    F::convert(vr[u], vf);
+                    const float pv = p * vr[u].s;
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) acc[i][c] = fmaf(pv, vf[c], acc[i][c]);
+                }
+                l[i] = lsum;
                 m[i] = mn;
             }
         }

@@ -89,21 +89,50 @@ __global__ void kv_append_kernel(const float* __restrict__ k, const float* __res
 // map[r / group] * group + r % group.
 __global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t ld, int64_t n_rows, int W, int8_t* q,
                                      __half* d, const int32_t* __restrict__ map, int group) {
+    // One thread per 32-element block: 8 float4 loads, then the BlockQ8_0::pack
+    // arithmetic (the same expressions as q8_0_block_warp, sequentially).
     const int nb = W / 32;
-    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (gw >= n_rows * nb) return;
-    const int64_t row = gw / nb;
-    const int b = (int)(gw % nb);
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n_rows * nb) return;
+    const int64_t row = t / nb;
+    const int b = (int)(t % nb);
+    const float4* src = reinterpret_cast<const float4*>(x + row * ld + b * 32);
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float4 f = src[i];
+        v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const float dd = amax == 0.0f ? 0.0f : amax / 127.0f;
+    const float inv = dd == 0.0f ? 0.0f : 1.0f / dd;
+    uint32_t packed[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        uint32_t wv = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            float s = v[4 * i + e] * inv;
+            float c = s < -127.0f ? -127.0f : (s > 127.0f ? 127.0f : s);
+            int qv = isnan(c) ? 0 : (int)roundf(c);
+            wv |= ((uint32_t)(qv & 0xff)) << (8 * e);
+        }
+        packed[i] = wv;
+    }
     const int64_t dst = map ? (int64_t)map[row / group] * group + row % group : row;
-    q8_0_block_warp(x[row * ld + b * 32 + lane], lane, q + dst * W + b * 32, d + dst * nb + b);
+    uint4* qo = reinterpret_cast<uint4*>(q + dst * W + b * 32);
+    qo[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    qo[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+    *reinterpret_cast<uint16_t*>(d + dst * nb + b) = f32_to_f16_bits(dd);
 }
 
 // ---------------------------------------------------------------------------
 // Attention kernels
 // ---------------------------------------------------------------------------
 template <int MAXQ>
-__global__ void __launch_bounds__(MAXQ > 1 ? ATTN_MAX_THREADS / 2 : ATTN_MAX_THREADS) paged_attn_kernel(FetchPagedQ8 f, const float* __restrict__ q, int64_t q_ld, const AttnGroup* __restrict__ groups,
+__global__ void __launch_bounds__(ATTN_MAX_THREADS, MAXQ > 1 ? 1 : 2) paged_attn_kernel(FetchPagedQ8 f, const float* __restrict__ q, int64_t q_ld, const AttnGroup* __restrict__ groups,
                                   int n_head, int d_head, int keys_per_split, int n_splits, void* ctx_out,
                                   int out_fmt, float* ws, int per_seq_base, int ppseq, int64_t out_plane) {
     const AttnGroup g = groups[blockIdx.x];
@@ -119,7 +148,7 @@ __global__ void __launch_bounds__(MAXQ > 1 ? ATTN_MAX_THREADS / 2 : ATTN_MAX_THR
 }
 
 template <class F>
-__global__ void __launch_bounds__(ATTN_MAX_THREADS) dense_attn_kernel(F f, const float* __restrict__ q, const int32_t* __restrict__ seq_of_tok, int n_ctx,
+__global__ void __launch_bounds__(ATTN_MAX_THREADS, 2) dense_attn_kernel(F f, const float* __restrict__ q, const int32_t* __restrict__ seq_of_tok, int n_ctx,
                                   int n_head, int d_head, int keys_per_split, int n_splits, void* ctx_out,
                                   int out_fmt, float* ws, int64_t out_plane) {
     AttnGroup g;
@@ -166,7 +195,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ ws, int n_tok, int
 // Thread shape of the attention CTA: R row-groups of W/16 threads with
 // R*W/16 a multiple of 32 and at most ATTN_MAX_THREADS threads.
 static int attn_rowgroups(int W, int maxq = 1) {
-    const int limit = maxq > 1 ? ATTN_MAX_THREADS / 2 : ATTN_MAX_THREADS;  // MAXQ=4 uses ~2x the registers
+    const int limit = ATTN_MAX_THREADS;
     int tpr = W / 16;
     int best = 0;
     for (int R = 1; R * tpr <= limit; ++R)
@@ -191,7 +220,7 @@ void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, co
     const int W = n_head * d_head;
     const int R = attn_rowgroups(W);
     // Splits: about 4 CTAs per SM overall, at least 2*R keys per split.
-    int splits = std::max(1, std::min((4 * ctx->sm_count + n_tok - 1) / n_tok, n_ctx / (2 * R)));
+    int splits = std::max(1, std::min((8 * ctx->sm_count + n_tok - 1) / n_tok, n_ctx / (4 * R)));
     int kps = (n_ctx + splits - 1) / splits;
     splits = (n_ctx + kps - 1) / kps;
     float* ws = nullptr;
@@ -234,9 +263,9 @@ void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, co
 void run_quantize_rows(vkb_context* ctx, const float* x, int64_t ld, int64_t n_rows, int W, int8_t* q, __half* d,
                        const int32_t* map, int group) {
     if (W % 32) fail(VKB_ERROR_INVALID_ARGUMENT, "quantize_rows: row width must be a multiple of 32");
-    int64_t warps = n_rows * (W / 32);
-    quantize_rows_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, ctx->stream>>>(x, ld, n_rows, W, q, d, map,
-                                                                                        group);
+    if (ld % 4 || ((uintptr_t)x & 15)) fail(VKB_ERROR_INVALID_ARGUMENT, "quantize_rows: rows must be 16-byte aligned");
+    int64_t blocks = n_rows * (W / 32);
+    quantize_rows_kernel<<<(unsigned)((blocks + 255) / 256), 256, 0, ctx->stream>>>(x, ld, n_rows, W, q, d, map, group);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
@@ -415,7 +444,7 @@ void kv_begin_step(vkb_kv_pool* p, int n_tok, const int32_t* seq, const int32_t*
     // Key splits: about 4 CTAs per SM, at least 2*R keys per split, and the
     // partials must fit the pool's buffer.
     const int R = attn_rowgroups(p->W, maxq);
-    int splits = std::max(1, std::min((4 * p->ctx->sm_count + ng - 1) / ng, max_keys / (2 * R)));
+    int splits = std::max(1, std::min((8 * p->ctx->sm_count + ng - 1) / ng, max_keys / (4 * R)));
     while ((int64_t)ng * splits > 4096 && splits > 1) --splits;
     int kps = (max_keys + splits - 1) / splits;
     splits = (max_keys + kps - 1) / kps;
