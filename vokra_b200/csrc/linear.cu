@@ -304,7 +304,8 @@ struct TcCfg {
     static constexpr int SMEM = 1024 /*align slack*/ + S * STAGE_BYTES + 1024 /*barriers*/;
     static constexpr int ACC_COLS = BN < 32 ? 32 : BN;
     static constexpr int A_COL0 = ACC_COLS;                     // first A column
-    static constexpr int NEED_COLS = ACC_COLS + 2 * NP * 32;
+    static constexpr int AS = 4;                                // A stages in tensor memory
+    static constexpr int NEED_COLS = ACC_COLS + AS * NP * 32;
     static constexpr uint32_t TMEM_COLS = NEED_COLS <= 32 ? 32 : NEED_COLS <= 64 ? 64 : NEED_COLS <= 128 ? 128
                                           : NEED_COLS <= 256 ? 256 : 512;
     static_assert(NEED_COLS <= 512, "tensor memory budget");
@@ -337,8 +338,8 @@ __global__ void __launch_bounds__(192, 1)
     uint64_t* full = bars;
     uint64_t* empty = bars + C::S;
     uint64_t* a_full = bars + 2 * C::S;
-    uint64_t* a_empty = a_full + 2;
-    uint64_t* acc_full = a_empty + 2;
+    uint64_t* a_empty = a_full + C::AS;
+    uint64_t* acc_full = a_empty + C::AS;
     uint64_t* res_full = acc_full + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 1);
 
@@ -358,7 +359,7 @@ __global__ void __launch_bounds__(192, 1)
             ptx::mbar_init(&full[i], 1);
             ptx::mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < C::AS; ++i) {
             ptx::mbar_init(&a_full[i], 128);
             ptx::mbar_init(&a_empty[i], 1);
         }
@@ -398,9 +399,9 @@ __global__ void __launch_bounds__(192, 1)
         if (lane == 0) {
             constexpr uint32_t idesc = ptx::idesc_f16_f32(TILE_N, BN);
             for (int i = 0; i < nst && ok; ++i) {
-                int s = i % C::S, a = i & 1;
+                int s = i % C::S, a = i % C::AS;
                 if (!ptx::mbar_wait(&full[s], (i / C::S) & 1)) { ok = false; break; }
-                if (!ptx::mbar_wait(&a_full[a], (i >> 1) & 1)) { ok = false; break; }
+                if (!ptx::mbar_wait(&a_full[a], (i / C::AS) & 1)) { ok = false; break; }
                 stamp(1, i);
                 ptx::tc_fence_after();
                 const uint32_t a_t = tmem + C::A_COL0 + a * C::NP * 32;
@@ -425,9 +426,9 @@ __global__ void __launch_bounds__(192, 1)
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
         for (int i = 0; i < nst && ok; ++i) {
-            int s = i % C::S, a = i & 1;
+            int s = i % C::S, a = i % C::AS;
             if (!ptx::mbar_wait(&full[s], (i / C::S) & 1)) { ok = false; break; }
-            if (!ptx::mbar_wait(&a_empty[a], ((i >> 1) & 1) ^ 1)) { ok = false; break; }
+            if (!ptx::mbar_wait(&a_empty[a], ((i / C::AS) & 1) ^ 1)) { ok = false; break; }
             if (threadIdx.x == 64) stamp(2, i);
             const uint8_t* raw = st_ring + s * C::STAGE_BYTES + C::NP * C::B_BYTES;
             uint32_t hi[32], lo[32];
@@ -453,7 +454,8 @@ __global__ void __launch_bounds__(192, 1)
                 // TMA tensor store per plane writes whole row segments.
                 float* sf = reinterpret_cast<float*>(st_ring);
                 __half* sh = reinterpret_cast<__half*>(st_ring);
-                if (e.kind == VKB_EPI_RESIDUAL) {
+                const bool partial = tma_epi == 2;  // split-K: raw fp32 partial sums, no epilogue op
+                if (!partial && e.kind == VKB_EPI_RESIDUAL) {
                     if (threadIdx.x == 64) {
                         ptx::mbar_expect_tx(res_full, BN * TILE_N * 4);
                         ptx::tma_load_2d(st_ring, &rmap, res_full, n_tile * TILE_N, m_tile * BN);
@@ -468,6 +470,10 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int row = c0 + j;
+                        if (partial) {
+                            sf[row * TILE_N + r] = __uint_as_float(v[j]);
+                            continue;
+                        }
                         float x = __uint_as_float(v[j]) + bias_n;
                         if (e.kind == VKB_EPI_GELU) x = gelu_as(x);
                         else if (e.kind == VKB_EPI_SCALE) x = n < e.n_scaled ? x * e.scale : x;
@@ -483,7 +489,11 @@ __global__ void __launch_bounds__(192, 1)
                 }
                 ptx::fence_proxy_async_smem();
                 ptx::named_bar(1, 128);
-                if (threadIdx.x == 64 && ok) {
+                if (threadIdx.x == 64 && ok && partial) {
+                    ptx::tma_store_3d(&omap, st_ring, n_tile * TILE_N, m_tile * BN, split);
+                    ptx::bulk_commit();
+                    ptx::bulk_wait0();
+                } else if (threadIdx.x == 64 && ok) {
                     ptx::tma_store_2d(&omap, st_ring, n_tile * TILE_N, m_tile * BN);
                     if (e.out_fmt == VKB_DT_F16X2) ptx::tma_store_2d(&omap_lo, sh + BN * TILE_N, n_tile * TILE_N, m_tile * BN);
                     ptx::bulk_commit();
@@ -567,6 +577,19 @@ void make_tmap_2d(CUtensorMap* map, const void* base, int esz, int64_t rows, int
     if (r != CUDA_SUCCESS) fail(VKB_ERROR_BACKEND_UNAVAILABLE, "cuTensorMapEncodeTiled (epilogue) failed: " + std::to_string(r));
 }
 
+// 3-D f32 tensor map over [planes][rows][cols], box [1][box_rows][box_cols] (split-K partials).
+void make_tmap_3d_f32(CUtensorMap* map, const void* base, int64_t planes, int64_t rows, int64_t cols, int box_cols,
+                      int box_rows) {
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)planes};
+    cuuint64_t strides[2] = {(cuuint64_t)(cols * 4), (cuuint64_t)(cols * 4 * rows)};
+    cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = get_encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                 CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(VKB_ERROR_BACKEND_UNAVAILABLE, "cuTensorMapEncodeTiled (partials) failed: " + std::to_string(r));
+}
+
 static int* device_err_flag(vkb_context* ctx) { return ctx->err_flag.as<int>(); }
 
 int gemv_max_m() { return 4; }
@@ -611,10 +634,17 @@ static void launch_tc(vkb_context* ctx, const vkb_weight* w, int64_t m, const __
     else map_lo = map;
     // TMA epilogue: plain row-major output whose rows are 16-byte aligned.
     const int esz = e.out_fmt == VKB_DT_F32 ? 4 : 2;
-    int tma_epi = splits == 1 && e.col_block == 0 && e.row_map == nullptr && ((uintptr_t)e.out % 16) == 0 &&
+    int tma_epi = e.col_block == 0 && e.row_map == nullptr && ((uintptr_t)e.out % 16) == 0 &&
                   (w->n * esz) % 16 == 0 && (e.kind != VKB_EPI_RESIDUAL || ((uintptr_t)e.residual % 16) == 0) &&
                   (int64_t)BN * TILE_N * 4 * (e.out_fmt == VKB_DT_F16X2 ? 1 : 1) <= (int64_t)C::S * C::STAGE_BYTES;
-    if (tma_epi) {
+    const bool partial_ok = (w->n * 4) % 16 == 0 && ((uintptr_t)ws % 16) == 0 &&
+                            (int64_t)BN * TILE_N * 4 <= (int64_t)C::S * C::STAGE_BYTES;
+    if (splits > 1) {
+        tma_epi = partial_ok ? 2 : 0;
+        if (tma_epi) make_tmap_3d_f32(&omap, ws, splits, m, w->n, TILE_N, BN);
+        omap_lo = rmap = map;
+        if (!tma_epi) omap = map;
+    } else if (tma_epi) {
         make_tmap_2d(&omap, e.out, esz, m, w->n, TILE_N, BN);
         if (e.out_fmt == VKB_DT_F16X2) make_tmap_2d(&omap_lo, reinterpret_cast<const __half*>(e.out) + e.plane, 2, m, w->n, TILE_N, BN);
         else omap_lo = omap;
