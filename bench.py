@@ -192,6 +192,30 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_kernel_only(args):
+    """The encoder fc1 GEMM alone (the profiling target of profiles/tc_gemm_q4_0_fc1.md)."""
+    import ctypes as C
+    import torch
+    from vokra_b200 import _lib, ops, synth
+    ctx = ops.Context(0)
+    if args.precision == "f16":
+        _lib.check(_lib.load().vkb_context_set_precision(ctx.h, _lib.PREC_F16))
+    M = 1500 if args.kernel == "fc1_m1500" else args.clips * 1500
+    N, K = 5120, 1280
+    wq = synth.quantize(synth.Q4_0, np.random.default_rng(7).standard_normal(N * K).astype(np.float32) * 0.02)
+    w = ops.Weight(ctx, synth.Q4_0, N, K, wq)
+    planes = 2 if args.precision == "split" else 1
+    a = (torch.randn((planes * M, K), device="cuda") * 0.5).half()
+    out = torch.empty((M, N), device="cuda", dtype=torch.float16)
+    for _ in range(3):
+        _lib.check(_lib.load().vkb_linear(ctx.h, w.h, M, C.c_void_p(a.data_ptr()),
+                                          _lib.DT_F16X2 if planes == 2 else _lib.DT_F16, None,
+                                          C.c_void_p(out.data_ptr()), _lib.DT_F16, _lib.EPI_NONE, None,
+                                          C.c_float(1.0)))
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel": args.kernel, "M": M, "N": N, "K": K, "ok": True}))
+
+
 # ---------------------------------------------------------------------------
 # GPU leg
 # ---------------------------------------------------------------------------
@@ -205,6 +229,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=128)
     ap.add_argument("--precision", default="split", choices=["split", "f16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", default=None, choices=["fc1", "fc1_m1500"],
+                    help="run only the encoder fc1 GEMM (M = clips x 1500, or 1500) three times, for ncu")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -213,6 +239,9 @@ def main():
 
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.kernel:
+        run_kernel_only(args)
         return
 
     import torch
