@@ -254,6 +254,30 @@ VKB_API vkb_status vkb_attention_dense(vkb_context* ctx, int32_t n_tok, int32_t 
                                const void* k_scale_dev, const void* v_scale_dev,
                                int32_t n_ctx, int32_t kv_dtype, void* ctx_out_dev, int32_t out_dtype);
 
+/* Same computation as vkb_attention_dense, for callers that cannot let the
+ * library allocate device memory during a call (a host that owns a fixed
+ * device-memory budget, a real-time audio path, an engine recording work that
+ * a callee must not interrupt with an allocation). This entry point has no
+ * counterpart in the reference. Its split partials live in a fixed array
+ * inside the library (VKB_NOALLOC_ATTN_SCRATCH_FLOATS floats = 16 MiB, held by
+ * every GPU that loads the library until the process exits); it never calls
+ * cudaMalloc or cudaFree. The first call on a device looks up that array's
+ * device address (cudaGetSymbolAddress) with the device current; make that
+ * first call before any stream capture. Calls that need more than
+ * n_tok * (n_head*d_head + 2*n_head) <= VKB_NOALLOC_ATTN_SCRATCH_FLOATS are
+ * rejected with VKB_ERROR_INVALID_ARGUMENT. Every call on a device shares the
+ * array and it keeps the last call's partials (each call overwrites the slots
+ * it reads, nothing needs to start at zero): calls that overlap on the GPU,
+ * on any streams or contexts of the same device, race and must be ordered by
+ * the caller. */
+#define VKB_NOALLOC_ATTN_SCRATCH_FLOATS (4u * 1024u * 1024u)
+VKB_API vkb_status vkb_attention_dense_noalloc(vkb_context* ctx, int32_t n_tok, int32_t n_head, int32_t d_head,
+                                               const float* q_dev, const int32_t* seq_of_tok_dev,
+                                               const void* k_dev, const void* v_dev,
+                                               const void* k_scale_dev, const void* v_scale_dev,
+                                               int32_t n_ctx, int32_t kv_dtype, void* ctx_out_dev,
+                                               int32_t out_dtype);
+
 /* Quantizes f32 rows [n_rows][width] (width % 32 == 0) into int8 quants
  * q_dev [n_rows][width] and f16 scales d_dev [n_rows][width/32] with the
  * arithmetic of BlockQ8_0::pack (crates/vokra-core/src/kv_quant/q8_0.rs:40),

@@ -215,12 +215,16 @@ static void check_heads(int n_head, int d_head) {
 // Dense attention (cross-attention): launch helper shared with the session.
 void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, const float* q, const int32_t* seq_of_tok,
                          const void* k, const void* v, const void* k_scale, const void* v_scale, int n_ctx,
-                         int kv_fmt, void* out, int out_dtype, float* ws_override) {
+                         int kv_fmt, void* out, int out_dtype, float* ws_override, size_t ws_cap_floats) {
     check_heads(n_head, d_head);
     const int W = n_head * d_head;
     const int R = attn_rowgroups(W);
-    // Splits: about 4 CTAs per SM overall, at least 2*R keys per split.
+    // Splits: about 8 CTAs per SM overall, at least 4*R keys per split.
     int splits = std::max(1, std::min((8 * ctx->sm_count + n_tok - 1) / n_tok, n_ctx / (4 * R)));
+    if (ws_cap_floats) {  // a caller-fixed scratch bounds the number of split partials
+        const size_t per_split = (size_t)n_tok * (W + 2 * n_head);
+        splits = (int)std::max<size_t>(1, std::min<size_t>((size_t)splits, ws_cap_floats / per_split));
+    }
     int kps = (n_ctx + splits - 1) / splits;
     splits = (n_ctx + kps - 1) / kps;
     float* ws = nullptr;
