@@ -249,6 +249,41 @@ def test_dense_cross_attention(ctx, kv):
         assert np.max(np.abs(got[i] - ref)) <= 1e-4
 
 
+@pytest.mark.parametrize("n_head,n_ctx,n_tok,n_seq", [
+    (8, 1000, 40, 10),   # ragged last chunk of keys, several CTAs per query row
+    (20, 7, 3, 2),       # fewer keys than one chunk
+    (12, 1500, 1, 1),    # one query row spread over every SM
+    (6, 100, 4, 2),      # n_head*d_head = 384: served by the row-group kernel
+    (16, 333, 300, 5),   # many query rows per stream, rows crossing CTA ranges
+])
+def test_dense_cross_attention_q8_shapes(ctx, n_head, n_ctx, n_tok, n_seq):
+    import torch
+    from vokra_b200 import ops
+    rng = np.random.default_rng(n_head * 1000 + n_ctx)
+    d_head = 64
+    w = n_head * d_head
+    K = rng.standard_normal((n_seq * n_ctx, w)).astype(np.float32)
+    V = rng.standard_normal((n_seq * n_ctx, w)).astype(np.float32)
+    q = rng.standard_normal((n_tok, w)).astype(np.float32) * np.float32(0.125)
+    seq_of_tok = rng.integers(0, n_seq, n_tok).astype(np.int32)
+    kq = torch.zeros((n_seq * n_ctx, w), dtype=torch.int8, device="cuda:0")
+    vq = torch.zeros_like(kq)
+    kd = torch.zeros((n_seq * n_ctx, w // 32), dtype=torch.float16, device="cuda:0")
+    vd = torch.zeros_like(kd)
+    ops.quantize_rows_q8_0(ctx, _dev(K), kq, kd)
+    ops.quantize_rows_q8_0(ctx, _dev(V), vq, vd)
+    out = torch.zeros((n_tok, w), dtype=torch.float32, device="cuda:0")
+    st = torch.from_numpy(seq_of_tok).to("cuda:0")
+    ops.attention_dense(ctx, _dev(q), st, kq, vq, n_ctx, n_head, d_head, out, k_scale=kd, v_scale=vd)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    Kr = o.kv_unpack(3, o.kv_pack(3, K)).reshape(K.shape)
+    Vr = o.kv_unpack(3, o.kv_pack(3, V)).reshape(V.shape)
+    for i, s in enumerate(seq_of_tok):
+        ref = o.attention(q[i:i + 1], Kr[s * n_ctx:(s + 1) * n_ctx], Vr[s * n_ctx:(s + 1) * n_ctx], n_head)[0]
+        assert np.max(np.abs(got[i] - ref)) <= 1e-4, (i, s)
+
+
 @pytest.mark.parametrize("mode", [_lib.KV_Q4_0, _lib.KV_Q5_0, _lib.KV_Q8_0])
 def test_dequant_gemv_m3_04_shapes(ctx, kats, mode):
     from vokra_b200 import ops

@@ -17,6 +17,8 @@
 #include "common.cuh"
 #include "attn_core.cuh"
 #include "kv.cuh"
+#include "xattn.cuh"
+#include <cstdlib>
 #include <algorithm>
 
 using namespace vkb;
@@ -218,6 +220,20 @@ void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, co
                          int kv_fmt, void* out, int out_dtype, float* ws_override, size_t ws_cap_floats) {
     check_heads(n_head, d_head);
     const int W = n_head * d_head;
+    if (kv_fmt != VKB_DT_F16) {
+        static const bool old_path = std::getenv("VKB_XATTN_ROWGROUPS") != nullptr;
+        XaPlan xp = old_path ? XaPlan{} : xattn_q8_plan(ctx, n_tok, n_head, d_head, n_ctx, q, k, v, k_scale, v_scale,
+                                                        ws_cap_floats);
+        if (xp.ok) {
+            float* ws = ws_override;
+            if (!ws) {
+                ctx->ensure_workspace(xp.ws_floats * sizeof(float));
+                ws = ctx->workspace.as<float>();
+            }
+            run_xattn_q8(ctx, xp, n_tok, n_head, n_ctx, q, seq_of_tok, k, v, k_scale, v_scale, out, out_dtype, ws);
+            return;
+        }
+    }
     const int R = attn_rowgroups(W);
     // Splits: about 8 CTAs per SM overall, at least 4*R keys per split.
     int splits = std::max(1, std::min((8 * ctx->sm_count + n_tok - 1) / n_tok, n_ctx / (4 * R)));

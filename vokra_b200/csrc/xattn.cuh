@@ -1,0 +1,17 @@
+// xattn.cuh — the bandwidth-oriented decode cross-attention over a dense Q8_0
+// store (xattn.cu).
+#pragma once
+#include "common.cuh"
+namespace vkb {
+struct XaPlan {
+    bool ok = false;     // false: the shape / alignment is not one this kernel takes
+    int G = 0;           // CTAs (one per SM at most)
+    int max_seg = 0;     // partial slots per CTA
+    size_t ws_floats = 0;
+};
+XaPlan xattn_q8_plan(const vkb_context* ctx, int n_tok, int n_head, int d_head, int n_ctx, const float* q,
+                     const void* k, const void* v, const void* ks, const void* vs, size_t ws_cap_floats);
+void run_xattn_q8(vkb_context* ctx, const XaPlan& plan, int n_tok, int n_head, int n_ctx, const float* q,
+                  const int32_t* seq_of_tok, const void* k, const void* v, const void* ks, const void* vs, void* out,
+                  int out_fmt, float* ws);
+}  // namespace vkb
