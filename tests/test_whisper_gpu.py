@@ -84,3 +84,46 @@ def test_tiny_whisper_f16_cross_store(ctx, tiny):
     for got, ref in results:
         assert np.max(np.abs(got - ref)) <= 1e-2
         assert _rel_rms(got, ref) <= 1e-3
+
+
+def _decode_fixed_buffer(ctx, path, n_streams, n_steps, graphs, seed=7):
+    """Prefix + n_steps decode steps writing into one logits buffer, so that
+    every decode step after the second replays the recorded step."""
+    import torch
+    from vokra_b200 import whisper
+    a = synth.WHISPER_TINY_TEST
+    rng = np.random.default_rng(seed)
+    logmel = rng.uniform(-1.0, 1.5, (n_streams, a.n_mels, 2 * a.n_audio_ctx)).astype(np.float32)
+    old = os.environ.get("VKB_STEP_GRAPHS")
+    os.environ["VKB_STEP_GRAPHS"] = "1" if graphs else "0"
+    try:
+        model = whisper.WhisperModel(ctx, path)
+        sess = whisper.Session(model, max_streams=n_streams, max_clips=n_streams)
+    finally:
+        if old is None:
+            del os.environ["VKB_STEP_GRAPHS"]
+        else:
+            os.environ["VKB_STEP_GRAPHS"] = old
+    sess.encode(torch.from_numpy(logmel).cuda(), list(range(n_streams)))
+    prefix = list(a.start_ids)
+    sess.step([s for s in range(n_streams) for _ in prefix], [p for _ in range(n_streams) for p in range(len(prefix))],
+              prefix * n_streams)
+    out = torch.zeros((n_streams, a.n_vocab), dtype=torch.float32, device="cuda:0")
+    toks = rng.integers(0, a.n_vocab, (n_steps, n_streams))
+    got = []
+    for t in range(n_steps):
+        sess.step(list(range(n_streams)), [len(prefix) + t] * n_streams, toks[t].tolist(), logits_dev=out)
+        got.append(out.cpu().numpy().copy())
+    sess.close()
+    model.close()
+    return np.stack(got)
+
+
+def test_recorded_decode_step_replays_bit_exact(ctx, tiny):
+    """A decode step recorded as a CUDA graph and replayed gives the same
+    logits, bit for bit, as the same steps launched one kernel at a time
+    (the replays read the new tokens, positions and page-table entries)."""
+    eager = _decode_fixed_buffer(ctx, tiny, n_streams=3, n_steps=20, graphs=False)
+    replay = _decode_fixed_buffer(ctx, tiny, n_streams=3, n_steps=20, graphs=True)
+    assert np.isfinite(eager).all()
+    assert np.array_equal(eager, replay)

@@ -6,45 +6,69 @@
 
 namespace vkb {
 
-// One warp per row; two passes over the row held in registers (cols <= 2048).
-template <int PER>
+// One warp per row; two passes over the row held in registers (cols <= 2048,
+// a multiple of 4). All of a lane's float4 loads are issued before the first
+// use, so a row costs one memory round trip even when there are few rows (the
+// decode step normalizes one row per stream).
+template <int PER4>
 __global__ void layer_norm_kernel(const float* __restrict__ x, int64_t rows, int cols, const float* __restrict__ g,
                                   const float* __restrict__ b, float eps, void* out, int out_fmt) {
     const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
-    const float* xr = x + row * cols;
-    float v[PER];
+    const int n4 = cols >> 2;
+    const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
+    float4 v[PER4];
+#pragma unroll
+    for (int i = 0; i < PER4; ++i) {
+        const int c = lane + 32 * i;
+        v[i] = c < n4 ? __ldg(xr + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
     float s = 0.0f;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-        int c = lane + 32 * i;
-        v[i] = c < cols ? xr[c] : 0.0f;
-        s += v[i];
-    }
+    for (int i = 0; i < PER4; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
     s = warp_sum(s);
     const float inv_cols = 1.0f / (float)cols;
     const float mean = s * inv_cols;
     float q = 0.0f;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-        int c = lane + 32 * i;
-        float d = c < cols ? v[i] - mean : 0.0f;
-        q += d * d;
+    for (int i = 0; i < PER4; ++i) {
+        const int c = lane + 32 * i;
+        if (c < n4) {
+            const float d0 = v[i].x - mean, d1 = v[i].y - mean, d2 = v[i].z - mean, d3 = v[i].w - mean;
+            q += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+        }
     }
     q = warp_sum(q);
     const float inv_std = 1.0f / sqrtf(q * inv_cols + eps);
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-        int c = lane + 32 * i;
-        if (c >= cols) break;
-        float y = (v[i] - mean) * inv_std * g[c] + b[c];
+    for (int i = 0; i < PER4; ++i) {
+        const int c = lane + 32 * i;
+        if (c >= n4) break;
+        const float4 gg = __ldg(g4 + c), bb = __ldg(b4 + c);
+        const float y[4] = {(v[i].x - mean) * inv_std * gg.x + bb.x, (v[i].y - mean) * inv_std * gg.y + bb.y,
+                            (v[i].z - mean) * inv_std * gg.z + bb.z, (v[i].w - mean) * inv_std * gg.w + bb.w};
+        const int64_t o = row * cols + 4 * c;
         if (out_fmt == 0) {
-            reinterpret_cast<float*>(out)[row * cols + c] = y;
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + o) = make_float4(y[0], y[1], y[2], y[3]);
         } else {
-            __half hi = __float2half_rn(y);
-            reinterpret_cast<__half*>(out)[row * cols + c] = hi;
-            if (out_fmt == 2) reinterpret_cast<__half*>(out)[rows * cols + row * cols + c] = __float2half_rn(y - __half2float(hi));
+            __half* oh = reinterpret_cast<__half*>(out);
+            const __half2 h01 = __floats2half2_rn(y[0], y[1]), h23 = __floats2half2_rn(y[2], y[3]);
+            uint2 hv;
+            hv.x = *reinterpret_cast<const uint32_t*>(&h01);
+            hv.y = *reinterpret_cast<const uint32_t*>(&h23);
+            *reinterpret_cast<uint2*>(oh + o) = hv;
+            if (out_fmt == 2) {
+                const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+                const __half2 l01 = __floats2half2_rn(y[0] - f01.x, y[1] - f01.y);
+                const __half2 l23 = __floats2half2_rn(y[2] - f23.x, y[3] - f23.y);
+                uint2 lv;
+                lv.x = *reinterpret_cast<const uint32_t*>(&l01);
+                lv.y = *reinterpret_cast<const uint32_t*>(&l23);
+                *reinterpret_cast<uint2*>(oh + rows * cols + o) = lv;
+            }
         }
     }
 }
@@ -52,10 +76,11 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, int64_t rows, int
 void run_layer_norm(vkb_context* ctx, const float* x, int64_t rows, int cols, const float* g, const float* b, float eps,
                     void* out, int out_fmt) {
     if (cols > 2048) fail(VKB_ERROR_UNSUPPORTED_OP, "layer_norm: row width above 2048");
+    if (cols % 4) fail(VKB_ERROR_UNSUPPORTED_OP, "layer_norm: row width must be a multiple of 4");
     unsigned grid = (unsigned)((rows * 32 + 255) / 256);
-    if (cols <= 512) layer_norm_kernel<16><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_fmt);
-    else if (cols <= 1280) layer_norm_kernel<40><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_fmt);
-    else layer_norm_kernel<64><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_fmt);
+    if (cols <= 512) layer_norm_kernel<4><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_fmt);
+    else if (cols <= 1280) layer_norm_kernel<10><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_fmt);
+    else layer_norm_kernel<16><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_fmt);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }

@@ -44,7 +44,7 @@ struct vkb_kv_pool {
     cudaEvent_t staged = nullptr;
     bool staged_pending = false;
     // current step
-    int n_tok = 0, n_groups = 0, maxq = 1, splits = 1, keys_per_split = 0, max_keys = 0;
+    int n_tok = 0, n_groups = 0, maxq = 1, splits = 1, max_keys = 0;
     std::vector<int32_t> step_seq, step_pos;
     int64_t rows_in_arena() const { return n_pages * rpp; }
 };
@@ -133,19 +133,22 @@ __global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t ld, in
 // ---------------------------------------------------------------------------
 // Attention kernels
 // ---------------------------------------------------------------------------
+// Key splits are fixed per launch (n_splits); each CTA derives its key range
+// from its group's key count, so the launch shape does not depend on the step.
 template <int MAXQ>
 __global__ void __launch_bounds__(ATTN_MAX_THREADS, MAXQ > 1 ? 1 : 2) paged_attn_kernel(FetchPagedQ8 f, const float* __restrict__ q, int64_t q_ld, const AttnGroup* __restrict__ groups,
-                                  int n_head, int d_head, int keys_per_split, int n_splits, void* ctx_out,
+                                  int n_head, int d_head, int n_splits, void* ctx_out,
                                   int out_fmt, float* ws, int per_seq_base, int ppseq, int64_t out_plane) {
     const AttnGroup g = groups[blockIdx.x];
     const int split = blockIdx.y;
     const int n_keys = g.pos0 + g.n_q;  // keys 0 .. last query's position
-    const int kb = split * keys_per_split;
-    const int ke = min(n_keys, kb + keys_per_split);
+    const int kps = (n_keys + n_splits - 1) / n_splits;
+    const int kb = min(n_keys, split * kps);
+    const int ke = min(n_keys, kb + kps);
     FetchPagedQ8 ff = f;
     if (per_seq_base) ff.table_base = g.seq * ppseq;
     else ff.slot = g.seq;
-    attn_body<FetchPagedQ8, MAXQ>(ff, q, q_ld, g, n_head, d_head, f.W, kb, max(kb, ke), split, n_splits, ctx_out,
+    attn_body<FetchPagedQ8, MAXQ>(ff, q, q_ld, g, n_head, d_head, f.W, kb, ke, split, n_splits, ctx_out,
                                   out_fmt, out_plane, ws);
 }
 
@@ -461,16 +464,18 @@ void kv_begin_step(vkb_kv_pool* p, int n_tok, const int32_t* seq, const int32_t*
     p->max_keys = max_keys;
     p->step_seq.assign(seq, seq + n_tok);
     p->step_pos.assign(pos, pos + n_tok);
-    // Key splits: about 4 CTAs per SM, at least 2*R keys per split, and the
-    // partials must fit the pool's buffer.
-    const int R = attn_rowgroups(p->W, maxq);
-    int splits = std::max(1, std::min((8 * p->ctx->sm_count + ng - 1) / ng, max_keys / (4 * R)));
+    // Key splits: about 64 keys per split of the longest possible context, at
+    // most ~8 CTAs per SM, and the partials must fit the pool's buffer. The
+    // count depends only on the step's shape (not on its positions), so a
+    // recorded step replays unchanged; each CTA computes its own key range.
+    int splits = std::max(1, std::min((8 * p->ctx->sm_count + ng - 1) / ng, (d.max_time + 63) / 64));
     while ((int64_t)ng * splits > 4096 && splits > 1) --splits;
-    int kps = (max_keys + splits - 1) / splits;
-    splits = (max_keys + kps - 1) / kps;
     p->splits = splits;
-    p->keys_per_split = kps;
 }
+
+int pool_groups(const vkb_kv_pool* p) { return p->n_groups; }
+int pool_maxq(const vkb_kv_pool* p) { return p->maxq; }
+int pool_splits(const vkb_kv_pool* p) { return p->splits; }
 
 void kv_append_ex(vkb_kv_pool* p, int layer, const float* k, const float* v, int64_t ld) {
     if (p->n_tok == 0) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_append: no step was begun");
@@ -545,13 +550,13 @@ void kv_attention_ex(vkb_kv_pool* p, int layer, const float* q, int64_t q_ld, vo
         static bool attr = false;
         if (!attr) { VKB_CUDA(cudaFuncSetAttribute(paged_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
         paged_attn_kernel<1><<<grid, threads, attn_smem_bytes(R, 1, W, d.n_head), p->ctx->stream>>>(
-            f, q, q_ld, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->keys_per_split, p->splits, out, of16, ws,
+            f, q, q_ld, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->splits, out, of16, ws,
             per_seq_base, p->ppseq, oplane);
     } else {
         static bool attr = false;
         if (!attr) { VKB_CUDA(cudaFuncSetAttribute(paged_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
         paged_attn_kernel<4><<<grid, threads, attn_smem_bytes(R, 4, W, d.n_head), p->ctx->stream>>>(
-            f, q, q_ld, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->keys_per_split, p->splits, out, of16, ws,
+            f, q, q_ld, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->splits, out, of16, ws,
             per_seq_base, p->ppseq, oplane);
     }
     VKB_CUDA(cudaGetLastError());

@@ -6,6 +6,10 @@ vkb_kv_pool* kv_pool_create(vkb_context* ctx, const vkb_kv_pool_desc* desc);
 void kv_pool_destroy(vkb_kv_pool* p);
 void kv_begin_step(vkb_kv_pool* p, int n_tok, const int32_t* seq, const int32_t* pos);
 // k / v rows have stride ld floats (e.g. the fused q|k|v projection output).
+// Shape of the step begun last (what a recorded step's launches depend on).
+int pool_groups(const vkb_kv_pool* p);
+int pool_maxq(const vkb_kv_pool* p);
+int pool_splits(const vkb_kv_pool* p);
 void kv_append_ex(vkb_kv_pool* p, int layer, const float* k, const float* v, int64_t ld);
 void kv_attention_ex(vkb_kv_pool* p, int layer, const float* q, int64_t q_ld, void* out, int out_dtype);
 void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, const float* q, const int32_t* seq_of_tok,

@@ -23,6 +23,9 @@
 #include "enc_attn.cuh"
 #include <memory>
 #include <algorithm>
+#include <cstdlib>
+#include <map>
+#include <tuple>
 
 using namespace vkb;
 
@@ -98,7 +101,25 @@ struct vkb_session {
     DevBuf col1, bufA, bufB, eh, exln, ectx, eout, emap;
     int32_t* h_map = nullptr;
     int last_clips = 0;
+    // cross-attention partials of a step (session-owned, so a recorded step
+    // never points into a context workspace that a later call regrows)
+    DevBuf xws;
+    size_t xws_floats = 0;
+    // Recorded decode steps, keyed by everything that shapes their launches:
+    // (n_tok, query groups, queries per group, key splits, logits, ids, precision).
+    struct StepGraph {
+        cudaGraphExec_t exec = nullptr;
+        uint64_t launches = 0;
+        bool seen = false;    // ran once eagerly (buffers sized, attributes set)
+        bool failed = false;  // recording was refused: run eagerly
+    };
+    std::map<std::tuple<int, int, int, int, uintptr_t, uintptr_t, int>, StepGraph> graphs;
+    bool use_graphs = true;
+    cudaStream_t rec_stream = nullptr;  // private stream the step is recorded on
     ~vkb_session() {
+        if (rec_stream) cudaStreamDestroy(rec_stream);
+        for (auto& kv : graphs)
+            if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
         if (pool) kv_pool_destroy(pool);
         if (h_tok) cudaFreeHost(h_tok);
         if (h_map) cudaFreeHost(h_map);
@@ -318,7 +339,7 @@ vkb_session* create_session(vkb_whisper* m, const vkb_session_options* o) {
     const DecLayer& l0 = m->dec[0];
     for (const vkb_weight* w : {l0.qkv.get(), l0.o.get(), l0.cq.get(), l0.co.get(), l0.fc1.get(), l0.fc2.get(),
                                 m->tok_emb.get()})
-        for (int64_t mm : {(int64_t)1, (int64_t)2, (int64_t)4, mt}) ws = std::max(ws, ws_need(s->ctx, w, std::min(mm, mt)));
+        for (int64_t mm = 1; mm <= mt; ++mm) ws = std::max(ws, ws_need(s->ctx, w, mm));
     if (C > 0) {
         const int64_t M = C * T;
         const EncLayer& e0 = m->enc[0];
@@ -327,6 +348,17 @@ vkb_session* create_session(vkb_whisper* m, const vkb_session_options* o) {
             for (int64_t mm = T; mm <= 2 * M; mm *= 2) ws = std::max(ws, ws_need(s->ctx, w, mm));
     }
     s->ws.alloc(std::max<size_t>(ws, 256));
+    // Cross-attention partials: the balanced kernel keeps at most
+    // sm_count * (ceil(n_tok / sm_count) + 2) row partials; the row-group
+    // kernel (f16 store) at most (8 * sm_count + n_tok) split partials.
+    {
+        const int64_t H = D.n_text_head, sms = s->ctx->sm_count;
+        const int64_t per = d + 2 * H;
+        s->xws_floats = (size_t)std::max(sms * ((mt + sms - 1) / sms + 2), 8 * sms + mt) * per;
+        s->xws.alloc(s->xws_floats * sizeof(float));
+    }
+    const char* g = std::getenv("VKB_STEP_GRAPHS");
+    s->use_graphs = !(g && g[0] == '0');
     return s.release();
 }
 
@@ -437,55 +469,106 @@ void session_step(vkb_session* s, int n_tok, const int32_t* streams, const int32
     VKB_CUDA(cudaEventRecord(s->staged, ctx->stream));
     s->staged_pending = true;
 
-    float* h = s->h.as<float>();
-    __half* xln = s->xln.as<__half>();
-    float* qkv = s->qkv.as<float>();
-    __half* ctxb = s->ctxb.as<__half>();
-    float* qc = s->qc.as<float>();
-    __half* ffn = s->ffn.as<__half>();
-    float* ws = s->ws.as<float>();
-    const int AF = ctx->precision == VKB_PREC_SPLIT ? VKB_DT_F16X2 : VKB_DT_F16;
-    run_embed(ctx, m->tok_emb.get(), s->tok.as<int32_t>(), s->pos.as<int32_t>(), n_tok, m->dec_pos.as<float>(), h);
-    const float scale = 1.0f / sqrtf((float)(d / D.n_text_head));
-    const int64_t rows = (int64_t)s->opt.max_streams * T;
-    for (int l = 0; l < D.n_text_layer; ++l) {
-        const DecLayer& L = m->dec[l];
-        run_layer_norm(ctx, h, n_tok, (int)d, L.ln1g.as<float>(), L.ln1b.as<float>(), LN_EPS, xln, AF);
-        LinearExtra x;
-        x.n_scaled = d;
-        run_linear_ex(ctx, L.qkv.get(), n_tok, xln, AF, L.qkv_b.as<float>(), qkv, VKB_DT_F32, VKB_EPI_SCALE,
-                      nullptr, scale, ws, nullptr, x);
-        kv_append_ex(s->pool, l, qkv + d, qkv + 2 * d, 3 * d);
-        kv_attention_ex(s->pool, l, qkv, 3 * d, ctxb, AF);
-        run_linear(ctx, L.o.get(), n_tok, ctxb, AF, L.o_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h, 1.0f,
-                   ws, nullptr);
-        run_layer_norm(ctx, h, n_tok, (int)d, L.ln2g.as<float>(), L.ln2b.as<float>(), LN_EPS, xln, AF);
-        run_linear(ctx, L.cq.get(), n_tok, xln, AF, L.cq_b.as<float>(), qc, VKB_DT_F32, VKB_EPI_SCALE, nullptr,
-                   scale, ws, nullptr);
-        if (s->opt.cross_kv_q8) {
-            run_dense_attention(ctx, n_tok, D.n_text_head, 64, qc, s->seq.as<int32_t>(),
-                                s->ck.as<int8_t>() + (size_t)l * rows * d, s->cv.as<int8_t>() + (size_t)l * rows * d,
-                                s->cks.as<__half>() + (size_t)l * rows * (d / 32),
-                                s->cvs.as<__half>() + (size_t)l * rows * (d / 32), (int)T, VKB_KV_Q8_0, ctxb,
-                                AF, nullptr);
-        } else {
-            run_dense_attention(ctx, n_tok, D.n_text_head, 64, qc, s->seq.as<int32_t>(),
-                                s->ck.as<__half>() + (size_t)l * rows * d, s->cv.as<__half>() + (size_t)l * rows * d,
-                                nullptr, nullptr, (int)T, VKB_DT_F16, ctxb, AF, nullptr);
-        }
-        run_linear(ctx, L.co.get(), n_tok, ctxb, AF, L.co_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h,
-                   1.0f, ws, nullptr);
-        run_layer_norm(ctx, h, n_tok, (int)d, L.ln3g.as<float>(), L.ln3b.as<float>(), LN_EPS, xln, AF);
-        run_linear(ctx, L.fc1.get(), n_tok, xln, AF, L.fc1_b.as<float>(), ffn, AF, VKB_EPI_GELU,
-                   nullptr, 1.0f, ws, nullptr);
-        run_linear(ctx, L.fc2.get(), n_tok, ffn, AF, L.fc2_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h,
-                   1.0f, ws, nullptr);
-    }
-    run_layer_norm(ctx, h, n_tok, (int)d, m->dec_lng.as<float>(), m->dec_lnb.as<float>(), LN_EPS, xln, AF);
+    // Launch sequence of the step. Every pointer and shape it uses is fixed
+    // for a given key, and the per-step inputs (tokens, positions, streams,
+    // page table, rows, query groups) were copied into fixed device buffers
+    // above, so after one eager run the sequence is recorded once into a CUDA
+    // graph and replayed with a single launch (host cost per step: one graph
+    // launch instead of ~600 kernel launches).
     float* lg = logits_out ? logits_out : s->logits.as<float>();
-    run_linear(ctx, m->tok_emb.get(), n_tok, xln, AF, nullptr, lg, VKB_DT_F32, VKB_EPI_NONE, nullptr, 1.0f, ws,
-               nullptr);
-    run_argmax(ctx, lg, n_tok, D.n_vocab, ids_out ? ids_out : s->ids.as<int32_t>());
+    int32_t* ids = ids_out ? ids_out : s->ids.as<int32_t>();
+    auto launch_all = [&]() {
+        float* h = s->h.as<float>();
+        __half* xln = s->xln.as<__half>();
+        float* qkv = s->qkv.as<float>();
+        __half* ctxb = s->ctxb.as<__half>();
+        float* qc = s->qc.as<float>();
+        __half* ffn = s->ffn.as<__half>();
+        float* ws = s->ws.as<float>();
+        const int AF = ctx->precision == VKB_PREC_SPLIT ? VKB_DT_F16X2 : VKB_DT_F16;
+        run_embed(ctx, m->tok_emb.get(), s->tok.as<int32_t>(), s->pos.as<int32_t>(), n_tok, m->dec_pos.as<float>(), h);
+        const float scale = 1.0f / sqrtf((float)(d / D.n_text_head));
+        const int64_t rows = (int64_t)s->opt.max_streams * T;
+        for (int l = 0; l < D.n_text_layer; ++l) {
+            const DecLayer& L = m->dec[l];
+            run_layer_norm(ctx, h, n_tok, (int)d, L.ln1g.as<float>(), L.ln1b.as<float>(), LN_EPS, xln, AF);
+            LinearExtra x;
+            x.n_scaled = d;
+            run_linear_ex(ctx, L.qkv.get(), n_tok, xln, AF, L.qkv_b.as<float>(), qkv, VKB_DT_F32, VKB_EPI_SCALE,
+                          nullptr, scale, ws, nullptr, x);
+            kv_append_ex(s->pool, l, qkv + d, qkv + 2 * d, 3 * d);
+            kv_attention_ex(s->pool, l, qkv, 3 * d, ctxb, AF);
+            run_linear(ctx, L.o.get(), n_tok, ctxb, AF, L.o_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h, 1.0f,
+                       ws, nullptr);
+            run_layer_norm(ctx, h, n_tok, (int)d, L.ln2g.as<float>(), L.ln2b.as<float>(), LN_EPS, xln, AF);
+            run_linear(ctx, L.cq.get(), n_tok, xln, AF, L.cq_b.as<float>(), qc, VKB_DT_F32, VKB_EPI_SCALE, nullptr,
+                       scale, ws, nullptr);
+            if (s->opt.cross_kv_q8) {
+                run_dense_attention(ctx, n_tok, D.n_text_head, 64, qc, s->seq.as<int32_t>(),
+                                    s->ck.as<int8_t>() + (size_t)l * rows * d, s->cv.as<int8_t>() + (size_t)l * rows * d,
+                                    s->cks.as<__half>() + (size_t)l * rows * (d / 32),
+                                    s->cvs.as<__half>() + (size_t)l * rows * (d / 32), (int)T, VKB_KV_Q8_0, ctxb,
+                                    AF, s->xws.as<float>(), s->xws_floats);
+            } else {
+                run_dense_attention(ctx, n_tok, D.n_text_head, 64, qc, s->seq.as<int32_t>(),
+                                    s->ck.as<__half>() + (size_t)l * rows * d, s->cv.as<__half>() + (size_t)l * rows * d,
+                                    nullptr, nullptr, (int)T, VKB_DT_F16, ctxb, AF, s->xws.as<float>(), s->xws_floats);
+            }
+            run_linear(ctx, L.co.get(), n_tok, ctxb, AF, L.co_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h,
+                       1.0f, ws, nullptr);
+            run_layer_norm(ctx, h, n_tok, (int)d, L.ln3g.as<float>(), L.ln3b.as<float>(), LN_EPS, xln, AF);
+            run_linear(ctx, L.fc1.get(), n_tok, xln, AF, L.fc1_b.as<float>(), ffn, AF, VKB_EPI_GELU,
+                       nullptr, 1.0f, ws, nullptr);
+            run_linear(ctx, L.fc2.get(), n_tok, ffn, AF, L.fc2_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h,
+                       1.0f, ws, nullptr);
+        }
+        run_layer_norm(ctx, h, n_tok, (int)d, m->dec_lng.as<float>(), m->dec_lnb.as<float>(), LN_EPS, xln, AF);
+        run_linear(ctx, m->tok_emb.get(), n_tok, xln, AF, nullptr, lg, VKB_DT_F32, VKB_EPI_NONE, nullptr, 1.0f, ws,
+                   nullptr);
+        run_argmax(ctx, lg, n_tok, D.n_vocab, ids);
+    };
+    const auto key = std::make_tuple(n_tok, pool_groups(s->pool), pool_maxq(s->pool), pool_splits(s->pool),
+                                     (uintptr_t)lg, (uintptr_t)ids, ctx->precision);
+    vkb_session::StepGraph& sg = s->graphs[key];
+    if (!s->use_graphs || sg.failed || !sg.seen) {
+        launch_all();
+        sg.seen = true;
+        return;
+    }
+    if (!sg.exec) {
+        // Record on the session's private stream (the context's stream may be
+        // the legacy default stream, which cannot be recorded); nothing runs
+        // while recording, and the graph is then launched on the context's stream.
+        if (!s->rec_stream) VKB_CUDA(cudaStreamCreateWithFlags(&s->rec_stream, cudaStreamNonBlocking));
+        const uint64_t l0 = ctx->launches;
+        cudaStream_t user = ctx->stream;
+        cudaGraph_t graph = nullptr;
+        VKB_CUDA(cudaStreamBeginCapture(s->rec_stream, cudaStreamCaptureModeThreadLocal));
+        ctx->stream = s->rec_stream;
+        try {
+            launch_all();
+        } catch (...) {
+            ctx->stream = user;
+            cudaStreamEndCapture(s->rec_stream, &graph);
+            if (graph) cudaGraphDestroy(graph);
+            throw;
+        }
+        ctx->stream = user;
+        cudaError_t e = cudaStreamEndCapture(s->rec_stream, &graph);
+        if (e == cudaSuccess) e = cudaGraphInstantiate(&sg.exec, graph, 0);
+        if (graph) cudaGraphDestroy(graph);
+        sg.launches = ctx->launches - l0;  // recorded, not yet run: counted at each replay
+        ctx->launches = l0;
+        if (e != cudaSuccess) {
+            (void)cudaGetLastError();
+            sg.exec = nullptr;
+            sg.failed = true;
+            launch_all();
+            return;
+        }
+    }
+    VKB_CUDA(cudaGraphLaunch(sg.exec, ctx->stream));
+    ctx->count((int)sg.launches);
 }
 
 }  // namespace
