@@ -1,5 +1,6 @@
 // common.cuh — shared host/device helpers of libvkb200 (sm_100a only).
 #pragma once
+#include <utility>
 
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -86,11 +87,14 @@ struct vkb_context {
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
     uint64_t launches = 0;
-    int precision = VKB_PREC_SPLIT;
-    unsigned long long* trace = nullptr;
-    int debug = 0;  // debugging aid (VKB_DEBUG)  // debugging aid: GEMM block-0 timeline (VKB_TRACE)  // tensor-core operand precision (vkb_context_set_precision)
+    int precision = VKB_PREC_SPLIT;  // tensor-core operand precision (vkb_context_set_precision)
+    unsigned long long* trace = nullptr;  // debugging aid: GEMM block-0 timeline (VKB_TRACE)
     vkb::DevBuf workspace;
     vkb::DevBuf err_flag;  // int set by a kernel whose bounded wait gave up
+    // Programmatic dependent launch: each kernel may start while the previous
+    // one in the stream drains; it waits (griddepcontrol.wait) before touching
+    // anything that kernel wrote (VKB_PDL=0 turns it off).
+    bool pdl = true;
     void ensure_workspace(size_t bytes) {
         if (workspace.n < bytes) {
             VKB_CUDA(cudaStreamSynchronize(stream));
@@ -101,6 +105,36 @@ struct vkb_context {
 };
 
 namespace vkb {
+
+// Launch with programmatic stream serialization (see vkb_context::pdl). Every
+// kernel launched this way calls pdl_wait() before reading or writing memory
+// that an earlier kernel in the stream may still be using.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(vkb_context* ctx, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VKB_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
+// Lets the next kernel in the stream be scheduled (it still waits for this
+// one's memory in its own pdl_wait()).
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Waits until the previous kernel in the stream has completed and its memory
+// operations are visible.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_entry() {
+    pdl_launch();
+    pdl_wait();
+}
 
 // ---------------------------------------------------------------------------
 // Device helpers

@@ -38,6 +38,8 @@ vkb_status vkb_context_create(int device, vkb_context** out) {
             VKB_CUDA(cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking));
             c->stream = c->own_stream;
             c->err_flag.alloc(sizeof(int));
+            const char* pdl = getenv("VKB_PDL");
+            c->pdl = !(pdl && pdl[0] == '0');
             if (getenv("VKB_TRACE")) {
                 VKB_CUDA(cudaMallocManaged(&c->trace, 5 * 64 * 8));
                 memset(c->trace, 0, 5 * 64 * 8);

@@ -13,6 +13,7 @@ namespace vkb {
 template <int PER4>
 __global__ void layer_norm_kernel(const float* __restrict__ x, int64_t rows, int cols, const float* __restrict__ g,
                                   const float* __restrict__ b, float eps, void* out, int out_fmt) {
+    pdl_entry();
     const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -73,14 +74,74 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, int64_t rows, int
     }
 }
 
+// Few rows (a decode step): one CTA per row, one float4 of x, g and b per
+// thread, all loaded before the two block reductions.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float t = l < nw ? red[l] : 0.0f;
+    return warp_sum(t);
+}
+
+__global__ void layer_norm_row_kernel(const float* __restrict__ x, int64_t rows, int cols, const float* __restrict__ g,
+                                      const float* __restrict__ b, float eps, void* out, int out_fmt) {
+    pdl_entry();
+    __shared__ float red[32];
+    const int64_t row = blockIdx.x;
+    const int c = threadIdx.x, n4 = cols >> 2;
+    const bool on = c < n4;
+    const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float4 v = on ? __ldg(reinterpret_cast<const float4*>(x + row * cols) + c) : z;
+    const float4 gg = on ? __ldg(reinterpret_cast<const float4*>(g) + c) : z;
+    const float4 bb = on ? __ldg(reinterpret_cast<const float4*>(b) + c) : z;
+    const float inv_cols = 1.0f / (float)cols;
+    const float mean = block_sum((v.x + v.y) + (v.z + v.w), red) * inv_cols;
+    const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
+    const float q = block_sum(on ? (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3) : 0.0f, red);
+    const float inv_std = 1.0f / sqrtf(q * inv_cols + eps);
+    if (!on) return;
+    const float y[4] = {d0 * inv_std * gg.x + bb.x, d1 * inv_std * gg.y + bb.y, d2 * inv_std * gg.z + bb.z,
+                        d3 * inv_std * gg.w + bb.w};
+    const int64_t o = row * cols + 4 * c;
+    if (out_fmt == 0) {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + o) = make_float4(y[0], y[1], y[2], y[3]);
+    } else {
+        __half* oh = reinterpret_cast<__half*>(out);
+        const __half2 h01 = __floats2half2_rn(y[0], y[1]), h23 = __floats2half2_rn(y[2], y[3]);
+        uint2 hv;
+        hv.x = *reinterpret_cast<const uint32_t*>(&h01);
+        hv.y = *reinterpret_cast<const uint32_t*>(&h23);
+        *reinterpret_cast<uint2*>(oh + o) = hv;
+        if (out_fmt == 2) {
+            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+            const __half2 l01 = __floats2half2_rn(y[0] - f01.x, y[1] - f01.y);
+            const __half2 l23 = __floats2half2_rn(y[2] - f23.x, y[3] - f23.y);
+            uint2 lv;
+            lv.x = *reinterpret_cast<const uint32_t*>(&l01);
+            lv.y = *reinterpret_cast<const uint32_t*>(&l23);
+            *reinterpret_cast<uint2*>(oh + rows * cols + o) = lv;
+        }
+    }
+}
+
 void run_layer_norm(vkb_context* ctx, const float* x, int64_t rows, int cols, const float* g, const float* b, float eps,
                     void* out, int out_fmt) {
     if (cols > 2048) fail(VKB_ERROR_UNSUPPORTED_OP, "layer_norm: row width above 2048");
     if (cols % 4) fail(VKB_ERROR_UNSUPPORTED_OP, "layer_norm: row width must be a multiple of 4");
+    if (rows <= 4 * (int64_t)ctx->sm_count) {
+        const int threads = ((cols / 4 + 31) / 32) * 32;
+        launch_pdl(ctx, layer_norm_row_kernel, (unsigned)rows, threads, 0, x, rows, cols, g, b, eps, out, out_fmt);
+        VKB_CUDA(cudaGetLastError());
+        ctx->count();
+        return;
+    }
     unsigned grid = (unsigned)((rows * 32 + 255) / 256);
-    if (cols <= 512) layer_norm_kernel<4><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_fmt);
-    else if (cols <= 1280) layer_norm_kernel<10><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_fmt);
-    else layer_norm_kernel<16><<<grid, 256, 0, ctx->stream>>>(x, rows, cols, g, b, eps, out, out_fmt);
+    if (cols <= 512) launch_pdl(ctx, layer_norm_kernel<4>, grid, 256, 0, x, rows, cols, g, b, eps, out, out_fmt);
+    else if (cols <= 1280) launch_pdl(ctx, layer_norm_kernel<10>, grid, 256, 0, x, rows, cols, g, b, eps, out, out_fmt);
+    else launch_pdl(ctx, layer_norm_kernel<16>, grid, 256, 0, x, rows, cols, g, b, eps, out, out_fmt);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
@@ -90,6 +151,7 @@ template <int FMT>
 __global__ void embed_kernel(const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc, int64_t K,
                              const int32_t* __restrict__ tokens, const int32_t* __restrict__ positions, int n_tok,
                              const float* __restrict__ pos, float* __restrict__ h) {
+    pdl_entry();
     const int stages = (int)(K / STAGE_K);
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)n_tok * stages) return;
@@ -111,10 +173,10 @@ void run_embed(vkb_context* ctx, const vkb_weight* w, const int32_t* tokens, con
     const uint8_t* qs = w->qs.as<uint8_t>();
     const uint8_t* sc = w->sc.as<uint8_t>();
     switch (w->fmt) {
-        case W_Q4_0: embed_kernel<W_Q4_0><<<grid, 128, 0, ctx->stream>>>(qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
-        case W_Q8_0: embed_kernel<W_Q8_0><<<grid, 128, 0, ctx->stream>>>(qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
-        case W_Q4_K: embed_kernel<W_Q4_K><<<grid, 128, 0, ctx->stream>>>(qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
-        default: embed_kernel<W_F16><<<grid, 128, 0, ctx->stream>>>(qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
+        case W_Q4_0: launch_pdl(ctx, embed_kernel<W_Q4_0>, grid, 128, 0, qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
+        case W_Q8_0: launch_pdl(ctx, embed_kernel<W_Q8_0>, grid, 128, 0, qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
+        case W_Q4_K: launch_pdl(ctx, embed_kernel<W_Q4_K>, grid, 128, 0, qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
+        default: launch_pdl(ctx, embed_kernel<W_F16>, grid, 128, 0, qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
     }
     VKB_CUDA(cudaGetLastError());
     ctx->count();
@@ -123,6 +185,7 @@ void run_embed(vkb_context* ctx, const vkb_weight* w, const int32_t* tokens, con
 // col[b*To + t][c*3 + kk] = x[b][c][t*stride + kk - 1]; columns C*3 .. ldc-1 are zero
 __global__ void im2col_ct_kernel(const float* __restrict__ x, int B, int C, int T, int To, int stride, int ldc,
                                  __half* __restrict__ col, int split) {
+    pdl_entry();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t total = (int64_t)B * To * ldc;
     if (i >= total) return;
@@ -145,6 +208,7 @@ __global__ void im2col_ct_kernel(const float* __restrict__ x, int B, int C, int 
 // col[b*To + t][c*3 + kk] = x[b*T + t*stride + kk - 1][c]
 __global__ void im2col_tc_kernel(const __half* __restrict__ x, int B, int C, int T, int To, int stride,
                                  __half* __restrict__ col, int planes) {
+    pdl_entry();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t total = (int64_t)B * To * C * 3;
     if (i >= total) return;
@@ -164,7 +228,7 @@ void run_im2col_ct(vkb_context* ctx, const float* x, int B, int C, int T, int st
                    bool split) {
     int To = conv_out(T, stride);
     int64_t total = (int64_t)B * To * ldc;
-    im2col_ct_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(x, B, C, T, To, stride, ldc, col,
+    launch_pdl(ctx, im2col_ct_kernel, (unsigned)((total + 255) / 256), 256, 0, x, B, C, T, To, stride, ldc, col,
                                                                               split ? 1 : 0);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
@@ -173,13 +237,14 @@ void run_im2col_ct(vkb_context* ctx, const float* x, int B, int C, int T, int st
 void run_im2col_tc(vkb_context* ctx, const __half* x, int B, int C, int T, int stride, __half* col, int planes) {
     int To = conv_out(T, stride);
     int64_t total = (int64_t)B * To * C * 3;
-    im2col_tc_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(x, B, C, T, To, stride, col, planes);
+    launch_pdl(ctx, im2col_tc_kernel, (unsigned)((total + 255) / 256), 256, 0, x, B, C, T, To, stride, col, planes);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
 
 __global__ void add_pos_kernel(const __half* __restrict__ y, const float* __restrict__ pos, int B, int T, int C,
                                float* __restrict__ h, int planes) {
+    pdl_entry();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t total = (int64_t)B * T * C;
     if (i >= total) return;
@@ -191,19 +256,31 @@ __global__ void add_pos_kernel(const __half* __restrict__ y, const float* __rest
 
 void run_add_pos(vkb_context* ctx, const __half* y, const float* pos, int B, int T, int C, float* h, int planes) {
     int64_t total = (int64_t)B * T * C;
-    add_pos_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(y, pos, B, T, C, h, planes);
+    launch_pdl(ctx, add_pos_kernel, (unsigned)((total + 255) / 256), 256, 0, y, pos, B, T, C, h, planes);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
 
-// One CTA per row; first index of the maximum wins ties.
+// One CTA per row; first index of the maximum wins ties. Each thread loads
+// 8 values before comparing any, so a row costs a few memory round trips.
 __global__ void argmax_kernel(const float* __restrict__ logits, int n_cols, int32_t* __restrict__ ids) {
+    pdl_entry();
     const float* r = logits + (int64_t)blockIdx.x * n_cols;
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int j = threadIdx.x; j < n_cols; j += blockDim.x) {
-        float v = r[j];
-        if (v > best || (v == best && j < bi)) { best = v; bi = j; }
+    constexpr int U = 8;
+    for (int j0 = threadIdx.x; j0 < n_cols; j0 += U * blockDim.x) {
+        float v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int j = j0 + u * blockDim.x;
+            v[u] = j < n_cols ? __ldg(r + j) : -INFINITY;
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int j = j0 + u * blockDim.x;
+            if (j < n_cols && (v[u] > best || (v[u] == best && j < bi))) { best = v[u]; bi = j; }
+        }
     }
     __shared__ float sv[32];
     __shared__ int si[32];
@@ -231,7 +308,7 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int n_cols, int3
 }
 
 void run_argmax(vkb_context* ctx, const float* logits, int n_rows, int n_cols, int32_t* ids) {
-    argmax_kernel<<<n_rows, 512, 0, ctx->stream>>>(logits, n_cols, ids);
+    launch_pdl(ctx, argmax_kernel, n_rows, 1024, 0, logits, n_cols, ids);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }

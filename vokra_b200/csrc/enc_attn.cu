@@ -72,6 +72,7 @@ __device__ __forceinline__ void load_tile(__half* dst, const __half* base, int64
 __global__ void __launch_bounds__(128) enc_attn_kernel(const __half* __restrict__ qkv, int64_t ld, int kcol, int vcol,
                                                        int T, int n_head, __half* __restrict__ ctx, int64_t ctx_ld,
                                                        __half* __restrict__ ctx_lo) {
+    pdl_entry();
     __shared__ __align__(128) __half sQ[BQ * LDS];
     __shared__ __align__(128) __half sK[2][BK * LDS];
     __shared__ __align__(128) __half sV[2][BK * LDS];
@@ -222,7 +223,7 @@ void run_encoder_attention(vkb_context* ctx, const __half* qkv, int64_t ld, int 
     if (ld % 8 || kcol % 8 || vcol % 8 || out_ld % 2)
         fail(VKB_ERROR_INVALID_ARGUMENT, "encoder attention: rows must be 16-byte aligned");
     dim3 grid((unsigned)((T + BQ - 1) / BQ), (unsigned)(n_windows * n_head));
-    enc_attn_kernel<<<grid, 128, 0, ctx->stream>>>(qkv, ld, kcol, vcol, T, n_head, out, out_ld, out_lo);
+    launch_pdl(ctx, enc_attn_kernel, grid, 128, 0, qkv, ld, kcol, vcol, T, n_head, out, out_ld, out_lo);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }

@@ -72,6 +72,7 @@ __device__ __forceinline__ void q8_0_block_warp(float x, int lane, int8_t* q_out
 __global__ void kv_append_kernel(const float* __restrict__ k, const float* __restrict__ v, int64_t ld,
                                  const int64_t* __restrict__ rows, int n_tok, int W, int8_t* kq, __half* kd,
                                  int8_t* vq, __half* vd) {
+    pdl_entry();
     const int nb = W / 32;
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -91,6 +92,7 @@ __global__ void kv_append_kernel(const float* __restrict__ k, const float* __res
 // map[r / group] * group + r % group.
 __global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t ld, int64_t n_rows, int W, int8_t* q,
                                      __half* d, const int32_t* __restrict__ map, int group) {
+    pdl_entry();
     // One thread per 32-element block: 8 float4 loads, then the BlockQ8_0::pack
     // arithmetic (the same expressions as q8_0_block_warp, sequentially).
     const int nb = W / 32;
@@ -139,6 +141,7 @@ template <int MAXQ>
 __global__ void __launch_bounds__(ATTN_MAX_THREADS, MAXQ > 1 ? 1 : 2) paged_attn_kernel(FetchPagedQ8 f, const float* __restrict__ q, int64_t q_ld, const AttnGroup* __restrict__ groups,
                                   int n_head, int d_head, int n_splits, void* ctx_out,
                                   int out_fmt, float* ws, int per_seq_base, int ppseq, int64_t out_plane) {
+    pdl_entry();
     const AttnGroup g = groups[blockIdx.x];
     const int split = blockIdx.y;
     const int n_keys = g.pos0 + g.n_q;  // keys 0 .. last query's position
@@ -156,6 +159,7 @@ template <class F>
 __global__ void __launch_bounds__(ATTN_MAX_THREADS, 2) dense_attn_kernel(F f, const float* __restrict__ q, const int32_t* __restrict__ seq_of_tok, int n_ctx,
                                   int n_head, int d_head, int keys_per_split, int n_splits, void* ctx_out,
                                   int out_fmt, float* ws, int64_t out_plane) {
+    pdl_entry();
     AttnGroup g;
     g.first_tok = blockIdx.x;
     g.n_q = 1;
@@ -172,6 +176,7 @@ __global__ void __launch_bounds__(ATTN_MAX_THREADS, 2) dense_attn_kernel(F f, co
 
 __global__ void attn_combine_kernel(const float* __restrict__ ws, int n_tok, int n_splits, int n_head, int d_head,
                                     void* ctx_out, int out_fmt) {
+    pdl_entry();
     const int W = n_head * d_head;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)n_tok * W) return;
@@ -262,21 +267,21 @@ void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, co
         FetchDenseF16 f{reinterpret_cast<const __half*>(k), reinterpret_cast<const __half*>(v), W, 0};
         static bool attr = false;
         if (!attr) { VKB_CUDA(cudaFuncSetAttribute(dense_attn_kernel<FetchDenseF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
-        dense_attn_kernel<FetchDenseF16><<<grid, threads, sm, ctx->stream>>>(f, q, seq_of_tok, n_ctx, n_head, d_head, kps,
+        launch_pdl(ctx, dense_attn_kernel<FetchDenseF16>, grid, threads, sm, f, q, seq_of_tok, n_ctx, n_head, d_head, kps,
                                                                             splits, out, out_dtype, ws, (int64_t)n_tok * W);
     } else {
         FetchDenseQ8 f{reinterpret_cast<const int8_t*>(k), reinterpret_cast<const __half*>(k_scale),
                        reinterpret_cast<const int8_t*>(v), reinterpret_cast<const __half*>(v_scale), W, 0};
         static bool attr = false;
         if (!attr) { VKB_CUDA(cudaFuncSetAttribute(dense_attn_kernel<FetchDenseQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
-        dense_attn_kernel<FetchDenseQ8><<<grid, threads, sm, ctx->stream>>>(f, q, seq_of_tok, n_ctx, n_head, d_head, kps,
+        launch_pdl(ctx, dense_attn_kernel<FetchDenseQ8>, grid, threads, sm, f, q, seq_of_tok, n_ctx, n_head, d_head, kps,
                                                                            splits, out, out_dtype, ws, (int64_t)n_tok * W);
     }
     VKB_CUDA(cudaGetLastError());
     ctx->count();
     if (splits > 1) {
         int64_t tot = (int64_t)n_tok * W;
-        attn_combine_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, ctx->stream>>>(ws, n_tok, splits, n_head, d_head,
+        launch_pdl(ctx, attn_combine_kernel, (unsigned)((tot + 255) / 256), 256, 0, ws, n_tok, splits, n_head, d_head,
                                                                                    out, out_dtype);
         VKB_CUDA(cudaGetLastError());
         ctx->count();
@@ -288,7 +293,7 @@ void run_quantize_rows(vkb_context* ctx, const float* x, int64_t ld, int64_t n_r
     if (W % 32) fail(VKB_ERROR_INVALID_ARGUMENT, "quantize_rows: row width must be a multiple of 32");
     if (ld % 4 || ((uintptr_t)x & 15)) fail(VKB_ERROR_INVALID_ARGUMENT, "quantize_rows: rows must be 16-byte aligned");
     int64_t blocks = n_rows * (W / 32);
-    quantize_rows_kernel<<<(unsigned)((blocks + 255) / 256), 256, 0, ctx->stream>>>(x, ld, n_rows, W, q, d, map, group);
+    launch_pdl(ctx, quantize_rows_kernel, (unsigned)((blocks + 255) / 256), 256, 0, x, ld, n_rows, W, q, d, map, group);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
@@ -503,7 +508,7 @@ void kv_append_ex(vkb_kv_pool* p, int layer, const float* k, const float* v, int
     }
     const int64_t warps = (int64_t)p->n_tok * p->row_blocks * 2;
     const int64_t* rows = p->rows_dev.as<int64_t>() + (size_t)layer * p->n_tok;
-    kv_append_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, p->ctx->stream>>>(
+    launch_pdl(p->ctx, kv_append_kernel, (unsigned)((warps * 32 + 255) / 256), 256, 0, 
         k, v, ld, rows, p->n_tok, p->W, p->kq.as<int8_t>(), p->kd.as<__half>(), p->vq.as<int8_t>(), p->vd.as<__half>());
     VKB_CUDA(cudaGetLastError());
     p->ctx->count();
@@ -549,13 +554,13 @@ void kv_attention_ex(vkb_kv_pool* p, int layer, const float* q, int64_t q_ld, vo
     if (p->maxq == 1) {
         static bool attr = false;
         if (!attr) { VKB_CUDA(cudaFuncSetAttribute(paged_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
-        paged_attn_kernel<1><<<grid, threads, attn_smem_bytes(R, 1, W, d.n_head), p->ctx->stream>>>(
+        launch_pdl(p->ctx, paged_attn_kernel<1>, grid, threads, attn_smem_bytes(R, 1, W, d.n_head), 
             f, q, q_ld, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->splits, out, of16, ws,
             per_seq_base, p->ppseq, oplane);
     } else {
         static bool attr = false;
         if (!attr) { VKB_CUDA(cudaFuncSetAttribute(paged_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
-        paged_attn_kernel<4><<<grid, threads, attn_smem_bytes(R, 4, W, d.n_head), p->ctx->stream>>>(
+        launch_pdl(p->ctx, paged_attn_kernel<4>, grid, threads, attn_smem_bytes(R, 4, W, d.n_head), 
             f, q, q_ld, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->splits, out, of16, ws,
             per_seq_base, p->ppseq, oplane);
     }
@@ -563,7 +568,7 @@ void kv_attention_ex(vkb_kv_pool* p, int layer, const float* q, int64_t q_ld, vo
     p->ctx->count();
     if (p->splits > 1) {
         int64_t tot = (int64_t)p->n_tok * W;
-        attn_combine_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, p->ctx->stream>>>(ws, p->n_tok, p->splits,
+        launch_pdl(p->ctx, attn_combine_kernel, (unsigned)((tot + 255) / 256), 256, 0, ws, p->n_tok, p->splits,
                                                                                        d.n_head, d.d_head, out, of16);
         VKB_CUDA(cudaGetLastError());
         p->ctx->count();
@@ -589,6 +594,7 @@ static void zero_page(vkb_kv_pool* p, int32_t pid, int layer_for_seq) {
 template <int MODE>
 __global__ void kv_dequant_gemv_kernel(const uint8_t* __restrict__ blocks, int64_t n_rows, int64_t nbpr,
                                        const float* __restrict__ x, float* __restrict__ y) {
+    pdl_entry();
     const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= n_rows) return;
@@ -646,9 +652,9 @@ static void run_dequant_gemv(vkb_context* ctx, int mode, const void* blocks, siz
     if (n_rows == 0) return;
     unsigned grid = (unsigned)((n_rows * 32 + 255) / 256);
     const uint8_t* b = reinterpret_cast<const uint8_t*>(blocks);
-    if (mode == VKB_KV_Q8_0) kv_dequant_gemv_kernel<VKB_KV_Q8_0><<<grid, 256, 0, ctx->stream>>>(b, n_rows, nbpr, x, y);
-    else if (mode == VKB_KV_Q4_0) kv_dequant_gemv_kernel<VKB_KV_Q4_0><<<grid, 256, 0, ctx->stream>>>(b, n_rows, nbpr, x, y);
-    else kv_dequant_gemv_kernel<VKB_KV_Q5_0><<<grid, 256, 0, ctx->stream>>>(b, n_rows, nbpr, x, y);
+    if (mode == VKB_KV_Q8_0) launch_pdl(ctx, kv_dequant_gemv_kernel<VKB_KV_Q8_0>, grid, 256, 0, b, n_rows, nbpr, x, y);
+    else if (mode == VKB_KV_Q4_0) launch_pdl(ctx, kv_dequant_gemv_kernel<VKB_KV_Q4_0>, grid, 256, 0, b, n_rows, nbpr, x, y);
+    else launch_pdl(ctx, kv_dequant_gemv_kernel<VKB_KV_Q5_0>, grid, 256, 0, b, n_rows, nbpr, x, y);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }

@@ -179,6 +179,7 @@ template <int FMT, int MM>
 __global__ void __launch_bounds__(128) gemv_kernel(const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc,
                                                    int64_t K, int64_t N, int64_t M, const void* __restrict__ a,
                                                    int a_fmt, int stages_per_split, int n_splits, float* ws, Epi e) {
+    pdl_entry();
     extern __shared__ float xs[];  // [MM][stages_per_split*64]
     const int tile = blockIdx.x, split = blockIdx.y, r = threadIdx.x;
     const int64_t total_stages = K / STAGE_K;
@@ -241,16 +242,25 @@ __global__ void __launch_bounds__(128) gemv_kernel(const uint8_t* __restrict__ q
 
 // Sums split-K partials ws[split][m][n] in split order and applies the epilogue.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int n_splits, int64_t M, int64_t N, Epi e) {
+    pdl_entry();
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= M * N) return;
-    int64_t m = i / N, n = i % N;
+    int64_t m, n;
+    if (M * N < (int64_t(1) << 31)) {  // 32-bit division where it is exact
+        m = (unsigned)i / (unsigned)N;
+        n = (unsigned)i - (unsigned)m * (unsigned)N;
+    } else {
+        m = i / N;
+        n = i % N;
+    }
     float acc = 0.0f;
-    for (int s = 0; s < n_splits; ++s) acc += ws[(int64_t)s * M * N + i];
+    for (int s = 0; s < n_splits; ++s) acc += __ldg(ws + (int64_t)s * M * N + i);
     epi_store(e, m, n, acc, e.bias ? e.bias[n] : 0.0f);
 }
 
 // x (f32) -> f16 plane, or hi / lo f16 planes (x = hi + lo to ~2^-22) when split.
 __global__ void split_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, int64_t n, int split) {
+    pdl_entry();
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     float v = x[i];
@@ -260,7 +270,7 @@ __global__ void split_f16_kernel(const float* __restrict__ x, __half* __restrict
 }
 
 void run_split_f16(vkb_context* ctx, const float* x, int64_t n, __half* y, bool split) {
-    split_f16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(x, y, n, split ? 1 : 0);
+    launch_pdl(ctx, split_f16_kernel, (unsigned)((n + 255) / 256), 256, 0, x, y, n, split ? 1 : 0);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
@@ -302,7 +312,14 @@ struct TcCfg {
     static constexpr int S0 = BUDGET / STAGE_BYTES;
     static constexpr int S = S0 > 6 ? 6 : S0;
     static constexpr int SMEM = 1024 /*align slack*/ + S * STAGE_BYTES + 1024 /*barriers*/;
-    static constexpr int ACC_COLS = BN < 32 ? 32 : BN;
+    // Stacked split mode (token tiles up to 128): the hi and lo activation
+    // tiles, adjacent in shared memory, form ONE B operand of 2*BN rows, so a
+    // K=16 step is two MMAs (W_hi and W_lo against [X_hi; X_lo]) instead of
+    // three at N=BN; the accumulator holds W.X_hi in columns [0, BN) and W.X_lo
+    // in [BN, 2BN), added in the epilogue. Small-N MMAs cost about the same
+    // issue time as N=128..256 ones, so this is faster where M is small.
+    static constexpr bool STACK = SPLIT && BN <= 128;
+    static constexpr int ACC_COLS = STACK ? 2 * BN : (BN < 32 ? 32 : BN);
     static constexpr int A_COL0 = ACC_COLS;                     // first A column
     static constexpr int AS = 4;                                // A stages in tensor memory
     static constexpr int NEED_COLS = ACC_COLS + AS * NP * 32;
@@ -376,28 +393,45 @@ __global__ void __launch_bounds__(192, 1)
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     bool ok = true;
+    // Programmatic dependent launch: the next kernel may be scheduled now; this
+    // one waits for the previous kernel only where it reads activations
+    // (producer) or writes results (epilogue). Weights are never written by a
+    // kernel, so their first stages are fetched before that wait.
+    pdl_launch();
 
     if (warp == 0) {
         if (lane == 0) {
+            // weights of the first ring stages, then wait for the previous kernel
+            const int pre = nst < C::S ? nst : C::S;
+            for (int i = 0; i < pre; ++i) {
+                uint8_t* raw_dst = st_ring + i * C::STAGE_BYTES + C::NP * C::B_BYTES;
+                StagePtrs p = stage_ptrs(FMT, qs, sc, K, n_tile, s0 + i);
+                ptx::mbar_expect_tx(&full[i], C::NP * C::B_BYTES + C::RAW_Q + C::RAW_S);
+                ptx::bulk_load(raw_dst, p.qs, C::RAW_Q, &full[i]);
+                if (C::RAW_S) ptx::bulk_load(raw_dst + C::RAW_Q, p.sc, C::RAW_S, &full[i]);
+            }
+            pdl_wait();
             for (int i = 0; i < nst && ok; ++i) {
                 int s = i % C::S;
-                if (!ptx::mbar_wait(&empty[s], ((i / C::S) & 1) ^ 1)) { ok = false; break; }
                 uint8_t* b_dst = st_ring + s * C::STAGE_BYTES;
-                uint8_t* raw_dst = b_dst + C::NP * C::B_BYTES;
                 int64_t stage = s0 + i;
-                StagePtrs p = stage_ptrs(FMT, qs, sc, K, n_tile, stage);
+                if (i >= pre) {
+                    if (!ptx::mbar_wait(&empty[s], ((i / C::S) & 1) ^ 1)) { ok = false; break; }
+                    uint8_t* raw_dst = b_dst + C::NP * C::B_BYTES;
+                    StagePtrs p = stage_ptrs(FMT, qs, sc, K, n_tile, stage);
+                    ptx::mbar_expect_tx(&full[s], C::NP * C::B_BYTES + C::RAW_Q + C::RAW_S);
+                    ptx::bulk_load(raw_dst, p.qs, C::RAW_Q, &full[s]);
+                    if (C::RAW_S) ptx::bulk_load(raw_dst + C::RAW_Q, p.sc, C::RAW_S, &full[s]);
+                }
                 stamp(0, i);
-                ptx::mbar_expect_tx(&full[s], C::NP * C::B_BYTES + C::RAW_Q + C::RAW_S);
                 ptx::tma_load_2d(b_dst, &xmap, &full[s], (int32_t)(stage * STAGE_K), m_tile * BN);
                 if (SPLIT)
                     ptx::tma_load_2d(b_dst + C::B_BYTES, &xmap_lo, &full[s], (int32_t)(stage * STAGE_K), m_tile * BN);
-                ptx::bulk_load(raw_dst, p.qs, C::RAW_Q, &full[s]);
-                if (C::RAW_S) ptx::bulk_load(raw_dst + C::RAW_Q, p.sc, C::RAW_S, &full[s]);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = ptx::idesc_f16_f32(TILE_N, BN);
+            constexpr uint32_t idesc = ptx::idesc_f16_f32(TILE_N, C::STACK ? 2 * BN : BN);
             for (int i = 0; i < nst && ok; ++i) {
                 int s = i % C::S, a = i % C::AS;
                 if (!ptx::mbar_wait(&full[s], (i / C::S) & 1)) { ok = false; break; }
@@ -410,7 +444,9 @@ __global__ void __launch_bounds__(192, 1)
                 for (int kk = 0; kk < 4; ++kk) {
                     uint64_t bd = ptx::sdesc_sw128(b_addr + kk * 32);
                     ptx::mma_f16_ts(tmem, a_t + kk * 8, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-                    if (SPLIT) {
+                    if (C::STACK) {
+                        ptx::mma_f16_ts(tmem, a_t + 32 + kk * 8, bd, idesc, 1u);
+                    } else if (SPLIT) {
                         uint64_t bd_lo = ptx::sdesc_sw128(b_addr + C::B_BYTES + kk * 32);
                         ptx::mma_f16_ts(tmem, a_t + kk * 8, bd_lo, idesc, 1u);
                         ptx::mma_f16_ts(tmem, a_t + 32 + kk * 8, bd, idesc, 1u);
@@ -442,7 +478,8 @@ __global__ void __launch_bounds__(192, 1)
             if (threadIdx.x == 64) stamp(3, i);
             ptx::mbar_arrive(&a_full[a]);
         }
-        // Epilogue.
+        // Epilogue (after the previous kernel: it may still read what we overwrite).
+        pdl_wait();
         if (ok && ptx::mbar_wait(acc_full, 0)) {
             if (threadIdx.x == 64) stamp(4, 0);
             ptx::tc_fence_after();
@@ -466,7 +503,15 @@ __global__ void __launch_bounds__(192, 1)
                 for (int c0 = 0; c0 < BN && ok; c0 += 16) {
                     uint32_t v[16];
                     ptx::tmem_ld16(lane_addr + c0, v);
-                    ptx::tmem_ld_wait();
+                    if (C::STACK) {
+                        uint32_t v2[16];
+                        ptx::tmem_ld16(lane_addr + BN + c0, v2);
+                        ptx::tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(v2[j]));
+                    } else {
+                        ptx::tmem_ld_wait();
+                    }
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int row = c0 + j;
@@ -492,19 +537,27 @@ __global__ void __launch_bounds__(192, 1)
                 if (threadIdx.x == 64 && ok && partial) {
                     ptx::tma_store_3d(&omap, st_ring, n_tile * TILE_N, m_tile * BN, split);
                     ptx::bulk_commit();
-                    ptx::bulk_wait0();
+                    ptx::bulk_wait_read0();
                 } else if (threadIdx.x == 64 && ok) {
                     ptx::tma_store_2d(&omap, st_ring, n_tile * TILE_N, m_tile * BN);
                     if (e.out_fmt == VKB_DT_F16X2) ptx::tma_store_2d(&omap_lo, sh + BN * TILE_N, n_tile * TILE_N, m_tile * BN);
                     ptx::bulk_commit();
-                    ptx::bulk_wait0();
+                    ptx::bulk_wait_read0();
                 }
             } else {
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN; c0 += 16) {
                     uint32_t v[16];
                     ptx::tmem_ld16(lane_addr + c0, v);
-                    ptx::tmem_ld_wait();
+                    if (C::STACK) {
+                        uint32_t v2[16];
+                        ptx::tmem_ld16(lane_addr + BN + c0, v2);
+                        ptx::tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(v2[j]));
+                    } else {
+                        ptx::tmem_ld_wait();
+                    }
                     if (n < N) {
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
@@ -609,7 +662,7 @@ static void launch_gemv(vkb_context* ctx, const vkb_weight* w, int64_t m, const 
                                           200 * 1024));                                                         \
             attr = true;                                                                                        \
         }                                                                                                       \
-        gemv_kernel<FMT, MMv><<<grid, 128, sm, ctx->stream>>>(qs, sc, w->k, w->n, m, a, a_fmt, stages_per_split, \
+        launch_pdl(ctx, gemv_kernel<FMT, MMv>, grid, 128, sm, qs, sc, w->k, w->n, m, a, a_fmt, stages_per_split, \
                                                               splits, ws, e);                                   \
     }
     if (m <= 1) VKB_GEMV(1) else if (m <= 2) VKB_GEMV(2) else VKB_GEMV(4)
@@ -655,7 +708,7 @@ static void launch_tc(vkb_context* ctx, const vkb_weight* w, int64_t m, const __
     }
     int n_tiles = (int)(w->n_pad / TILE_N);
     dim3 grid((unsigned)(n_tiles * m_tiles * splits));
-    tc_gemm_kernel<FMT, BN, SPLIT><<<grid, 192, C::SMEM, ctx->stream>>>(
+    launch_pdl(ctx, tc_gemm_kernel<FMT, BN, SPLIT>, grid, 192, C::SMEM, 
         map, map_lo, w->qs.as<uint8_t>(), w->sc.as<uint8_t>(), w->k, w->n, m, n_tiles, m_tiles, stages_per_split,
         splits, ws, e, device_err_flag(ctx), ctx->trace, omap, omap_lo, rmap, tma_epi);
     VKB_CUDA(cudaGetLastError());
@@ -783,7 +836,7 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
     }
     if (p.splits > 1) {
         int64_t tot = m * w->n;
-        splitk_reduce_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, ctx->stream>>>(ws, p.splits, m, w->n, e);
+        launch_pdl(ctx, splitk_reduce_kernel, (unsigned)((tot + 255) / 256), 256, 0, ws, p.splits, m, w->n, e);
         VKB_CUDA(cudaGetLastError());
         ctx->count();
     }

@@ -33,6 +33,7 @@ namespace vkb {
 // f32 rows -> f16 rows with the stream remap (the f16 cross store)
 __global__ void copy_rows_f16_kernel(const float* __restrict__ x, int64_t ld, int64_t n_rows, int W,
                                      __half* __restrict__ y, const int32_t* __restrict__ map, int group) {
+    pdl_entry();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_rows * W) return;
     const int64_t r = i / W;
@@ -43,7 +44,7 @@ __global__ void copy_rows_f16_kernel(const float* __restrict__ x, int64_t ld, in
 static void run_copy_rows_f16(vkb_context* ctx, const float* x, int64_t ld, int64_t n_rows, int W, __half* y,
                               const int32_t* map, int group) {
     int64_t tot = n_rows * W;
-    copy_rows_f16_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, ctx->stream>>>(x, ld, n_rows, W, y, map, group);
+    launch_pdl(ctx, copy_rows_f16_kernel, (unsigned)((tot + 255) / 256), 256, 0, x, ld, n_rows, W, y, map, group);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }

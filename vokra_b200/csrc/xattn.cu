@@ -119,6 +119,7 @@ __device__ __forceinline__ void xa_load_q(const float* __restrict__ qrow, int ro
 }
 
 __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
+    pdl_entry();
     extern __shared__ __align__(128) uint8_t xa_smem[];
     const int W = a.W, H = a.H, S = a.S;
     const int nb = W / 32;
@@ -318,6 +319,7 @@ __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
 // One CTA per query row: thread 0 lists the partial slots of the CTAs whose
 // range covers the row (in shared memory), then each thread merges 4 channels.
 __global__ void xattn_combine_kernel(XaArgs a, void* out, int out_fmt) {
+    pdl_entry();
     extern __shared__ int s_slot[];  // [G]
     __shared__ int s_n;
     const int W = a.W, H = a.H;
@@ -436,10 +438,10 @@ void run_xattn_q8(vkb_context* ctx, const XaPlan& plan, int n_tok, int n_head, i
         VKB_CUDA(cudaFuncSetAttribute(xattn_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, XA_SMEM_BUDGET));
         attr = true;
     }
-    xattn_q8_kernel<<<plan.G, 16 * n_head + 32, smem, ctx->stream>>>(a);
+    launch_pdl(ctx, xattn_q8_kernel, plan.G, 16 * n_head + 32, smem, a);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
-    xattn_combine_kernel<<<(unsigned)n_tok, std::min(256, W / 4), (size_t)plan.G * sizeof(int), ctx->stream>>>(a, out, out_fmt);
+    launch_pdl(ctx, xattn_combine_kernel, (unsigned)n_tok, std::min(256, W / 4), (size_t)plan.G * sizeof(int), a, out, out_fmt);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
