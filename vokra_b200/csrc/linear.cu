@@ -577,6 +577,9 @@ __global__ void __launch_bounds__(192, 1)
     }
     if (threadIdx.x == 64) stamp(4, 1);
     if (!ok && err) atomicExch(err, 1);
+    // Reconverge each warp (only one lane of the producer and MMA warps ran its
+    // role) before the block barrier: bar.sync requires converged warps.
+    __syncwarp();
     ptx::tc_fence_before();
     __syncthreads();
     if (warp == 1) {

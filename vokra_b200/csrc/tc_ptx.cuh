@@ -74,7 +74,10 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Named barrier over `count` threads.
+// bar.sync is an aligned barrier: every participating warp must be converged,
+// so the warp reconverges first (callers may come from one-lane branches).
 __device__ __forceinline__ void named_bar(int id, int count) {
+    __syncwarp();
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 

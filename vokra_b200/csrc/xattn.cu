@@ -305,6 +305,7 @@ __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
         }
         if (!failed && cur_tok >= 0) flush();
     }
+    __syncwarp();  // the producer warp ran on one lane: reconverge before the block barrier
     if (__syncthreads_or(failed)) {
         if (tid == 0) atomicExch(a.err, 1);
         if (warp == n_cw && lane == 0) {
@@ -312,6 +313,7 @@ __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
             for (int i = max(0, issued - S); i < issued; ++i)
                 ptx::mbar_wait(&full[i % S], (uint32_t)((i / S) & 1), 1u << 20);
         }
+        __syncwarp();
         __syncthreads();
     }
 }
