@@ -127,6 +127,83 @@ __global__ void layer_norm_row_kernel(const float* __restrict__ x, int64_t rows,
     }
 }
 
+// One CTA per row, one float4 of the row per thread: sums the split-K partials
+// of a residual projection (split order, as splitk_reduce_kernel), adds bias
+// and the residual, writes h, then normalizes the new row like
+// layer_norm_row_kernel.
+__global__ void reduce_residual_ln_kernel(const float* __restrict__ part, int splits, int64_t rows, int cols,
+                                          const float* __restrict__ bias, float* __restrict__ h,
+                                          const float* __restrict__ g, const float* __restrict__ b, float eps,
+                                          void* out, int out_fmt) {
+    pdl_entry();
+    __shared__ float red[32];
+    const int64_t row = blockIdx.x;
+    const int c = threadIdx.x, n4 = cols >> 2;
+    const bool on = c < n4;
+    const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float4 v = z, gg = z, bb = z;
+    if (on) {
+        const int64_t o4 = row * n4 + c;
+        const float4 bi = bias ? __ldg(reinterpret_cast<const float4*>(bias) + c) : z;
+        float4 acc = z;
+        constexpr int U = 8;
+        for (int s0 = 0; s0 < splits; s0 += U) {
+            float4 t[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (s0 + u < splits) t[u] = __ldcg(reinterpret_cast<const float4*>(part) + (int64_t)(s0 + u) * rows * n4 + o4);
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (s0 + u < splits) {
+                    acc.x += t[u].x; acc.y += t[u].y; acc.z += t[u].z; acc.w += t[u].w;
+                }
+        }
+        const float4 r = reinterpret_cast<const float4*>(h)[o4];
+        v = make_float4(r.x + (acc.x + bi.x), r.y + (acc.y + bi.y), r.z + (acc.z + bi.z), r.w + (acc.w + bi.w));
+        reinterpret_cast<float4*>(h)[o4] = v;
+        gg = __ldg(reinterpret_cast<const float4*>(g) + c);
+        bb = __ldg(reinterpret_cast<const float4*>(b) + c);
+    }
+    const float inv_cols = 1.0f / (float)cols;
+    const float mean = block_sum((v.x + v.y) + (v.z + v.w), red) * inv_cols;
+    const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
+    const float q = block_sum(on ? (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3) : 0.0f, red);
+    const float inv_std = 1.0f / sqrtf(q * inv_cols + eps);
+    if (!on) return;
+    const float y[4] = {d0 * inv_std * gg.x + bb.x, d1 * inv_std * gg.y + bb.y, d2 * inv_std * gg.z + bb.z,
+                        d3 * inv_std * gg.w + bb.w};
+    const int64_t o = row * cols + 4 * c;
+    if (out_fmt == 0) {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + o) = make_float4(y[0], y[1], y[2], y[3]);
+    } else {
+        __half* oh = reinterpret_cast<__half*>(out);
+        const __half2 h01 = __floats2half2_rn(y[0], y[1]), h23 = __floats2half2_rn(y[2], y[3]);
+        uint2 hv;
+        hv.x = *reinterpret_cast<const uint32_t*>(&h01);
+        hv.y = *reinterpret_cast<const uint32_t*>(&h23);
+        *reinterpret_cast<uint2*>(oh + o) = hv;
+        if (out_fmt == 2) {
+            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+            const __half2 l01 = __floats2half2_rn(y[0] - f01.x, y[1] - f01.y);
+            const __half2 l23 = __floats2half2_rn(y[2] - f23.x, y[3] - f23.y);
+            uint2 lv;
+            lv.x = *reinterpret_cast<const uint32_t*>(&l01);
+            lv.y = *reinterpret_cast<const uint32_t*>(&l23);
+            *reinterpret_cast<uint2*>(oh + rows * cols + o) = lv;
+        }
+    }
+}
+
+void run_reduce_residual_ln(vkb_context* ctx, const float* part, int splits, int64_t rows, int cols, const float* bias,
+                            float* h, const float* g, const float* b, float eps, void* out, int out_fmt) {
+    if (cols % 4 || cols / 4 > 1024) fail(VKB_ERROR_UNSUPPORTED_OP, "reduce_residual_ln: row width");
+    const int threads = ((cols / 4 + 31) / 32) * 32;
+    launch_pdl(ctx, reduce_residual_ln_kernel, (unsigned)rows, threads, 0, part, splits, rows, cols, bias, h, g, b,
+               eps, out, out_fmt);
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
+}
+
 void run_layer_norm(vkb_context* ctx, const float* x, int64_t rows, int cols, const float* g, const float* b, float eps,
                     void* out, int out_fmt) {
     if (cols > 2048) fail(VKB_ERROR_UNSUPPORTED_OP, "layer_norm: row width above 2048");

@@ -8,6 +8,11 @@ namespace vkb {
 // out_fmt 0 f32, 1 f16, 2 f16 hi + lo planes.
 void run_layer_norm(vkb_context* ctx, const float* x, int64_t rows, int cols, const float* g, const float* b, float eps,
                     void* out, int out_fmt);
+// The residual update of a split-K projection fused with the next LayerNorm:
+// h[r] += bias + sum_s part[s][r] (partials summed in split order), then
+// out = LayerNorm(h[r]) as run_layer_norm. rows * cols floats per partial.
+void run_reduce_residual_ln(vkb_context* ctx, const float* part, int splits, int64_t rows, int cols, const float* bias,
+                            float* h, const float* g, const float* b, float eps, void* out, int out_fmt);
 // h[i] = dequant(tok_emb[tokens[i]]) + pos[positions[i]]  (whisper/decoder.rs:440-452)
 void run_embed(vkb_context* ctx, const vkb_weight* tok_emb, const int32_t* tokens, const int32_t* positions, int n_tok,
                const float* pos, float* h);

@@ -837,7 +837,8 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
         if (p.split) dispatch_fmt<true>(ctx, w, m, a16, e, ws, p);
         else dispatch_fmt<false>(ctx, w, m, a16, e, ws, p);
     }
-    if (p.splits > 1) {
+    if (x.splits_out) *x.splits_out = p.splits;
+    if (p.splits > 1 && !x.splits_out) {
         int64_t tot = m * w->n;
         launch_pdl(ctx, splitk_reduce_kernel, (unsigned)((tot + 255) / 256), 256, 0, ws, p.splits, m, w->n, e);
         VKB_CUDA(cudaGetLastError());

@@ -23,6 +23,11 @@ struct LinearExtra {
     int64_t out_rows = 0;         // rows per plane (default m)
     const int32_t* row_map = nullptr;  // device map of row groups to destination groups
     int row_group = 1;
+    // Split-K GEMMs: leave the fp32 partials [splits][m][n] in the workspace
+    // instead of reducing them (the caller's next kernel reduces them and
+    // applies bias / residual); *splits_out = number of partials (1 = the
+    // output was written with its epilogue as usual).
+    int* splits_out = nullptr;
 };
 
 vkb_weight* upload_weight(vkb_context* ctx, uint32_t tag, int64_t n, int64_t k, const void* bytes, size_t len);

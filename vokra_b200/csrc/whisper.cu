@@ -490,18 +490,29 @@ void session_step(vkb_session* s, int n_tok, const int32_t* streams, const int32
         run_embed(ctx, m->tok_emb.get(), s->tok.as<int32_t>(), s->pos.as<int32_t>(), n_tok, m->dec_pos.as<float>(), h);
         const float scale = 1.0f / sqrtf((float)(d / D.n_text_head));
         const int64_t rows = (int64_t)s->opt.max_streams * T;
+        // A residual projection (h += x.W^T + bias) followed by the next
+        // LayerNorm: with split-K, the partials are reduced inside the fused
+        // residual + LayerNorm kernel instead of a separate reduce kernel.
+        auto residual_ln = [&](const vkb_weight* w, const void* x_in, const float* bias, const float* g,
+                               const float* b) {
+            int sp = 1;
+            LinearExtra rx;
+            rx.splits_out = &sp;
+            run_linear_ex(ctx, w, n_tok, x_in, AF, bias, h, VKB_DT_F32, VKB_EPI_RESIDUAL, h, 1.0f, ws, nullptr, rx);
+            if (sp > 1) run_reduce_residual_ln(ctx, ws, sp, n_tok, (int)d, bias, h, g, b, LN_EPS, xln, AF);
+            else run_layer_norm(ctx, h, n_tok, (int)d, g, b, LN_EPS, xln, AF);
+        };
+        run_layer_norm(ctx, h, n_tok, (int)d, m->dec[0].ln1g.as<float>(), m->dec[0].ln1b.as<float>(), LN_EPS, xln,
+                       AF);
         for (int l = 0; l < D.n_text_layer; ++l) {
             const DecLayer& L = m->dec[l];
-            run_layer_norm(ctx, h, n_tok, (int)d, L.ln1g.as<float>(), L.ln1b.as<float>(), LN_EPS, xln, AF);
             LinearExtra x;
             x.n_scaled = d;
             run_linear_ex(ctx, L.qkv.get(), n_tok, xln, AF, L.qkv_b.as<float>(), qkv, VKB_DT_F32, VKB_EPI_SCALE,
                           nullptr, scale, ws, nullptr, x);
             kv_append_ex(s->pool, l, qkv + d, qkv + 2 * d, 3 * d);
             kv_attention_ex(s->pool, l, qkv, 3 * d, ctxb, AF);
-            run_linear(ctx, L.o.get(), n_tok, ctxb, AF, L.o_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h, 1.0f,
-                       ws, nullptr);
-            run_layer_norm(ctx, h, n_tok, (int)d, L.ln2g.as<float>(), L.ln2b.as<float>(), LN_EPS, xln, AF);
+            residual_ln(L.o.get(), ctxb, L.o_b.as<float>(), L.ln2g.as<float>(), L.ln2b.as<float>());
             run_linear(ctx, L.cq.get(), n_tok, xln, AF, L.cq_b.as<float>(), qc, VKB_DT_F32, VKB_EPI_SCALE, nullptr,
                        scale, ws, nullptr);
             if (s->opt.cross_kv_q8) {
@@ -515,15 +526,14 @@ void session_step(vkb_session* s, int n_tok, const int32_t* streams, const int32
                                     s->ck.as<__half>() + (size_t)l * rows * d, s->cv.as<__half>() + (size_t)l * rows * d,
                                     nullptr, nullptr, (int)T, VKB_DT_F16, ctxb, AF, s->xws.as<float>(), s->xws_floats);
             }
-            run_linear(ctx, L.co.get(), n_tok, ctxb, AF, L.co_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h,
-                       1.0f, ws, nullptr);
-            run_layer_norm(ctx, h, n_tok, (int)d, L.ln3g.as<float>(), L.ln3b.as<float>(), LN_EPS, xln, AF);
+            residual_ln(L.co.get(), ctxb, L.co_b.as<float>(), L.ln3g.as<float>(), L.ln3b.as<float>());
             run_linear(ctx, L.fc1.get(), n_tok, xln, AF, L.fc1_b.as<float>(), ffn, AF, VKB_EPI_GELU,
                        nullptr, 1.0f, ws, nullptr);
-            run_linear(ctx, L.fc2.get(), n_tok, ffn, AF, L.fc2_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h,
-                       1.0f, ws, nullptr);
+            const bool last = l + 1 == D.n_text_layer;
+            residual_ln(L.fc2.get(), ffn, L.fc2_b.as<float>(),
+                        last ? m->dec_lng.as<float>() : m->dec[l + 1].ln1g.as<float>(),
+                        last ? m->dec_lnb.as<float>() : m->dec[l + 1].ln1b.as<float>());
         }
-        run_layer_norm(ctx, h, n_tok, (int)d, m->dec_lng.as<float>(), m->dec_lnb.as<float>(), LN_EPS, xln, AF);
         run_linear(ctx, m->tok_emb.get(), n_tok, xln, AF, nullptr, lg, VKB_DT_F32, VKB_EPI_NONE, nullptr, 1.0f, ws,
                    nullptr);
         run_argmax(ctx, lg, n_tok, D.n_vocab, ids);
