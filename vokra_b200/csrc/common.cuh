@@ -200,6 +200,19 @@ __device__ __forceinline__ float gelu_as(float v) {
     return 0.5f * v * (1.0f + sign * y);
 }
 
+// The same formula and constants evaluated with CUDA's fast exponential and
+// division intrinsics (a few ulp from gelu_as; used in GEMM epilogues, where
+// the full-precision version dominated the tile's epilogue time).
+__device__ __forceinline__ float gelu_as_fast(float v) {
+    const float P = 0.3275911f, A1 = 0.254829592f, A2 = -0.284496736f, A3 = 1.421413741f,
+                A4 = -1.453152027f, A5 = 1.061405429f;
+    const float x = fabsf(v * 0.70710678118654752f);
+    const float t = __fdividef(1.0f, 1.0f + P * x);
+    const float poly = ((((A5 * t + A4) * t + A3) * t + A2) * t + A1) * t;
+    const float y = 1.0f - poly * __expf(-x * x);
+    return 0.5f * v * (1.0f + copysignf(y, v));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -157,7 +157,7 @@ __device__ __forceinline__ void epi_store(const Epi& e, int64_t m, int64_t n, fl
     int64_t mr = e.row_map ? (int64_t)e.row_map[m / e.row_group] * e.row_group + m % e.row_group : m;
     int64_t idx = e.col_block > 0 ? (n / e.col_block) * (e.out_rows * e.col_block) + mr * e.col_block + n % e.col_block
                                   : mr * e.ldo + n;
-    if (e.kind == VKB_EPI_GELU) v = gelu_as(v);
+    if (e.kind == VKB_EPI_GELU) v = gelu_as_fast(v);
     else if (e.kind == VKB_EPI_SCALE) v = n < e.n_scaled ? v * e.scale : v;
     else if (e.kind == VKB_EPI_RESIDUAL) v = e.residual[idx] + v;
     if (e.out_fmt == VKB_DT_F32) {
@@ -290,12 +290,14 @@ void run_split_f16(vkb_context* ctx, const float* x, int64_t n, __half* y, bool 
 // K=16 step issues W_hi.X_hi + W_hi.X_lo + W_lo.X_hi, which reproduces the
 // fp32 product to about 2^-21 relative (the W_lo.X_lo term is below that).
 //
-// Warp roles (192 threads):
+// Warp roles (320 threads):
 //   warp 0      : producer — TMA for X, bulk copies for the raw weight stage
 //   warp 1      : TMEM allocator; lane 0 issues tcgen05.mma and commits
 //   warps 2..5  : dequantize raw stage -> A tile(s); then the epilogue
 //                 (thread = one weight row = one TMEM lane)
-// Rings: S stages of (X tile(s) + raw weights) in shared memory, 2 stages of
+//   warps 6..9  : epilogue only, on the same TMEM lanes as warps 2..5 and the
+//                 other half of the token columns
+// Rings: S stages of (X tile(s) + raw weights) in shared memory, AS stages of
 // A tiles in tensor memory.
 // Every mbarrier wait is bounded; on timeout the kernel records an error flag
 // and returns without hanging.
@@ -332,7 +334,7 @@ struct TcCfg {
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 template <int FMT, int BN, bool SPLIT>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_lo,
                    const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc, int64_t K, int64_t N, int64_t M,
                    int n_tiles, int m_tiles, int stages_per_split, int n_splits, float* ws, Epi e, int* err,
@@ -457,8 +459,8 @@ __global__ void __launch_bounds__(192, 1)
             }
             ptx::mma_commit(acc_full);
         }
-    } else {
-        // Dequant + epilogue warps: row r of the 128-row tile = TMEM lane r.
+    } else if (warp < 6) {
+        // Dequant warps: row r of the 128-row tile = TMEM lane r.
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
         for (int i = 0; i < nst && ok; ++i) {
@@ -478,49 +480,66 @@ __global__ void __launch_bounds__(192, 1)
             if (threadIdx.x == 64) stamp(3, i);
             ptx::mbar_arrive(&a_full[a]);
         }
-        // Epilogue (after the previous kernel: it may still read what we overwrite).
+    }
+    if (warp >= 2) {
+        // Epilogue, 8 warps: warp w and w + 4 read the same TMEM lanes (quarter
+        // w % 4, thread = weight row) and split the BN token columns in halves.
+        // It runs after the previous kernel (which may still read what it overwrites).
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        constexpr int HALF = BN / 2;
+        const int cb = warp >= 6 ? HALF : 0;
         pdl_wait();
-        if (ok && ptx::mbar_wait(acc_full, 0)) {
-            if (threadIdx.x == 64) stamp(4, 0);
-            ptx::tc_fence_after();
-            const int64_t n = (int64_t)n_tile * TILE_N + r;
-            const float bias_n = (e.bias && n < N) ? e.bias[n] : 0.0f;
-            const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-            if (tma_epi) {
-                // Stage the [BN tokens][128 features] tile in the idle ring, then one
-                // TMA tensor store per plane writes whole row segments.
-                float* sf = reinterpret_cast<float*>(st_ring);
-                __half* sh = reinterpret_cast<__half*>(st_ring);
-                const bool partial = tma_epi == 2;  // split-K: raw fp32 partial sums, no epilogue op
-                if (!partial && e.kind == VKB_EPI_RESIDUAL) {
-                    if (threadIdx.x == 64) {
-                        ptx::mbar_expect_tx(res_full, BN * TILE_N * 4);
-                        ptx::tma_load_2d(st_ring, &rmap, res_full, n_tile * TILE_N, m_tile * BN);
-                    }
-                    if (!ptx::mbar_wait(res_full, 0)) ok = false;
+        const bool go = ok && ptx::mbar_wait(acc_full, 0);
+        if (threadIdx.x == 64) stamp(4, 0);
+        ptx::tc_fence_after();
+        const int64_t n = (int64_t)n_tile * TILE_N + r;
+        const float bias_n = (go && e.bias && n < N) ? e.bias[n] : 0.0f;
+        const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+        // 32 accumulator columns per tcgen05.ld (16 for narrow tiles)
+        constexpr int CW = HALF >= 32 ? 32 : 16;
+        auto load_cols = [&](int c0, uint32_t(&v)[CW]) {
+            if constexpr (CW == 32) ptx::tmem_ld32(lane_addr + c0, v);
+            else ptx::tmem_ld16(lane_addr + c0, v);
+            if (C::STACK) {
+                uint32_t v2[CW];
+                if constexpr (CW == 32) ptx::tmem_ld32(lane_addr + BN + c0, v2);
+                else ptx::tmem_ld16(lane_addr + BN + c0, v2);
+                ptx::tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < CW; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(v2[j]));
+            } else {
+                ptx::tmem_ld_wait();
+            }
+        };
+        if (tma_epi) {
+            // Stage the [BN tokens][128 features] tile in the idle ring, then one
+            // TMA tensor store per plane writes whole row segments.
+            float* sf = reinterpret_cast<float*>(st_ring);
+            __half* sh = reinterpret_cast<__half*>(st_ring);
+            const bool partial = tma_epi == 2;  // split-K: raw fp32 partial sums, no epilogue op
+            bool good = go;
+            if (good && !partial && e.kind == VKB_EPI_RESIDUAL) {
+                if (threadIdx.x == 64) {
+                    ptx::mbar_expect_tx(res_full, BN * TILE_N * 4);
+                    ptx::tma_load_2d(st_ring, &rmap, res_full, n_tile * TILE_N, m_tile * BN);
                 }
+                if (!ptx::mbar_wait(res_full, 0)) good = false;
+            }
+            if (good) {
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN && ok; c0 += 16) {
-                    uint32_t v[16];
-                    ptx::tmem_ld16(lane_addr + c0, v);
-                    if (C::STACK) {
-                        uint32_t v2[16];
-                        ptx::tmem_ld16(lane_addr + BN + c0, v2);
-                        ptx::tmem_ld_wait();
+                for (int c0 = cb; c0 < cb + HALF; c0 += CW) {
+                    uint32_t v[CW];
+                    load_cols(c0, v);
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(v2[j]));
-                    } else {
-                        ptx::tmem_ld_wait();
-                    }
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
+                    for (int j = 0; j < CW; ++j) {
                         const int row = c0 + j;
                         if (partial) {
                             sf[row * TILE_N + r] = __uint_as_float(v[j]);
                             continue;
                         }
                         float x = __uint_as_float(v[j]) + bias_n;
-                        if (e.kind == VKB_EPI_GELU) x = gelu_as(x);
+                        if (e.kind == VKB_EPI_GELU) x = gelu_as_fast(x);
                         else if (e.kind == VKB_EPI_SCALE) x = n < e.n_scaled ? x * e.scale : x;
                         else if (e.kind == VKB_EPI_RESIDUAL) x += sf[row * TILE_N + r];
                         if (e.out_fmt == VKB_DT_F32) {
@@ -532,41 +551,34 @@ __global__ void __launch_bounds__(192, 1)
                         }
                     }
                 }
-                ptx::fence_proxy_async_smem();
-                ptx::named_bar(1, 128);
-                if (threadIdx.x == 64 && ok && partial) {
-                    ptx::tma_store_3d(&omap, st_ring, n_tile * TILE_N, m_tile * BN, split);
-                    ptx::bulk_commit();
-                    ptx::bulk_wait_read0();
-                } else if (threadIdx.x == 64 && ok) {
-                    ptx::tma_store_2d(&omap, st_ring, n_tile * TILE_N, m_tile * BN);
-                    if (e.out_fmt == VKB_DT_F16X2) ptx::tma_store_2d(&omap_lo, sh + BN * TILE_N, n_tile * TILE_N, m_tile * BN);
-                    ptx::bulk_commit();
-                    ptx::bulk_wait_read0();
-                }
-            } else {
+            }
+            ptx::fence_proxy_async_smem();
+            // every epilogue thread reaches this barrier; the store needs all of them good
+            const bool all_good = !ptx::named_bar_or(1, 256, !good);
+            if (!good) ok = false;
+            if (threadIdx.x == 64 && all_good && partial) {
+                ptx::tma_store_3d(&omap, st_ring, n_tile * TILE_N, m_tile * BN, split);
+                ptx::bulk_commit();
+                ptx::bulk_wait_read0();
+            } else if (threadIdx.x == 64 && all_good) {
+                ptx::tma_store_2d(&omap, st_ring, n_tile * TILE_N, m_tile * BN);
+                if (e.out_fmt == VKB_DT_F16X2) ptx::tma_store_2d(&omap_lo, sh + BN * TILE_N, n_tile * TILE_N, m_tile * BN);
+                ptx::bulk_commit();
+                ptx::bulk_wait_read0();
+            }
+        } else if (go) {
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
-                    uint32_t v[16];
-                    ptx::tmem_ld16(lane_addr + c0, v);
-                    if (C::STACK) {
-                        uint32_t v2[16];
-                        ptx::tmem_ld16(lane_addr + BN + c0, v2);
-                        ptx::tmem_ld_wait();
+            for (int c0 = cb; c0 < cb + HALF; c0 += CW) {
+                uint32_t v[CW];
+                load_cols(c0, v);
+                if (n < N) {
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(v2[j]));
-                    } else {
-                        ptx::tmem_ld_wait();
-                    }
-                    if (n < N) {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            int64_t m = (int64_t)m_tile * BN + c0 + j;
-                            if (m < M) {
-                                float acc = __uint_as_float(v[j]);
-                                if (n_splits == 1) epi_store(e, m, n, acc, bias_n);
-                                else ws[((int64_t)split * M + m) * N + n] = acc;
-                            }
+                    for (int j = 0; j < CW; ++j) {
+                        int64_t m = (int64_t)m_tile * BN + c0 + j;
+                        if (m < M) {
+                            float acc = __uint_as_float(v[j]);
+                            if (n_splits == 1) epi_store(e, m, n, acc, bias_n);
+                            else ws[((int64_t)split * M + m) * N + n] = acc;
                         }
                     }
                 }
@@ -711,7 +723,7 @@ static void launch_tc(vkb_context* ctx, const vkb_weight* w, int64_t m, const __
     }
     int n_tiles = (int)(w->n_pad / TILE_N);
     dim3 grid((unsigned)(n_tiles * m_tiles * splits));
-    launch_pdl(ctx, tc_gemm_kernel<FMT, BN, SPLIT>, grid, 192, C::SMEM, 
+    launch_pdl(ctx, tc_gemm_kernel<FMT, BN, SPLIT>, grid, 320, C::SMEM, 
         map, map_lo, w->qs.as<uint8_t>(), w->sc.as<uint8_t>(), w->k, w->n, m, n_tiles, m_tiles, stages_per_split,
         splits, ws, e, device_err_flag(ctx), ctx->trace, omap, omap_lo, rmap, tma_epi);
     VKB_CUDA(cudaGetLastError());
