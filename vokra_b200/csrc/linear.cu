@@ -290,13 +290,13 @@ void run_split_f16(vkb_context* ctx, const float* x, int64_t n, __half* y, bool 
 // K=16 step issues W_hi.X_hi + W_hi.X_lo + W_lo.X_hi, which reproduces the
 // fp32 product to about 2^-21 relative (the W_lo.X_lo term is below that).
 //
-// Warp roles (320 threads):
+// Warp roles (64 + 128 * EG threads):
 //   warp 0      : producer — TMA for X, bulk copies for the raw weight stage
 //   warp 1      : TMEM allocator; lane 0 issues tcgen05.mma and commits
 //   warps 2..5  : dequantize raw stage -> A tile(s); then the epilogue
 //                 (thread = one weight row = one TMEM lane)
-//   warps 6..9  : epilogue only, on the same TMEM lanes as warps 2..5 and the
-//                 other half of the token columns
+//   warps 6..   : epilogue only (up to 3 more groups of 4 warps), on the same
+//                 TMEM lanes as warps 2..5 and their share of the token columns
 // Rings: S stages of (X tile(s) + raw weights) in shared memory, AS stages of
 // A tiles in tensor memory.
 // Every mbarrier wait is bounded; on timeout the kernel records an error flag
@@ -329,12 +329,16 @@ struct TcCfg {
                                           : NEED_COLS <= 256 ? 256 : 512;
     static_assert(NEED_COLS <= 512, "tensor memory budget");
     static_assert(S >= 2, "pipeline needs at least two stages");
+    // epilogue groups of 4 warps (one per TMEM lane quarter), each taking
+    // BN / EG token columns; group 0 is also the dequant group
+    static constexpr int EG = BN / 16 < 4 ? BN / 16 : 4;
+    static constexpr int THREADS = 64 + 128 * EG;
 };
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 template <int FMT, int BN, bool SPLIT>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_lo,
                    const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc, int64_t K, int64_t N, int64_t M,
                    int n_tiles, int m_tiles, int stages_per_split, int n_splits, float* ws, Epi e, int* err,
@@ -482,13 +486,14 @@ __global__ void __launch_bounds__(320, 1)
         }
     }
     if (warp >= 2) {
-        // Epilogue, 8 warps: warp w and w + 4 read the same TMEM lanes (quarter
-        // w % 4, thread = weight row) and split the BN token columns in halves.
-        // It runs after the previous kernel (which may still read what it overwrites).
+        // Epilogue, EG groups of 4 warps: warps w, w + 4, ... read the same TMEM
+        // lanes (quarter w % 4, thread = weight row) and split the BN token
+        // columns. It runs after the previous kernel (which may still read what
+        // it overwrites).
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
-        constexpr int HALF = BN / 2;
-        const int cb = warp >= 6 ? HALF : 0;
+        constexpr int HALF = BN / C::EG;  // columns per group
+        const int cb = ((warp - 2) >> 2) * HALF;
         pdl_wait();
         const bool go = ok && ptx::mbar_wait(acc_full, 0);
         if (threadIdx.x == 64) stamp(4, 0);
@@ -554,7 +559,7 @@ __global__ void __launch_bounds__(320, 1)
             }
             ptx::fence_proxy_async_smem();
             // every epilogue thread reaches this barrier; the store needs all of them good
-            const bool all_good = !ptx::named_bar_or(1, 256, !good);
+            const bool all_good = !ptx::named_bar_or(1, 128 * C::EG, !good);
             if (!good) ok = false;
             if (threadIdx.x == 64 && all_good && partial) {
                 ptx::tma_store_3d(&omap, st_ring, n_tile * TILE_N, m_tile * BN, split);
@@ -723,7 +728,7 @@ static void launch_tc(vkb_context* ctx, const vkb_weight* w, int64_t m, const __
     }
     int n_tiles = (int)(w->n_pad / TILE_N);
     dim3 grid((unsigned)(n_tiles * m_tiles * splits));
-    launch_pdl(ctx, tc_gemm_kernel<FMT, BN, SPLIT>, grid, 320, C::SMEM, 
+    launch_pdl(ctx, tc_gemm_kernel<FMT, BN, SPLIT>, grid, C::THREADS, C::SMEM, 
         map, map_lo, w->qs.as<uint8_t>(), w->sc.as<uint8_t>(), w->k, w->n, m, n_tiles, m_tiles, stages_per_split,
         splits, ws, e, device_err_flag(ctx), ctx->trace, omap, omap_lo, rmap, tma_epi);
     VKB_CUDA(cudaGetLastError());
