@@ -282,21 +282,44 @@ __global__ void im2col_ct_kernel(const float* __restrict__ x, int B, int C, int 
     if (split) col[total + i] = __float2half_rn(v - __half2float(hi));
 }
 
-// col[b*To + t][c*3 + kk] = x[b*T + t*stride + kk - 1][c]
+// col[b*To + t][c*3 + kk] = x[b*T + t*stride + kk - 1][c]; one thread per
+// (output row, 8 channels): three 16-byte tap loads, interleaved in registers
+// into 24 contiguous halves (48 bytes).
 __global__ void im2col_tc_kernel(const __half* __restrict__ x, int B, int C, int T, int To, int stride,
                                  __half* __restrict__ col, int planes) {
     pdl_entry();
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t total = (int64_t)B * To * C * 3;
-    if (i >= total) return;
-    const int64_t r = i / (C * 3);
-    const int cc = (int)(i % (C * 3));
-    const int c = cc / 3, kk = cc % 3;
-    const int b = (int)(r / To), t = (int)(r % To);
-    const int p = t * stride + kk - 1;
-    const int64_t in_plane = (int64_t)B * T * C;
-    for (int pl = 0; pl < planes; ++pl)
-        col[pl * total + i] = (p >= 0 && p < T) ? x[pl * in_plane + ((int64_t)b * T + p) * C + c] : __float2half_rn(0.0f);
+    const int nchunk = C >> 3;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= B * To * nchunk) return;
+    const int r = i / nchunk, ch = i - r * nchunk;
+    const int b = r / To, t = r - b * To;
+    const int64_t in_plane = (int64_t)B * T * C, out_plane = (int64_t)B * To * C * 3;
+    for (int pl = 0; pl < planes; ++pl) {
+        uint4 tap[3];
+#pragma unroll
+        for (int kk = 0; kk < 3; ++kk) {
+            const int p = t * stride + kk - 1;
+            tap[kk] = (p >= 0 && p < T)
+                          ? __ldg(reinterpret_cast<const uint4*>(x + pl * in_plane + ((int64_t)b * T + p) * C) + ch)
+                          : make_uint4(0, 0, 0, 0);
+        }
+        const uint16_t* h0 = reinterpret_cast<const uint16_t*>(&tap[0]);
+        const uint16_t* h1 = reinterpret_cast<const uint16_t*>(&tap[1]);
+        const uint16_t* h2 = reinterpret_cast<const uint16_t*>(&tap[2]);
+        uint32_t o[12];
+#pragma unroll
+        for (int q = 0; q < 12; ++q) {
+            // output halves 2q and 2q+1: channel (2q)/3 tap (2q)%3, channel (2q+1)/3 tap (2q+1)%3
+            const int e0 = 2 * q, e1 = 2 * q + 1;
+            const uint16_t* s0 = (e0 % 3 == 0) ? h0 : (e0 % 3 == 1) ? h1 : h2;
+            const uint16_t* s1 = (e1 % 3 == 0) ? h0 : (e1 % 3 == 1) ? h1 : h2;
+            o[q] = (uint32_t)s0[e0 / 3] | ((uint32_t)s1[e1 / 3] << 16);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(col + pl * out_plane + (int64_t)r * C * 3 + ch * 24);
+        dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
+    }
 }
 
 static int conv_out(int T, int stride) { return (T + 2 - 3) / stride + 1; }
@@ -313,27 +336,40 @@ void run_im2col_ct(vkb_context* ctx, const float* x, int B, int C, int T, int st
 
 void run_im2col_tc(vkb_context* ctx, const __half* x, int B, int C, int T, int stride, __half* col, int planes) {
     int To = conv_out(T, stride);
-    int64_t total = (int64_t)B * To * C * 3;
+    if (C % 8 || ((uintptr_t)x & 15) || ((uintptr_t)col & 15))
+        fail(VKB_ERROR_UNSUPPORTED_OP, "im2col: channels must be a multiple of 8 with 16-byte aligned buffers");
+    const int64_t total = (int64_t)B * To * (C / 8);
+    if (total >= (int64_t(1) << 31)) fail(VKB_ERROR_UNSUPPORTED_OP, "im2col: too many rows");
     launch_pdl(ctx, im2col_tc_kernel, (unsigned)((total + 255) / 256), 256, 0, x, B, C, T, To, stride, col, planes);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
 
+// 4 channels per thread (C % 4 == 0).
 __global__ void add_pos_kernel(const __half* __restrict__ y, const float* __restrict__ pos, int B, int T, int C,
                                float* __restrict__ h, int planes) {
     pdl_entry();
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t total = (int64_t)B * T * C;
-    if (i >= total) return;
-    const int64_t tc = i % ((int64_t)T * C);
-    float v = __half2float(y[i]);
-    if (planes == 2) v += __half2float(y[total + i]);
-    h[i] = v + pos[tc];
+    const int i4 = blockIdx.x * blockDim.x + threadIdx.x;  // float4 index
+    const int total4 = B * T * C / 4;
+    if (i4 >= total4) return;
+    const int tc4 = i4 % (T * C / 4);
+    const uint2 hv = __ldg(reinterpret_cast<const uint2*>(y) + i4);
+    float2 a = __half22float2(*reinterpret_cast<const __half2*>(&hv.x));
+    float2 c = __half22float2(*reinterpret_cast<const __half2*>(&hv.y));
+    if (planes == 2) {
+        const uint2 lv = __ldg(reinterpret_cast<const uint2*>(y + (int64_t)total4 * 4) + i4);
+        const float2 la = __half22float2(*reinterpret_cast<const __half2*>(&lv.x));
+        const float2 lc = __half22float2(*reinterpret_cast<const __half2*>(&lv.y));
+        a.x += la.x; a.y += la.y; c.x += lc.x; c.y += lc.y;
+    }
+    const float4 p = __ldg(reinterpret_cast<const float4*>(pos) + tc4);
+    reinterpret_cast<float4*>(h)[i4] = make_float4(a.x + p.x, a.y + p.y, c.x + p.z, c.y + p.w);
 }
 
 void run_add_pos(vkb_context* ctx, const __half* y, const float* pos, int B, int T, int C, float* h, int planes) {
-    int64_t total = (int64_t)B * T * C;
-    launch_pdl(ctx, add_pos_kernel, (unsigned)((total + 255) / 256), 256, 0, y, pos, B, T, C, h, planes);
+    const int64_t total4 = (int64_t)B * T * C / 4;
+    if (C % 4 || total4 >= (int64_t(1) << 31)) fail(VKB_ERROR_UNSUPPORTED_OP, "add_pos: shape");
+    launch_pdl(ctx, add_pos_kernel, (unsigned)((total4 + 255) / 256), 256, 0, y, pos, B, T, C, h, planes);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }

@@ -1,6 +1,6 @@
 // enc_attn.cu — non-causal multi-head attention over a whole window (the
 // Whisper encoder's 1500x1500 self-attention, whisper/nn.rs:209-300 with
-// causal=false), FlashAttention-2 style: 64 queries per CTA (16 per warp),
+// causal=false), FlashAttention-2 style: 128 queries per CTA (16 per warp),
 // K/V tiles of 64 keys double-buffered in shared memory with cp.async,
 // S = Q K^T and O += P V on m16n8k16 f16 tensor-core MMAs with fp32
 // accumulators, online softmax in fp32 registers.
@@ -16,7 +16,8 @@ namespace vkb {
 
 namespace {
 constexpr int HD = 64;       // head dim
-constexpr int BQ = 64;       // queries per CTA
+constexpr int BQ = 128;      // queries per CTA (8 warps)
+constexpr int NT = 256;      // threads
 constexpr int BK = 64;       // keys per tile
 constexpr int LDS = HD + 8;  // padded smem row (halves)
 
@@ -54,13 +55,14 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Loads a [64 rows][64 halves] tile (rows r0.., column col) into padded smem.
+// Loads a [ROWS rows][64 halves] tile (rows r0.., column col) into padded smem.
+template <int ROWS>
 __device__ __forceinline__ void load_tile(__half* dst, const __half* base, int64_t row0, int rows_valid, int64_t ld,
                                           int col) {
     const int tid = threadIdx.x;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        int chunk = tid + i * 128;  // 512 chunks of 8 halves
+    for (int i = 0; i < ROWS * 8 / NT; ++i) {
+        int chunk = tid + i * NT;  // ROWS * 8 chunks of 8 halves
         int r = chunk >> 3, c8 = (chunk & 7) * 8;
         bool valid = r < rows_valid;
         const __half* src = base + (row0 + (valid ? r : 0)) * ld + col + c8;
@@ -69,13 +71,14 @@ __device__ __forceinline__ void load_tile(__half* dst, const __half* base, int64
 }
 }  // namespace
 
-__global__ void __launch_bounds__(128) enc_attn_kernel(const __half* __restrict__ qkv, int64_t ld, int kcol, int vcol,
-                                                       int T, int n_head, __half* __restrict__ ctx, int64_t ctx_ld,
-                                                       __half* __restrict__ ctx_lo) {
+__global__ void __launch_bounds__(NT) enc_attn_kernel(const __half* __restrict__ qkv, int64_t ld, int kcol, int vcol,
+                                                      int T, int n_head, __half* __restrict__ ctx, int64_t ctx_ld,
+                                                      __half* __restrict__ ctx_lo) {
     pdl_entry();
-    __shared__ __align__(128) __half sQ[BQ * LDS];
-    __shared__ __align__(128) __half sK[2][BK * LDS];
-    __shared__ __align__(128) __half sV[2][BK * LDS];
+    extern __shared__ __align__(128) __half enc_smem[];
+    __half* sQ = enc_smem;                             // [BQ][LDS]
+    auto sK = [&](int i) { return sQ + (BQ + i * BK) * LDS; };        // 2 x [BK][LDS]
+    auto sV = [&](int i) { return sQ + (BQ + (2 + i) * BK) * LDS; };  // 2 x [BK][LDS]
     const int qt = blockIdx.x;
     const int bh = blockIdx.y;
     const int b = bh / n_head, h = bh % n_head;
@@ -83,9 +86,9 @@ __global__ void __launch_bounds__(128) enc_attn_kernel(const __half* __restrict_
     const int64_t row_base = (int64_t)b * T;
     const int q0 = qt * BQ;
 
-    load_tile(sQ, qkv, row_base + q0, min(BQ, T - q0), ld, h * HD);
-    load_tile(sK[0], qkv, row_base, min(BK, T), ld, kcol + h * HD);
-    load_tile(sV[0], qkv, row_base, min(BK, T), ld, vcol + h * HD);
+    load_tile<BQ>(sQ, qkv, row_base + q0, min(BQ, T - q0), ld, h * HD);
+    load_tile<BK>(sK(0), qkv, row_base, min(BK, T), ld, kcol + h * HD);
+    load_tile<BK>(sV(0), qkv, row_base, min(BK, T), ld, vcol + h * HD);
     cp_async_commit();
 
     // Q fragments: 16 rows of this warp x 64 dims = 4 k-steps.
@@ -102,8 +105,8 @@ __global__ void __launch_bounds__(128) enc_attn_kernel(const __half* __restrict_
         const int buf = kt & 1;
         if (kt + 1 < n_tiles) {
             int k0 = (kt + 1) * BK;
-            load_tile(sK[buf ^ 1], qkv, row_base + k0, min(BK, T - k0), ld, kcol + h * HD);
-            load_tile(sV[buf ^ 1], qkv, row_base + k0, min(BK, T - k0), ld, vcol + h * HD);
+            load_tile<BK>(sK(buf ^ 1), qkv, row_base + k0, min(BK, T - k0), ld, kcol + h * HD);
+            load_tile<BK>(sV(buf ^ 1), qkv, row_base + k0, min(BK, T - k0), ld, vcol + h * HD);
             cp_async_commit();
             cp_async_wait<1>();
         } else {
@@ -124,7 +127,7 @@ __global__ void __launch_bounds__(128) enc_attn_kernel(const __half* __restrict_
         for (int j = 0; j < 8; ++j)
 #pragma unroll
             for (int e = 0; e < 4; ++e) s[j][e] = 0.0f;
-        const __half* K = sK[buf];
+        const __half* K = sK(buf);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
@@ -155,13 +158,16 @@ __global__ void __launch_bounds__(128) enc_attn_kernel(const __half* __restrict_
             for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fmaxf(s[j][2 * hr], s[j][2 * hr + 1]));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            // scores are in natural-log units; exp(x - m) = exp2((x - m) * log2 e)
+            constexpr float L2E = 1.4426950408889634f;
             float mn = fmaxf(m_r[hr], mx);
-            float corr = __expf(m_r[hr] - mn);
+            float corr = exp2f((m_r[hr] - mn) * L2E);
+            const float mb = mn * L2E;
             float rs = 0.0f;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                float p0 = __expf(s[j][2 * hr] - mn);
-                float p1 = __expf(s[j][2 * hr + 1] - mn);
+                float p0 = exp2f(fmaf(s[j][2 * hr], L2E, -mb));
+                float p1 = exp2f(fmaf(s[j][2 * hr + 1], L2E, -mb));
                 s[j][2 * hr] = p0;
                 s[j][2 * hr + 1] = p1;
                 rs += p0 + p1;
@@ -177,7 +183,7 @@ __global__ void __launch_bounds__(128) enc_attn_kernel(const __half* __restrict_
             }
         }
         // O += P V : P (16 x 64 keys) from the S accumulators, V via ldmatrix.trans
-        const __half* V = sV[buf];
+        const __half* V = sV(buf);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {  // 16 keys per k-step
             uint32_t a0 = pack_h2(s[2 * kk][0], s[2 * kk][1]);
@@ -223,7 +229,13 @@ void run_encoder_attention(vkb_context* ctx, const __half* qkv, int64_t ld, int 
     if (ld % 8 || kcol % 8 || vcol % 8 || out_ld % 2)
         fail(VKB_ERROR_INVALID_ARGUMENT, "encoder attention: rows must be 16-byte aligned");
     dim3 grid((unsigned)((T + BQ - 1) / BQ), (unsigned)(n_windows * n_head));
-    launch_pdl(ctx, enc_attn_kernel, grid, 128, 0, qkv, ld, kcol, vcol, T, n_head, out, out_ld, out_lo);
+    const size_t smem = (size_t)(BQ + 4 * BK) * LDS * sizeof(__half);
+    static bool attr = false;
+    if (!attr) {
+        VKB_CUDA(cudaFuncSetAttribute(enc_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr = true;
+    }
+    launch_pdl(ctx, enc_attn_kernel, grid, NT, smem, qkv, ld, kcol, vcol, T, n_head, out, out_ld, out_lo);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
