@@ -193,11 +193,29 @@ def run_reference(args, rank):
 
 
 def run_kernel_only(args):
-    """The encoder fc1 GEMM alone (the profiling target of profiles/tc_gemm_q4_0_fc1.md)."""
+    """One kernel alone, for ncu: the encoder fc1 GEMM, or the decode cross-attention."""
     import ctypes as C
     import torch
     from vokra_b200 import _lib, ops, synth
     ctx = ops.Context(0)
+    if args.kernel == "xattn":
+        B, T, H, D = args.clips, 1500, 20, 64
+        W = H * D
+        g = torch.Generator(device="cuda").manual_seed(3)
+        kq = torch.empty((B * T, W), dtype=torch.int8, device="cuda")
+        vq = torch.empty_like(kq)
+        kd = torch.empty((B * T, W // 32), dtype=torch.float16, device="cuda")
+        vd = torch.empty_like(kd)
+        for q8, dd in ((kq, kd), (vq, vd)):
+            ops.quantize_rows_q8_0(ctx, torch.randn((B * T, W), device="cuda", generator=g), q8, dd)
+        q = torch.randn((B, W), device="cuda", generator=g) * 0.125
+        seq = torch.arange(B, dtype=torch.int32, device="cuda")
+        out = torch.empty((B, W), device="cuda")
+        for _ in range(3):
+            ops.attention_dense(ctx, q, seq, kq, vq, T, H, D, out, k_scale=kd, v_scale=vd)
+        torch.cuda.synchronize()
+        print(json.dumps({"kernel": args.kernel, "streams": B, "keys": T, "width": W, "ok": True}))
+        return
     if args.precision == "f16":
         _lib.check(_lib.load().vkb_context_set_precision(ctx.h, _lib.PREC_F16))
     M = 1500 if args.kernel == "fc1_m1500" else args.clips * 1500
@@ -229,8 +247,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=128)
     ap.add_argument("--precision", default="split", choices=["split", "f16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", default=None, choices=["fc1", "fc1_m1500"],
-                    help="run only the encoder fc1 GEMM (M = clips x 1500, or 1500) three times, for ncu")
+    ap.add_argument("--kernel", default=None, choices=["fc1", "fc1_m1500", "xattn"],
+                    help="run only one kernel three times, for ncu: the encoder fc1 GEMM (M = clips x 1500, or "
+                         "1500) or the decode cross-attention over the Q8_0 store (clips streams x 1500 keys)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
