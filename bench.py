@@ -121,6 +121,45 @@ def synthetic_logmels(n: int, n_mels: int, n_frames: int, seed: int) -> np.ndarr
 
 
 # ---------------------------------------------------------------------------
+# Multi-rank host logic (one process per GPU; utterances shard by request, no
+# collective on the data path). Kept free of CUDA so it runs under gloo on CPU.
+# ---------------------------------------------------------------------------
+def rank_input_seed(rank: int) -> int:
+    """Each rank decodes its own clips: distinct seeded inputs per rank."""
+    return 1000 + rank
+
+
+def init_process_group(world: int, local_rank: int, backend: str):
+    """Joins the job's process group (torchrun's env:// rendezvous on 127.0.0.1)."""
+    import torch
+    import torch.distributed as dist
+    if world <= 1:
+        return None
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    if backend == "nccl":
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
+    else:
+        dist.init_process_group(backend)
+    return dist
+
+
+def max_over_ranks(ms: float, dist, device) -> float:
+    """The job's time is the slowest rank's device time."""
+    if dist is None:
+        return ms
+    import torch
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_throughput(world: int, clips: int, steps: int, tokens: int, ms: float):
+    """Whole-job audio-seconds/s and decode tokens/s: every rank's clips over the max-over-ranks time."""
+    audio = world * clips * CLIP_SECONDS * steps
+    return audio / (ms / 1e3), world * clips * tokens * steps / (ms / 1e3)
+
+
+# ---------------------------------------------------------------------------
 # CPU leg: the oracle (reference algorithm restated in C++) on a bounded sample
 # ---------------------------------------------------------------------------
 def cpu_sample(arch, qtag, qname, n_tokens: int, threads: int):
@@ -264,14 +303,11 @@ def main():
         return
 
     import torch
-    import torch.distributed as dist
     torch.cuda.set_device(local_rank)
-    if world > 1:
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
+    dist = init_process_group(world, local_rank, "nccl")
 
     def barrier():
-        if world > 1:
+        if dist is not None:
             dist.barrier()
 
     from vokra_b200 import _lib, ops, synth, whisper
@@ -288,7 +324,7 @@ def main():
     B, NT = args.clips, args.tokens
     sess = whisper.Session(model, max_streams=B, max_step_tokens=B * PREFIX, max_clips=B, cross_kv_q8=True)
     dev = f"cuda:{local_rank}"
-    logmel_host = torch.from_numpy(synthetic_logmels(B, arch.n_mels, 2 * arch.n_audio_ctx, 1000 + rank)).pin_memory()
+    logmel_host = torch.from_numpy(synthetic_logmels(B, arch.n_mels, 2 * arch.n_audio_ctx, rank_input_seed(rank))).pin_memory()
     logmel_dev = logmel_host.to(dev)
     rng = np.random.default_rng(2 + rank)
     toks = rng.integers(0, arch.n_vocab, (NT, B)).astype(np.int32)
@@ -329,11 +365,7 @@ def main():
         ev1.record(stream)
         torch.cuda.synchronize()
         barrier()
-        ms = ev0.elapsed_time(ev1)
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
+        ms = max_over_ranks(ev0.elapsed_time(ev1), dist, dev)
         return ms, ctx.launch_count - l0
 
     phys = local_rank
@@ -347,10 +379,8 @@ def main():
         ms, launches = timed(False)
     ms_e2e, _ = timed(True)
 
-    audio = world * B * CLIP_SECONDS * args.steps
-    value = audio / (ms / 1e3)
-    tok_s = world * B * NT * args.steps / (ms / 1e3)
-    e2e_value = audio / (ms_e2e / 1e3)
+    value, tok_s = job_throughput(world, B, args.steps, NT, ms)
+    e2e_value, _ = job_throughput(world, B, args.steps, NT, ms_e2e)
 
     # Dominant kernel: the encoder MLP fc1 GEMM (Q4_0, M = 64 x 1500 tokens, N = 5120, K = 1280,
     # f16 hi+lo activations in the default precision), timed alone with CUDA events.

@@ -1,0 +1,65 @@
+"""The N>1 host path of bench.py on CPU: two gloo ranks on 127.0.0.1.
+
+One process per GPU in the real job; here each rank is a CPU process running
+the same host logic: per-rank inputs (utterances shard by request, no
+collective on the data path), the max-over-ranks time, the whole-job
+throughput, and the reference arm that only rank 0 runs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _rank_main(rank, world, port, out_dir):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import bench
+    dist = bench.init_process_group(world, rank, "gloo")
+    try:
+        x = bench.synthetic_logmels(2, 8, 16, bench.rank_input_seed(rank))
+        # a rank-dependent device time; the job time is the slowest rank's
+        ms = 10.0 + 20.0 * rank
+        job_ms = bench.max_over_ranks(ms, dist, "cpu")
+        value, tok_s = bench.job_throughput(world, clips=64, steps=3, tokens=128, ms=job_ms)
+
+        class A:
+            warmup, steps, tokens, gpus = 0, 1, 1, world
+        printed = rank != 0  # rank 0 would run the CPU reference; only check that the others do nothing
+        if rank != 0:
+            import io, contextlib
+            buf = io.StringIO()
+            with contextlib.redirect_stdout(buf):
+                bench.run_reference(A, rank)
+            printed = buf.getvalue() == ""
+        np.savez(os.path.join(out_dir, f"r{rank}.npz"), x=x, job_ms=job_ms, value=value, tok_s=tok_s,
+                 ref_silent=printed)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_ranks_gloo(tmp_path):
+    import torch.multiprocessing as mp
+    port = _free_port()
+    mp.spawn(_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    r = [np.load(tmp_path / f"r{i}.npz") for i in range(2)]
+    # each rank decodes different utterances
+    assert not np.array_equal(r[0]["x"], r[1]["x"])
+    # max over ranks, identical on every rank
+    assert float(r[0]["job_ms"]) == float(r[1]["job_ms"]) == 30.0
+    # whole-job throughput: both ranks' clips over the slowest rank's time
+    assert float(r[0]["value"]) == pytest.approx(2 * 64 * 30.0 * 3 / 0.030)
+    assert float(r[0]["tok_s"]) == pytest.approx(2 * 64 * 128 * 3 / 0.030)
+    # the reference arm prints from rank 0 only
+    assert bool(r[1]["ref_silent"])
