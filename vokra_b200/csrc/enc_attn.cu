@@ -11,6 +11,7 @@
 // window b are b*T .. b*T+T-1.
 #include "common.cuh"
 #include "enc_attn.cuh"
+#include <cstdlib>
 
 namespace vkb {
 
@@ -224,8 +225,13 @@ __global__ void __launch_bounds__(NT) enc_attn_kernel(const __half* __restrict__
 }
 
 void run_encoder_attention(vkb_context* ctx, const __half* qkv, int64_t ld, int kcol, int vcol, int n_windows, int T,
-                           int n_head, int d_head, __half* out, int64_t out_ld, __half* out_lo) {
+                           int n_head, int d_head, __half* out, int64_t out_ld, __half* out_lo, __half* vt_scratch,
+                           size_t scratch_halves) {
     if (d_head != HD) fail(VKB_ERROR_UNSUPPORTED_OP, "encoder attention: d_head must be 64");
+    static const bool legacy = std::getenv("VKB_ENC_ATTN_MMA_SYNC") != nullptr;
+    if (!legacy && run_encoder_attention_tc(ctx, qkv, ld, kcol, vcol, n_windows, T, n_head, out, out_ld, out_lo,
+                                            vt_scratch, scratch_halves))
+        return;
     if (ld % 8 || kcol % 8 || vcol % 8 || out_ld % 2)
         fail(VKB_ERROR_INVALID_ARGUMENT, "encoder attention: rows must be 16-byte aligned");
     dim3 grid((unsigned)((T + BQ - 1) / BQ), (unsigned)(n_windows * n_head));

@@ -399,8 +399,9 @@ void session_encode(vkb_session* s, int n, const float* logmel, const int32_t* s
         x.n_scaled = d;
         run_linear_ex(ctx, L.qkv.get(), M, xln, AF, L.qkv_b.as<float>(), bufB, VKB_DT_F16, VKB_EPI_SCALE, nullptr,
                       scale, ws, nullptr, x);
+        // bufA (the MLP hidden) is idle here: it holds the transposed V of the tensor-core attention
         run_encoder_attention(ctx, bufB, 3 * d, (int)d, (int)(2 * d), n, (int)T, D.n_audio_head, 64, ectx, d,
-                              split ? ectx + M * d : nullptr);
+                              split ? ectx + M * d : nullptr, reinterpret_cast<__half*>(s->bufA.p), s->bufA.n / 2);
         run_linear(ctx, L.o.get(), M, ectx, AF, L.o_b.as<float>(), h, VKB_DT_F32, VKB_EPI_RESIDUAL, h, 1.0f, ws,
                    nullptr);
         run_layer_norm(ctx, h, M, (int)d, L.ln2g.as<float>(), L.ln2b.as<float>(), LN_EPS, xln, AF);
