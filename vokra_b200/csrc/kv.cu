@@ -87,6 +87,114 @@ __global__ void kv_append_kernel(const float* __restrict__ k, const float* __res
     q8_0_block_warp(src[lane], lane, q, d);
 }
 
+// ---------------------------------------------------------------------------
+// Fused decode self-attention (one query per stream, SEQUENCE layout, d_head
+// 64): one CTA of 256 threads per (stream, group of 4 heads = 256 channels).
+// It appends the step's K/V for its channels (the bit-exact BlockQ8_0::pack of
+// kv_append_kernel), then attends over every key of the stream without key
+// splits, so no partials and no combine launch:
+//   scores  thread (head h = t/64, key slot t%64): 64 int8 K of the key
+//           converted exactly, dotted with q (shared memory), x block scales
+//   softmax one warp per head over the scores in shared memory
+//   P.V     thread = channel; per key one byte of V, its block scale, p
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) paged_decode_kernel(
+    const float* __restrict__ q, const float* __restrict__ knew, const float* __restrict__ vnew, int64_t ld,
+    const AttnGroup* __restrict__ groups, const int64_t* __restrict__ new_rows, const int32_t* __restrict__ table,
+    int ppseq, int64_t arena_row0, int bs, int8_t* kq, __half* kd, int8_t* vq, __half* vd, int W, int max_keys,
+    void* out, int out_fmt, int64_t out_plane) {
+    pdl_entry();
+    extern __shared__ __align__(16) float pd_smem[];
+    float* sc = pd_smem;                                                  // [4][max_keys]
+    float* qs = sc + 4 * max_keys;                                        // [256]
+    int64_t* rows_s = reinterpret_cast<int64_t*>(qs + 256);               // [max_keys]
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const AttnGroup g = groups[blockIdx.x];
+    const int tok = g.first_tok, n_keys = g.pos0 + 1;
+    const int c0 = blockIdx.y * 256, nb = W / 32, b0 = c0 / 32;
+    // phase 0: append this token's K and V blocks of the group (warp w: block w)
+    {
+        const int64_t row = new_rows[tok];
+        q8_0_block_warp(knew[(int64_t)tok * ld + c0 + warp * 32 + lane], lane, kq + row * W + c0 + warp * 32,
+                        kd + row * nb + b0 + warp);
+        q8_0_block_warp(vnew[(int64_t)tok * ld + c0 + warp * 32 + lane], lane, vq + row * W + c0 + warp * 32,
+                        vd + row * nb + b0 + warp);
+        qs[t] = q[(int64_t)tok * ld + c0 + t];
+        for (int k = t; k < n_keys; k += 256) {
+            const int pid = table[g.seq * ppseq + k / bs];
+            rows_s[k] = arena_row0 + (int64_t)pid * bs + k % bs;
+        }
+    }
+    __syncthreads();
+    // phase 1: scores
+    {
+        const int hl = t >> 6, slot = t & 63;
+        const float* qh = qs + hl * 64;
+        for (int k = slot; k < n_keys; k += 64) {
+            const int64_t row = rows_s[k];
+            const uint4* kp = reinterpret_cast<const uint4*>(kq + row * W + c0 + hl * 64);
+            uint4 kv4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) kv4[i] = __ldcg(kp + i);
+            const __half2 s2 = __ldcg(reinterpret_cast<const __half2*>(kd + row * nb + b0 + hl * 2));
+            float part[2] = {0.0f, 0.0f};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t w4[4] = {kv4[i].x ^ 0x80808080u, kv4[i].y ^ 0x80808080u, kv4[i].z ^ 0x80808080u,
+                                        kv4[i].w ^ 0x80808080u};
+#pragma unroll
+                for (int wd = 0; wd < 4; ++wd)
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        const float kf = __uint_as_float(__byte_perm(w4[wd], 0x4B000000u, 0x7440u + b)) - 8388736.0f;
+                        part[i >> 1] = fmaf(qh[16 * i + 4 * wd + b], kf, part[i >> 1]);
+                    }
+            }
+            sc[hl * max_keys + k] = part[0] * __low2float(s2) + part[1] * __high2float(s2);
+        }
+    }
+    __syncthreads();
+    // phase 2: softmax per head (warps 0..3), p normalised in place
+    if (warp < 4) {
+        float* s = sc + warp * max_keys;
+        float m = -INFINITY;
+        for (int k = lane; k < n_keys; k += 32) m = fmaxf(m, s[k]);
+        m = warp_max(m);
+        float l = 0.0f;
+        for (int k = lane; k < n_keys; k += 32) {
+            const float e = __expf(s[k] - m);
+            s[k] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        const float inv = 1.0f / l;
+        for (int k = lane; k < n_keys; k += 32) s[k] *= inv;
+    }
+    __syncthreads();
+    // phase 3: P.V, thread = channel c0 + t
+    {
+        const float* p = sc + (t >> 6) * max_keys;
+        const int8_t* vcol = vq + c0 + t;
+        const __half* vdc = vd + b0 + (t >> 5);
+        float acc = 0.0f;
+#pragma unroll 4
+        for (int k = 0; k < n_keys; ++k) {
+            const int64_t row = rows_s[k];
+            const float v = (float)__ldcg(vcol + row * W);
+            const float sv = __half2float(__ldcg(vdc + row * nb));
+            acc = fmaf(p[k] * sv, v, acc);
+        }
+        const int64_t o = (int64_t)tok * W + c0 + t;
+        if (out_fmt == 0) {
+            reinterpret_cast<float*>(out)[o] = acc;
+        } else {
+            const __half hi = __float2half_rn(acc);
+            reinterpret_cast<__half*>(out)[o] = hi;
+            if (out_fmt == 2) reinterpret_cast<__half*>(out)[out_plane + o] = __float2half_rn(acc - __half2float(hi));
+        }
+    }
+}
+
 // Quantizes dense rows [n_rows][W] (row stride ld) into the two planes (same
 // arithmetic). With a group map, source row r lands in destination row
 // map[r / group] * group + r % group.
@@ -510,6 +618,39 @@ void kv_append_ex(vkb_kv_pool* p, int layer, const float* k, const float* v, int
     const int64_t* rows = p->rows_dev.as<int64_t>() + (size_t)layer * p->n_tok;
     launch_pdl(p->ctx, kv_append_kernel, (unsigned)((warps * 32 + 255) / 256), 256, 0, 
         k, v, ld, rows, p->n_tok, p->W, p->kq.as<int8_t>(), p->kd.as<__half>(), p->vq.as<int8_t>(), p->vd.as<__half>());
+    VKB_CUDA(cudaGetLastError());
+    p->ctx->count();
+}
+
+// Append + attention of one decode step for one layer. One query per stream in
+// the SEQUENCE layout with d_head 64 and heads in groups of 4 takes the fused
+// paged_decode_kernel; every other shape runs kv_append_ex + kv_attention_ex.
+void kv_append_attention_ex(vkb_kv_pool* p, int layer, const float* q, const float* k, const float* v, int64_t ld,
+                            void* out, int out_dtype) {
+    const auto& d = p->d;
+    static const bool off = std::getenv("VKB_DECODE_ATTN_SPLIT") != nullptr;
+    const bool fused = !off && p->n_tok > 0 && d.layout == VKB_KV_LAYOUT_SEQUENCE && p->maxq == 1 &&
+                       p->n_groups == p->n_tok && d.d_head == 64 && d.n_head % 4 == 0 && layer >= 0 &&
+                       layer < d.n_layer && q && k && v && out &&
+                       (out_dtype == VKB_DT_F32 || out_dtype == VKB_DT_F16 || out_dtype == VKB_DT_F16X2);
+    if (!fused) {
+        kv_append_ex(p, layer, k, v, ld);
+        kv_attention_ex(p, layer, q, ld, out, out_dtype);
+        return;
+    }
+    const int max_keys = d.max_time;
+    const size_t smem = (size_t)(4 * max_keys + 256) * sizeof(float) + (size_t)max_keys * sizeof(int64_t);
+    static bool attr = false;
+    if (!attr) {
+        VKB_CUDA(cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        attr = true;
+    }
+    if (smem > 200 * 1024) fail(VKB_ERROR_UNSUPPORTED_OP, "decode attention: max_time too large");
+    dim3 grid((unsigned)p->n_tok, (unsigned)(d.n_head / 4));
+    launch_pdl(p->ctx, paged_decode_kernel, grid, 256, smem, q, k, v, ld, p->groups_dev.as<AttnGroup>(),
+               p->rows_dev.as<int64_t>() + (size_t)layer * p->n_tok, p->table_dev.as<int32_t>(), p->ppseq,
+               (int64_t)layer * p->n_pages * p->rpp, d.page_tokens, p->kq.as<int8_t>(), p->kd.as<__half>(),
+               p->vq.as<int8_t>(), p->vd.as<__half>(), p->W, max_keys, out, out_dtype, (int64_t)p->n_tok * p->W);
     VKB_CUDA(cudaGetLastError());
     p->ctx->count();
 }

@@ -511,8 +511,7 @@ void session_step(vkb_session* s, int n_tok, const int32_t* streams, const int32
             x.n_scaled = d;
             run_linear_ex(ctx, L.qkv.get(), n_tok, xln, AF, L.qkv_b.as<float>(), qkv, VKB_DT_F32, VKB_EPI_SCALE,
                           nullptr, scale, ws, nullptr, x);
-            kv_append_ex(s->pool, l, qkv + d, qkv + 2 * d, 3 * d);
-            kv_attention_ex(s->pool, l, qkv, 3 * d, ctxb, AF);
+            kv_append_attention_ex(s->pool, l, qkv, qkv + d, qkv + 2 * d, 3 * d, ctxb, AF);
             residual_ln(L.o.get(), ctxb, L.o_b.as<float>(), L.ln2g.as<float>(), L.ln2b.as<float>());
             run_linear(ctx, L.cq.get(), n_tok, xln, AF, L.cq_b.as<float>(), qc, VKB_DT_F32, VKB_EPI_SCALE, nullptr,
                        scale, ws, nullptr);
