@@ -98,8 +98,12 @@ __global__ void kv_append_kernel(const float* __restrict__ k, const float* __res
 //   softmax one warp per head over the scores in shared memory
 //   P.V     thread = channel; per key one byte of V, its block scale, p
 // ---------------------------------------------------------------------------
+// With splits > 0 the q|k|v row is read from the QKV projection's split-K
+// partials [splits][n_tok][ld] instead: value = (sum of partials in split
+// order + bias) x (qscale for the q columns), the reduce kernel's epilogue.
 __global__ void __launch_bounds__(256) paged_decode_kernel(
-    const float* __restrict__ q, const float* __restrict__ knew, const float* __restrict__ vnew, int64_t ld,
+    const float* __restrict__ qkv, int64_t ld, const float* __restrict__ part, int splits, int64_t plane,
+    const float* __restrict__ bias, float qscale,
     const AttnGroup* __restrict__ groups, const int64_t* __restrict__ new_rows, const int32_t* __restrict__ table,
     int ppseq, int64_t arena_row0, int bs, int8_t* kq, __half* kd, int8_t* vq, __half* vd, int W, int max_keys,
     void* out, int out_fmt, int64_t out_plane) {
@@ -112,14 +116,21 @@ __global__ void __launch_bounds__(256) paged_decode_kernel(
     const AttnGroup g = groups[blockIdx.x];
     const int tok = g.first_tok, n_keys = g.pos0 + 1;
     const int c0 = blockIdx.y * 256, nb = W / 32, b0 = c0 / 32;
+    auto val = [&](int col) {
+        const int64_t i = (int64_t)tok * ld + col;
+        if (splits == 0) return qkv[i];
+        float acc = 0.0f;
+        for (int sp = 0; sp < splits; ++sp) acc += __ldcg(part + sp * plane + i);
+        const float x = acc + (bias ? bias[col] : 0.0f);
+        return col < W ? x * qscale : x;
+    };
     // phase 0: append this token's K and V blocks of the group (warp w: block w)
     {
         const int64_t row = new_rows[tok];
-        q8_0_block_warp(knew[(int64_t)tok * ld + c0 + warp * 32 + lane], lane, kq + row * W + c0 + warp * 32,
-                        kd + row * nb + b0 + warp);
-        q8_0_block_warp(vnew[(int64_t)tok * ld + c0 + warp * 32 + lane], lane, vq + row * W + c0 + warp * 32,
+        q8_0_block_warp(val(W + c0 + warp * 32 + lane), lane, kq + row * W + c0 + warp * 32, kd + row * nb + b0 + warp);
+        q8_0_block_warp(val(2 * W + c0 + warp * 32 + lane), lane, vq + row * W + c0 + warp * 32,
                         vd + row * nb + b0 + warp);
-        qs[t] = q[(int64_t)tok * ld + c0 + t];
+        qs[t] = val(c0 + t);
         for (int k = t; k < n_keys; k += 256) {
             const int pid = table[g.seq * ppseq + k / bs];
             rows_s[k] = arena_row0 + (int64_t)pid * bs + k % bs;
@@ -622,20 +633,30 @@ void kv_append_ex(vkb_kv_pool* p, int layer, const float* k, const float* v, int
     p->ctx->count();
 }
 
-// Append + attention of one decode step for one layer. One query per stream in
-// the SEQUENCE layout with d_head 64 and heads in groups of 4 takes the fused
-// paged_decode_kernel; every other shape runs kv_append_ex + kv_attention_ex.
-void kv_append_attention_ex(vkb_kv_pool* p, int layer, const float* q, const float* k, const float* v, int64_t ld,
-                            void* out, int out_dtype) {
-    const auto& d = p->d;
+// Whether the decode step's append + attention of this pool runs as the fused
+// paged_decode_kernel: one query per stream in the SEQUENCE layout, d_head 64,
+// heads in groups of 4.
+bool kv_decode_fused(const vkb_kv_pool* p) {
     static const bool off = std::getenv("VKB_DECODE_ATTN_SPLIT") != nullptr;
-    const bool fused = !off && p->n_tok > 0 && d.layout == VKB_KV_LAYOUT_SEQUENCE && p->maxq == 1 &&
-                       p->n_groups == p->n_tok && d.d_head == 64 && d.n_head % 4 == 0 && layer >= 0 &&
-                       layer < d.n_layer && q && k && v && out &&
-                       (out_dtype == VKB_DT_F32 || out_dtype == VKB_DT_F16 || out_dtype == VKB_DT_F16X2);
-    if (!fused) {
-        kv_append_ex(p, layer, k, v, ld);
-        kv_attention_ex(p, layer, q, ld, out, out_dtype);
+    const auto& d = p->d;
+    return !off && p->n_tok > 0 && d.layout == VKB_KV_LAYOUT_SEQUENCE && p->maxq == 1 && p->n_groups == p->n_tok &&
+           d.d_head == 64 && d.n_head % 4 == 0;
+}
+
+// Append + attention of one decode step for one layer: the fused kernel when
+// kv_decode_fused(p), else kv_append_ex + kv_attention_ex. `qkv` rows hold
+// q | k | v (stride ld); with splits > 0 (fused path only) they are read from
+// the projection's split-K partials with its bias and q scale.
+void kv_append_attention_ex(vkb_kv_pool* p, int layer, const float* qkv, int64_t ld, void* out, int out_dtype,
+                            const float* part, int splits, const float* bias, float qscale) {
+    const auto& d = p->d;
+    if (layer < 0 || layer >= d.n_layer) fail(VKB_ERROR_INVALID_ARGUMENT, "decode attention: layer out of range");
+    if (out_dtype != VKB_DT_F32 && out_dtype != VKB_DT_F16 && out_dtype != VKB_DT_F16X2)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "decode attention: bad out dtype");
+    if (!kv_decode_fused(p)) {
+        if (splits > 0) fail(VKB_ERROR_OTHER, "decode attention: partials need the fused kernel");
+        kv_append_ex(p, layer, qkv + p->W, qkv + 2 * p->W, ld);
+        kv_attention_ex(p, layer, qkv, ld, out, out_dtype);
         return;
     }
     const int max_keys = d.max_time;
@@ -647,10 +668,11 @@ void kv_append_attention_ex(vkb_kv_pool* p, int layer, const float* q, const flo
     }
     if (smem > 200 * 1024) fail(VKB_ERROR_UNSUPPORTED_OP, "decode attention: max_time too large");
     dim3 grid((unsigned)p->n_tok, (unsigned)(d.n_head / 4));
-    launch_pdl(p->ctx, paged_decode_kernel, grid, 256, smem, q, k, v, ld, p->groups_dev.as<AttnGroup>(),
-               p->rows_dev.as<int64_t>() + (size_t)layer * p->n_tok, p->table_dev.as<int32_t>(), p->ppseq,
-               (int64_t)layer * p->n_pages * p->rpp, d.page_tokens, p->kq.as<int8_t>(), p->kd.as<__half>(),
-               p->vq.as<int8_t>(), p->vd.as<__half>(), p->W, max_keys, out, out_dtype, (int64_t)p->n_tok * p->W);
+    launch_pdl(p->ctx, paged_decode_kernel, grid, 256, smem, qkv, ld, part, splits, (int64_t)p->n_tok * ld, bias,
+               qscale, p->groups_dev.as<AttnGroup>(), p->rows_dev.as<int64_t>() + (size_t)layer * p->n_tok,
+               p->table_dev.as<int32_t>(), p->ppseq, (int64_t)layer * p->n_pages * p->rpp, d.page_tokens,
+               p->kq.as<int8_t>(), p->kd.as<__half>(), p->vq.as<int8_t>(), p->vd.as<__half>(), p->W, max_keys, out,
+               out_dtype, (int64_t)p->n_tok * p->W);
     VKB_CUDA(cudaGetLastError());
     p->ctx->count();
 }

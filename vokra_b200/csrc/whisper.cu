@@ -509,9 +509,16 @@ void session_step(vkb_session* s, int n_tok, const int32_t* streams, const int32
             const DecLayer& L = m->dec[l];
             LinearExtra x;
             x.n_scaled = d;
+            // with the fused decode attention the split-K partials are summed there
+            int qkv_splits = 1;
+            const bool fused = kv_decode_fused(s->pool);
+            if (fused) x.splits_out = &qkv_splits;
             run_linear_ex(ctx, L.qkv.get(), n_tok, xln, AF, L.qkv_b.as<float>(), qkv, VKB_DT_F32, VKB_EPI_SCALE,
                           nullptr, scale, ws, nullptr, x);
-            kv_append_attention_ex(s->pool, l, qkv, qkv + d, qkv + 2 * d, 3 * d, ctxb, AF);
+            if (fused && qkv_splits > 1)
+                kv_append_attention_ex(s->pool, l, qkv, 3 * d, ctxb, AF, ws, qkv_splits, L.qkv_b.as<float>(), scale);
+            else
+                kv_append_attention_ex(s->pool, l, qkv, 3 * d, ctxb, AF);
             residual_ln(L.o.get(), ctxb, L.o_b.as<float>(), L.ln2g.as<float>(), L.ln2b.as<float>());
             run_linear(ctx, L.cq.get(), n_tok, xln, AF, L.cq_b.as<float>(), qc, VKB_DT_F32, VKB_EPI_SCALE, nullptr,
                        scale, ws, nullptr);
