@@ -224,6 +224,23 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// One Q8_0 block of 32 values held by the 32 lanes of a warp: the arithmetic
+// of BlockQ8_0::pack (crates/vokra-core/src/kv_quant/q8_0.rs:40-66) in IEEE
+// fp32 with Rust's NaN rules (max ignores NaN, clamp keeps NaN, NaN casts to
+// 0); lane i writes quant i, lane 0 the f16 scale.
+__device__ __forceinline__ void q8_0_block_warp(float x, int lane, int8_t* q_out, __half* d_out) {
+    float a = fabsf(x);
+    a = warp_max(a);
+    float amax = fmaxf(0.0f, a);
+    float d = amax == 0.0f ? 0.0f : amax / 127.0f;
+    float inv = d == 0.0f ? 0.0f : 1.0f / d;
+    float s = x * inv;
+    float c = s < -127.0f ? -127.0f : (s > 127.0f ? 127.0f : s);
+    int8_t qv = isnan(c) ? (int8_t)0 : (int8_t)(int)roundf(c);
+    q_out[lane] = qv;
+    if (lane == 0) *reinterpret_cast<uint16_t*>(d_out) = f32_to_f16_bits(d);
+}
+
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 
 }  // namespace vkb

@@ -56,18 +56,6 @@ namespace vkb {
 // (crates/vokra-core/src/kv_quant/q8_0.rs:40-66) in IEEE fp32 with Rust's
 // NaN rules (max ignores NaN, clamp keeps NaN, NaN casts to 0).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void q8_0_block_warp(float x, int lane, int8_t* q_out, __half* d_out) {
-    float a = fabsf(x);
-    a = warp_max(a);
-    float amax = fmaxf(0.0f, a);
-    float d = amax == 0.0f ? 0.0f : amax / 127.0f;
-    float inv = d == 0.0f ? 0.0f : 1.0f / d;
-    float s = x * inv;
-    float c = s < -127.0f ? -127.0f : (s > 127.0f ? 127.0f : s);
-    int8_t qv = isnan(c) ? (int8_t)0 : (int8_t)(int)roundf(c);
-    q_out[lane] = qv;
-    if (lane == 0) *reinterpret_cast<uint16_t*>(d_out) = f32_to_f16_bits(d);
-}
 
 __global__ void kv_append_kernel(const float* __restrict__ k, const float* __restrict__ v, int64_t ld,
                                  const int64_t* __restrict__ rows, int n_tok, int W, int8_t* kq, __half* kd,

@@ -152,9 +152,17 @@ struct Epi {
     int64_t plane;     // elements per plane of an F16X2 output
 };
 
+// Destination row of token m under the row-group map (32-bit division: token
+// counts stay far below 2^31).
+__device__ __forceinline__ int64_t epi_row(const Epi& e, int64_t m) {
+    if (!e.row_map) return m;
+    const unsigned g = (unsigned)m / (unsigned)e.row_group;
+    return (int64_t)e.row_map[g] * e.row_group + ((unsigned)m - g * (unsigned)e.row_group);
+}
+
 __device__ __forceinline__ void epi_store(const Epi& e, int64_t m, int64_t n, float acc, float bias_n) {
     float v = acc + bias_n;
-    int64_t mr = e.row_map ? (int64_t)e.row_map[m / e.row_group] * e.row_group + m % e.row_group : m;
+    int64_t mr = epi_row(e, m);
     int64_t idx = e.col_block > 0 ? (n / e.col_block) * (e.out_rows * e.col_block) + mr * e.col_block + n % e.col_block
                                   : mr * e.ldo + n;
     if (e.kind == VKB_EPI_GELU) v = gelu_as_fast(v);
