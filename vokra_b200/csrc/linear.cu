@@ -312,15 +312,21 @@ void run_split_f16(vkb_context* ctx, const float* x, int64_t n, __half* y, bool 
 // ---------------------------------------------------------------------------
 template <int FMT, int BN, bool SPLIT>
 struct TcCfg {
+    // Token tiles up to 64 (the decode step) run two CTAs per SM: half the
+    // shared memory, 256 TMEM columns, 2 epilogue groups, so one CTA's setup and
+    // epilogue (and the next GEMM's, launched early) overlap another's MMAs.
+    static constexpr bool DUAL = BN <= 64;
+    static constexpr int MINB = DUAL ? 2 : 1;
     static constexpr int NP = SPLIT ? 2 : 1;                   // operand planes
     static constexpr int B_BYTES = BN * 128;                   // BN rows x 128 B per plane
     static constexpr int RAW_Q = stage_qs_bytes(FMT);
     static constexpr int RAW_S = stage_sc_bytes(FMT);
     static constexpr int RAW_BYTES = ((RAW_Q + RAW_S) + 1023) / 1024 * 1024;
     static constexpr int STAGE_BYTES = NP * B_BYTES + RAW_BYTES;
-    static constexpr int BUDGET = 225 * 1024 - 2048;
+    static constexpr int BUDGET = (DUAL ? 110 * 1024 : 225 * 1024) - 2048;
     static constexpr int S0 = BUDGET / STAGE_BYTES;
-    static constexpr int S = S0 > 6 ? 6 : S0;
+    static constexpr int SMAX = DUAL ? 4 : 6;
+    static constexpr int S = S0 > SMAX ? SMAX : S0;
     static constexpr int SMEM = 1024 /*align slack*/ + S * STAGE_BYTES + 1024 /*barriers*/;
     // Stacked split mode (token tiles up to 128): the hi and lo activation
     // tiles, adjacent in shared memory, form ONE B operand of 2*BN rows, so a
@@ -331,22 +337,24 @@ struct TcCfg {
     static constexpr bool STACK = SPLIT && BN <= 128;
     static constexpr int ACC_COLS = STACK ? 2 * BN : (BN < 32 ? 32 : BN);
     static constexpr int A_COL0 = ACC_COLS;                     // first A column
-    static constexpr int AS = 4;                                // A stages in tensor memory
+    static constexpr int AS = DUAL ? 2 : 4;                     // A stages in tensor memory
     static constexpr int NEED_COLS = ACC_COLS + AS * NP * 32;
     static constexpr uint32_t TMEM_COLS = NEED_COLS <= 32 ? 32 : NEED_COLS <= 64 ? 64 : NEED_COLS <= 128 ? 128
                                           : NEED_COLS <= 256 ? 256 : 512;
     static_assert(NEED_COLS <= 512, "tensor memory budget");
+    static_assert(!DUAL || TMEM_COLS <= 256, "two CTAs per SM share 512 TMEM columns");
     static_assert(S >= 2, "pipeline needs at least two stages");
     // epilogue groups of 4 warps (one per TMEM lane quarter), each taking
     // BN / EG token columns; group 0 is also the dequant group
-    static constexpr int EG = BN / 16 < 4 ? BN / 16 : 4;
+    static constexpr int EG0 = BN / 16 < 4 ? BN / 16 : 4;
+    static constexpr int EG = DUAL && EG0 > 2 ? 2 : EG0;
     static constexpr int THREADS = 64 + 128 * EG;
 };
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 template <int FMT, int BN, bool SPLIT>
-__global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, 1)
+__global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN, SPLIT>::MINB)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_lo,
                    const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc, int64_t K, int64_t N, int64_t M,
                    int n_tiles, int m_tiles, int stages_per_split, int n_splits, float* ws, Epi e, int* err,
