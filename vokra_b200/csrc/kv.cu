@@ -97,8 +97,8 @@ __global__ void __launch_bounds__(256) paged_decode_kernel(
     void* out, int out_fmt, int64_t out_plane) {
     pdl_entry();
     extern __shared__ __align__(16) float pd_smem[];
-    float* sc = pd_smem;                                                  // [4][max_keys]
-    float* qs = sc + 4 * max_keys;                                        // [256]
+    float* sc = pd_smem;                               // [4][max_keys]; later the [4][256] P.V sums
+    float* qs = sc + (4 * max_keys > 1024 ? 4 * max_keys : 1024);  // [256]
     int64_t* rows_s = reinterpret_cast<int64_t*>(qs + 256);               // [max_keys]
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const AttnGroup g = groups[blockIdx.x];
@@ -170,19 +170,32 @@ __global__ void __launch_bounds__(256) paged_decode_kernel(
         for (int k = lane; k < n_keys; k += 32) s[k] *= inv;
     }
     __syncthreads();
-    // phase 3: P.V, thread = channel c0 + t
+    // phase 3: P.V; thread = (channel quad t % 64, key group t / 64): 4 bytes
+    // of V per key over every 4th key, the 4 key groups summed in shared memory
     {
-        const float* p = sc + (t >> 6) * max_keys;
-        const int8_t* vcol = vq + c0 + t;
-        const __half* vdc = vd + b0 + (t >> 5);
-        float acc = 0.0f;
+        const int cq = t & 63, kg = t >> 6;
+        const float* p = sc + (cq >> 4) * max_keys;
+        const uint32_t* vcol = reinterpret_cast<const uint32_t*>(vq + c0) + cq;
+        const __half* vdc = vd + b0 + (cq >> 3);
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
 #pragma unroll 4
-        for (int k = 0; k < n_keys; ++k) {
+        for (int k = kg; k < n_keys; k += 4) {
             const int64_t row = rows_s[k];
-            const float v = (float)__ldcg(vcol + row * W);
-            const float sv = __half2float(__ldcg(vdc + row * nb));
-            acc = fmaf(p[k] * sv, v, acc);
+            const uint32_t v = __ldcg(vcol + row * (W / 4)) ^ 0x80808080u;
+            const float w = p[k] * __half2float(__ldcg(vdc + row * nb));
+            a0 = fmaf(w, __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7440u)) - 8388736.0f, a0);
+            a1 = fmaf(w, __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7441u)) - 8388736.0f, a1);
+            a2 = fmaf(w, __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7442u)) - 8388736.0f, a2);
+            a3 = fmaf(w, __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7443u)) - 8388736.0f, a3);
         }
+        __syncthreads();  // the score rows are no longer read: reuse them for the key-group sums
+        float* red = sc;  // [4][256]
+        red[kg * 256 + 4 * cq + 0] = a0;
+        red[kg * 256 + 4 * cq + 1] = a1;
+        red[kg * 256 + 4 * cq + 2] = a2;
+        red[kg * 256 + 4 * cq + 3] = a3;
+        __syncthreads();
+        const float acc = (red[t] + red[256 + t]) + (red[512 + t] + red[768 + t]);
         const int64_t o = (int64_t)tok * W + c0 + t;
         if (out_fmt == 0) {
             reinterpret_cast<float*>(out)[o] = acc;
@@ -648,7 +661,7 @@ void kv_append_attention_ex(vkb_kv_pool* p, int layer, const float* qkv, int64_t
         return;
     }
     const int max_keys = d.max_time;
-    const size_t smem = (size_t)(4 * max_keys + 256) * sizeof(float) + (size_t)max_keys * sizeof(int64_t);
+    const size_t smem = (size_t)(std::max(4 * max_keys, 1024) + 256) * sizeof(float) + (size_t)max_keys * sizeof(int64_t);
     static bool attr = false;
     if (!attr) {
         VKB_CUDA(cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
