@@ -127,3 +127,18 @@ def test_recorded_decode_step_replays_bit_exact(ctx, tiny):
     replay = _decode_fixed_buffer(ctx, tiny, n_streams=3, n_steps=20, graphs=True)
     assert np.isfinite(eager).all()
     assert np.array_equal(eager, replay)
+
+
+def test_whisper_full_window_matches_oracle(ctx, tmp_path):
+    """A one-layer model at Whisper's real window (1500 encoder frames) with 8
+    heads: the tensor-core encoder attention over 12 key tiles with a ragged
+    last tile, the streaming cross-attention over 1500 keys, and the fused
+    decode self-attention over two head groups, against the oracle forward."""
+    arch = synth.WhisperArch(80, 1500, 512, 8, 1, 64, 8, 1, 1000, 2048, 999, (1, 2, 3, 4))
+    path = str(tmp_path / "window.gguf")
+    synth.write_synthetic_whisper(path, arch, synth.Q8_0, seed=4)
+    enc, ref_enc, results = _run(ctx, path, n_streams=2, n_steps=12, arch=arch, seed=9)
+    assert _rel_rms(enc, ref_enc) <= 2e-3
+    for got, ref in results:
+        assert np.max(np.abs(got - ref)) <= 1e-2
+        assert _rel_rms(got, ref) <= 1e-3
