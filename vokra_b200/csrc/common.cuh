@@ -213,6 +213,30 @@ __device__ __forceinline__ float gelu_as_fast(float v) {
     return 0.5f * v * (1.0f + copysignf(y, v));
 }
 
+// gelu_as_fast on two values with packed f32x2 arithmetic (same operations
+// and rounding per element; half the floating-point instructions).
+__device__ __forceinline__ float2 gelu_as_fast2(float2 v) {
+    const float2 P = make_float2(0.3275911f, 0.3275911f), one = make_float2(1.0f, 1.0f);
+    const float2 A1 = make_float2(0.254829592f, 0.254829592f), A2 = make_float2(-0.284496736f, -0.284496736f),
+                 A3 = make_float2(1.421413741f, 1.421413741f), A4 = make_float2(-1.453152027f, -1.453152027f),
+                 A5 = make_float2(1.061405429f, 1.061405429f);
+    float2 x = __fmul2_rn(v, make_float2(0.70710678118654752f, 0.70710678118654752f));
+    x.x = fabsf(x.x);
+    x.y = fabsf(x.y);
+    const float2 den = __ffma2_rn(P, x, one);
+    const float2 t = make_float2(__fdividef(1.0f, den.x), __fdividef(1.0f, den.y));
+    float2 poly = __ffma2_rn(A5, t, A4);
+    poly = __ffma2_rn(poly, t, A3);
+    poly = __ffma2_rn(poly, t, A2);
+    poly = __ffma2_rn(poly, t, A1);
+    poly = __fmul2_rn(poly, t);
+    const float2 xx = __fmul2_rn(x, x);
+    const float2 ex = make_float2(__expf(-xx.x), __expf(-xx.y));
+    const float2 y = __ffma2_rn(make_float2(-poly.x, -poly.y), ex, one);
+    const float2 hv = __fmul2_rn(make_float2(0.5f, 0.5f), v);
+    return __fmul2_rn(hv, __fadd2_rn(one, make_float2(copysignf(y.x, v.x), copysignf(y.y, v.y))));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -552,6 +552,21 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
                 for (int c0 = cb; c0 < cb + HALF; c0 += CW) {
                     uint32_t v[CW];
                     load_cols(c0, v);
+                    if (!partial && e.kind == VKB_EPI_GELU && e.out_fmt == VKB_DT_F16X2) {
+                        // the MLP's hidden layer: GELU on pairs of tokens with packed f32x2 math
+#pragma unroll
+                        for (int j = 0; j < CW; j += 2) {
+                            const float2 x = gelu_as_fast2(make_float2(__uint_as_float(v[j]) + bias_n,
+                                                                       __uint_as_float(v[j + 1]) + bias_n));
+                            const __half h0 = __float2half_rn(x.x), h1 = __float2half_rn(x.y);
+                            const int row = c0 + j;
+                            sh[row * TILE_N + r] = h0;
+                            sh[(row + 1) * TILE_N + r] = h1;
+                            sh[BN * TILE_N + row * TILE_N + r] = __float2half_rn(x.x - __half2float(h0));
+                            sh[BN * TILE_N + (row + 1) * TILE_N + r] = __float2half_rn(x.y - __half2float(h1));
+                        }
+                        continue;
+                    }
 #pragma unroll
                     for (int j = 0; j < CW; ++j) {
                         const int row = c0 + j;
