@@ -93,7 +93,9 @@ __global__ void __launch_bounds__(192, 2)
     uint64_t* s_full = bars + 5;
     uint64_t* p_full = bars + 6;
     uint64_t* o_full = bars + 7;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+    uint64_t* s_free = bars + 8;   // softmax(j) holds S(j) in registers: S may be overwritten
+    uint64_t* pv_done = bars + 9;  // O += P(j) V(j) completed: P may be overwritten, O rescaled
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q0 = blockIdx.x * BQ;
@@ -110,6 +112,8 @@ __global__ void __launch_bounds__(192, 2)
         ptx::mbar_init(s_full, 1);
         ptx::mbar_init(p_full, 128);
         ptx::mbar_init(o_full, 1);
+        ptx::mbar_init(s_free, 128);
+        ptx::mbar_init(pv_done, 1);
         ptx::fence_mbar_init();
     }
     if (warp == 1) {
@@ -151,30 +155,32 @@ __global__ void __launch_bounds__(192, 2)
                     ptx::mma_f16_ts(tmem + O_COL, tmem + P_COL + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
                 }
                 ptx::mma_commit(&kv_empty[j & 1]);
+                ptx::mma_commit(pv_done);
             };
-            if (!ptx::mbar_wait(q_full, 0)) ok = false;
-            for (int j = 0; j < n_tiles && ok; ++j) {
-                if (!ptx::mbar_wait(&kv_full[j & 1], (j >> 1) & 1)) { ok = false; break; }
-                if (j > 0) {
-                    // softmax(j-1) has read S and written P(j-1): O += P V, then S is free
-                    if (!ptx::mbar_wait(p_full, (j - 1) & 1)) { ok = false; break; }
-                    ptx::tc_fence_after();
-                    issue_pv(j - 1);
-                }
+            auto issue_s = [&](int j) {
                 const uint32_t k_addr = ptx::smem_u32(sK + (j & 1) * TILE_BYTES);
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk)
                     ptx::mma_f16_ss(tmem + S_COL, ptx::sdesc_sw128(q_addr + kk * 32),
                                     ptx::sdesc_sw128(k_addr + kk * 32), idesc_s, kk > 0 ? 1u : 0u);
-                ptx::mma_commit(s_full);  // also covers PV(j-1): softmax(j) may then overwrite P
-            }
-            if (ok && ptx::mbar_wait(p_full, (n_tiles - 1) & 1)) {
+                ptx::mma_commit(s_full);
+            };
+            // S(j+1) is issued as soon as softmax(j) has S(j) in registers, so it
+            // runs while softmax(j) computes; O += P(j) V(j) follows P(j).
+            if (!ptx::mbar_wait(q_full, 0) || !ptx::mbar_wait(&kv_full[0], 0)) ok = false;
+            if (ok) issue_s(0);
+            for (int j = 0; j < n_tiles && ok; ++j) {
+                if (j + 1 < n_tiles) {
+                    if (!ptx::mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+                    if (!ptx::mbar_wait(s_free, j & 1)) { ok = false; break; }
+                    ptx::tc_fence_after();
+                    issue_s(j + 1);
+                }
+                if (!ptx::mbar_wait(p_full, j & 1)) { ok = false; break; }
                 ptx::tc_fence_after();
-                issue_pv(n_tiles - 1);
-                ptx::mma_commit(o_full);
-            } else {
-                ok = false;
+                issue_pv(j);
             }
+            if (ok) ptx::mma_commit(o_full);
         }
     } else {
         // softmax + epilogue: thread = query row r = TMEM lane r
@@ -194,6 +200,8 @@ __global__ void __launch_bounds__(192, 2)
             ptx::tmem_ld32(tmem + lane_off + S_COL + 64, *reinterpret_cast<uint32_t(*)[32]>(sv + 64));
             ptx::tmem_ld32(tmem + lane_off + S_COL + 96, *reinterpret_cast<uint32_t(*)[32]>(sv + 96));
             ptx::tmem_ld_wait();
+            ptx::tc_fence_before();
+            ptx::mbar_arrive(s_free);  // S(j+1) may now be computed into the same columns
             if (kvalid < BKEY) {
 #pragma unroll
                 for (int c = 0; c < BKEY; ++c)
@@ -207,8 +215,11 @@ __global__ void __launch_bounds__(192, 2)
             const bool raise = mt > m_used + RESCALE_LOG2;
             const float m_new = raise ? mt : m_used;
             const float corr = raise ? ex2_approx(m_used - m_new) : 1.0f;  // 0 on the first tile
+            // O += P(j-1) V(j-1) must be complete before O is rescaled or P rewritten
+            if (j > 0 && !ptx::mbar_wait(pv_done, (j - 1) & 1)) { ok = false; break; }
+            ptx::tc_fence_after();
             if (__any_sync(0xffffffffu, raise && j > 0)) {
-                // O += P V of tile j-1 has completed (ordered before S(j)); rescale O
+                // rescale O
                 uint32_t o[32];
 #pragma unroll
                 for (int c0 = 0; c0 < HD; c0 += 32) {
