@@ -237,6 +237,21 @@ def run_kernel_only(args):
     import torch
     from vokra_b200 import _lib, ops, synth
     ctx = ops.Context(0)
+    if args.kernel == "encoder":
+        from vokra_b200 import whisper
+        big = synth.WHISPER_LARGE_V3
+        arch = dataclasses.replace(big, n_audio_layer=1, n_text_layer=1, n_vocab=1000, eot=999,
+                                   start_ids=(1, 2, 3, 4))
+        path = ensure_model(model_path("large_v3_dims_e1d1_q4_0"), arch, synth.Q4_0)
+        model = whisper.WhisperModel(ctx, path)
+        B = 8
+        sess = whisper.Session(model, max_streams=B, max_clips=B)
+        lm = torch.from_numpy(synthetic_logmels(B, arch.n_mels, 2 * arch.n_audio_ctx, 5)).cuda()
+        for _ in range(3):
+            sess.encode(lm, list(range(B)))
+        torch.cuda.synchronize()
+        print(json.dumps({"kernel": args.kernel, "clips": B, "frames": arch.n_audio_ctx, "ok": True}))
+        return
     if args.kernel == "xattn":
         B, T, H, D = args.clips, 1500, 20, 64
         W = H * D
@@ -286,9 +301,10 @@ def main():
     ap.add_argument("--tokens", type=int, default=128)
     ap.add_argument("--precision", default="split", choices=["split", "f16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", default=None, choices=["fc1", "fc1_m1500", "xattn"],
+    ap.add_argument("--kernel", default=None, choices=["fc1", "fc1_m1500", "xattn", "encoder"],
                     help="run only one kernel three times, for ncu: the encoder fc1 GEMM (M = clips x 1500, or "
-                         "1500) or the decode cross-attention over the Q8_0 store (clips streams x 1500 keys)")
+                         "1500), the decode cross-attention over the Q8_0 store (clips streams x 1500 keys), or "
+                         "the encoder of a one-layer model with large-v3's dimensions on 8 clips")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
