@@ -114,3 +114,30 @@ def test_rejections(ctx):
     with pytest.raises(ops.VkbError) as e:
         ops.Weight(ctx, 6, 4, 64, b"\0" * 10)
     assert e.value.code == _lib.ERROR_UNSUPPORTED_OP
+
+
+# Large M (encoder-sized): the persistent tensor-core GEMM with the double-
+# buffered accumulator takes these (>= 4 tiles per SM; 192-token tiles, so
+# m = 11000 leaves a ragged last tile and n = 1300 a ragged weight tile).
+@pytest.mark.parametrize("tag", TAGS)
+def test_persistent_gemm_matches_oracle(ctx, tag):
+    for k in (1280, 768):
+        got, ref = _run(ctx, tag, 1300, k, 11000, seed=5 + k)
+        assert _rel_rms(got, ref) <= 1e-4, k
+        assert np.max(np.abs(got - ref)) <= 2e-3, k
+
+
+@pytest.mark.parametrize("epi,out_f16", [(_lib.EPI_GELU, True), (_lib.EPI_SCALE, True), (_lib.EPI_RESIDUAL, False),
+                                         (_lib.EPI_NONE, True)])
+def test_persistent_gemm_epilogues(ctx, epi, out_f16):
+    got, ref = _run(ctx, synth.Q4_0, 1280, 1280, 12000, epi=epi, out_f16=out_f16, scale=0.125)
+    tol = 1e-3 if out_f16 else 1e-4  # an f16 output rounds at 2^-11 relative
+    assert _rel_rms(got, ref) <= tol
+
+
+def test_persistent_gemm_long_k(ctx, monkeypatch):
+    # K = 5120 runs on the classic kernel by default; forced onto the persistent one here
+    monkeypatch.setenv("VKB_GEMM_PERSIST", "force")
+    got, ref = _run(ctx, synth.Q4_0, 1280, 5120, 11000, seed=9)
+    assert _rel_rms(got, ref) <= 1e-4
+    assert np.max(np.abs(got - ref)) <= 5e-3

@@ -142,3 +142,18 @@ def test_whisper_full_window_matches_oracle(ctx, tmp_path):
     for got, ref in results:
         assert np.max(np.abs(got - ref)) <= 1e-2
         assert _rel_rms(got, ref) <= 1e-3
+
+
+def test_whisper_full_window_persistent_gemm(ctx, tmp_path, monkeypatch):
+    """The same window with every unsplit-K GEMM on the persistent kernel
+    (conv stem GELU to f16 hi+lo planes, scaled QKV to f16, residual f32,
+    cross K/V f32), against the oracle forward."""
+    monkeypatch.setenv("VKB_GEMM_PERSIST", "force")
+    arch = synth.WhisperArch(80, 1500, 512, 8, 1, 64, 8, 1, 1000, 2048, 999, (1, 2, 3, 4))
+    path = str(tmp_path / "window_p.gguf")
+    synth.write_synthetic_whisper(path, arch, synth.Q8_0, seed=4)
+    enc, ref_enc, results = _run(ctx, path, n_streams=2, n_steps=4, arch=arch, seed=9)
+    assert _rel_rms(enc, ref_enc) <= 2e-3
+    for got, ref in results:
+        assert np.max(np.abs(got - ref)) <= 1e-2
+        assert _rel_rms(got, ref) <= 1e-3

@@ -1,0 +1,304 @@
+// gemm_persist.cu — persistent tcgen05 GEMM for the large-M Linear layers of
+// the encoder (M = clips x 1500 tokens), split precision (W_hi/W_lo x X_hi/X_lo).
+//
+// Same product as tc_gemm_kernel's non-stacked split mode (three MMAs per
+// K=16 step: W_hi.X_hi + W_hi.X_lo + W_lo.X_hi, weights dequantized into
+// tensor memory as the A operand, activations by TMA as the B operand), but
+// one CTA per SM walks a static list of output tiles (tile t, t + grid, ...)
+// and the accumulator is double-buffered in tensor memory:
+//   columns [0, 192)    accumulator 0      (128 weight rows x 192 tokens, f32)
+//   columns [192, 384)  accumulator 1
+//   columns [384, 512)  two A stages of W_hi | W_lo (64 K each)
+// so the epilogue of tile i (its own 8 warps: tensor-memory load, bias, GELU /
+// scale / residual, stores) runs while the MMAs of tile i+1 fill the other
+// buffer, and the TMA ring never drains between tiles. The non-persistent
+// kernel pays CTA setup, pipeline fill and the epilogue with the tensor pipe
+// idle, once per tile.
+//
+// Warp roles (448 threads): warp 0 producer (one lane: weight bulk copies +
+// activation TMA), warp 1 MMA issuer (one lane), warps 2-5 dequantization
+// (thread = weight row = tensor-memory lane), warps 6-13 epilogue (two groups
+// of four warps; a group covers the 128 lanes and half of the 192 columns).
+// The epilogue needs both groups to stay shorter than a tile's MMAs at K = 1280
+// (measured: one group of four made fc1's GELU epilogue the bottleneck).
+// Every mbarrier wait is bounded; a timeout flags the context error.
+#include "common.cuh"
+#include "weights.cuh"
+#include "tc_ptx.cuh"
+#include "linear.cuh"
+
+namespace vkb {
+
+template <int FMT>
+struct PCfg {
+    static constexpr int BN = 192;                          // tokens per tile
+    static constexpr int B_BYTES = BN * 128;                // one activation plane per stage
+    static constexpr int RAW_Q = stage_qs_bytes(FMT);
+    static constexpr int RAW_S = stage_sc_bytes(FMT);
+    static constexpr int RAW_BYTES = ((RAW_Q + RAW_S) + 1023) / 1024 * 1024;
+    static constexpr int STAGE_BYTES = 2 * B_BYTES + RAW_BYTES;
+    static constexpr int S0 = (225 * 1024 - 2048) / STAGE_BYTES;
+    static constexpr int S = S0 > 4 ? 4 : S0;
+    static constexpr int SMEM = 1024 + S * STAGE_BYTES + 1024;
+    static constexpr int AS = 2;
+    static constexpr int A_COL0 = 2 * BN;
+    static constexpr int DEQ_WARPS = 4;
+    static constexpr int EPI_WARPS = 8;
+    static constexpr int THREADS = 32 * (2 + DEQ_WARPS + EPI_WARPS);
+    static_assert(A_COL0 + AS * 64 <= 512, "tensor memory budget");
+    static_assert(S >= 2, "pipeline needs at least two stages");
+    static_assert(B_BYTES % 1024 == 0, "128-byte swizzle atoms");
+};
+
+__device__ __forceinline__ void pstore(const PEpi& e, int64_t i, float x) {
+    if (e.out_fmt == VKB_DT_F32) {
+        reinterpret_cast<float*>(e.out)[i] = x;
+    } else {
+        const __half h = __float2half_rn(x);
+        reinterpret_cast<__half*>(e.out)[i] = h;
+        if (e.out_fmt == VKB_DT_F16X2) reinterpret_cast<__half*>(e.out)[e.plane + i] = __float2half_rn(x - __half2float(h));
+    }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(PCfg<FMT>::THREADS, 1)
+    tc_gemm_persist_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_lo,
+                           const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc, int64_t K, int64_t N,
+                           int64_t M, int n_tiles, int total_tiles, PEpi e, int* err) {
+    using C = PCfg<FMT>;
+    constexpr int BN = C::BN, S = C::S, AS = C::AS;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + S * C::STAGE_BYTES);
+    uint64_t* empty = full + S;
+    uint64_t* a_full = empty + S;
+    uint64_t* a_empty = a_full + AS;
+    uint64_t* acc_full = a_empty + AS;   // [2]
+    uint64_t* acc_empty = acc_full + 2;  // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nst = (int)(K / STAGE_K);
+    const int first = blockIdx.x, stride = gridDim.x;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            ptx::mbar_init(&full[i], 1);
+            ptx::mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < AS; ++i) {
+            ptx::mbar_init(&a_full[i], 32 * C::DEQ_WARPS);
+            ptx::mbar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            ptx::mbar_init(&acc_full[i], 1);
+            ptx::mbar_init(&acc_empty[i], C::EPI_WARPS);
+        }
+        ptx::fence_mbar_init();
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc(tmem_slot, 512);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+    // Programmatic dependent launch: weights are never written by a kernel, so
+    // the first ring stages' weights are fetched before waiting for the
+    // previous kernel; activations (producer) and outputs (epilogue) wait.
+    pdl_launch();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            auto load_weights = [&](int s, int n_tile, int i) {
+                uint8_t* raw_dst = ring + s * C::STAGE_BYTES + 2 * C::B_BYTES;
+                StagePtrs p = stage_ptrs(FMT, qs, sc, K, n_tile, i);
+                ptx::mbar_expect_tx(&full[s], 2 * C::B_BYTES + C::RAW_Q + C::RAW_S);
+                ptx::bulk_load(raw_dst, p.qs, C::RAW_Q, &full[s]);
+                if (C::RAW_S) ptx::bulk_load(raw_dst + C::RAW_Q, p.sc, C::RAW_S, &full[s]);
+            };
+            const int pre = nst < S ? nst : S;
+            for (int i = 0; i < pre; ++i) load_weights(i, first % n_tiles, i);
+            pdl_wait();
+            int g = 0;
+            for (int t = first; t < total_tiles && ok; t += stride) {
+                const int n_tile = t % n_tiles, m_tile = t / n_tiles;
+                for (int i = 0; i < nst; ++i, ++g) {
+                    const int s = g % S;
+                    if (g >= pre) {
+                        if (!ptx::mbar_wait(&empty[s], ((g / S) & 1) ^ 1)) {
+                            ok = false;
+                            break;
+                        }
+                        load_weights(s, n_tile, i);
+                    }
+                    uint8_t* b_dst = ring + s * C::STAGE_BYTES;
+                    ptx::tma_load_2d(b_dst, &xmap, &full[s], i * STAGE_K, m_tile * BN);
+                    ptx::tma_load_2d(b_dst + C::B_BYTES, &xmap_lo, &full[s], i * STAGE_K, m_tile * BN);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = ptx::idesc_f16_f32(TILE_N, BN);
+            int g = 0, tt = 0;
+            for (int t = first; t < total_tiles && ok; t += stride, ++tt) {
+                const int b = tt & 1;
+                if (!ptx::mbar_wait(&acc_empty[b], ((tt >> 1) & 1) ^ 1)) {
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                const uint32_t d_t = tmem + b * BN;
+                for (int i = 0; i < nst; ++i, ++g) {
+                    const int s = g % S, a = g % AS;
+                    if (!ptx::mbar_wait(&full[s], (g / S) & 1) || !ptx::mbar_wait(&a_full[a], (g / AS) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after();
+                    const uint32_t a_t = tmem + C::A_COL0 + a * 64;
+                    const uint32_t b_addr = ptx::smem_u32(ring + s * C::STAGE_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t bd = ptx::sdesc_sw128(b_addr + kk * 32);
+                        const uint64_t bd_lo = ptx::sdesc_sw128(b_addr + C::B_BYTES + kk * 32);
+                        ptx::mma_f16_ts(d_t, a_t + kk * 8, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                        ptx::mma_f16_ts(d_t, a_t + kk * 8, bd_lo, idesc, 1u);
+                        ptx::mma_f16_ts(d_t, a_t + 32 + kk * 8, bd, idesc, 1u);
+                    }
+                    ptx::mma_commit(&empty[s]);
+                    ptx::mma_commit(&a_empty[a]);
+                }
+                if (!ok) break;
+                ptx::mma_commit(&acc_full[b]);
+            }
+        }
+    } else if (warp < 2 + C::DEQ_WARPS) {
+        // dequantization: row r of the 128-row weight tile = tensor-memory lane r
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        int g = 0;
+        for (int t = first; t < total_tiles && ok; t += stride) {
+            for (int i = 0; i < nst; ++i, ++g) {
+                const int s = g % S, a = g % AS;
+                if (!ptx::mbar_wait(&full[s], (g / S) & 1) || !ptx::mbar_wait(&a_empty[a], ((g / AS) & 1) ^ 1)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* raw = ring + s * C::STAGE_BYTES + 2 * C::B_BYTES;
+                const uint32_t a_t = tmem + ((uint32_t)(quarter * 32) << 16) + C::A_COL0 + a * 64;
+                uint32_t hi[32], lo[32];
+                dequant_row_stage_h<FMT, true>(raw, raw + C::RAW_Q, r, i, hi, lo);
+                ptx::tc_fence_after();
+                ptx::tmem_st32(a_t, hi);
+                ptx::tmem_st32(a_t + 32, lo);
+                ptx::tmem_st_wait();
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(&a_full[a]);
+            }
+        }
+    } else {
+        // epilogue: warp w reads lane quarter w % 4; group (w - 6) / 4 takes half the columns
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const int cb = ((warp - 2 - C::DEQ_WARPS) >> 2) * (BN / 2);
+        const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+        pdl_wait();
+        int tt = 0;
+        for (int t = first; t < total_tiles && ok; t += stride, ++tt) {
+            const int b = tt & 1;
+            const int n_tile = t % n_tiles, m_tile = t / n_tiles;
+            if (!ptx::mbar_wait(&acc_full[b], (tt >> 1) & 1)) {
+                ok = false;
+                break;
+            }
+            ptx::tc_fence_after();
+            const int64_t n = (int64_t)n_tile * TILE_N + r;
+            const bool nv = n < N;
+            const float bias_n = (nv && e.bias) ? e.bias[n] : 0.0f;
+            const float scl = (e.kind == VKB_EPI_SCALE && n < e.n_scaled) ? e.scale : 1.0f;
+#pragma unroll 1
+            for (int c0 = cb; c0 < cb + BN / 2; c0 += 32) {
+                uint32_t v[32];
+                ptx::tmem_ld32(lane_base + b * BN + c0, v);
+                ptx::tmem_ld_wait();
+                const int64_t m0 = (int64_t)m_tile * BN + c0;
+                if (nv) {
+                    if (e.kind == VKB_EPI_RESIDUAL) {
+                        // all 32 residual loads in flight before any store (out may alias residual)
+                        float res[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            res[j] = (m0 + j < M) ? e.residual[(m0 + j) * e.ldo + n] : 0.0f;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + res[j]);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        float2 x = make_float2(__uint_as_float(v[j]) + bias_n, __uint_as_float(v[j + 1]) + bias_n);
+                        if (e.kind == VKB_EPI_GELU) {
+                            x = gelu_as_fast2(x);
+                        } else {
+                            x.x *= scl;
+                            x.y *= scl;
+                        }
+                        const int64_t i0 = (m0 + j) * e.ldo + n;
+                        if (m0 + j < M) pstore(e, i0, x.x);
+                        if (m0 + j + 1 < M) pstore(e, i0 + e.ldo, x.y);
+                    }
+                }
+            }
+            // accumulator buffer b may be overwritten by the MMAs of tile tt + 2
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&acc_empty[b]);
+        }
+    }
+    if (!ok && err) atomicExch(err, 1);
+    __syncwarp();
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, 512);
+    }
+}
+
+int persist_bn() { return PCfg<W_Q4_0>::BN; }
+
+template <int FMT>
+static void launch_persist(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e,
+                           int* err) {
+    using C = PCfg<FMT>;
+    static bool attr = false;
+    if (!attr) {
+        VKB_CUDA(cudaFuncSetAttribute(tc_gemm_persist_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      C::SMEM));
+        attr = true;
+    }
+    CUtensorMap map, map_lo;
+    make_tmap_f16(&map, a16, m, w->k, C::BN);
+    make_tmap_f16(&map_lo, a16 + m * w->k, m, w->k, C::BN);
+    const int n_tiles = (int)(w->n_pad / TILE_N);
+    const int m_tiles = (int)((m + C::BN - 1) / C::BN);
+    const int total = n_tiles * m_tiles;
+    const int grid = std::min(total, ctx->sm_count);
+    launch_pdl(ctx, tc_gemm_persist_kernel<FMT>, grid, C::THREADS, C::SMEM, map, map_lo, w->qs.as<uint8_t>(),
+               w->sc.as<uint8_t>(), w->k, w->n, m, n_tiles, total, e, err);
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
+}
+
+void run_tc_persistent(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e, int* err) {
+    switch (w->fmt) {
+        case W_Q4_0: launch_persist<W_Q4_0>(ctx, w, m, a16, e, err); break;
+        case W_Q8_0: launch_persist<W_Q8_0>(ctx, w, m, a16, e, err); break;
+        case W_Q4_K: launch_persist<W_Q4_K>(ctx, w, m, a16, e, err); break;
+        default: launch_persist<W_F16>(ctx, w, m, a16, e, err); break;
+    }
+}
+
+}  // namespace vkb

@@ -882,8 +882,24 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
             run_split_f16(ctx, reinterpret_cast<const float*>(a), m * w->k, dst, split);
             a16 = dst;
         }
-        if (p.split) dispatch_fmt<true>(ctx, w, m, a16, e, ws, p);
-        else dispatch_fmt<false>(ctx, w, m, a16, e, ws, p);
+        // Large-M split-precision GEMMs (the encoder): the persistent kernel
+        // with a double-buffered accumulator, when there are tiles for several
+        // waves and K is short enough (<= 20 stages) for the per-tile setup and
+        // epilogue it hides to matter; at longer K the 256-token tile of the
+        // classic kernel streams faster (encoder fc2, K = 5120: 2.45 vs 2.65 ms).
+        // VKB_GEMM_PERSIST: "0" never, "force" for every unsplit-K GEMM (tests).
+        const char* pv = std::getenv("VKB_GEMM_PERSIST");
+        const bool p_off = pv && pv[0] == '0', p_force = pv && pv[0] == 'f';
+        const int64_t p_tiles = (w->n_pad / TILE_N) * ((m + persist_bn() - 1) / persist_bn());
+        if (!p_off && p.split && p.splits == 1 && x.col_block == 0 && !x.row_map &&
+            (p_force || (p_tiles >= 4 * (int64_t)ctx->sm_count && w->k <= 20 * STAGE_K))) {
+            PEpi pe{bias, residual, out, out_dtype, epilogue, scale, w->n, e.n_scaled, e.plane};
+            run_tc_persistent(ctx, w, m, a16, pe, device_err_flag(ctx));
+        } else if (p.split) {
+            dispatch_fmt<true>(ctx, w, m, a16, e, ws, p);
+        } else {
+            dispatch_fmt<false>(ctx, w, m, a16, e, ws, p);
+        }
     }
     if (x.splits_out) *x.splits_out = p.splits;
     if (p.splits > 1 && !x.splits_out) {

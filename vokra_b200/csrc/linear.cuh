@@ -45,6 +45,24 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
                    __half* a16_override, const LinearExtra& x);
 void make_tmap_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows);
 int read_and_clear_err_flag(vkb_context* ctx);
+
+// Epilogue of the persistent encoder GEMM (gemm_persist.cu): out[m][n] =
+// op(acc + bias[n]) with op = GELU, scale (columns < n_scaled) or + residual.
+struct PEpi {
+    const float* bias;
+    const float* residual;
+    void* out;
+    int out_fmt;
+    int kind;
+    float scale;
+    int64_t ldo;
+    int64_t n_scaled;
+    int64_t plane;  // elements per plane of an F16X2 output
+};
+// Split-precision (hi+lo) GEMM over f16 activation planes a16 [2][m][k], one
+// CTA per SM over a static tile list; token tile persist_bn().
+void run_tc_persistent(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e, int* err);
+int persist_bn();
 int gemv_max_m();
 
 }  // namespace vkb
