@@ -53,6 +53,10 @@ def lib():
             "orc_pkv_page_bytes": (C.c_size_t, [P]),
             "orc_pkv_on_wire_bytes": (C.c_size_t, [P]),
             "orc_pkv_page": (None, [P, C.c_int, P, P]),
+            "orc_mel_filterbank": (None, [C.c_int, C.c_int, C.c_double, C.c_double, C.c_double, P]),
+            "orc_hann_periodic": (None, [C.c_int, P]),
+            "orc_log_mel_raw": (C.c_float, [P, C.c_int64, C.c_int, P]),
+            "orc_log_mel": (None, [P, C.c_int64, C.c_int, P]),
         }
         for n, (r, a) in sig.items():
             f = getattr(_l, n)
@@ -263,3 +267,24 @@ class PagedKv:
             lib().orc_pkv_destroy(self.h)
         except Exception:
             pass
+
+
+def mel_filterbank(n_mels: int, n_fft: int = 400, sr: float = 16000.0, fmin: float = 0.0, fmax: float = 8000.0):
+    """MelFilterbank::new (Slaney scale and norm, Hz interpolation): [n_mels, n_fft/2+1] f32."""
+    w = np.empty((n_mels, n_fft // 2 + 1), np.float32)
+    lib().orc_mel_filterbank(n_fft, n_mels, sr, fmin, fmax, _p(w))
+    return w
+
+
+def hann_periodic(n: int):
+    w = np.empty(n, np.float32)
+    lib().orc_hann_periodic(n, _p(w))
+    return w
+
+
+def log_mel(pcm, n_mels: int):
+    """whisper::mel::log_mel: [n_mels, 3000] log-mel features of one clip of 16 kHz PCM."""
+    x = np.ascontiguousarray(pcm, dtype=np.float32)
+    out = np.empty((n_mels, 3000), np.float32)
+    lib().orc_log_mel(_p(x) if x.size else None, x.size, n_mels, _p(out))
+    return out
