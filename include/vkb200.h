@@ -342,6 +342,19 @@ VKB_API const int32_t* vkb_session_ids(const vkb_session* s);
 /* Returns a finished stream's KV pages to the pool (continuous batching). */
 VKB_API vkb_status vkb_session_release(vkb_session* s, int32_t stream);
 
+/* ---- Whisper log-mel frontend --------------------------------------------
+ * Replaces vokra_models::whisper::mel::log_mel(pcm, n_mels)
+ * (crates/vokra-models/src/whisper/mel.rs:123, via
+ * crates/vokra-ops/src/fused_logmel.rs:80) for a batch of clips.
+ * pcm_dev: n_clips rows of `stride` f32 samples at 16 kHz (row c starts at
+ * pcm_dev + c*stride); lengths_dev (device int32, may be NULL = all `stride`)
+ * gives each clip's valid samples, the rest reads as zeros. Every clip is
+ * zero-padded or trimmed to 30 s as the reference does. out_dev: f32
+ * [n_clips][n_mels][3000], the layout vkb_session_encode takes. n_mels in
+ * 1..256 (80 or 128 for Whisper). Asynchronous on the context's stream. */
+VKB_API vkb_status vkb_log_mel(vkb_context* ctx, const float* pcm_dev, int64_t n_clips, int64_t stride,
+                               const int32_t* lengths_dev, int32_t n_mels, float* out_dev);
+
 #ifdef __cplusplus
 }
 #endif

@@ -91,6 +91,8 @@ struct vkb_context {
     unsigned long long* trace = nullptr;  // debugging aid: GEMM block-0 timeline (VKB_TRACE)
     vkb::DevBuf workspace;
     vkb::DevBuf err_flag;  // int set by a kernel whose bounded wait gave up
+    vkb::DevBuf frontend;  // log-mel tables (window, twiddles, mel bank) + per-clip maxima
+    int frontend_mels = 0; // mel count the tables were built for
     // Programmatic dependent launch: each kernel may start while the previous
     // one in the stream drains; it waits (griddepcontrol.wait) before touching
     // anything that kernel wrote (VKB_PDL=0 turns it off).

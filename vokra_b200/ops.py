@@ -283,3 +283,20 @@ def attention_dense(ctx: Context, q, seq_of_tok, k, v, n_ctx: int, n_head: int, 
 def quantize_rows_q8_0(ctx: Context, x, q_out, d_out):
     check(_L.vkb_quantize_rows_q8_0(ctx.h, C.c_void_p(_ptr(x)), x.shape[0], x.shape[1], C.c_void_p(_ptr(q_out)),
                                     C.c_void_p(_ptr(d_out))))
+
+
+def log_mel(ctx: Context, pcm, n_mels: int, out=None, lengths=None):
+    """whisper::mel::log_mel on the device for a batch: pcm is a torch f32
+    [n_clips, n_samples] CUDA tensor (16 kHz); lengths (optional int32 CUDA
+    tensor) the valid samples per clip. Returns (or fills) f32
+    [n_clips, n_mels, 3000]."""
+    import torch
+    if pcm.dim() == 1:
+        pcm = pcm.unsqueeze(0)
+    assert pcm.dtype == torch.float32 and pcm.is_contiguous()
+    n = pcm.shape[0]
+    if out is None:
+        out = torch.empty((n, n_mels, 3000), dtype=torch.float32, device=pcm.device)
+    check(_L.vkb_log_mel(ctx.h, C.c_void_p(_ptr(pcm)) if pcm.numel() else None, n, pcm.shape[1],
+                         C.c_void_p(_ptr(lengths)) if lengths is not None else None, n_mels, C.c_void_p(_ptr(out))))
+    return out
