@@ -328,6 +328,14 @@ VKB_API vkb_status vkb_session_encode(vkb_session* s, int32_t n_clips, const flo
 VKB_API const float* vkb_session_encoder_output(const vkb_session* s);
 /* Synchronous copy of the first n_floats of that output to host memory. */
 VKB_API vkb_status vkb_session_read_encoder_output(const vkb_session* s, float* host, size_t n_floats);
+/* Device pointers to decoder layer `layer`'s cross-attention K/V store, rows
+ * stream*n_audio_ctx + t of d_model channels: Q8_0 quants (int8) with one f16
+ * scale per 32 channels when the session was created with cross_kv_q8 (the
+ * scale pointers are NULL for the f16 store). Rows of a stream are valid after
+ * vkb_session_encode wrote it. The counterpart of the reference's
+ * project_kv_into result (whisper/nn.rs:185, decoder.rs:205-216). */
+VKB_API vkb_status vkb_session_cross_kv(const vkb_session* s, int32_t layer, const void** k, const void** v,
+                                        const void** k_scale, const void** v_scale);
 /* One decoder step over n_tok tokens (token i of stream streams_host[i] at
  * position positions_host[i]; tokens of one stream contiguous and
  * consecutive): appends their self-attention K/V, writes logits

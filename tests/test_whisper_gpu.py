@@ -157,3 +157,47 @@ def test_whisper_full_window_persistent_gemm(ctx, tmp_path, monkeypatch):
     for got, ref in results:
         assert np.max(np.abs(got - ref)) <= 1e-2
         assert _rel_rms(got, ref) <= 1e-3
+
+
+def _cross_store(sess, layer, rows, d):
+    """Host copies of a session's Q8_0 cross K/V store of one decoder layer."""
+    import ctypes as C
+    from cuda.bindings import runtime as rt
+    from vokra_b200 import _lib
+    ptr = [C.c_void_p() for _ in range(4)]
+    _lib.check(_lib.load().vkb_session_cross_kv(sess.h, layer, *[C.byref(p) for p in ptr]))
+    out = []
+    for p, n in zip(ptr, (rows * d, rows * d, rows * d // 16, rows * d // 16)):
+        h = np.empty(n, np.uint8)
+        err, = rt.cudaMemcpy(h.ctypes.data, p.value, n, rt.cudaMemcpyKind.cudaMemcpyDeviceToHost)
+        assert int(err) == 0
+        out.append(h)
+    return out
+
+
+def test_fused_cross_kv_q8_bytes(ctx, tmp_path, monkeypatch):
+    """The cross K/V projection with Q8_0 packing in the persistent GEMM's
+    epilogue writes the same store bytes as the f32 projection followed by
+    the quantize kernel (BlockQ8_0::pack), clips remapped to stream slots."""
+    import torch
+    from vokra_b200 import whisper
+    monkeypatch.setenv("VKB_GEMM_PERSIST", "force")
+    arch = synth.WhisperArch(80, 1500, 512, 8, 1, 64, 8, 2, 1000, 2048, 999, (1, 2, 3, 4))
+    path = str(tmp_path / "xq.gguf")
+    synth.write_synthetic_whisper(path, arch, synth.Q4_0, seed=6)
+    rng = np.random.default_rng(3)
+    logmel = torch.from_numpy(rng.uniform(-1.0, 1.5, (2, 80, 3000)).astype(np.float32)).cuda()
+    model = whisper.WhisperModel(ctx, path)
+    stores = []
+    for fused in ("1", "0"):
+        monkeypatch.setenv("VKB_FUSED_CROSS_Q8", fused)
+        sess = whisper.Session(model, max_streams=3, max_clips=2, cross_kv_q8=True)
+        sess.encode(logmel, [2, 0])  # clips land in stream slots 2 and 0
+        torch.cuda.synchronize()
+        stores.append([_cross_store(sess, layer, 3 * 1500, 512) for layer in range(2)])
+        sess.close()
+    rows = np.r_[0:1500, 3000:4500]  # the written slots
+    for layer in range(2):
+        for a, b, per_row in zip(stores[0][layer], stores[1][layer], (512, 512, 32, 32)):
+            a2, b2 = a.reshape(-1, per_row)[rows], b.reshape(-1, per_row)[rows]
+            assert np.array_equal(a2, b2), layer

@@ -60,6 +60,56 @@ __device__ __forceinline__ void pstore(const PEpi& e, int64_t i, float x) {
     }
 }
 
+// Max over the warp's 32 lanes of each of 32 values, transposed: lane l returns
+// the maximum of x[l] over all lanes. A butterfly that halves the values each
+// lane carries (16 + 8 + 4 + 2 + 1 shuffles, all independent within a step);
+// fmaxf drops NaN as the reference's f32::max does.
+__device__ __forceinline__ float transpose_max32(const float (&x)[32], int lane) {
+    float a[16], b[8], c[4], d[2];
+    {
+        const bool hi = lane & 16;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const float keep = fabsf(hi ? x[k + 16] : x[k]), send = fabsf(hi ? x[k] : x[k + 16]);
+            a[k] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 16));
+        }
+    }
+    {
+        const bool hi = lane & 8;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float keep = hi ? a[k + 8] : a[k], send = hi ? a[k] : a[k + 8];
+            b[k] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+        }
+    }
+    {
+        const bool hi = lane & 4;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float keep = hi ? b[k + 4] : b[k], send = hi ? b[k] : b[k + 4];
+            c[k] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+        }
+    }
+    {
+        const bool hi = lane & 2;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const float keep = hi ? c[k + 2] : c[k], send = hi ? c[k] : c[k + 2];
+            d[k] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+        }
+    }
+    const bool hi = lane & 1;
+    const float keep = hi ? d[1] : d[0], send = hi ? d[0] : d[1];
+    return fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 1));
+}
+
+// Store row of token m under the Q8 pair output's row-group map.
+__device__ __forceinline__ int64_t q8_row(const PEpi& e, int64_t m) {
+    if (!e.row_map) return m;
+    const unsigned g = (unsigned)m / (unsigned)e.row_group;
+    return (int64_t)e.row_map[g] * e.row_group + ((unsigned)m - g * (unsigned)e.row_group);
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(PCfg<FMT>::THREADS, 1)
     tc_gemm_persist_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_lo,
@@ -218,6 +268,45 @@ __global__ void __launch_bounds__(PCfg<FMT>::THREADS, 1)
             ptx::tc_fence_after();
             const int64_t n = (int64_t)n_tile * TILE_N + r;
             const bool nv = n < N;
+            if (e.q8_width > 0) {
+                // Q8_0 pair output: this warp's 32 rows (features) are one 32-channel block of the
+                // K or V store row of each token (BlockQ8_0::pack, q8_0.rs:40-66), 32 tokens at a time
+                const int half = n_tile * TILE_N >= e.q8_width;
+                const int64_t c = n - half * e.q8_width;
+                const int blk = (int)(c >> 5), nb = (int)(e.q8_width >> 5);
+                int8_t* qb = half ? e.q8[1] : e.q8[0];
+                __half* db = half ? e.q8d[1] : e.q8d[0];
+                const float bias_q = e.bias ? e.bias[n] : 0.0f;
+#pragma unroll 1
+                for (int c0 = cb; c0 < cb + BN / 2; c0 += 32) {
+                    uint32_t v[32];
+                    ptx::tmem_ld32(lane_base + b * BN + c0, v);
+                    ptx::tmem_ld_wait();
+                    const int64_t m0 = (int64_t)m_tile * BN + c0;
+                    float x[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(v[j]) + bias_q;
+                    // lane l ends with the block amax of token m0 + l, then its scale and inverse
+                    const float amax = fmaxf(0.0f, transpose_max32(x, lane));
+                    const float dq = amax == 0.0f ? 0.0f : amax / 127.0f;
+                    const float inv = dq == 0.0f ? 0.0f : 1.0f / dq;
+                    const int64_t my_m = m0 + lane;
+                    if (my_m < M)
+                        *reinterpret_cast<uint16_t*>(db + q8_row(e, my_m) * nb + blk) = f32_to_f16_bits(dq);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float inv_j = __shfl_sync(0xffffffffu, inv, j);
+                        if (m0 + j >= M) continue;  // uniform across the warp
+                        const float sq = x[j] * inv_j;
+                        const float c = sq < -127.0f ? -127.0f : (sq > 127.0f ? 127.0f : sq);
+                        qb[q8_row(e, m0 + j) * e.q8_width + blk * 32 + lane] = isnan(c) ? (int8_t)0 : (int8_t)(int)roundf(c);
+                    }
+                }
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&acc_empty[b]);
+                continue;
+            }
             const float bias_n = (nv && e.bias) ? e.bias[n] : 0.0f;
             const float scl = (e.kind == VKB_EPI_SCALE && n < e.n_scaled) ? e.scale : 1.0f;
 #pragma unroll 1

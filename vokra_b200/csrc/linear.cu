@@ -893,7 +893,16 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
         const int64_t p_tiles = (w->n_pad / TILE_N) * ((m + persist_bn() - 1) / persist_bn());
         if (!p_off && p.split && p.splits == 1 && x.col_block == 0 && !x.row_map &&
             (p_force || (p_tiles >= 4 * (int64_t)ctx->sm_count && w->k <= 20 * STAGE_K))) {
-            PEpi pe{bias, residual, out, out_dtype, epilogue, scale, w->n, e.n_scaled, e.plane};
+            PEpi pe;
+            pe.bias = bias;
+            pe.residual = residual;
+            pe.out = out;
+            pe.out_fmt = out_dtype;
+            pe.kind = epilogue;
+            pe.scale = scale;
+            pe.ldo = w->n;
+            pe.n_scaled = e.n_scaled;
+            pe.plane = e.plane;
             run_tc_persistent(ctx, w, m, a16, pe, device_err_flag(ctx));
         } else if (p.split) {
             dispatch_fmt<true>(ctx, w, m, a16, e, ws, p);
@@ -908,6 +917,37 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
         VKB_CUDA(cudaGetLastError());
         ctx->count();
     }
+}
+
+bool run_linear_q8_pair(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const float* bias,
+                        int64_t width, int8_t* kq, __half* kd, int8_t* vq, __half* vd, const int32_t* row_map,
+                        int row_group) {
+    const char* pv = std::getenv("VKB_GEMM_PERSIST");
+    if (pv && pv[0] == '0') return false;
+    const char* fq = std::getenv("VKB_FUSED_CROSS_Q8");
+    if (fq && fq[0] == '0') return false;
+    if (ctx->precision != VKB_PREC_SPLIT || m <= 0 || w->n != 2 * width || width % TILE_N || w->n_pad != w->n)
+        return false;
+    if (plan_linear(ctx, w, m, true).splits != 1) return false;
+    PEpi pe;
+    pe.bias = bias;
+    pe.residual = nullptr;
+    pe.out = nullptr;
+    pe.out_fmt = VKB_DT_F32;
+    pe.kind = VKB_EPI_NONE;
+    pe.scale = 1.0f;
+    pe.ldo = w->n;
+    pe.n_scaled = w->n;
+    pe.plane = 0;
+    pe.q8_width = width;
+    pe.q8[0] = kq;
+    pe.q8[1] = vq;
+    pe.q8d[0] = kd;
+    pe.q8d[1] = vd;
+    pe.row_map = row_map;
+    pe.row_group = row_group > 0 ? row_group : 1;
+    run_tc_persistent(ctx, w, m, a16, pe, device_err_flag(ctx));
+    return true;
 }
 
 int read_and_clear_err_flag(vkb_context* ctx) {

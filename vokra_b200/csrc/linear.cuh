@@ -58,11 +58,27 @@ struct PEpi {
     int64_t ldo;
     int64_t n_scaled;
     int64_t plane;  // elements per plane of an F16X2 output
+    // Q8_0 pair output (the cross K/V projection): when q8_width > 0, columns
+    // [0, q8_width) are packed as Q8_0 rows into q8[0] / q8d[0] and columns
+    // [q8_width, 2 q8_width) into q8[1] / q8d[1] (BlockQ8_0::pack per 32
+    // columns); token m lands in row row_map[m / row_group] * row_group +
+    // m % row_group. out / out_fmt are unused then.
+    int64_t q8_width = 0;
+    int8_t* q8[2] = {nullptr, nullptr};
+    __half* q8d[2] = {nullptr, nullptr};
+    const int32_t* row_map = nullptr;
+    int row_group = 1;
 };
 // Split-precision (hi+lo) GEMM over f16 activation planes a16 [2][m][k], one
 // CTA per SM over a static tile list; token tile persist_bn().
 void run_tc_persistent(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e, int* err);
 int persist_bn();
+// out = Q8_0(a . W^T + bias) split into a K and a V store (see PEpi::q8_width)
+// on the persistent kernel; false (nothing launched) when the shape or
+// precision does not take it.
+bool run_linear_q8_pair(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const float* bias,
+                        int64_t width, int8_t* kq, __half* kd, int8_t* vq, __half* vd, const int32_t* row_map,
+                        int row_group);
 int gemv_max_m();
 
 }  // namespace vkb

@@ -424,13 +424,17 @@ void session_encode(vkb_session* s, int n, const float* logmel, const int32_t* s
     for (int l = 0; l < D.n_text_layer; ++l) {
         const DecLayer& L = m->dec[l];
         if (s->opt.cross_kv_q8) {
-            float* tmp = reinterpret_cast<float*>(bufA);  // [M][2d] f32
-            run_linear(ctx, L.ckv.get(), M, xln, AF, L.ckv_b.as<float>(), tmp, VKB_DT_F32, VKB_EPI_NONE,
-                       nullptr, 1.0f, ws, nullptr);
             int8_t* kq = s->ck.as<int8_t>() + (size_t)l * rows * d;
             int8_t* vq = s->cv.as<int8_t>() + (size_t)l * rows * d;
             __half* ks = s->cks.as<__half>() + (size_t)l * rows * (d / 32);
             __half* vs = s->cvs.as<__half>() + (size_t)l * rows * (d / 32);
+            // the projection's epilogue packs Q8_0 rows straight into the store (no f32 round trip)
+            if (split && run_linear_q8_pair(ctx, L.ckv.get(), M, xln, L.ckv_b.as<float>(), d, kq, ks, vq, vs, map,
+                                            (int)T))
+                continue;
+            float* tmp = reinterpret_cast<float*>(bufA);  // [M][2d] f32
+            run_linear(ctx, L.ckv.get(), M, xln, AF, L.ckv_b.as<float>(), tmp, VKB_DT_F32, VKB_EPI_NONE,
+                       nullptr, 1.0f, ws, nullptr);
             run_quantize_rows(ctx, tmp, 2 * d, M, (int)d, kq, ks, map, (int)T);
             run_quantize_rows(ctx, tmp + d, 2 * d, M, (int)d, vq, vs, map, (int)T);
         } else {
@@ -636,6 +640,26 @@ vkb_status vkb_session_encode(vkb_session* s, int32_t n_clips, const float* logm
 }
 
 const float* vkb_session_encoder_output(const vkb_session* s) { return s ? s->eout.as<float>() : nullptr; }
+
+vkb_status vkb_session_cross_kv(const vkb_session* s, int32_t layer, const void** k, const void** v,
+                                const void** k_scale, const void** v_scale) {
+    return guard([&] {
+        if (!s || !k || !v || !k_scale || !v_scale) fail(VKB_ERROR_INVALID_ARGUMENT, "cross_kv: null argument");
+        if (layer < 0 || layer >= s->m->dims.n_text_layer) fail(VKB_ERROR_INVALID_ARGUMENT, "cross_kv: bad layer");
+        const int64_t d = s->m->dims.d_model;
+        const size_t rows = (size_t)s->opt.max_streams * s->m->dims.n_audio_ctx;
+        if (s->opt.cross_kv_q8) {
+            *k = s->ck.as<int8_t>() + (size_t)layer * rows * d;
+            *v = s->cv.as<int8_t>() + (size_t)layer * rows * d;
+            *k_scale = s->cks.as<__half>() + (size_t)layer * rows * (d / 32);
+            *v_scale = s->cvs.as<__half>() + (size_t)layer * rows * (d / 32);
+        } else {
+            *k = s->ck.as<__half>() + (size_t)layer * rows * d;
+            *v = s->cv.as<__half>() + (size_t)layer * rows * d;
+            *k_scale = *v_scale = nullptr;
+        }
+    });
+}
 
 vkb_status vkb_session_read_encoder_output(const vkb_session* s, float* host, size_t n_floats) {
     return guard([&] {
