@@ -97,8 +97,8 @@ __global__ void __launch_bounds__(256) paged_decode_kernel(
     void* out, int out_fmt, int64_t out_plane) {
     pdl_entry();
     extern __shared__ __align__(16) float pd_smem[];
-    float* sc = pd_smem;                               // [4][max_keys]; later the [4][256] P.V sums
-    float* qs = sc + (4 * max_keys > 1024 ? 4 * max_keys : 1024);  // [256]
+    float* sc = pd_smem;                               // [4][max_keys]; later the [16][256] P.V sums
+    float* qs = sc + (4 * max_keys > 4096 ? 4 * max_keys : 4096);  // [256]
     int64_t* rows_s = reinterpret_cast<int64_t*>(qs + 256);               // [max_keys]
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const AttnGroup g = groups[blockIdx.x];
@@ -170,32 +170,40 @@ __global__ void __launch_bounds__(256) paged_decode_kernel(
         for (int k = lane; k < n_keys; k += 32) s[k] *= inv;
     }
     __syncthreads();
-    // phase 3: P.V; thread = (channel quad t % 64, key group t / 64): 4 bytes
-    // of V per key over every 4th key, the 4 key groups summed in shared memory
+    // phase 3: P.V; thread = (16-channel group t % 16, key group t / 16): one
+    // 16-byte load of V per key over every 16th key (16 loads in flight per
+    // 16 keys), the 16 key groups summed in shared memory
     {
-        const int cq = t & 63, kg = t >> 6;
-        const float* p = sc + (cq >> 4) * max_keys;
-        const uint32_t* vcol = reinterpret_cast<const uint32_t*>(vq + c0) + cq;
-        const __half* vdc = vd + b0 + (cq >> 3);
-        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-#pragma unroll 4
-        for (int k = kg; k < n_keys; k += 4) {
+        const int cg = t & 15, kg = t >> 4;
+        const float* p = sc + (cg >> 2) * max_keys;
+        const int8_t* vcol = vq + c0 + 16 * cg;
+        const __half* vdc = vd + b0 + (cg >> 1);
+        float a[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) a[i] = 0.0f;
+#pragma unroll 2
+        for (int k = kg; k < n_keys; k += 16) {
             const int64_t row = rows_s[k];
-            const uint32_t v = __ldcg(vcol + row * (W / 4)) ^ 0x80808080u;
+            const uint4 v4 = __ldcg(reinterpret_cast<const uint4*>(vcol + row * W));
             const float w = p[k] * __half2float(__ldcg(vdc + row * nb));
-            a0 = fmaf(w, __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7440u)) - 8388736.0f, a0);
-            a1 = fmaf(w, __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7441u)) - 8388736.0f, a1);
-            a2 = fmaf(w, __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7442u)) - 8388736.0f, a2);
-            a3 = fmaf(w, __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7443u)) - 8388736.0f, a3);
+            const uint32_t vw[4] = {v4.x ^ 0x80808080u, v4.y ^ 0x80808080u, v4.z ^ 0x80808080u, v4.w ^ 0x80808080u};
+#pragma unroll
+            for (int wd = 0; wd < 4; ++wd)
+#pragma unroll
+                for (int bb = 0; bb < 4; ++bb)
+                    a[4 * wd + bb] = fmaf(w, __uint_as_float(__byte_perm(vw[wd], 0x4B000000u, 0x7440u + bb)) - 8388736.0f,
+                                          a[4 * wd + bb]);
         }
         __syncthreads();  // the score rows are no longer read: reuse them for the key-group sums
-        float* red = sc;  // [4][256]
-        red[kg * 256 + 4 * cq + 0] = a0;
-        red[kg * 256 + 4 * cq + 1] = a1;
-        red[kg * 256 + 4 * cq + 2] = a2;
-        red[kg * 256 + 4 * cq + 3] = a3;
+        float* red = sc;  // [16][256]
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<float4*>(red + kg * 256 + 16 * cg + 4 * i) =
+                make_float4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]);
         __syncthreads();
-        const float acc = (red[t] + red[256 + t]) + (red[512 + t] + red[768 + t]);
+        float acc = 0.0f;
+#pragma unroll
+        for (int g2 = 0; g2 < 16; ++g2) acc += red[g2 * 256 + t];
         const int64_t o = (int64_t)tok * W + c0 + t;
         if (out_fmt == 0) {
             reinterpret_cast<float*>(out)[o] = acc;
@@ -661,7 +669,7 @@ void kv_append_attention_ex(vkb_kv_pool* p, int layer, const float* qkv, int64_t
         return;
     }
     const int max_keys = d.max_time;
-    const size_t smem = (size_t)(std::max(4 * max_keys, 1024) + 256) * sizeof(float) + (size_t)max_keys * sizeof(int64_t);
+    const size_t smem = (size_t)(std::max(4 * max_keys, 4096) + 256) * sizeof(float) + (size_t)max_keys * sizeof(int64_t);
     static bool attr = false;
     if (!attr) {
         VKB_CUDA(cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
