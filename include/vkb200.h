@@ -349,6 +349,17 @@ VKB_API const float* vkb_session_logits(const vkb_session* s);
 VKB_API const int32_t* vkb_session_ids(const vkb_session* s);
 /* Returns a finished stream's KV pages to the pool (continuous batching). */
 VKB_API vkb_status vkb_session_release(vkb_session* s, int32_t stream);
+/* Branches a decode stream: stream dst becomes a copy of the first n_pos
+ * positions of stream src's self-attention cache (dst's own pages are
+ * released first), so dst continues at position n_pos exactly as src would.
+ * With copy_cross != 0 dst's cross-attention K/V rows are also copied from
+ * src (once per clip: beams of one clip share them afterwards). This is the
+ * per-beam branch of beam search: the reference deep-copies the host cache
+ * (selfkv_snapshot / selfkv_restore, whisper/decoder.rs:343-368); here the
+ * pages are copied on the device in one launch. Asynchronous on the context's
+ * stream. */
+VKB_API vkb_status vkb_session_copy_stream(vkb_session* s, int32_t src, int32_t dst, int32_t n_pos,
+                                           int32_t copy_cross);
 
 /* ---- Whisper log-mel frontend --------------------------------------------
  * Replaces vokra_models::whisper::mel::log_mel(pcm, n_mels)

@@ -113,6 +113,7 @@ SIGNATURES = {
     "vkb_kv_read_step": (C.c_int, [P, I32, I32, I32, P, P]),
     "vkb_attention_dense": (C.c_int, [P, I32, I32, I32, P, P, P, P, P, P, I32, I32, P, I32]),
     "vkb_log_mel": (C.c_int, [P, P, I64, I64, P, I32, P]),
+    "vkb_session_copy_stream": (C.c_int, [P, I32, I32, I32, I32]),
     "vkb_session_cross_kv": (C.c_int, [P, I32, P, P, P, P]),
     "vkb_quantize_rows_q8_0": (C.c_int, [P, P, I64, I32, P, P]),
     "vkb_attention_dense_noalloc": (C.c_int, [P, I32, I32, I32, P, P, P, P, P, P, I32, I32, P, I32]),

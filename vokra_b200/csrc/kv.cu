@@ -36,6 +36,7 @@ struct vkb_kv_pool {
     DevBuf rows_dev;                 // int64 [n_layer][max_step]: row of each step token per layer
     DevBuf groups_dev;               // AttnGroup [max_groups]
     DevBuf part_dev;                 // split partials of the attention
+    DevBuf pairs_dev;                // (source, destination) pages of a stream copy
     int max_step = 0;
     // pinned staging
     int32_t* h_table = nullptr;
@@ -748,6 +749,81 @@ void kv_attention_ex(vkb_kv_pool* p, int layer, const float* q, int64_t q_ld, vo
 }
 
 // Zeroes the device rows of one page (all layers' arenas for SEQUENCE layout).
+// Copies whole pages of every layer (SEQUENCE layout): pair i = (source page,
+// destination page); one CTA per (pair, layer), 16-byte moves of the K and V
+// quants and scales of the page's rows.
+__global__ void kv_copy_pages_kernel(const int2* __restrict__ pairs, int64_t n_pages, int bs, int W, int8_t* kq,
+                                     __half* kd, int8_t* vq, __half* vd) {
+    pdl_entry();
+    const int2 pr = pairs[blockIdx.x];
+    const int64_t layer = blockIdx.y;
+    const int nb = W / 32;
+    const int64_t src = (layer * n_pages + pr.x) * bs, dst = (layer * n_pages + pr.y) * bs;
+    const int qn = bs * W / 16, sn = bs * nb * 2 / 16;
+    const uint4* ks = reinterpret_cast<const uint4*>(kq + src * W);
+    const uint4* vs = reinterpret_cast<const uint4*>(vq + src * W);
+    uint4* kdst = reinterpret_cast<uint4*>(kq + dst * W);
+    uint4* vdst = reinterpret_cast<uint4*>(vq + dst * W);
+    for (int i = threadIdx.x; i < qn; i += blockDim.x) {
+        kdst[i] = ks[i];
+        vdst[i] = vs[i];
+    }
+    const uint4* kss = reinterpret_cast<const uint4*>(kd + src * nb);
+    const uint4* vss = reinterpret_cast<const uint4*>(vd + src * nb);
+    uint4* ksd = reinterpret_cast<uint4*>(kd + dst * nb);
+    uint4* vsd = reinterpret_cast<uint4*>(vd + dst * nb);
+    for (int i = threadIdx.x; i < sn; i += blockDim.x) {
+        ksd[i] = kss[i];
+        vsd[i] = vss[i];
+    }
+}
+
+// Makes stream dst a copy of the first n_pos positions of stream src (the
+// per-beam branch of the self-attention cache; the reference deep-copies the
+// host cache, whisper/decoder.rs:343-368): dst's pages are released, fresh
+// pages are acquired for src's first ceil(n_pos / page_tokens) pages and
+// filled on the device in one launch.
+void kv_copy_stream(vkb_kv_pool* p, int src, int dst, int n_pos) {
+    const auto& d = p->d;
+    if (d.layout != VKB_KV_LAYOUT_SEQUENCE) fail(VKB_ERROR_INVALID_ARGUMENT, "copy_stream: sequence layout only");
+    if (src < 0 || src >= d.n_stream || dst < 0 || dst >= d.n_stream)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "copy_stream: bad stream");
+    if (n_pos < 0 || n_pos > d.max_time) fail(VKB_ERROR_INVALID_ARGUMENT, "copy_stream: bad position count");
+    if (src == dst) return;
+    if (d.page_tokens * (p->W / 32) * 2 % 16) fail(VKB_ERROR_UNSUPPORTED_OP, "copy_stream: page scales not 16-byte sized");
+    for (int i = 0; i < p->ppseq; ++i) {
+        int32_t& e = p->table[(int64_t)dst * p->ppseq + i];
+        if (e >= 0) {
+            p->free_list.push_back(e);
+            e = -1;
+        }
+    }
+    std::vector<int2> pairs;
+    const int n_pg = (n_pos + d.page_tokens - 1) / d.page_tokens;
+    for (int i = 0; i < n_pg; ++i) {
+        const int32_t sp = p->table[(int64_t)src * p->ppseq + i];
+        if (sp < 0) fail(VKB_ERROR_INVALID_ARGUMENT, "copy_stream: source stream has no page for position " +
+                                                         std::to_string(i * d.page_tokens));
+        const int32_t dp = acquire(p);
+        p->table[(int64_t)dst * p->ppseq + i] = dp;
+        pairs.push_back(make_int2(sp, dp));
+    }
+    upload_table(p);
+    if (pairs.empty()) return;
+    if (p->pairs_dev.n < pairs.size() * sizeof(int2)) {
+        VKB_CUDA(cudaStreamSynchronize(p->ctx->stream));
+        p->pairs_dev.alloc((size_t)p->ppseq * sizeof(int2));
+    }
+    // pageable source: the copy is staged before cudaMemcpyAsync returns
+    VKB_CUDA(cudaMemcpyAsync(p->pairs_dev.p, pairs.data(), pairs.size() * sizeof(int2), cudaMemcpyHostToDevice,
+                             p->ctx->stream));
+    dim3 grid((unsigned)pairs.size(), (unsigned)d.n_layer);
+    launch_pdl(p->ctx, kv_copy_pages_kernel, grid, 256, 0, p->pairs_dev.as<int2>(), p->n_pages, d.page_tokens, p->W,
+               p->kq.as<int8_t>(), p->kd.as<__half>(), p->vq.as<int8_t>(), p->vd.as<__half>());
+    VKB_CUDA(cudaGetLastError());
+    p->ctx->count();
+}
+
 static void zero_page(vkb_kv_pool* p, int32_t pid, int layer_for_seq) {
     cudaStream_t st = p->ctx->stream;
     auto z = [&](int64_t row0, int64_t nrows) {

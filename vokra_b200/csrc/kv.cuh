@@ -17,6 +17,7 @@ bool kv_decode_fused(const vkb_kv_pool* p);
 void kv_append_attention_ex(vkb_kv_pool* p, int layer, const float* qkv, int64_t ld, void* out, int out_dtype,
                             const float* part = nullptr, int splits = 0, const float* bias = nullptr,
                             float qscale = 1.0f);
+void kv_copy_stream(vkb_kv_pool* p, int src, int dst, int n_pos);
 void kv_attention_ex(vkb_kv_pool* p, int layer, const float* q, int64_t q_ld, void* out, int out_dtype);
 void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, const float* q, const int32_t* seq_of_tok,
                          const void* k, const void* v, const void* k_scale, const void* v_scale, int n_ctx,

@@ -681,6 +681,40 @@ vkb_status vkb_session_step(vkb_session* s, int32_t n_tok, const int32_t* stream
 const float* vkb_session_logits(const vkb_session* s) { return s ? s->logits.as<float>() : nullptr; }
 const int32_t* vkb_session_ids(const vkb_session* s) { return s ? s->ids.as<int32_t>() : nullptr; }
 
+vkb_status vkb_session_copy_stream(vkb_session* s, int32_t src, int32_t dst, int32_t n_pos, int32_t copy_cross) {
+    return guard([&] {
+        if (!s) fail(VKB_ERROR_INVALID_ARGUMENT, "session_copy_stream: null session");
+        if (src < 0 || src >= s->opt.max_streams || dst < 0 || dst >= s->opt.max_streams)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "session_copy_stream: stream out of range");
+        if (n_pos < 0 || n_pos > s->m->dims.n_text_ctx)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "session_copy_stream: n_pos out of range");
+        kv_copy_stream(s->pool, src, dst, n_pos);
+        if (copy_cross && src != dst) {
+            const auto& D = s->m->dims;
+            const int64_t d = D.d_model, T = D.n_audio_ctx, rows = (int64_t)s->opt.max_streams * T;
+            const size_t qb = s->opt.cross_kv_q8 ? 1 : 2;  // bytes per element of the store
+            for (int l = 0; l < D.n_text_layer; ++l) {
+                const size_t layer0 = (size_t)l * rows, sz = (size_t)T * d * qb;
+                uint8_t* ck = s->ck.as<uint8_t>() + layer0 * d * qb;
+                uint8_t* cv = s->cv.as<uint8_t>() + layer0 * d * qb;
+                VKB_CUDA(cudaMemcpyAsync(ck + (size_t)dst * sz, ck + (size_t)src * sz, sz, cudaMemcpyDeviceToDevice,
+                                         s->ctx->stream));
+                VKB_CUDA(cudaMemcpyAsync(cv + (size_t)dst * sz, cv + (size_t)src * sz, sz, cudaMemcpyDeviceToDevice,
+                                         s->ctx->stream));
+                if (s->opt.cross_kv_q8) {
+                    const size_t ssz = (size_t)T * (d / 32) * 2;
+                    uint8_t* ks = s->cks.as<uint8_t>() + layer0 * (d / 32) * 2;
+                    uint8_t* vs = s->cvs.as<uint8_t>() + layer0 * (d / 32) * 2;
+                    VKB_CUDA(cudaMemcpyAsync(ks + (size_t)dst * ssz, ks + (size_t)src * ssz, ssz,
+                                             cudaMemcpyDeviceToDevice, s->ctx->stream));
+                    VKB_CUDA(cudaMemcpyAsync(vs + (size_t)dst * ssz, vs + (size_t)src * ssz, ssz,
+                                             cudaMemcpyDeviceToDevice, s->ctx->stream));
+                }
+            }
+        }
+    });
+}
+
 vkb_status vkb_session_release(vkb_session* s, int32_t stream) {
     return guard([&] {
         if (!s) fail(VKB_ERROR_INVALID_ARGUMENT, "session_release: null session");
