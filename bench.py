@@ -307,6 +307,75 @@ def run_kernel_only(args):
     print(json.dumps({"kernel": args.kernel, "M": M, "N": N, "K": K, "ok": True}))
 
 
+def throughput_utterances(n: int, rank: int, pool: int):
+    """configs[4] workload of one rank: clip lengths U[5, 30] s (padded to 30 s by the
+    frontend), decode lengths U[32, 224]; clip i reads row i % pool of the PCM pool."""
+    from vokra_b200.batching import Utterance
+    rng = np.random.default_rng(50 + rank)
+    secs = rng.uniform(5.0, 30.0, n)
+    toks = rng.integers(32, 225, n)
+    return [Utterance(i % pool, int(secs[i] * 16000), int(toks[i])) for i in range(n)], float(secs.sum())
+
+
+def run_throughput(args, world, rank, local_rank):
+    """continuous batching of up to 128 streams per GPU over the whole
+    utterance list of this rank; audio-s/s counts each clip's own length."""
+    import torch
+    from vokra_b200 import ops, synth, whisper
+    from vokra_b200.batching import ContinuousBatcher
+    torch.cuda.set_device(local_rank)
+    dist = init_process_group(world, local_rank, "nccl")
+    arch = synth.WHISPER_LARGE_V3
+    path = model_path("large_v3_q4_0")
+    if rank == 0:
+        ensure_model(path, arch, synth.Q4_0)
+    if dist is not None:
+        dist.barrier()
+    ctx = ops.Context(local_rank)
+    model = whisper.WhisperModel(ctx, path)
+    SLOTS, ENC, POOL = 128, 32, 64
+    sess = whisper.Session(model, max_streams=SLOTS, max_step_tokens=4 * SLOTS, max_clips=ENC, cross_kv_q8=True)
+    dev = f"cuda:{local_rank}"
+    pcm = torch.from_numpy(synthetic_pcm(POOL, rank_input_seed(rank))).to(dev)
+    n_rank = max(1, args.utterances // world)
+    warm, _ = throughput_utterances(min(n_rank, 2 * SLOTS), rank + 1000, POOL)
+    ContinuousBatcher(ctx, sess, SLOTS, ENC, arch.start_ids[:PREFIX], arch.n_mels).run(warm, pcm)
+    utts, audio = throughput_utterances(n_rank, rank, POOL)
+    batcher = ContinuousBatcher(ctx, sess, SLOTS, ENC, arch.start_ids[:PREFIX], arch.n_mels)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    l0 = ctx.launch_count
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    batcher.run(utts, pcm)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), dist, dev)
+    tokens = float(batcher.tokens)
+    if dist is not None:
+        t = torch.tensor([audio, tokens], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        audio, tokens = float(t[0]), float(t[1])
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(audio / (ms / 1e3), 2), "unit": "audio-s/s",
+            "decode_tok_s": round(tokens / (ms / 1e3), 1), "n_gpus": world, "steps": 1, "warmup": 1,
+            "ms_per_step": round(ms, 1), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 hi+lo tensor-core operands, fp32 accumulate (Q4_0 weights, Q8_0 KV)", "data": "synthetic",
+            "config": {"workload": f"configs[4]: {n_rank * world} utterances of whisper-large-v3 q4_0 ({n_rank} per "
+                                   f"GPU), clip lengths U[5, 30] s padded to 30 s, greedy decode lengths U[32, 224]; "
+                                   f"continuous batching of up to {SLOTS} streams per GPU, clips encoded {ENC} at a "
+                                   f"time as slots free up; PCM rows drawn from a pool of {POOL} seeded synthetic "
+                                   f"clips, each utterance with its own length",
+                       "decode_steps": batcher.steps, "parallelism": f"dp{world} (utterances sharded by request)"},
+            "gpu_launches": int(ctx.launch_count - l0),
+        }), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 # ---------------------------------------------------------------------------
 # GPU leg
 # ---------------------------------------------------------------------------
@@ -324,6 +393,10 @@ def main():
                     help="run only one kernel three times, for ncu: the encoder fc1 GEMM (M = clips x 1500, or "
                          "1500), the decode cross-attention over the Q8_0 store (clips streams x 1500 keys), or "
                          "the encoder of a one-layer model with large-v3's dimensions on 8 clips")
+    ap.add_argument("--config", default="batch", choices=["batch", "throughput"],
+                    help="batch: configs[3] (the default bench line); throughput: configs[4], continuous batching "
+                         "of --utterances utterances per job (an extra measurement, not the driver's line)")
+    ap.add_argument("--utterances", type=int, default=2048)
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -335,6 +408,9 @@ def main():
         return
     if args.kernel:
         run_kernel_only(args)
+        return
+    if args.config == "throughput":
+        run_throughput(args, world, rank, local_rank)
         return
 
     import torch
