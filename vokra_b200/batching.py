@@ -31,7 +31,7 @@ class Utterance:
 
 class ContinuousBatcher:
     def __init__(self, ctx, session, n_slots: int, encode_batch: int, prefix, n_mels: int, eot: int | None = None,
-                 stop_at_eot: bool = False):
+                 stop_at_eot: bool = False, device: str = "cuda"):
         import torch
         if 2 * session.model.dims.n_audio_ctx != 3000:
             raise ValueError("ContinuousBatcher: the log-mel frontend feeds models with a 30 s window (1500 frames)")
@@ -39,13 +39,14 @@ class ContinuousBatcher:
         self.n_slots, self.encode_batch = n_slots, encode_batch
         self.prefix = [int(t) for t in prefix]
         self.n_mels, self.eot, self.stop_at_eot = n_mels, eot, stop_at_eot
-        self.ids = torch.zeros(n_slots * (len(self.prefix) + 1), dtype=torch.int32, device="cuda")
-        self.logmel = torch.empty((encode_batch, n_mels, 3000), dtype=torch.float32, device="cuda")
+        self.device = device
+        self.ids = torch.zeros(n_slots * (len(self.prefix) + 1), dtype=torch.int32, device=device)
+        self.logmel = torch.empty((encode_batch, n_mels, 3000), dtype=torch.float32, device=device)
         self.steps = 0
         self.tokens = 0
 
     def run(self, utterances, pcm_dev):
-        """Decodes every utterance; pcm_dev is a CUDA f32 [rows, samples] tensor."""
+        """Decodes every utterance; pcm_dev is an f32 [rows, samples] tensor on the batcher's device."""
         import torch
         from . import ops
         queue = deque(utterances)
@@ -57,8 +58,8 @@ class ContinuousBatcher:
             if queue and len(free) >= min(self.encode_batch, len(queue)):
                 batch = [queue.popleft() for _ in range(min(self.encode_batch, len(queue), len(free)))]
                 slots = [free.pop(0) for _ in batch]
-                rows = torch.tensor([u.pcm_index for u in batch], dtype=torch.long, device="cuda")
-                lens = torch.tensor([u.n_samples for u in batch], dtype=torch.int32, device="cuda")
+                rows = torch.tensor([u.pcm_index for u in batch], dtype=torch.long, device=self.device)
+                lens = torch.tensor([u.n_samples for u in batch], dtype=torch.int32, device=self.device)
                 pcm = pcm_dev.index_select(0, rows).contiguous()
                 lm = self.logmel[:len(batch)]
                 ops.log_mel(self.ctx, pcm, self.n_mels, out=lm, lengths=lens)
