@@ -82,3 +82,59 @@ def test_helpers():
     m = ngram_block_mask([5, 6, 5], 2, 8)  # bigram (5, 6) seen: after 5, 6 is blocked
     assert m[6] and m.sum() == 1
     assert not ngram_block_mask([5], 3, 8).any()
+
+
+def _row(hist, vocab):
+    # a deterministic log-probability row that depends on the whole history
+    rng = np.random.default_rng(abs(hash(tuple(hist))) % (2 ** 32))
+    x = rng.standard_normal(vocab).astype(np.float32) * 2.0
+    return x
+
+
+class HistoryScorer:
+    def __init__(self, vocab):
+        self.vocab_size = vocab
+
+    def logprobs_batch(self, prefixes):
+        from vokra_b200.beam import log_softmax
+        return [log_softmax(_row(list(p), self.vocab_size)) for p in prefixes]
+
+
+class FakeBeamSession:
+    """Keeps each stream's token history the way the device KV would: step
+    appends at the given positions, copy_stream copies the first n positions."""
+
+    class model:
+        class dims:
+            n_vocab = 11
+
+    def __init__(self):
+        self.hist = {}
+
+    def copy_stream(self, src, dst, n, cross):
+        self.hist[dst] = list(self.hist.get(src, []))[:n]
+
+    def release(self, slot):
+        self.hist.pop(slot, None)
+
+    def step(self, streams, positions, tokens, logits_dev=None):
+        rows = {}
+        for i, (s, p, t) in enumerate(zip(streams, positions, tokens)):
+            h = self.hist.setdefault(s, [])
+            assert p == len(h), (s, p, len(h))
+            h.append(int(t))
+            rows[i] = _row(h, 11)
+        for i, r in rows.items():
+            logits_dev[i] = __import__("torch").from_numpy(r)
+
+
+def test_session_scorer_banks_match_history_scorer():
+    from vokra_b200.beam import SessionBeamScorer
+    cfg = BeamSearchConfig.new(3, 7).with_(n_best=3, early_stopping=False)
+    fake = FakeBeamSession()
+    fake.hist[9] = []
+    sc = SessionBeamScorer(fake, 9, list(range(6)), 3, copy_stream=fake.copy_stream, device="cpu")
+    got = beam_search(sc, [1, 2], 10, cfg)
+    want = beam_search(HistoryScorer(11), [1, 2], 10, cfg)
+    assert [h.tokens for h in got] == [h.tokens for h in want]
+    assert all(abs(a.score - b.score) < 1e-6 for a, b in zip(got, want))

@@ -21,7 +21,6 @@ log-softmax of the step's f32 logits (whisper/beam_glue.rs:204-207).
 """
 from __future__ import annotations
 
-import ctypes as C
 from dataclasses import dataclass, replace
 
 import numpy as np
@@ -141,22 +140,27 @@ class SessionBeamScorer:
     """Scores the beams of one encoded clip on the device (see the module docstring).
 
     session: a whisper.Session; clip_stream: the stream slot the clip was encoded
-    into; slots: 2 * beam_width free stream slots (may include clip_stream)."""
+    into; slots: 2 * beam_width free stream slots (may include clip_stream).
+    copy_stream(src, dst, n_pos, copy_cross) defaults to vkb_session_copy_stream;
+    device is where the step's logits are written."""
 
-    def __init__(self, session, clip_stream: int, slots, beam_width: int):
+    def __init__(self, session, clip_stream: int, slots, beam_width: int, copy_stream=None, device: str = "cuda"):
         import torch
         if len(slots) < 2 * beam_width:
             raise ValueError("SessionBeamScorer: needs 2 * beam_width stream slots")
         self.s, self.W = session, beam_width
         self.slots = list(slots[:2 * beam_width])
         self.vocab_size = session.model.dims.n_vocab
-        self._L = _lib.load()
+        if copy_stream is None:
+            L = _lib.load()
+            copy_stream = lambda src, dst, n, cross: _lib.check(L.vkb_session_copy_stream(session.h, src, dst, n, cross))
+        self._copy, self._device = copy_stream, device
         for slot in self.slots:
             if slot != clip_stream:
-                _lib.check(self._L.vkb_session_copy_stream(session.h, clip_stream, slot, 0, 1))
+                self._copy(clip_stream, slot, 0, 1)
         self.calls = 0
         self.cache = {}  # token tuple -> slot, for the beams of the last call
-        self._logits = torch.empty((max(4 * beam_width, 64), self.vocab_size), dtype=torch.float32, device="cuda")
+        self._logits = torch.empty((max(4 * beam_width, 64), self.vocab_size), dtype=torch.float32, device=device)
 
     def logprobs_batch(self, prefixes):
         import torch
@@ -170,7 +174,8 @@ class SessionBeamScorer:
             self.s.release(slot)
             n = len(toks)
             self.s.step([slot] * n, list(range(n)), toks, logits_dev=self._logits)
-            torch.cuda.synchronize()
+            if self._device != "cpu":
+                torch.cuda.synchronize()
             rows = [self._logits[n - 1].cpu().numpy()]
             new_cache[tuple(toks)] = slot
         else:
@@ -179,13 +184,14 @@ class SessionBeamScorer:
                 parent = tuple(toks[:-1])
                 if parent not in self.cache:
                     raise ValueError("SessionBeamScorer: a prefix does not extend a beam of the previous call")
-                _lib.check(self._L.vkb_session_copy_stream(self.s.h, self.cache[parent], bank[i], len(parent), 0))
+                self._copy(self.cache[parent], bank[i], len(parent), 0)
                 streams.append(bank[i])
                 pos.append(len(toks) - 1)
                 last.append(int(toks[-1]))
                 new_cache[tuple(toks)] = bank[i]
             self.s.step(streams, pos, last, logits_dev=self._logits)
-            torch.cuda.synchronize()
+            if self._device != "cpu":
+                torch.cuda.synchronize()
             rows = list(self._logits[:len(prefixes)].cpu().numpy())
         self.cache = new_cache
         self.calls += 1
