@@ -138,3 +138,23 @@ def test_session_scorer_banks_match_history_scorer():
     want = beam_search(HistoryScorer(11), [1, 2], 10, cfg)
     assert [h.tokens for h in got] == [h.tokens for h in want]
     assert all(abs(a.score - b.score) < 1e-6 for a, b in zip(got, want))
+
+
+def test_ngram_block_mask_reference_cases():
+    # crates/vokra-models/src/voxtral/beam_search.rs:889-930 (the same semantics as decode/beam_search.rs:442)
+    for n in (0, 1):
+        assert not ngram_block_mask([1, 2, 3, 1, 2], n, 5).any()
+    m = ngram_block_mask([1, 2, 3, 1], 2, 5)
+    assert m[2] and not m[3]
+    m = ngram_block_mask([1, 2, 3, 1, 2], 3, 5)
+    assert m[3] and not m[4]
+    assert not ngram_block_mask([1], 3, 5).any()
+
+
+def test_no_repeat_ngram_blocks_repeats():
+    # a scorer that always prefers token 1 then 2: without blocking the beam loops 1,2,1,2,...
+    row = np.log(np.array([0.01, 0.6, 0.38, 0.01], np.float32))
+    h = beam_search(Const(row), [0], 3, BeamSearchConfig.greedy(8).with_(no_repeat_ngram_size=2))
+    toks = h[0].tokens
+    bigrams = list(zip(toks, toks[1:]))
+    assert len(bigrams) == len(set(bigrams))
