@@ -63,3 +63,17 @@ def test_two_ranks_gloo(tmp_path):
     assert float(r[0]["tok_s"]) == pytest.approx(2 * 64 * 128 * 3 / 0.030)
     # the reference arm prints from rank 0 only
     assert bool(r[1]["ref_silent"])
+
+
+def test_throughput_workload_shards():
+    """configs[4] workload per rank: seeded, distinct across ranks, within the
+    config's ranges (clips 5-30 s, decode lengths 32-224)."""
+    import bench
+    a, sa = bench.throughput_utterances(256, 0, 64)
+    b, sb = bench.throughput_utterances(256, 0, 64)
+    c, _ = bench.throughput_utterances(256, 1, 64)
+    assert [(u.n_samples, u.n_new_tokens) for u in a] == [(u.n_samples, u.n_new_tokens) for u in b] and sa == sb
+    assert [(u.n_samples, u.n_new_tokens) for u in a] != [(u.n_samples, u.n_new_tokens) for u in c]
+    assert all(5 * 16000 <= u.n_samples <= 30 * 16000 and 32 <= u.n_new_tokens <= 224 for u in a)
+    assert all(u.pcm_index == i % 64 for i, u in enumerate(a))
+    assert abs(sa - sum(u.n_samples for u in a) / 16000) < 256 / 16000 + 1e-6
