@@ -177,13 +177,18 @@ def job_throughput(world: int, clips: int, steps: int, tokens: int, ms: float):
 # CPU leg: the oracle (reference algorithm restated in C++) on a bounded sample
 # ---------------------------------------------------------------------------
 def cpu_sample(arch, qtag, qname, n_tokens: int, threads: int):
-    """Times 1 clip on a 2+2-layer model of the same dims; extrapolates to the full depth."""
+    """Times 1 clip on a 2+2-layer model of the same dims and extrapolates to the full depth.
+
+    The decoder keeps the reference's own caches: a dense f32 self-attention KvCache and f32
+    cross K/V (crates/vokra-models/src/whisper/decoder.rs:183-216, 455-470). Returns the
+    extrapolated full-depth rates and the measured wall time of the sample itself."""
     from oracle import py as o, whisper_ref
     o.lib().orc_set_threads(threads)
     small = dataclasses.replace(arch, n_audio_layer=2, n_text_layer=2)
     path = ensure_model(model_path(f"sample_{qname}_e2d2"), small, qtag)
     ref = whisper_ref.RefWhisper(path)
     pcm = synthetic_pcm(1, 123)[0]
+    t_sample0 = time.perf_counter()
     t0 = time.perf_counter()
     lm = o.log_mel(pcm, arch.n_mels)
     t_front = time.perf_counter() - t0
@@ -196,7 +201,7 @@ def cpu_sample(arch, qtag, qname, n_tokens: int, threads: int):
     enc = ref.encode(lm)
     t_enc2 = time.perf_counter() - t0
     t0 = time.perf_counter()
-    dec = ref.decoder(enc, kv_mode="q8", cross_mode="q8")
+    dec = ref.decoder(enc, kv_mode="f32", cross_mode="f32")
     t_cross2 = time.perf_counter() - t0
     dec.step(list(arch.start_ids))
     steps = 3
@@ -208,21 +213,25 @@ def cpu_sample(arch, qtag, qname, n_tokens: int, threads: int):
     t0 = time.perf_counter()
     o.gemm_kn(x, ref.emb_t)
     t_head = time.perf_counter() - t0
+    t_sample = time.perf_counter() - t_sample0
     L_e, L_d = arch.n_audio_layer, arch.n_text_layer
     t_enc = t_conv + (t_enc2 - t_conv) * L_e / 2
     t_cross = t_cross2 * L_d / 2
     t_step = t_head + max(0.0, t_step2 - t_head) * L_d / 2
     t_clip = t_front + t_enc + t_cross + n_tokens * t_step
-    sample = (f"1 clip on a 2+2-layer {qname} model of the same dims (log-mel {t_front:.2f}s, conv {t_conv:.2f}s, "
-              f"2 enc layers "
-              f"{t_enc2 - t_conv:.2f}s, cross K/V {t_cross2:.2f}s, decode step {t_step2 * 1e3:.1f}ms), "
-              f"extrapolated linearly to {L_e}+{L_d} layers and {n_tokens} tokens; the reference CPU "
-              f"algorithm restated in C++ (oracle/)")
+    sample = (f"1 clip on a 2+2-layer {qname} model of the same dims, dense f32 self-KV and f32 cross K/V as the "
+              f"reference decoder keeps them (log-mel {t_front:.2f}s, conv {t_conv:.2f}s, 2 enc layers "
+              f"{t_enc2 - t_conv:.2f}s, cross K/V {t_cross2:.2f}s, decode step {t_step2 * 1e3:.1f}ms; "
+              f"{t_sample:.1f}s wall per sample), extrapolated linearly to {L_e}+{L_d} layers and {n_tokens} "
+              f"tokens = {t_clip:.1f}s per clip; the reference CPU algorithm restated in C++ (oracle/)")
     return {"audio_s_per_s": CLIP_SECONDS / t_clip, "tok_s": n_tokens / (t_cross + n_tokens * t_step),
-            "sample": sample}
+            "sample": sample, "sample_wall_s": t_sample, "clip_s": t_clip}
 
 
 def run_reference(args, rank):
+    """The reference arm: the reference's CPU algorithm (oracle/, the Rust crate cannot be
+    built here) on the host cores. Only numpy, the GGUF writer and the oracle's C++ library
+    are loaded; nothing of libvkb200 runs in this process."""
     if rank != 0:
         return
     from vokra_b200 import synth
@@ -235,14 +244,18 @@ def run_reference(args, rank):
             vals.append(r)
     v = float(np.median([r["audio_s_per_s"] for r in vals]))
     tok = float(np.median([r["tok_s"] for r in vals]))
+    step_ms = 1000.0 * float(np.median([r["sample_wall_s"] for r in vals]))
     line = {
         "metric": METRIC, "impl": "reference", "value": v, "unit": "audio-s/s", "decode_tok_s": tok,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * CLIP_SECONDS / v, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(step_ms, 1), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "configs[3]: whisper-large-v3 q4_0, log-mel frontend + encoder + 4-token prefix + "
-                               "128 teacher-forced "
-                               "tokens; one utterance sampled per step on the host cores"},
+                               "128 teacher-forced tokens, f32 self-KV and f32 cross K/V",
+                   "step": "one sampled utterance on a 2+2-layer model of the same dims (ms_per_step is its "
+                           "measured wall time); value extrapolates the sample's per-layer times to 32+32 "
+                           "layers and 128 tokens (clip_s_extrapolated)",
+                   "clip_s_extrapolated": round(float(np.median([r["clip_s"] for r in vals])), 2)},
         "cpu_baseline": {"value": v, "unit": "audio-s/s", "cores": threads, "kind": "port",
                          "sample": vals[-1]["sample"]},
         "e2e": {"value": v, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -289,6 +302,9 @@ def run_kernel_only(args):
         torch.cuda.synchronize()
         print(json.dumps({"kernel": args.kernel, "streams": B, "keys": T, "width": W, "ok": True}))
         return
+    if args.kernel == "paged_decode":
+        run_paged_decode(ctx, args)
+        return
     if args.precision == "f16":
         _lib.check(_lib.load().vkb_context_set_precision(ctx.h, _lib.PREC_F16))
     M = 1500 if args.kernel == "fc1_m1500" else args.clips * 1500
@@ -305,6 +321,64 @@ def run_kernel_only(args):
                                           C.c_float(1.0)))
     torch.cuda.synchronize()
     print(json.dumps({"kernel": args.kernel, "M": M, "N": N, "K": K, "ok": True}))
+
+
+def run_paged_decode(ctx, args):
+    """the decode step's fused append + self-attention over the paged
+    Q8_0 cache (vkb_kv_append_attention, the kernel the session runs): 256 sequences, 20
+    heads x 64, lengths U[16, 448] in 16-token pages scattered by a seeded permutation,
+    Q/K/V N(0, 1). Prints one JSON line with the kernel's HBM roofline fraction."""
+    import torch
+    from vokra_b200 import _lib, ops
+    n_seq, H, D, T, bs = 256, 20, 64, 448, 16
+    W = H * D
+    rng = np.random.default_rng(2024)
+    pool = ops.QuantizedPagedKvCache(ctx, ops.KvDims(1, H, D, n_seq, 1, T), bs, _lib.KV_Q8_0,
+                                     _lib.KV_LAYOUT_SEQUENCE)
+    pool.set_page_table(rng.permutation(n_seq * (T // bs)).astype(np.int32))
+    lengths = rng.integers(16, T + 1, n_seq)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    s0 = 0
+    while s0 < n_seq:
+        s1, n_tok = s0, 0
+        while s1 < n_seq and n_tok + int(lengths[s1]) - 1 <= 2048:
+            n_tok += int(lengths[s1]) - 1
+            s1 += 1
+        seqs = np.concatenate([np.full(int(lengths[s]) - 1, s) for s in range(s0, s1)])
+        poss = np.concatenate([np.arange(int(lengths[s]) - 1) for s in range(s0, s1)])
+        pool.begin_step(seqs, poss)
+        pool.append(0, torch.randn((len(seqs), W), device="cuda", generator=g),
+                    torch.randn((len(seqs), W), device="cuda", generator=g))
+        s0 = s1
+    pool.begin_step(np.arange(n_seq), lengths - 1)
+    assert pool.decode_fused()
+    qkv = torch.randn((n_seq, 3 * W), device="cuda", generator=g)
+    qkv[:, :W] *= D ** -0.5
+    out = torch.empty((n_seq, W), device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > L2: every launch reads the pages from HBM
+    for _ in range(3):
+        pool.append_attention(0, qkv, out)
+    reps, ms = 20, 0.0
+    stream = torch.cuda.current_stream()
+    for _ in range(reps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        pool.append_attention(0, qkv, out)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms += e0.elapsed_time(e1) / reps
+    keys = int(lengths.sum())
+    # K and V int8 quants + one f16 scale per 32 channels of every key, the q|k|v rows in, the context out
+    alg = keys * 2 * (W + W // 16) + n_seq * 3 * W * 4 + n_seq * W * 4
+    hbm, _, _, peak_kind = _peaks()
+    gbs = alg / (ms / 1e3) / 1e9
+    print(json.dumps({"kernel": "paged_decode_kernel (vkb_kv_append_attention)",
+                      "workload": "configs[2]: 256 sequences, 20 heads x 64, lengths U[16, 448], 16-token Q8_0 "
+                                  "pages, seeded page permutation; L2 flushed before every launch",
+                      "keys": keys, "algorithmic_bytes": alg, "us_per_launch": round(ms * 1e3, 2),
+                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                                   "frac": round(gbs / hbm, 4), "peak_kind": peak_kind}}), flush=True)
 
 
 def throughput_utterances(n: int, rank: int, pool: int):
@@ -389,10 +463,11 @@ def main():
     ap.add_argument("--tokens", type=int, default=128)
     ap.add_argument("--precision", default="split", choices=["split", "f16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", default=None, choices=["fc1", "fc1_m1500", "xattn", "encoder"],
+    ap.add_argument("--kernel", default=None, choices=["fc1", "fc1_m1500", "xattn", "encoder", "paged_decode"],
                     help="run only one kernel three times, for ncu: the encoder fc1 GEMM (M = clips x 1500, or "
                          "1500), the decode cross-attention over the Q8_0 store (clips streams x 1500 keys), or "
-                         "the encoder of a one-layer model with large-v3's dimensions on 8 clips")
+                         "the encoder of a one-layer model with large-v3's dimensions on 8 clips, or the fused decode "
+                         "self-attention over configs[2] (prints its own JSON line with the HBM roofline)")
     ap.add_argument("--config", default="batch", choices=["batch", "throughput"],
                     help="batch: configs[3] (the default bench line); throughput: configs[4], continuous batching "
                          "of --utterances utterances per job (an extra measurement, not the driver's line)")

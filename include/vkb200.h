@@ -2,7 +2,7 @@
  * vkb200.h — C ABI of the B200 (sm_100a) quantized-Whisper hot path.
  *
  * A drop-in for the seams of ayutaz/vokra that a Rust backend crate would bind
- * with `extern "C"` (see INTEGRATION.md for the binding stubs). Every function
+ * with `extern "C"`. Every function
  * takes plain pointers and sizes; no C++ or torch type crosses this boundary
  * and no C++ exception escapes it (each entry point catches and converts, like
  * the reference's panic firewall crates/vokra-capi/src/ffi_guard.rs:27).
@@ -212,6 +212,22 @@ VKB_API vkb_status vkb_kv_append(vkb_kv_pool* pool, int32_t layer, const float* 
  * softmax in fp32 over the int8 pages gathered through the page table. */
 VKB_API vkb_status vkb_kv_attention(vkb_kv_pool* pool, int32_t layer, const float* q_dev,
                             void* ctx_out_dev, int out_dtype);
+/* The decode step's append + attention of one layer in one call: row i of
+ * qkv_dev ([n_tok][ld] f32, device) holds token i's q (already scaled by
+ * d_head^-0.5) in columns [0, W), its k in [W, 2W) and its v in [2W, 3W),
+ * W = n_head*d_head. K and V are stored exactly as vkb_kv_append stores them
+ * (bit-exact BlockQ8_0::pack), then the queries attend as in
+ * vkb_kv_attention. When every stream of the step has one token (a decode
+ * step), the pool is in the SEQUENCE layout, d_head is 64 and n_head a
+ * multiple of 4, this is one fused kernel (the one vkb_session_step runs);
+ * otherwise it is vkb_kv_append followed by vkb_kv_attention. The
+ * reference's decoder does the same pair per layer (cache append, then
+ * nn::attention_from_kv_into, crates/vokra-models/src/whisper/decoder.rs:455-470,
+ * nn.rs:209-300). */
+VKB_API vkb_status vkb_kv_append_attention(vkb_kv_pool* pool, int32_t layer, const float* qkv_dev, int64_t ld,
+                                           void* ctx_out_dev, int out_dtype);
+/* 1 when the step begun last runs vkb_kv_append_attention as the fused kernel. */
+VKB_API int32_t vkb_kv_decode_fused(const vkb_kv_pool* pool);
 /* Frees every page of one stream (SEQUENCE layout). */
 VKB_API vkb_status vkb_kv_release_seq(vkb_kv_pool* pool, int32_t seq_id);
 /* release_layer (paged_quant.rs:500): REFERENCE layout only. */
@@ -285,6 +301,19 @@ VKB_API vkb_status vkb_attention_dense_noalloc(vkb_context* ctx, int32_t n_tok, 
 VKB_API vkb_status vkb_quantize_rows_q8_0(vkb_context* ctx, const float* x_dev, int64_t n_rows, int32_t width,
                                   void* q_dev, void* d_dev);
 
+
+/* ---- GGUF reader (GgufFile::parse, crates/vokra-core/src/gguf/reader.rs:132) */
+
+/* Parses a GGUF v3 image held in host memory with the checks the model
+ * loader applies (host only, no device work): magic, version 3, counts
+ * bounded by the file size, metadata values, general.alignment a power of
+ * two, at most 8 dimensions, known dtype tags (the reference's F32, F16,
+ * BF16, Q4_K, Q5_K, Q6_K plus Q4_0 and Q8_0), unique names, whole blocks,
+ * aligned offsets, every tensor inside the file. Malformed input returns
+ * VKB_ERROR_MODEL_LOAD with the reference's GgufError variant named in
+ * vkb_last_error() (e.g. "(BadMagic)", "(UnsupportedVersion)",
+ * "(Truncated)"). On success the counts are written where non-NULL. */
+VKB_API vkb_status vkb_gguf_inspect(const void* bytes, size_t len, int64_t* n_tensors, int64_t* n_metadata);
 
 /* ---- Whisper model and decode session ------------------------------------ */
 

@@ -83,3 +83,13 @@ def test_batcher_stops_at_eot(monkeypatch):
     b = batching.ContinuousBatcher(None, sess, 2, 1, prefix, 80, eot=eot, stop_at_eot=True, device="cpu")
     b.run([u], torch.zeros((1, 100)))
     assert u.ids == full[:full.index(eot) + 1]
+
+
+def test_batcher_rejects_encode_batch_above_slots():
+    """An encode batch larger than the slot count could never be admitted (the
+    loop would spin with nothing active), so the constructor refuses it."""
+    import pytest
+    sess = FakeSession(2, max_step=16)
+    for bad in (0, 3):
+        with pytest.raises(ValueError):
+            batching.ContinuousBatcher(None, sess, 2, bad, [5], 80, device="cpu")

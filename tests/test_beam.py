@@ -158,3 +158,17 @@ def test_no_repeat_ngram_blocks_repeats():
     toks = h[0].tokens
     bigrams = list(zip(toks, toks[1:]))
     assert len(bigrams) == len(set(bigrams))
+
+
+def test_session_scorer_long_prefix():
+    """A prompt longer than the scorer's initial logits buffer (a Whisper prompt
+    of previous text can be 224 tokens) is scored without writing past it."""
+    from vokra_b200.beam import SessionBeamScorer
+    cfg = BeamSearchConfig.new(2, 3).with_(n_best=2, early_stopping=False)
+    prefix = [int(t) for t in np.random.default_rng(1).integers(0, 10, 150)]
+    fake = FakeBeamSession()
+    fake.hist[9] = []
+    sc = SessionBeamScorer(fake, 9, list(range(4)), 2, copy_stream=fake.copy_stream, device="cpu")
+    got = beam_search(sc, prefix, 10, cfg)
+    want = beam_search(HistoryScorer(11), prefix, 10, cfg)
+    assert [h.tokens for h in got] == [h.tokens for h in want]

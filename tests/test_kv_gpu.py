@@ -301,3 +301,95 @@ def test_dequant_gemv_m3_04_shapes(ctx, kats, mode):
     with pytest.raises(ops.VkbError) as e:
         gemv.fused_dequant_gemv(_lib.KV_FP32, b"", 0, 0, np.zeros(0, np.float32))
     assert e.value.code == _lib.ERROR_INVALID_ARGUMENT
+
+
+def _config2_pool(ctx, rng, n_seq=256, n_head=20, d_head=64, max_time=448, bs=16):
+    """n_seq sequences, lengths U[16, 448], 16-token int8
+    pages with one f16 scale per 32 channels, pages scattered by a seeded
+    permutation; K/V of every position but the last already stored."""
+    from vokra_b200 import ops
+    w = n_head * d_head
+    pool = ops.QuantizedPagedKvCache(ctx, ops.KvDims(1, n_head, d_head, n_seq, 1, max_time), bs, _lib.KV_Q8_0,
+                                     _lib.KV_LAYOUT_SEQUENCE)
+    pps = (max_time + bs - 1) // bs
+    pool.set_page_table(rng.permutation(n_seq * pps).astype(np.int32))
+    lengths = rng.integers(16, max_time + 1, n_seq)
+    K = [rng.standard_normal((int(L), w)).astype(np.float32) for L in lengths]
+    V = [rng.standard_normal((int(L), w)).astype(np.float32) for L in lengths]
+    s0 = 0
+    while s0 < n_seq:  # prefill steps of whole sequences, at most 2048 tokens each
+        s1, n_tok = s0, 0
+        while s1 < n_seq and n_tok + int(lengths[s1]) - 1 <= 2048:
+            n_tok += int(lengths[s1]) - 1
+            s1 += 1
+        seqs, poss = [], []
+        for s in range(s0, s1):
+            seqs += [s] * (int(lengths[s]) - 1)
+            poss += list(range(int(lengths[s]) - 1))
+        pool.begin_step(seqs, poss)
+        pool.append(0, _dev(np.concatenate([K[s][:-1] for s in range(s0, s1)])),
+                    _dev(np.concatenate([V[s][:-1] for s in range(s0, s1)])))
+        s0 = s1
+    return pool, lengths, K, V
+
+
+def test_fused_decode_step_config2(ctx):
+    """The decode step's fused append + attention (the kernel vkb_session_step
+    runs) over BASELINE configs[2]: 256 sequences, 20 heads, d_head 64, lengths
+    U[16, 448], permuted pages. Each sequence appends its last K/V row and its
+    one query attends over all of its keys; the context matches the oracle's
+    attention over the Q8_0-dequantized K/V (nn.rs:209-300) within 1e-4, and
+    the appended rows' page bytes equal BlockQ8_0::pack."""
+    import torch
+    rng = np.random.default_rng(2024)
+    pool, lengths, K, V = _config2_pool(ctx, rng)
+    n_seq, w, n_head = len(lengths), K[0].shape[1], 20
+    pool.begin_step(list(range(n_seq)), [int(L) - 1 for L in lengths])
+    assert pool.decode_fused()
+    q = rng.standard_normal((n_seq, w)).astype(np.float32) * np.float32(64 ** -0.5)
+    qkv = np.concatenate([q, np.stack([k[-1] for k in K]), np.stack([v[-1] for v in V])], axis=1)
+    out = torch.zeros((n_seq, w), dtype=torch.float32, device="cuda:0")
+    pool.append_attention(0, _dev(qkv), out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    worst = 0.0
+    for s, L in enumerate(lengths):
+        kd = o.kv_unpack(3, o.kv_pack(3, K[s])).reshape(int(L), w)
+        vd = o.kv_unpack(3, o.kv_pack(3, V[s])).reshape(int(L), w)
+        ref = o.attention(q[s:s + 1], kd, vd, n_head)[0]
+        worst = max(worst, float(np.max(np.abs(got[s] - ref))))
+    assert worst <= 1e-4, worst
+    # the page holding each sequence's last row: bytes of the whole page prefix
+    table = pool.page_table().reshape(n_seq, -1)
+    for s in (0, 1, 100, n_seq - 1):
+        L = int(lengths[s])
+        pid = int(table[s, (L - 1) // 16])
+        kp, vp = pool.read_page(pid, 0)
+        n_rows = (L - 1) % 16 + 1
+        rows = slice((L - 1) // 16 * 16, L)
+        assert np.array_equal(kp.reshape(16, -1)[:n_rows].reshape(-1), o.kv_pack(3, K[s][rows]))
+        assert np.array_equal(vp.reshape(16, -1)[:n_rows].reshape(-1), o.kv_pack(3, V[s][rows]))
+
+
+def test_fused_decode_matches_unfused_route(ctx):
+    """The fused kernel and the separate append + attention kernels give the
+    same context (within 1e-5) on one decode step of 40 sequences."""
+    import torch
+    outs = []
+    for fused in (True, False):
+        rng = np.random.default_rng(77)
+        pool, lengths, K, V = _config2_pool(ctx, rng, n_seq=40)
+        n_seq, w = len(lengths), K[0].shape[1]
+        pool.begin_step(list(range(n_seq)), [int(L) - 1 for L in lengths])
+        q = rng.standard_normal((n_seq, w)).astype(np.float32) * np.float32(0.125)
+        kl, vl = np.stack([k[-1] for k in K]), np.stack([v[-1] for v in V])
+        out = torch.zeros((n_seq, w), dtype=torch.float32, device="cuda:0")
+        if fused:
+            pool.append_attention(0, _dev(np.concatenate([q, kl, vl], axis=1)), out)
+        else:
+            pool.append(0, _dev(kl), _dev(vl))
+            pool.attention(0, _dev(q), out)
+        torch.cuda.synchronize()
+        outs.append(out.cpu().numpy())
+        pool.close()
+    assert np.max(np.abs(outs[0] - outs[1])) <= 1e-5

@@ -1,0 +1,197 @@
+"""Whisper on the B200 against the reference's own decode numerics, at full depth.
+
+The oracle decoder here keeps exactly the caches the reference decoder keeps:
+a dense f32 self-attention KvCache and f32 cross-attention K/V
+(crates/vokra-models/src/whisper/decoder.rs:183-216, 455-470). The device runs
+its default configuration: Q8_0 self-attention pages and the Q8_0 cross store
+(or the f16 store where a test says so). So the whole quantized-KV design is
+charged against the parity budget: logits within 1e-2 max-abs and 1e-3
+relative RMS at every step, and identical teacher-forced argmax ids except
+where the oracle's own top-2 gap is below 1e-3.
+
+Inputs follow BASELINE configs[0]: a 30 s 16 kHz clip of seeded white noise at
+-20 dBFS plus three tones, turned into a log-mel by the frontend (the device
+frontend for the device, the oracle's restatement of mel.rs for the oracle),
+then teacher-forced decode of ids uniform in [0, n_vocab).
+"""
+import dataclasses
+
+import numpy as np
+import pytest
+
+from oracle import py as o, whisper_ref
+from vokra_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+GAP = 1e-3
+
+
+def _rel_rms(a, b):
+    return float(np.sqrt(np.mean((a - b) ** 2)) / (np.sqrt(np.mean(b ** 2)) + 1e-30))
+
+
+class Budget:
+    """Accumulates the per-step logit errors and the teacher-forced argmax check."""
+
+    def __init__(self):
+        self.max_abs = self.max_rms = 0.0
+        self.mismatch = self.excluded = self.rows = 0
+
+    def add(self, got, ref):
+        got, ref = np.atleast_2d(got), np.atleast_2d(ref)
+        self.max_abs = max(self.max_abs, float(np.max(np.abs(got - ref))))
+        for r in range(ref.shape[0]):
+            self.max_rms = max(self.max_rms, _rel_rms(got[r], ref[r]))
+            top2 = np.sort(ref[r])[-2:]
+            self.rows += 1
+            if top2[1] - top2[0] < GAP:
+                self.excluded += 1
+            elif int(np.argmax(got[r])) != int(np.argmax(ref[r])):
+                self.mismatch += 1
+
+    def report(self, name):
+        print(f"{name}: logits max-abs {self.max_abs:.3e} rel-rms {self.max_rms:.3e}; argmax mismatches "
+              f"{self.mismatch} of {self.rows} rows ({self.excluded} excluded, oracle top-2 gap < {GAP})")
+
+    def check(self):
+        assert self.max_abs <= 1e-2, self.max_abs
+        assert self.max_rms <= 1e-3, self.max_rms
+        assert self.mismatch == 0
+
+
+def _teacher_forced(ctx, path, arch, n_clips, n_tokens, seed, cross_q8=True, check_enc=True):
+    """Device session vs the f32-KV oracle on n_clips synthetic clips: prefix step
+    of the start ids for every clip, then n_tokens one-token steps."""
+    import torch
+    from vokra_b200 import ops, whisper
+    pcm = np.stack([synth.synthetic_audio(seed + i) for i in range(n_clips)])
+    model = whisper.WhisperModel(ctx, path)
+    sess = whisper.Session(model, max_streams=n_clips, max_clips=n_clips, cross_kv_q8=cross_q8)
+    lm = ops.log_mel(ctx, torch.from_numpy(pcm).cuda(), arch.n_mels)
+    sess.encode(lm, list(range(n_clips)))
+    enc = sess.encoder_output(n_clips)
+    ref = whisper_ref.RefWhisper(path)
+    budget = Budget()
+    rng = np.random.default_rng(seed)
+    toks = rng.integers(0, arch.n_vocab, (n_clips, n_tokens))
+    prefix = list(arch.start_ids)
+    decs = []
+    for i in range(n_clips):
+        ref_enc = ref.encode(o.log_mel(pcm[i], arch.n_mels))
+        if check_enc:
+            assert _rel_rms(enc[i], ref_enc) <= 2e-3
+        decs.append(ref.decoder(ref_enc, kv_mode="f32", cross_mode="f32"))
+    V = arch.n_vocab
+    out = torch.zeros((n_clips * len(prefix), V), dtype=torch.float32, device="cuda:0")
+    sess.step([s for s in range(n_clips) for _ in prefix], list(range(len(prefix))) * n_clips, prefix * n_clips,
+              logits_dev=out)
+    got = out.cpu().numpy().reshape(n_clips, len(prefix), V)
+    for s in range(n_clips):
+        budget.add(got[s], decs[s].step(prefix))
+    out = torch.zeros((n_clips, V), dtype=torch.float32, device="cuda:0")
+    for t in range(n_tokens):
+        sess.step(list(range(n_clips)), [len(prefix) + t] * n_clips, toks[:, t].tolist(), logits_dev=out)
+        got = out.cpu().numpy()
+        for s in range(n_clips):
+            budget.add(got[s], decs[s].step([int(toks[s, t])]))
+    sess.close()
+    model.close()
+    return budget
+
+
+@pytest.fixture(scope="module")
+def base_q8(tmp_path_factory):
+    path = str(tmp_path_factory.mktemp("base") / "whisper_base_q8_0.gguf")
+    synth.write_synthetic_whisper(path, synth.WHISPER_BASE, synth.Q8_0, seed=11)
+    return path
+
+
+@pytest.mark.parametrize("cross", ["q8", "f16"])
+def test_config0_whisper_base_q8_0(ctx, base_q8, cross):
+    """BASELINE configs[0] exactly: Whisper-base (6+6 layers, 8 heads, full
+    51865-token vocabulary) in Q8_0, one 30 s clip from the frontend, 64
+    teacher-forced tokens at batch 1, against the reference decoder's f32
+    caches; both cross-attention stores of the session."""
+    b = _teacher_forced(ctx, base_q8, synth.WHISPER_BASE, 1, 64, seed=30, cross_q8=(cross == "q8"))
+    b.report(f"whisper-base q8_0, cross store {cross}")
+    b.check()
+
+
+LARGE_4x4 = dataclasses.replace(synth.WHISPER_LARGE_V3, n_audio_layer=4, n_text_layer=4)
+
+
+def test_large_v3_dims_q4_0_4x4(ctx, tmp_path):
+    """Whisper-large-v3 dimensions (d_model 1280, 20 heads, FFN 5120, 128 mels,
+    51866-token vocabulary) with 4 encoder + 4 decoder layers in Q4_0, two
+    clips decoded together, against the reference decoder's f32 caches."""
+    path = str(tmp_path / "large_4x4_q4_0.gguf")
+    synth.write_synthetic_whisper(path, LARGE_4x4, synth.Q4_0, seed=12)
+    b = _teacher_forced(ctx, path, LARGE_4x4, 2, 24, seed=40)
+    b.report("large-v3 dims 4+4 q4_0")
+    b.check()
+
+
+def test_fused_decode_attention_long_contexts(ctx, tmp_path):
+    """The fused decode self-attention as vkb_session_step runs it, at the
+    bench's shapes: 20 heads of 64, 64 streams in one step, per-stream
+    contexts that differ (16, 130, 300 and the full 448-token window among
+    them), pages handed out in an interleaved order by chunked prefills.
+    A one-layer d_model 1280 model keeps the oracle cheap; the oracle keeps
+    the reference's f32 self-KV."""
+    import torch
+    from vokra_b200 import whisper
+    arch = synth.WhisperArch(80, 64, 1280, 20, 1, 448, 20, 1, 1000, 5120, 999, (1, 2, 3, 4))
+    path = str(tmp_path / "d1280_l1.gguf")
+    synth.write_synthetic_whisper(path, arch, synth.Q4_0, seed=13)
+    n = 64
+    rng = np.random.default_rng(5)
+    finals = [16, 130, 300, 448] + [int(x) for x in rng.integers(16, 97, n - 4)]  # tokens per stream at the end
+    DEC = 4  # closing one-token steps of all streams together (the fused path)
+    pre = [f - DEC for f in finals]  # tokens before them (prefix included)
+    toks = [[int(t) for t in rng.integers(0, arch.n_vocab, f)] for f in finals]
+    for s in range(n):
+        toks[s][:4] = list(arch.start_ids)
+    model = whisper.WhisperModel(ctx, path)
+    sess = whisper.Session(model, max_streams=n, max_step_tokens=16 * n, max_clips=n)
+    logmel = rng.uniform(-1.0, 1.5, (n, arch.n_mels, 2 * arch.n_audio_ctx)).astype(np.float32)
+    sess.encode(torch.from_numpy(logmel).cuda(), list(range(n)))
+    enc = sess.encoder_output(n)
+    ref = whisper_ref.RefWhisper(path)
+    ref_enc = [ref.encode(logmel[s]) for s in range(n)]
+    assert _rel_rms(enc, np.stack(ref_enc)) <= 2e-3
+    decs = [ref.decoder(e, kv_mode="f32", cross_mode="f32") for e in ref_enc]
+    budget = Budget()
+    # chunked prefill: every step takes the next 16 tokens of every stream still filling
+    done = [0] * n
+    while any(done[s] < pre[s] for s in range(n)):
+        streams, pos, tk, spans = [], [], [], []
+        for s in range(n):
+            c = min(16, pre[s] - done[s])
+            if c <= 0:
+                continue
+            spans.append((s, len(streams), c))
+            streams += [s] * c
+            pos += list(range(done[s], done[s] + c))
+            tk += toks[s][done[s]:done[s] + c]
+        out = torch.zeros((len(streams), arch.n_vocab), dtype=torch.float32, device="cuda:0")
+        sess.step(streams, pos, tk, logits_dev=out)
+        got = out.cpu().numpy()
+        for s, r0, c in spans:
+            budget.add(got[r0:r0 + c], decs[s].step(toks[s][done[s]:done[s] + c]))
+            done[s] += c
+    fused = Budget()
+    out = torch.zeros((n, arch.n_vocab), dtype=torch.float32, device="cuda:0")
+    for t in range(DEC):
+        sess.step(list(range(n)), [pre[s] + t for s in range(n)], [toks[s][pre[s] + t] for s in range(n)],
+                  logits_dev=out)
+        got = out.cpu().numpy()
+        for s in range(n):
+            fused.add(got[s], decs[s].step([toks[s][pre[s] + t]]))
+    assert max(pre[s] + DEC - 1 for s in range(n)) == 447  # the last position of Whisper's text window
+    budget.report("chunked prefill (paged_attn_kernel)")
+    fused.report("64-stream decode steps (paged_decode_kernel)")
+    budget.check()
+    fused.check()
+    sess.close()
+    model.close()

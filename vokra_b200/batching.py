@@ -33,6 +33,8 @@ class ContinuousBatcher:
     def __init__(self, ctx, session, n_slots: int, encode_batch: int, prefix, n_mels: int, eot: int | None = None,
                  stop_at_eot: bool = False, device: str = "cuda"):
         import torch
+        if not 0 < encode_batch <= n_slots:
+            raise ValueError(f"ContinuousBatcher: encode_batch must be in [1, n_slots={n_slots}], got {encode_batch}")
         if 2 * session.model.dims.n_audio_ctx != 3000:
             raise ValueError("ContinuousBatcher: the log-mel frontend feeds models with a 30 s window (1500 frames)")
         self.ctx, self.s = ctx, session

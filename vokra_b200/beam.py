@@ -173,6 +173,9 @@ class SessionBeamScorer:
             slot = bank[0]
             self.s.release(slot)
             n = len(toks)
+            if n > self._logits.shape[0]:
+                # the prefix step writes one logits row per prefix token
+                self._logits = torch.empty((n, self.vocab_size), dtype=torch.float32, device=self._device)
             self.s.step([slot] * n, list(range(n)), toks, logits_dev=self._logits)
             if self._device != "cpu":
                 torch.cuda.synchronize()

@@ -1,6 +1,9 @@
 // common.cuh — shared host/device helpers of libvkb200 (sm_100a only).
 #pragma once
 #include <utility>
+#include <mutex>
+#include <set>
+#include <tuple>
 
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -28,6 +31,22 @@ inline void cuda_check(cudaError_t e, const char* what) {
         fail(VKB_ERROR_BACKEND_UNAVAILABLE, std::string(what) + ": " + cudaGetErrorString(e));
 }
 #define VKB_CUDA(x) ::vkb::cuda_check((x), #x)
+
+// Opts a kernel into `bytes` of dynamic shared memory on the current device.
+// The attribute belongs to the device's context, so it is recorded per
+// (kernel, device, bytes) and set once for each device a process uses.
+template <class F>
+inline void smem_optin(F* kernel, int bytes) {
+    static std::mutex mu;
+    static std::set<std::tuple<const void*, int, int>> done;
+    int dev = 0;
+    VKB_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> g(mu);
+    auto key = std::make_tuple((const void*)kernel, dev, bytes);
+    if (done.count(key)) return;
+    VKB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.insert(key);
+}
 
 void set_last_error(const std::string& m);
 
@@ -88,7 +107,6 @@ struct vkb_context {
     cudaStream_t stream = nullptr;
     uint64_t launches = 0;
     int precision = VKB_PREC_SPLIT;  // tensor-core operand precision (vkb_context_set_precision)
-    unsigned long long* trace = nullptr;  // debugging aid: GEMM block-0 timeline (VKB_TRACE)
     vkb::DevBuf workspace;
     vkb::DevBuf err_flag;  // int set by a kernel whose bounded wait gave up
     vkb::DevBuf frontend;  // log-mel tables (window, twiddles, mel bank) + per-clip maxima

@@ -40,10 +40,6 @@ vkb_status vkb_context_create(int device, vkb_context** out) {
             c->err_flag.alloc(sizeof(int));
             const char* pdl = getenv("VKB_PDL");
             c->pdl = !(pdl && pdl[0] == '0');
-            if (getenv("VKB_TRACE")) {
-                VKB_CUDA(cudaMallocManaged(&c->trace, 5 * 64 * 8));
-                memset(c->trace, 0, 5 * 64 * 8);
-            }
             VKB_CUDA(cudaMemset(c->err_flag.p, 0, sizeof(int)));
         } catch (...) {
             delete c;
@@ -58,17 +54,6 @@ vkb_status vkb_context_destroy(vkb_context* ctx) {
         if (!ctx) return;
         cudaSetDevice(ctx->device);
         cudaStreamSynchronize(ctx->stream);
-        if (ctx->trace) {  // debugging aid: print the last GEMM's block-0 timeline (us from start)
-            unsigned long long t0 = ctx->trace[0];
-            const char* names[5] = {"produce", "mma", "deq_start", "deq_done", "epilogue"};
-            for (int r = 0; r < 5; ++r) {
-                fprintf(stderr, "%-10s", names[r]);
-                for (int i = 0; i < 24; ++i)
-                    fprintf(stderr, " %7.2f", ctx->trace[r * 64 + i] ? (ctx->trace[r * 64 + i] - t0) / 1000.0 : -1.0);
-                fprintf(stderr, "\n");
-            }
-            cudaFree(ctx->trace);
-        }
         if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
         delete ctx;
     });

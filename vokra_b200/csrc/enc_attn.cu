@@ -236,11 +236,7 @@ void run_encoder_attention(vkb_context* ctx, const __half* qkv, int64_t ld, int 
         fail(VKB_ERROR_INVALID_ARGUMENT, "encoder attention: rows must be 16-byte aligned");
     dim3 grid((unsigned)((T + BQ - 1) / BQ), (unsigned)(n_windows * n_head));
     const size_t smem = (size_t)(BQ + 4 * BK) * LDS * sizeof(__half);
-    static bool attr = false;
-    if (!attr) {
-        VKB_CUDA(cudaFuncSetAttribute(enc_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr = true;
-    }
+    smem_optin(enc_attn_kernel, (int)smem);
     launch_pdl(ctx, enc_attn_kernel, grid, NT, smem, qkv, ld, kcol, vcol, T, n_head, out, out_ld, out_lo);
     VKB_CUDA(cudaGetLastError());
     ctx->count();

@@ -309,11 +309,7 @@ bool run_encoder_attention_tc(vkb_context* ctx, const __half* qkv, int64_t ld, i
     CUtensorMap qk_map, vt_map;
     make_tmap_f16(&qk_map, qkv, (int64_t)n_windows * T, ld, BQ);
     make_tmap_f16(&vt_map, vt_scratch, (int64_t)n_windows * n_head * HD, Tp, HD);
-    static bool attr = false;
-    if (!attr) {
-        VKB_CUDA(cudaFuncSetAttribute(enc_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-        attr = true;
-    }
+    smem_optin(enc_attn_tc_kernel, SMEM);
     dim3 grid((unsigned)((T + BQ - 1) / BQ), (unsigned)(n_windows * n_head));
     launch_pdl(ctx, enc_attn_tc_kernel, grid, 192, SMEM, qk_map, vt_map, kcol, T, n_head, out, out_ld, out_lo,
                ctx->err_flag.as<int>());

@@ -224,11 +224,7 @@ void run_log_mel(vkb_context* ctx, const float* pcm, int64_t n_clips, int64_t st
     unsigned* gmax = reinterpret_cast<unsigned*>(b + o_max);
     VKB_CUDA(cudaMemsetAsync(gmax, 0, (size_t)n_clips * 4, ctx->stream));
     const size_t smem = LM_NFFT * sizeof(double2) + (size_t)LM_FT * (LM_NFFT + LM_PSTRIDE) * 4;
-    static bool attr = false;
-    if (!attr) {
-        VKB_CUDA(cudaFuncSetAttribute(logmel_frames_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr = true;
-    }
+    smem_optin(logmel_frames_kernel, (int)smem);
     dim3 grid((LM_FRAMES + LM_FT - 1) / LM_FT, (unsigned)n_clips);
     launch_pdl(ctx, logmel_frames_kernel, grid, 256, smem, pcm, stride, lengths, n_mels, tb, out, gmax);
     VKB_CUDA(cudaGetLastError());

@@ -362,12 +362,7 @@ template <int FMT>
 static void launch_persist(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e,
                            int* err) {
     using C = PCfg<FMT>;
-    static bool attr = false;
-    if (!attr) {
-        VKB_CUDA(cudaFuncSetAttribute(tc_gemm_persist_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      C::SMEM));
-        attr = true;
-    }
+    smem_optin(tc_gemm_persist_kernel<FMT>, C::SMEM);
     CUtensorMap map, map_lo;
     make_tmap_f16(&map, a16, m, w->k, C::BN);
     make_tmap_f16(&map_lo, a16 + m * w->k, m, w->k, C::BN);

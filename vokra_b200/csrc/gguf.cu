@@ -42,7 +42,7 @@ struct Cursor {
     }
     std::string str(const char* what) {
         uint64_t len = get<uint64_t>(what);
-        if (len > (1ull << 24)) fail(VKB_ERROR_MODEL_LOAD, std::string("gguf: string too long in ") + what);
+        if (len > n - i) fail(VKB_ERROR_MODEL_LOAD, std::string("gguf: truncated ") + what);
         need((size_t)len, what);
         std::string s((const char*)p + i, (size_t)len);
         i += (size_t)len;
@@ -61,13 +61,16 @@ static GgufValue read_value(Cursor& c, uint32_t type, int depth) {
         case 4: v.u = c.get<uint32_t>("u32"); break;
         case 5: v.i = c.get<int32_t>("i32"); break;
         case 6: v.f = c.get<float>("f32"); break;
-        case 7: v.u = c.get<uint8_t>("bool"); break;
+        case 7:
+            v.u = c.get<uint8_t>("bool");
+            if (v.u > 1) fail(VKB_ERROR_MODEL_LOAD, "gguf: bool value " + std::to_string(v.u) + " (InvalidBool)");
+            break;
         case 8: v.s = c.str("string"); break;
         case 9: {
-            if (depth > 2) fail(VKB_ERROR_MODEL_LOAD, "gguf: nested arrays too deep");
+            if (depth >= 64) fail(VKB_ERROR_MODEL_LOAD, "gguf: nested arrays too deep (ArrayTooDeep)");
             uint32_t et = c.get<uint32_t>("array type");
             uint64_t cnt = c.get<uint64_t>("array count");
-            if (cnt > (1ull << 28)) fail(VKB_ERROR_MODEL_LOAD, "gguf: array too long");
+            if (cnt > c.n - c.i) fail(VKB_ERROR_MODEL_LOAD, "gguf: array length exceeds file size (Truncated)");
             v.arr.reserve((size_t)std::min<uint64_t>(cnt, 1 << 16));
             for (uint64_t k = 0; k < cnt; ++k) v.arr.push_back(read_value(c, et, depth + 1));
             break;
@@ -97,62 +100,84 @@ GgufFile* gguf_open(const std::string& path) {
     return g;
 }
 
+// Errors carry the reference's GgufError variant name (gguf/mod.rs) in the
+// message, in the order parse_all (reader.rs:333-428) checks them.
 void gguf_parse(GgufFile& g) {
     Cursor c{g.bytes.data(), g.bytes.size()};
-    c.need(4, "magic");
-    if (memcmp(c.p, "GGUF", 4) != 0) fail(VKB_ERROR_MODEL_LOAD, "gguf: bad magic");
+    c.need(4, "magic (Truncated)");
+    if (memcmp(c.p, "GGUF", 4) != 0) fail(VKB_ERROR_MODEL_LOAD, "gguf: bad magic (BadMagic)");
     c.i = 4;
-    uint32_t ver = c.get<uint32_t>("version");
-    if (ver != 3) fail(VKB_ERROR_MODEL_LOAD, "gguf: unsupported version " + std::to_string(ver));
-    uint64_t n_t = c.get<uint64_t>("tensor count");
-    uint64_t n_kv = c.get<uint64_t>("metadata count");
-    if (n_t > (1ull << 24) || n_kv > (1ull << 24)) fail(VKB_ERROR_MODEL_LOAD, "gguf: implausible counts");
+    uint32_t ver = c.get<uint32_t>("version (Truncated)");
+    if (ver != 3) fail(VKB_ERROR_MODEL_LOAD, "gguf: unsupported version " + std::to_string(ver) + " (UnsupportedVersion)");
+    uint64_t n_t = c.get<uint64_t>("tensor count (Truncated)");
+    uint64_t n_kv = c.get<uint64_t>("metadata count (Truncated)");
+    // every entry takes at least one byte: larger counts are malformed, caught
+    // before any loop or allocation
+    if (n_t > c.n - c.i || n_kv > c.n - c.i)
+        fail(VKB_ERROR_MODEL_LOAD, "gguf: declared count exceeds file size (Truncated)");
     for (uint64_t k = 0; k < n_kv; ++k) {
-        std::string key = c.str("metadata key");
-        uint32_t t = c.get<uint32_t>("metadata type");
+        std::string key = c.str("metadata key (Truncated)");
+        uint32_t t = c.get<uint32_t>("metadata type (Truncated)");
         g.meta[key] = read_value(c, t, 0);
     }
     uint64_t align = 32;
     auto it = g.meta.find("general.alignment");
     if (it != g.meta.end()) {
+        const uint32_t at = it->second.type;
+        if (at != 0 && at != 2 && at != 4 && at != 10)
+            fail(VKB_ERROR_MODEL_LOAD, "gguf: general.alignment is not an integer (OffsetOutOfBounds)");
         align = it->second.u;
-        if (align == 0 || (align & (align - 1))) fail(VKB_ERROR_MODEL_LOAD, "gguf: alignment is not a power of two");
+        if (align == 0 || (align & (align - 1)))
+            fail(VKB_ERROR_MODEL_LOAD, "gguf: alignment " + std::to_string(align) +
+                                           " is not a power of two (InvalidAlignment)");
     }
     for (uint64_t k = 0; k < n_t; ++k) {
         GgufTensor t;
-        t.name = c.str("tensor name");
-        uint32_t nd = c.get<uint32_t>("n_dims");
-        if (nd > 8) fail(VKB_ERROR_MODEL_LOAD, "gguf: too many dimensions for " + t.name);
+        t.name = c.str("tensor name (Truncated)");
+        uint32_t nd = c.get<uint32_t>("tensor n_dims (Truncated)");
+        if (nd > 8) fail(VKB_ERROR_MODEL_LOAD, "gguf: " + std::to_string(nd) + " dimensions for " + t.name +
+                                                   " (TooManyDimensions)");
         uint64_t elems = 1;
+        bool overflow = false;
         for (uint32_t d = 0; d < nd; ++d) {
-            uint64_t dim = c.get<uint64_t>("dim");
-            if (dim && elems > UINT64_MAX / dim) fail(VKB_ERROR_MODEL_LOAD, "gguf: element count overflow");
+            uint64_t dim = c.get<uint64_t>("tensor dim (Truncated)");
+            if (dim && elems > UINT64_MAX / dim) overflow = true;
             elems *= dim;
             t.dims.push_back((int64_t)dim);
         }
-        t.tag = c.get<uint32_t>("dtype");
-        t.offset = c.get<uint64_t>("offset");
-        int64_t ps = tag_payload(t.tag, elems);
-        if (ps == -2) fail(VKB_ERROR_MODEL_LOAD, "gguf: unsupported dtype " + std::to_string(t.tag) + " for " + t.name);
-        if (ps < 0) fail(VKB_ERROR_MODEL_LOAD, "gguf: " + t.name + " is not a whole number of blocks");
-        t.nbytes = (uint64_t)ps;
+        t.tag = c.get<uint32_t>("tensor dtype (Truncated)");
+        if (tag_payload(t.tag, 0) == -2)
+            fail(VKB_ERROR_MODEL_LOAD, "gguf: unsupported dtype " + std::to_string(t.tag) + " for " + t.name +
+                                           " (UnsupportedDtype)");
+        t.offset = c.get<uint64_t>("tensor offset (Truncated)");
+        if (g.index.count(t.name)) fail(VKB_ERROR_MODEL_LOAD, "gguf: duplicate tensor " + t.name + " (DuplicateTensor)");
+        if (overflow) fail(VKB_ERROR_MODEL_LOAD, "gguf: element count of " + t.name + " overflows (Overflow)");
         t.n_elem = elems;
-        if (t.offset % align) fail(VKB_ERROR_MODEL_LOAD, "gguf: misaligned tensor offset for " + t.name);
-        if (g.index.count(t.name)) fail(VKB_ERROR_MODEL_LOAD, "gguf: duplicate tensor " + t.name);
         g.index[t.name] = g.tensors.size();
         g.tensors.push_back(t);
     }
     uint64_t base = (c.i + align - 1) / align * align;
     g.data_base = base;
+    if (!g.tensors.empty() && base > g.bytes.size())
+        fail(VKB_ERROR_MODEL_LOAD, "gguf: tensor-data region starts past end of file (OffsetOutOfBounds)");
     for (auto& t : g.tensors) {
-        if (base + t.offset + t.nbytes > g.bytes.size() || base + t.offset + t.nbytes < base)
-            fail(VKB_ERROR_MODEL_LOAD, "gguf: tensor " + t.name + " runs past the end of the file");
+        if (t.offset % align)
+            fail(VKB_ERROR_MODEL_LOAD, "gguf: tensor " + t.name + " offset " + std::to_string(t.offset) +
+                                           " is not a multiple of " + std::to_string(align) + " (UnalignedTensorOffset)");
+        int64_t ps = tag_payload(t.tag, t.n_elem);
+        if (ps < 0)
+            fail(VKB_ERROR_MODEL_LOAD, "gguf: " + t.name + " is not a whole number of blocks (BlockSizeMisaligned)");
+        t.nbytes = (uint64_t)ps;
+        if (base + t.offset < base || base + t.offset + t.nbytes < base + t.offset)
+            fail(VKB_ERROR_MODEL_LOAD, "gguf: offset of " + t.name + " overflows (Overflow)");
+        if (base + t.offset + t.nbytes > g.bytes.size())
+            fail(VKB_ERROR_MODEL_LOAD, "gguf: tensor " + t.name + " runs past the end of the file (OffsetOutOfBounds)");
     }
 }
 
 const GgufTensor& GgufFile::tensor(const std::string& name, const std::vector<int64_t>& dims) const {
     auto it = index.find(name);
-    if (it == index.end()) fail(VKB_ERROR_MODEL_LOAD, "gguf: missing tensor " + name);
+    if (it == index.end()) fail(VKB_ERROR_MODEL_LOAD, "gguf: missing tensor " + name + " (MissingTensor)");
     const GgufTensor& t = tensors[it->second];
     if (!dims.empty() && t.dims != dims) {
         std::string s;
@@ -200,3 +225,14 @@ std::vector<float> GgufFile::f32(const std::string& name, const std::vector<int6
 }
 
 }  // namespace vkb
+
+extern "C" vkb_status vkb_gguf_inspect(const void* bytes, size_t len, int64_t* n_tensors, int64_t* n_metadata) {
+    return vkb::guard([&] {
+        if (!bytes && len) vkb::fail(VKB_ERROR_INVALID_ARGUMENT, "gguf_inspect: null bytes");
+        vkb::GgufFile g;
+        g.bytes.assign((const uint8_t*)bytes, (const uint8_t*)bytes + len);
+        vkb::gguf_parse(g);
+        if (n_tensors) *n_tensors = (int64_t)g.tensors.size();
+        if (n_metadata) *n_metadata = (int64_t)g.meta.size();
+    });
+}

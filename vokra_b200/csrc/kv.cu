@@ -394,15 +394,13 @@ void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, co
     const int threads = R * (W / 16);
     if (kv_fmt == VKB_DT_F16) {
         FetchDenseF16 f{reinterpret_cast<const __half*>(k), reinterpret_cast<const __half*>(v), W, 0};
-        static bool attr = false;
-        if (!attr) { VKB_CUDA(cudaFuncSetAttribute(dense_attn_kernel<FetchDenseF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
+        smem_optin(dense_attn_kernel<FetchDenseF16>, 200 * 1024);
         launch_pdl(ctx, dense_attn_kernel<FetchDenseF16>, grid, threads, sm, f, q, seq_of_tok, n_ctx, n_head, d_head, kps,
                                                                             splits, out, out_dtype, ws, (int64_t)n_tok * W);
     } else {
         FetchDenseQ8 f{reinterpret_cast<const int8_t*>(k), reinterpret_cast<const __half*>(k_scale),
                        reinterpret_cast<const int8_t*>(v), reinterpret_cast<const __half*>(v_scale), W, 0};
-        static bool attr = false;
-        if (!attr) { VKB_CUDA(cudaFuncSetAttribute(dense_attn_kernel<FetchDenseQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
+        smem_optin(dense_attn_kernel<FetchDenseQ8>, 200 * 1024);
         launch_pdl(ctx, dense_attn_kernel<FetchDenseQ8>, grid, threads, sm, f, q, seq_of_tok, n_ctx, n_head, d_head, kps,
                                                                            splits, out, out_dtype, ws, (int64_t)n_tok * W);
     }
@@ -671,11 +669,7 @@ void kv_append_attention_ex(vkb_kv_pool* p, int layer, const float* qkv, int64_t
     }
     const int max_keys = d.max_time;
     const size_t smem = (size_t)(std::max(4 * max_keys, 4096) + 256) * sizeof(float) + (size_t)max_keys * sizeof(int64_t);
-    static bool attr = false;
-    if (!attr) {
-        VKB_CUDA(cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr = true;
-    }
+    smem_optin(paged_decode_kernel, 200 * 1024);
     if (smem > 200 * 1024) fail(VKB_ERROR_UNSUPPORTED_OP, "decode attention: max_time too large");
     dim3 grid((unsigned)p->n_tok, (unsigned)(d.n_head / 4));
     launch_pdl(p->ctx, paged_decode_kernel, grid, 256, smem, qkv, ld, part, splits, (int64_t)p->n_tok * ld, bias,
@@ -725,14 +719,12 @@ void kv_attention_ex(vkb_kv_pool* p, int layer, const float* q, int64_t q_ld, vo
     const int of16 = out_dtype;  // 0 f32, 1 f16, 2 f16 hi+lo planes
     const int64_t oplane = (int64_t)p->n_tok * W;
     if (p->maxq == 1) {
-        static bool attr = false;
-        if (!attr) { VKB_CUDA(cudaFuncSetAttribute(paged_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
+        smem_optin(paged_attn_kernel<1>, 200 * 1024);
         launch_pdl(p->ctx, paged_attn_kernel<1>, grid, threads, attn_smem_bytes(R, 1, W, d.n_head), 
             f, q, q_ld, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->splits, out, of16, ws,
             per_seq_base, p->ppseq, oplane);
     } else {
-        static bool attr = false;
-        if (!attr) { VKB_CUDA(cudaFuncSetAttribute(paged_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); attr = true; }
+        smem_optin(paged_attn_kernel<4>, 200 * 1024);
         launch_pdl(p->ctx, paged_attn_kernel<4>, grid, threads, attn_smem_bytes(R, 4, W, d.n_head), 
             f, q, q_ld, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->splits, out, of16, ws,
             per_seq_base, p->ppseq, oplane);
@@ -791,6 +783,18 @@ void kv_copy_stream(vkb_kv_pool* p, int src, int dst, int n_pos) {
     if (n_pos < 0 || n_pos > d.max_time) fail(VKB_ERROR_INVALID_ARGUMENT, "copy_stream: bad position count");
     if (src == dst) return;
     if (d.page_tokens * (p->W / 32) * 2 % 16) fail(VKB_ERROR_UNSUPPORTED_OP, "copy_stream: page scales not 16-byte sized");
+    const int n_pg = (n_pos + d.page_tokens - 1) / d.page_tokens;
+    // Validate everything before touching dst, so a failed call leaves both
+    // streams and the device page table as they were.
+    size_t dst_held = 0;
+    for (int i = 0; i < p->ppseq; ++i) dst_held += p->table[(int64_t)dst * p->ppseq + i] >= 0;
+    for (int i = 0; i < n_pg; ++i)
+        if (p->table[(int64_t)src * p->ppseq + i] < 0)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "copy_stream: source stream has no page for position " +
+                                                 std::to_string(i * d.page_tokens));
+    if (p->free_list.size() + dst_held < (size_t)n_pg)
+        fail(VKB_ERROR_KV_CACHE_EXHAUSTED, "copy_stream: " + std::to_string(n_pg) + " pages needed, " +
+                                               std::to_string(p->free_list.size() + dst_held) + " free");
     for (int i = 0; i < p->ppseq; ++i) {
         int32_t& e = p->table[(int64_t)dst * p->ppseq + i];
         if (e >= 0) {
@@ -799,11 +803,8 @@ void kv_copy_stream(vkb_kv_pool* p, int src, int dst, int n_pos) {
         }
     }
     std::vector<int2> pairs;
-    const int n_pg = (n_pos + d.page_tokens - 1) / d.page_tokens;
     for (int i = 0; i < n_pg; ++i) {
         const int32_t sp = p->table[(int64_t)src * p->ppseq + i];
-        if (sp < 0) fail(VKB_ERROR_INVALID_ARGUMENT, "copy_stream: source stream has no page for position " +
-                                                         std::to_string(i * d.page_tokens));
         const int32_t dp = acquire(p);
         p->table[(int64_t)dst * p->ppseq + i] = dp;
         pairs.push_back(make_int2(sp, dp));
@@ -943,6 +944,20 @@ vkb_status vkb_kv_attention(vkb_kv_pool* pool, int32_t layer, const float* q_dev
         kv_attention_ex(pool, layer, q_dev, pool->W, ctx_out_dev, out_dtype);
     });
 }
+
+vkb_status vkb_kv_append_attention(vkb_kv_pool* pool, int32_t layer, const float* qkv_dev, int64_t ld,
+                                   void* ctx_out_dev, int out_dtype) {
+    return guard([&] {
+        if (!pool) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_append_attention: null pool");
+        if (!qkv_dev || !ctx_out_dev) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_append_attention: null qkv/out");
+        if (pool->n_tok == 0) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_append_attention: no step was begun");
+        if (ld < 3 * (int64_t)pool->W || ld % 4)
+            fail(VKB_ERROR_INVALID_ARGUMENT, "kv_append_attention: ld must be >= 3*n_head*d_head and a multiple of 4");
+        kv_append_attention_ex(pool, layer, qkv_dev, ld, ctx_out_dev, out_dtype, nullptr, 0, nullptr, 1.0f);
+    });
+}
+
+int32_t vkb_kv_decode_fused(const vkb_kv_pool* pool) { return pool && kv_decode_fused(pool) ? 1 : 0; }
 
 vkb_status vkb_kv_release_seq(vkb_kv_pool* pool, int32_t seq_id) {
     return guard([&] {

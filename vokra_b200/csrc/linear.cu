@@ -358,18 +358,10 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
     tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_lo,
                    const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc, int64_t K, int64_t N, int64_t M,
                    int n_tiles, int m_tiles, int stages_per_split, int n_splits, float* ws, Epi e, int* err,
-                   unsigned long long* trace, const __grid_constant__ CUtensorMap omap,
+                   const __grid_constant__ CUtensorMap omap,
                    const __grid_constant__ CUtensorMap omap_lo, const __grid_constant__ CUtensorMap rmap,
                    int tma_epi) {
     using C = TcCfg<FMT, BN, SPLIT>;
-    // Optional timeline of block 0 (debugging aid): [role][stage] globaltimer stamps.
-    auto stamp = [&](int role, int i) {
-        if (trace && blockIdx.x == 0 && i < 64) {
-            unsigned long long t;
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-            trace[role * 64 + i] = t;
-        }
-    };
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* st_ring = smem;
@@ -445,7 +437,6 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
                     ptx::bulk_load(raw_dst, p.qs, C::RAW_Q, &full[s]);
                     if (C::RAW_S) ptx::bulk_load(raw_dst + C::RAW_Q, p.sc, C::RAW_S, &full[s]);
                 }
-                stamp(0, i);
                 ptx::tma_load_2d(b_dst, &xmap, &full[s], (int32_t)(stage * STAGE_K), m_tile * BN);
                 if (SPLIT)
                     ptx::tma_load_2d(b_dst + C::B_BYTES, &xmap_lo, &full[s], (int32_t)(stage * STAGE_K), m_tile * BN);
@@ -458,7 +449,6 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
                 int s = i % C::S, a = i % C::AS;
                 if (!ptx::mbar_wait(&full[s], (i / C::S) & 1)) { ok = false; break; }
                 if (!ptx::mbar_wait(&a_full[a], (i / C::AS) & 1)) { ok = false; break; }
-                stamp(1, i);
                 ptx::tc_fence_after();
                 const uint32_t a_t = tmem + C::A_COL0 + a * C::NP * 32;
                 uint32_t b_addr = ptx::smem_u32(st_ring + s * C::STAGE_BYTES);
@@ -487,7 +477,6 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
             int s = i % C::S, a = i % C::AS;
             if (!ptx::mbar_wait(&full[s], (i / C::S) & 1)) { ok = false; break; }
             if (!ptx::mbar_wait(&a_empty[a], ((i / C::AS) & 1) ^ 1)) { ok = false; break; }
-            if (threadIdx.x == 64) stamp(2, i);
             const uint8_t* raw = st_ring + s * C::STAGE_BYTES + C::NP * C::B_BYTES;
             uint32_t hi[32], lo[32];
             dequant_row_stage_h<FMT, SPLIT>(raw, raw + C::RAW_Q, r, (int)(s0 + i), hi, lo);
@@ -497,7 +486,6 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
             if (SPLIT) ptx::tmem_st32(a_t + 32, lo);
             ptx::tmem_st_wait();
             ptx::tc_fence_before();
-            if (threadIdx.x == 64) stamp(3, i);
             ptx::mbar_arrive(&a_full[a]);
         }
     }
@@ -512,7 +500,6 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
         const int cb = ((warp - 2) >> 2) * HALF;
         pdl_wait();
         const bool go = ok && ptx::mbar_wait(acc_full, 0);
-        if (threadIdx.x == 64) stamp(4, 0);
         ptx::tc_fence_after();
         const int64_t n = (int64_t)n_tile * TILE_N + r;
         const float bias_n = (go && e.bias && n < N) ? e.bias[n] : 0.0f;
@@ -623,7 +610,6 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
             ok = false;
         }
     }
-    if (threadIdx.x == 64) stamp(4, 1);
     if (!ok && err) atomicExch(err, 1);
     // Reconverge each warp (only one lane of the producer and MMA warps ran its
     // role) before the block barrier: bar.sync requires converged warps.
@@ -707,12 +693,7 @@ static void launch_gemv(vkb_context* ctx, const vkb_weight* w, int64_t m, const 
 #define VKB_GEMV(MMv)                                                                                           \
     {                                                                                                           \
         size_t sm = (size_t)(MMv)*stages_per_split * STAGE_K * sizeof(float);                                   \
-        static bool attr = false;                                                                               \
-        if (!attr) {                                                                                            \
-            VKB_CUDA(cudaFuncSetAttribute(gemv_kernel<FMT, MMv>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
-                                          200 * 1024));                                                         \
-            attr = true;                                                                                        \
-        }                                                                                                       \
+        smem_optin(gemv_kernel<FMT, MMv>, 200 * 1024);                                                          \
         launch_pdl(ctx, gemv_kernel<FMT, MMv>, grid, 128, sm, qs, sc, w->k, w->n, m, a, a_fmt, stages_per_split, \
                                                               splits, ws, e);                                   \
     }
@@ -726,12 +707,7 @@ template <int FMT, int BN, bool SPLIT>
 static void launch_tc(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const Epi& e, float* ws,
                       int stages_per_split, int splits, int m_tiles) {
     using C = TcCfg<FMT, BN, SPLIT>;
-    static bool attr = false;
-    if (!attr) {
-        VKB_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<FMT, BN, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      C::SMEM));
-        attr = true;
-    }
+    smem_optin(tc_gemm_kernel<FMT, BN, SPLIT>, C::SMEM);
     CUtensorMap map, map_lo, omap, omap_lo, rmap;
     make_tmap_f16(&map, a16, m, w->k, BN);
     if (SPLIT) make_tmap_f16(&map_lo, a16 + m * w->k, m, w->k, BN);
@@ -761,7 +737,7 @@ static void launch_tc(vkb_context* ctx, const vkb_weight* w, int64_t m, const __
     dim3 grid((unsigned)(n_tiles * m_tiles * splits));
     launch_pdl(ctx, tc_gemm_kernel<FMT, BN, SPLIT>, grid, C::THREADS, C::SMEM, 
         map, map_lo, w->qs.as<uint8_t>(), w->sc.as<uint8_t>(), w->k, w->n, m, n_tiles, m_tiles, stages_per_split,
-        splits, ws, e, device_err_flag(ctx), ctx->trace, omap, omap_lo, rmap, tma_epi);
+        splits, ws, e, device_err_flag(ctx), omap, omap_lo, rmap, tma_epi);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }

@@ -435,11 +435,7 @@ void run_xattn_q8(vkb_context* ctx, const XaPlan& plan, int n_tok, int n_head, i
 
     a.err = ctx->err_flag.as<int>();
     const size_t smem = (size_t)a.S * 2 * XA_T * (W + W / 16) + (size_t)XA_T * (W / 32) * 4 + (size_t)a.S * 16;
-    static bool attr = false;
-    if (!attr) {
-        VKB_CUDA(cudaFuncSetAttribute(xattn_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, XA_SMEM_BUDGET));
-        attr = true;
-    }
+    smem_optin(xattn_q8_kernel, XA_SMEM_BUDGET);
     launch_pdl(ctx, xattn_q8_kernel, plan.G, 16 * n_head + 32, smem, a);
     VKB_CUDA(cudaGetLastError());
     ctx->count();

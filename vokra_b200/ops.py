@@ -186,6 +186,17 @@ class QuantizedPagedKvCache:
         dt = _lib.DT_F16 if out.dtype == torch.float16 else _lib.DT_F32
         check(_L.vkb_kv_attention(self.h, layer, C.c_void_p(_ptr(q)), C.c_void_p(_ptr(out)), dt))
 
+    def append_attention(self, layer: int, qkv, out) -> None:
+        """Append the step's K/V and attend, one call (``vkb_kv_append_attention``):
+        qkv is f32 [n_tok][ld] holding scaled q | k | v."""
+        import torch
+        dt = _lib.DT_F16 if out.dtype == torch.float16 else _lib.DT_F32
+        check(_L.vkb_kv_append_attention(self.h, layer, C.c_void_p(_ptr(qkv)), qkv.stride(0),
+                                         C.c_void_p(_ptr(out)), dt))
+
+    def decode_fused(self) -> bool:
+        return bool(_L.vkb_kv_decode_fused(self.h))
+
     # ---- reference-shaped API ----------------------------------------------
     def append_step(self, layer: int, t: int, s: int, c: int, k_row: np.ndarray, v_row: np.ndarray):
         """``append_step`` (paged_quant.rs:396) for one (layer, t, stream) row, host arrays."""
