@@ -185,7 +185,8 @@ typedef struct vkb_kv_pool_desc {
     int32_t n_codebook;  /* 1 for Whisper (KvDims::n_codebook) */
     int32_t max_time;    /* KvDims::max_time */
     int32_t page_tokens; /* 2, 4 or 16 */
-    int32_t mode;        /* vkb_kv_quant; Q8_0 is the device-kernel format */
+    int32_t mode;        /* vkb_kv_quant: Q8_0, Q4_0 or Q5_0 (bit-exact block packs);
+                          * FP32 (dense f32 rows) in the SEQUENCE layout only */
     int32_t layout;      /* vkb_kv_layout */
     int32_t n_pages;     /* arena pages; 0 = enough for every stream at max_time */
 } vkb_kv_pool_desc;
@@ -340,11 +341,20 @@ typedef struct vkb_session_options {
     int32_t max_clips;        /* clips per vkb_session_encode call (0 = no encoder buffers) */
     int32_t cross_kv_q8;      /* 1: cross K/V stored as Q8_0 int8 + f16 scales; 0: f16 */
     int32_t kv_page_tokens;   /* self-attention page size (0 = 16) */
+    int32_t self_kv_mode;     /* vkb_self_kv: how the self-attention K/V pages are stored */
 } vkb_session_options;
 
+/* Self-attention KV storage of a session.
+ * Q8_0 (default): int8 pages, bit-exact BlockQ8_0 (the reference's
+ *   QuantizedPagedKvCache in KvQuant::Q8_0), decoded by the fused decode kernel.
+ * F32: dense f32 pages, the numerics of the KvCache the reference's Whisper
+ *   decoder keeps (whisper/decoder.rs:183-200, 455-470).
+ * Q4_0 / Q5_0: the reference's 4- and 5-bit KV blocks. */
+enum vkb_self_kv { VKB_SELF_KV_Q8_0 = 0, VKB_SELF_KV_F32 = 1, VKB_SELF_KV_Q4_0 = 2, VKB_SELF_KV_Q5_0 = 3 };
+
 /* A batched decoding session (the DecoderStepSession / CudaDecodeSession seam,
- * crates/vokra-models/src/compute.rs:2892-3140): owns the paged Q8_0
- * self-attention cache (sequence layout), the cross-attention store and every
+ * crates/vokra-models/src/compute.rs:2892-3140): owns the paged self-attention
+ * cache (sequence layout, Q8_0 unless self_kv_mode says otherwise), the cross-attention store and every
  * device buffer; nothing is allocated per step. */
 VKB_API vkb_status vkb_session_create(vkb_whisper* m, const vkb_session_options* opt, vkb_session** out);
 VKB_API vkb_status vkb_session_destroy(vkb_session* s);

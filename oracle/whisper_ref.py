@@ -7,8 +7,9 @@ at load and run through gemm_f32) with the C++ primitives of vkb_oracle.cpp:
            :413-566 (step_into), :754-773 (tied logits)
   nn       whisper/nn.rs:62-300
 The self-attention cache can be the reference's dense f32 KvCache
-(kv_mode="f32") or its QuantizedPagedKvCache in Q8_0 (kv_mode="q8": every
-appended K/V row goes through BlockQ8_0::pack / unpack); the cross K/V can be
+(kv_mode="f32") or its QuantizedPagedKvCache in Q8_0, Q4_0 or Q5_0
+(kv_mode="q8" / "q4" / "q5": every appended K/V row goes through the block's
+pack / unpack); the cross K/V can be
 kept f32, rounded to f16, or stored as Q8_0 (cross_mode="f32"|"f16"|"q8").
 """
 from __future__ import annotations
@@ -137,8 +138,11 @@ class RefWhisper:
 
 
 def _store(x: np.ndarray, mode: str) -> np.ndarray:
-    if mode == "q8":
-        return o.kv_unpack(3, o.kv_pack(3, x)).reshape(x.shape)
+    """K/V rows as a cache of `mode` returns them: "q8" / "q4" / "q5" through
+    BlockQ8_0 / BlockQ4_0 / BlockQ5_0 pack + unpack, "f16" rounded, "f32" as is."""
+    kv = {"q4": 1, "q5": 2, "q8": 3}
+    if mode in kv:
+        return o.kv_unpack(kv[mode], o.kv_pack(kv[mode], x)).reshape(x.shape)
     if mode == "f16":
         return x.astype(np.float16).astype(np.float32)
     return x
@@ -169,7 +173,7 @@ class RefDecoder:
             x = m.ln(h, p + ".self_attn_layer_norm")
             k = m.lin(x, p + ".self_attn.k_proj", bias=False)
             v = m.lin(x, p + ".self_attn.v_proj")
-            qk = "q8" if self.kv_mode == "q8" else "f32"
+            qk = self.kv_mode if self.kv_mode in ("q4", "q5", "q8") else "f32"
             self.k[i] = np.concatenate([self.k[i], _store(k, qk)])
             self.v[i] = np.concatenate([self.v[i], _store(v, qk)])
             h = h + m.attn_block(x, self.k[i], self.v[i], p + ".self_attn", m.n_text_head, causal=True, q_off=start)

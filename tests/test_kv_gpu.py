@@ -27,12 +27,15 @@ def _rows(rng, n, w):
     return x
 
 
-def test_append_bytes_and_page_table_match_reference_layout(ctx):
+@pytest.mark.parametrize("mode", [_lib.KV_Q8_0, _lib.KV_Q4_0, _lib.KV_Q5_0])
+def test_append_bytes_and_page_table_match_reference_layout(ctx, mode):
+    """BlockQ8_0 / BlockQ4_0 / BlockQ5_0 ::pack on the device: page bytes, page
+    table, read_step, release_layer and reset against the oracle cache."""
     from vokra_b200 import ops
     n_layer, n_head, d_head, n_stream, max_time, bs = 2, 2, 32, 3, 12, 4
     dims = ops.KvDims(n_layer, n_head, d_head, n_stream, 1, max_time)
-    dev = ops.QuantizedPagedKvCache(ctx, dims, bs, _lib.KV_Q8_0, _lib.KV_LAYOUT_REFERENCE)
-    ref = o.PagedKv(n_layer, n_head, d_head, n_stream, 1, max_time, bs, 3)
+    dev = ops.QuantizedPagedKvCache(ctx, dims, bs, mode, _lib.KV_LAYOUT_REFERENCE)
+    ref = o.PagedKv(n_layer, n_head, d_head, n_stream, 1, max_time, bs, mode)
     w = n_head * d_head
     rng = np.random.default_rng(0)
     steps = [([0, 0, 1], [0, 1, 0]), ([0, 1, 2], [2, 1, 0]), ([2], [1]), ([1, 1, 1, 1], [2, 3, 4, 5])]
@@ -101,15 +104,24 @@ def _oracle_attention(kv_rows_k, kv_rows_v, q, n_head, causal_pos):
     return out
 
 
-@pytest.mark.parametrize("n_head,d_head", [(2, 64), (20, 64), (8, 64)])
-def test_paged_attention_sequence_layout(ctx, n_head, d_head):
+def _store(mode, x):
+    """What a pool of `mode` gives back for rows x (the block pack round trip)."""
+    if mode == _lib.KV_FP32:
+        return x
+    return o.kv_unpack(mode, o.kv_pack(mode, x)).reshape(x.shape)
+
+
+@pytest.mark.parametrize("n_head,d_head,mode", [(2, 64, _lib.KV_Q8_0), (20, 64, _lib.KV_Q8_0), (8, 64, _lib.KV_Q8_0),
+                                                (20, 64, _lib.KV_Q4_0), (20, 64, _lib.KV_Q5_0),
+                                                (20, 64, _lib.KV_FP32), (4, 32, _lib.KV_Q5_0)])
+def test_paged_attention_sequence_layout(ctx, n_head, d_head, mode):
     import torch
     from vokra_b200 import ops
     rng = np.random.default_rng(n_head)
     n_layer, n_seq, max_time, bs = 2, 5, 200, 16
     w = n_head * d_head
     dims = ops.KvDims(n_layer, n_head, d_head, n_seq, 1, max_time)
-    pool = ops.QuantizedPagedKvCache(ctx, dims, bs, _lib.KV_Q8_0, _lib.KV_LAYOUT_SEQUENCE)
+    pool = ops.QuantizedPagedKvCache(ctx, dims, bs, mode, _lib.KV_LAYOUT_SEQUENCE)
     # scatter pages by a seeded permutation (config 3)
     pps = (max_time + bs - 1) // bs
     perm = rng.permutation(n_seq * pps).astype(np.int32)
@@ -148,10 +160,17 @@ def test_paged_attention_sequence_layout(ctx, n_head, d_head):
     torch.cuda.synchronize()
     got = out.cpu().numpy()
     for s, L in enumerate(lengths):
-        kd = o.kv_unpack(3, o.kv_pack(3, Ks[layer][s])).reshape(L, w)
-        vd = o.kv_unpack(3, o.kv_pack(3, Vs[layer][s])).reshape(L, w)
+        kd = _store(mode, Ks[layer][s])
+        vd = _store(mode, Vs[layer][s])
         ref = o.attention(q[s:s + 1], kd, vd, n_head)[0]
         assert np.max(np.abs(got[s] - ref)) <= 1e-4, (s, np.max(np.abs(got[s] - ref)))
+    if mode != _lib.KV_FP32:  # the last rows' page bytes: the reference block encoding
+        table = pool.page_table().reshape(n_seq, -1)
+        for s, L in enumerate(lengths):
+            kp, _ = pool.read_page(int(table[s, (L - 1) // bs]), layer)
+            n_rows = (L - 1) % bs + 1
+            rows = Ks[layer][s][(L - 1) // bs * bs:L]
+            assert np.array_equal(kp.reshape(bs, -1)[:n_rows].reshape(-1), o.kv_pack(mode, rows))
 
 
 def test_paged_attention_prefix_causal(ctx):

@@ -8,11 +8,16 @@ from vokra_b200 import _lib, synth
 
 pytestmark = pytest.mark.gpu
 
-TAGS = [synth.Q4_0, synth.Q8_0, synth.Q4_K]
+# Q4_0 / Q8_0 / Q4_K run dequant-fused; Q5_K and Q6_K too (the reference
+# dequantizes them at load, whisper/weights.rs:400-410, so route R1 is their
+# oracle); F32 and BF16 are kept as hi + lo f16 planes, F16 as one plane.
+TAGS = [synth.Q4_0, synth.Q8_0, synth.Q4_K, synth.Q5_K, synth.Q6_K, synth.F32, synth.BF16]
 
 
-def _weights(tag, n, k, seed):
+def _weights(tag, n, k, seed, rnd=False):
     rng = np.random.default_rng(seed)
+    if tag in (synth.Q5_K, synth.Q6_K) and rnd:
+        return synth.random_kquant_blocks(tag, n * k, rng)  # every sub-scale, min and high bit random
     w = (rng.standard_normal(n * k).astype(np.float32) * np.float32(0.02))
     return synth.quantize(tag, w)
 
@@ -21,10 +26,10 @@ def _rel_rms(a, b):
     return float(np.sqrt(np.mean((a - b) ** 2)) / (np.sqrt(np.mean(b ** 2)) + 1e-30))
 
 
-def _run(ctx, tag, n, k, m, seed=0, bias=True, a_f16=False, out_f16=False, epi=_lib.EPI_NONE, scale=1.0):
+def _run(ctx, tag, n, k, m, seed=0, bias=True, a_f16=False, out_f16=False, epi=_lib.EPI_NONE, scale=1.0, rnd=False):
     import torch
     from vokra_b200 import ops
-    wq = _weights(tag, n, k, seed)
+    wq = _weights(tag, n, k, seed, rnd)
     rng = np.random.default_rng(seed + 1)
     a = rng.standard_normal((m, k)).astype(np.float32)
     b = (rng.standard_normal(n).astype(np.float32) * np.float32(0.1)) if bias else None
@@ -54,8 +59,8 @@ def _run(ctx, tag, n, k, m, seed=0, bias=True, a_f16=False, out_f16=False, epi=_
 @pytest.mark.parametrize("tag", TAGS)
 @pytest.mark.parametrize("m", [1, 2, 3, 4])
 def test_gemv_path_matches_oracle(ctx, tag, m):
-    for (k, n) in [(256, 128), (512, 300), (1280, 1280)]:
-        got, ref = _run(ctx, tag, n, k, m, seed=k + n)
+    for i, (k, n) in enumerate([(256, 128), (512, 300), (1280, 1280)]):
+        got, ref = _run(ctx, tag, n, k, m, seed=k + n, rnd=i % 2 == 1)
         assert np.max(np.abs(got - ref)) <= 1e-4 * max(1.0, np.max(np.abs(ref)))
         assert _rel_rms(got, ref) <= 1e-5
 
@@ -64,15 +69,15 @@ def test_gemv_path_matches_oracle(ctx, tag, m):
 @pytest.mark.parametrize("m", [5, 8, 33, 64, 100, 256, 300, 1500])
 def test_tensor_core_path_matches_oracle(ctx, tag, m):
     # f16 operands on tcgen05 with fp32 accumulation: 1e-3 relative RMS, 1e-2 max-abs.
-    for (k, n) in [(256, 128), (1280, 384)]:
-        got, ref = _run(ctx, tag, n, k, m, seed=7 * k + n)
+    for i, (k, n) in enumerate([(256, 128), (1280, 384)]):
+        got, ref = _run(ctx, tag, n, k, m, seed=7 * k + n, rnd=i % 2 == 1)
         assert _rel_rms(got, ref) <= 1e-3, (k, n)
         assert np.max(np.abs(got - ref)) <= 1e-2, (k, n)
 
 
 @pytest.mark.parametrize("tag", TAGS)
 def test_tensor_core_large_k_and_ragged_n(ctx, tag):
-    got, ref = _run(ctx, tag, 1300, 5120, 96, seed=11)
+    got, ref = _run(ctx, tag, 1300, 5120, 96, seed=11, rnd=True)
     assert _rel_rms(got, ref) <= 1e-3
     assert np.max(np.abs(got - ref)) <= 2e-2
 

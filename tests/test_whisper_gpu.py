@@ -15,26 +15,29 @@ def _rel_rms(a, b):
     return float(np.sqrt(np.mean((a - b) ** 2)) / (np.sqrt(np.mean(b ** 2)) + 1e-30))
 
 
-@pytest.fixture(scope="module", params=[synth.Q8_0, synth.Q4_0, synth.Q4_K])
+@pytest.fixture(scope="module", params=[synth.Q8_0, synth.Q4_0, synth.Q4_K, synth.Q5_K, synth.Q6_K, synth.F32])
 def tiny(request, tmp_path_factory):
     path = str(tmp_path_factory.mktemp("w") / f"tiny_{request.param}.gguf")
     synth.write_synthetic_whisper(path, synth.WHISPER_TINY_TEST, request.param, seed=1)
     return path
 
 
-def _run(ctx, path, n_streams=3, n_steps=6, cross_q8=True, arch=synth.WHISPER_TINY_TEST, seed=2):
+def _run(ctx, path, n_streams=3, n_steps=6, cross_q8=True, arch=synth.WHISPER_TINY_TEST, seed=2, self_kv="q8"):
     import torch
     from vokra_b200 import whisper
     rng = np.random.default_rng(seed)
     a = arch
     logmel = rng.uniform(-1.0, 1.5, (n_streams, a.n_mels, 2 * a.n_audio_ctx)).astype(np.float32)
     model = whisper.WhisperModel(ctx, path)
-    sess = whisper.Session(model, max_streams=n_streams, max_clips=n_streams, cross_kv_q8=cross_q8)
+    from vokra_b200 import _lib
+    modes = {"q8": _lib.SELF_KV_Q8_0, "f32": _lib.SELF_KV_F32, "q4": _lib.SELF_KV_Q4_0, "q5": _lib.SELF_KV_Q5_0}
+    sess = whisper.Session(model, max_streams=n_streams, max_clips=n_streams, cross_kv_q8=cross_q8,
+                           self_kv=modes[self_kv])
     sess.encode(torch.from_numpy(logmel).cuda(), list(range(n_streams)))
     enc = sess.encoder_output(n_streams)
     ref = whisper_ref.RefWhisper(path)
     ref_enc = [ref.encode(logmel[i]) for i in range(n_streams)]
-    decs = [ref.decoder(ref_enc[i], kv_mode="q8", cross_mode="q8" if cross_q8 else "f16") for i in range(n_streams)]
+    decs = [ref.decoder(ref_enc[i], kv_mode=self_kv, cross_mode="q8" if cross_q8 else "f16") for i in range(n_streams)]
     toks = rng.integers(0, a.n_vocab, (n_streams, n_steps)).tolist()
     V = a.n_vocab
     results = []
@@ -77,6 +80,25 @@ def test_tiny_whisper_matches_oracle(ctx, tiny):
     assert worst_abs <= 1e-2
     assert worst_rms <= 1e-3
     assert mism == 0
+
+
+@pytest.mark.parametrize("self_kv", ["f32", "q4", "q5"])
+def test_tiny_whisper_self_kv_modes(ctx, tiny, self_kv):
+    """The session with f32, Q4_0 or Q5_0 self-attention pages against the
+    oracle keeping the same cache (prefix steps and decode steps take the
+    unfused append + paged attention kernels for these modes).
+
+    The packs themselves are bit-exact (test_kv_gpu); end to end, the device's
+    K/V rows differ from the oracle's in their last bits (split-precision
+    GEMMs), and a 4- or 5-bit pack turns a value that sits on a rounding
+    boundary into a whole quantum (1/7 or 1/15 of the block's amax), so the
+    relative-RMS bar for those two modes is 5e-3; f32 pages keep 1e-3."""
+    enc, ref_enc, results = _run(ctx, tiny, n_streams=2, n_steps=5, self_kv=self_kv)
+    tol = 1e-3 if self_kv == "f32" else 5e-3
+    for got, ref in results:
+        assert np.max(np.abs(got - ref)) <= 1e-2
+        assert _rel_rms(got, ref) <= tol
+        assert np.array_equal(np.argmax(got, axis=-1), np.argmax(ref, axis=-1)) or self_kv != "f32"
 
 
 def test_tiny_whisper_f16_cross_store(ctx, tiny):

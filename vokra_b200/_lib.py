@@ -59,9 +59,12 @@ class KvPoolDesc(C.Structure):
     ]
 
 
+SELF_KV_Q8_0, SELF_KV_F32, SELF_KV_Q4_0, SELF_KV_Q5_0 = 0, 1, 2, 3
+
+
 class SessionOptions(C.Structure):
     _fields_ = [("max_streams", C.c_int32), ("max_step_tokens", C.c_int32), ("max_clips", C.c_int32),
-                ("cross_kv_q8", C.c_int32), ("kv_page_tokens", C.c_int32)]
+                ("cross_kv_q8", C.c_int32), ("kv_page_tokens", C.c_int32), ("self_kv_mode", C.c_int32)]
 
 
 class WhisperDims(C.Structure):

@@ -29,20 +29,44 @@ __device__ __forceinline__ void i8x16_to_f32(uint4 q, float (&f)[16]) {
     }
 }
 
-// Raw bytes of 16 channels of one K or V row, kept in registers until use.
+// Raw bytes of 16 channels of one K or V row, kept in registers until use
+// (the fields a policy does not load are dropped by the compiler).
 struct RawRow {
-    uint4 a, b;   // int8: a only; f16: a then b
-    float s;      // block scale (1 for f16)
+    uint4 a, b, c, e;  // int8: a; Q4_0: a.xy; Q5_0: a.xy + 16 high bits in a.z; f16: a, b; f32: a, b, c, e
+    float s;           // block scale (1 for f16 / f32)
 };
 
+// 16 channels of a Q4_0 / Q5_0 KV block (kv_quant/q4_0.rs:73, q5_0.rs:84):
+// channel 2i / 2i+1 in the low / high nibble of byte i, biased by 8 (Q4_0) or,
+// with its 5th bit from qh, by 16 (Q5_0). Exact small integers.
+template <bool Q5>
+__device__ __forceinline__ void nib16_to_f32(const uint4& a, float (&f)[16]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t byte = ((i < 4 ? a.x : a.y) >> (8 * (i & 3))) & 0xffu;
+        uint32_t lo = byte & 0xfu, hi = byte >> 4;
+        if (Q5) {
+            lo |= ((a.z >> (2 * i)) & 1u) << 4;
+            hi |= ((a.z >> (2 * i + 1)) & 1u) << 4;
+        }
+        f[2 * i] = (float)((int)lo - (Q5 ? 16 : 8));
+        f[2 * i + 1] = (float)((int)hi - (Q5 ? 16 : 8));
+    }
+}
+
 // ---- fetch policies: value of 16 channels [c0, c0+16) of key j ------------
-struct FetchPagedQ8 {
-    const int8_t* kq;
+// Paged K/V of any pool mode (vkb_kv_quant): quant plane rows of qrow bytes,
+// Q5_0 high-bit rows of hrow bytes, f16 scale rows of W/32.
+template <int MODE>
+struct FetchPaged {
+    const uint8_t* kq;
     const __half* kd;
-    const int8_t* vq;
+    const uint8_t* kh;
+    const uint8_t* vq;
     const __half* vd;
+    const uint8_t* vh;
     const int32_t* table;
-    int W;
+    int W, qrow, hrow;
     int layout;      // 0 reference, 1 sequence
     int table_base;  // reference: layer*ppl ; sequence: seq*ppseq
     int bs;
@@ -54,11 +78,44 @@ struct FetchPagedQ8 {
         return arena_row0 + ((int64_t)pid * bs + (j % bs)) * n_sc + slot;
     }
     __device__ __forceinline__ void load_raw(int64_t rw, int c0, bool is_v, RawRow& r) const {
-        r.a = __ldg(reinterpret_cast<const uint4*>((is_v ? vq : kq) + rw * W + c0));
+        const uint8_t* q = (is_v ? vq : kq) + rw * qrow;
+        if constexpr (MODE == VKB_KV_Q8_0) {
+            r.a = __ldg(reinterpret_cast<const uint4*>(q + c0));
+        } else if constexpr (MODE == VKB_KV_FP32) {
+            const uint4* p = reinterpret_cast<const uint4*>(q + 4 * c0);
+            r.a = __ldg(p);
+            r.b = __ldg(p + 1);
+            r.c = __ldg(p + 2);
+            r.e = __ldg(p + 3);
+            r.s = 1.0f;
+            return;
+        } else {
+            const uint2 t = __ldg(reinterpret_cast<const uint2*>(q + c0 / 2));
+            r.a.x = t.x;
+            r.a.y = t.y;
+            if constexpr (MODE == VKB_KV_Q5_0)
+                r.a.z = __ldg(reinterpret_cast<const uint16_t*>((is_v ? vh : kh) + rw * hrow + c0 / 8));
+        }
         r.s = __half2float(__ldg((is_v ? vd : kd) + rw * (W / 32) + c0 / 32));
     }
-    static __device__ __forceinline__ void convert(const RawRow& r, float (&f)[16]) { i8x16_to_f32(r.a, f); }
+    static __device__ __forceinline__ void convert(const RawRow& r, float (&f)[16]) {
+        if constexpr (MODE == VKB_KV_Q8_0) {
+            i8x16_to_f32(r.a, f);
+        } else if constexpr (MODE == VKB_KV_FP32) {
+            const uint4 w[4] = {r.a, r.b, r.c, r.e};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                f[4 * i] = __uint_as_float(w[i].x);
+                f[4 * i + 1] = __uint_as_float(w[i].y);
+                f[4 * i + 2] = __uint_as_float(w[i].z);
+                f[4 * i + 3] = __uint_as_float(w[i].w);
+            }
+        } else {
+            nib16_to_f32<MODE == VKB_KV_Q5_0>(r.a, f);
+        }
+    }
 };
+using FetchPagedQ8 = FetchPaged<VKB_KV_Q8_0>;
 
 struct FetchDenseQ8 {
     const int8_t* kq;
@@ -164,7 +221,7 @@ __device__ __forceinline__ void attn_body(const F& fetch, const float* __restric
                     fetch.load_raw(rw, c0, true, vr[u]);
                 } else {
                     kr[u].a = make_uint4(0, 0, 0, 0);
-                    kr[u].b = kr[u].a;
+                    kr[u].b = kr[u].c = kr[u].e = kr[u].a;
                     kr[u].s = 0.0f;
                     vr[u] = kr[u];
                 }

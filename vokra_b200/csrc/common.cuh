@@ -161,6 +161,29 @@ __device__ __forceinline__ void pdl_entry() {
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
+// Exact half -> single on the host (every f16 value is an f32 value).
+inline float f16_bits_to_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h >> 15) << 31, ex = (h >> 10) & 0x1f, mant = h & 0x3ff;
+    uint32_t bits;
+    if (ex == 0) {
+        if (mant == 0) {
+            bits = sign;
+        } else {  // subnormal: normalise
+            int e = -1;
+            uint32_t m = mant;
+            do { m <<= 1; ++e; } while (!(m & 0x400));
+            bits = sign | (uint32_t)(127 - 15 - e) << 23 | (m & 0x3ff) << 13;
+        }
+    } else if (ex == 31) {
+        bits = sign | 0x7f800000u | mant << 13;
+    } else {
+        bits = sign | (ex + 112) << 23 | mant << 13;
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
 // IEEE single -> half, round to nearest even; restates the reference encoder
 // f32_to_f16_bits (crates/vokra-core/src/kv_quant/half.rs:80-155) so that the
 // stored scale bits match it exactly, including NaN canonicalisation.
@@ -283,6 +306,57 @@ __device__ __forceinline__ void q8_0_block_warp(float x, int lane, int8_t* q_out
     int8_t qv = isnan(c) ? (int8_t)0 : (int8_t)(int)roundf(c);
     q_out[lane] = qv;
     if (lane == 0) *reinterpret_cast<uint16_t*>(d_out) = f32_to_f16_bits(d);
+}
+
+// The BlockQ4_0::pack / BlockQ5_0::pack arithmetic (kv_quant/q4_0.rs:44-66 with
+// quantize_nibble :100, q5_0.rs:47-80 with quantize_5bit_biased :116), one
+// warp per 32-element block, lane = element: d = amax/7 (/15), scaled = x/d
+// clamped to [-8, 7] ([-16, 15]), rounded half away from zero, NaN to 0,
+// biased by 8 (16). Channel 2i / 2i+1 go to the low / high nibble of byte i;
+// Q5_0's 5th bits form the little-endian 32-bit qh word (bit i = channel i).
+template <int LEVELS_POS, int BIAS>
+__device__ __forceinline__ uint32_t kv_nibble_quant(float x, int lane, float& d_out) {
+    float amax = fmaxf(0.0f, warp_max(fabsf(x)));
+    const float d = amax == 0.0f ? 0.0f : amax / (float)LEVELS_POS;
+    const float inv = d == 0.0f ? 0.0f : 1.0f / d;
+    const float sc = x * inv;
+    const float c = sc < -(float)BIAS ? -(float)BIAS : (sc > (float)LEVELS_POS ? (float)LEVELS_POS : sc);
+    const int r = isnan(c) ? 0 : (int)roundf(c);
+    const int b = r + BIAS;
+    d_out = d;
+    return (uint32_t)(b < 0 ? 0 : (b > 2 * BIAS - 1 ? 2 * BIAS - 1 : b));
+}
+
+__device__ __forceinline__ void q4_0_block_warp(float x, int lane, uint8_t* qs_out, __half* d_out) {
+    float d;
+    const uint32_t q = kv_nibble_quant<7, 8>(x, lane, d);
+    const uint32_t odd = __shfl_down_sync(0xffffffffu, q, 1);
+    if (!(lane & 1)) qs_out[lane >> 1] = (uint8_t)((q & 0xfu) | ((odd & 0xfu) << 4));
+    if (lane == 0) *reinterpret_cast<uint16_t*>(d_out) = f32_to_f16_bits(d);
+}
+
+__device__ __forceinline__ void q5_0_block_warp(float x, int lane, uint8_t* qs_out, uint8_t* qh_out, __half* d_out) {
+    float d;
+    const uint32_t q = kv_nibble_quant<15, 16>(x, lane, d);
+    const uint32_t odd = __shfl_down_sync(0xffffffffu, q, 1);
+    const uint32_t hi = __ballot_sync(0xffffffffu, (q >> 4) & 1u);
+    if (!(lane & 1)) qs_out[lane >> 1] = (uint8_t)((q & 0xfu) | ((odd & 0xfu) << 4));
+    if (lane == 0) {
+        *reinterpret_cast<uint32_t*>(qh_out) = hi;
+        *reinterpret_cast<uint16_t*>(d_out) = f32_to_f16_bits(d);
+    }
+}
+
+// Calls f(std::integral_constant<int, MODE>{}) for a KV mode (vkb_kv_quant).
+template <class F>
+inline void with_kv_mode(int mode, F&& f) {
+    switch (mode) {
+        case VKB_KV_FP32: f(std::integral_constant<int, VKB_KV_FP32>{}); break;
+        case VKB_KV_Q4_0: f(std::integral_constant<int, VKB_KV_Q4_0>{}); break;
+        case VKB_KV_Q5_0: f(std::integral_constant<int, VKB_KV_Q5_0>{}); break;
+        case VKB_KV_Q8_0: f(std::integral_constant<int, VKB_KV_Q8_0>{}); break;
+        default: fail(VKB_ERROR_INVALID_ARGUMENT, "kv: unknown mode " + std::to_string(mode));
+    }
 }
 
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }

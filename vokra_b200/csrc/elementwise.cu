@@ -249,12 +249,9 @@ void run_embed(vkb_context* ctx, const vkb_weight* w, const int32_t* tokens, con
     unsigned grid = (unsigned)((n + 127) / 128);
     const uint8_t* qs = w->qs.as<uint8_t>();
     const uint8_t* sc = w->sc.as<uint8_t>();
-    switch (w->fmt) {
-        case W_Q4_0: launch_pdl(ctx, embed_kernel<W_Q4_0>, grid, 128, 0, qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
-        case W_Q8_0: launch_pdl(ctx, embed_kernel<W_Q8_0>, grid, 128, 0, qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
-        case W_Q4_K: launch_pdl(ctx, embed_kernel<W_Q4_K>, grid, 128, 0, qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
-        default: launch_pdl(ctx, embed_kernel<W_F16>, grid, 128, 0, qs, sc, w->k, tokens, positions, n_tok, pos, h); break;
-    }
+    with_fmt(w->fmt, [&](auto F) {
+        launch_pdl(ctx, embed_kernel<decltype(F)::value>, grid, 128, 0, qs, sc, w->k, tokens, positions, n_tok, pos, h);
+    });
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }

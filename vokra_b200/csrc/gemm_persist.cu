@@ -377,12 +377,7 @@ static void launch_persist(vkb_context* ctx, const vkb_weight* w, int64_t m, con
 }
 
 void run_tc_persistent(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e, int* err) {
-    switch (w->fmt) {
-        case W_Q4_0: launch_persist<W_Q4_0>(ctx, w, m, a16, e, err); break;
-        case W_Q8_0: launch_persist<W_Q8_0>(ctx, w, m, a16, e, err); break;
-        case W_Q4_K: launch_persist<W_Q4_K>(ctx, w, m, a16, e, err); break;
-        default: launch_persist<W_F16>(ctx, w, m, a16, e, err); break;
-    }
+    with_fmt(w->fmt, [&](auto F) { launch_persist<decltype(F)::value>(ctx, w, m, a16, e, err); });
 }
 
 }  // namespace vkb

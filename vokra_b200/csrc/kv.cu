@@ -9,8 +9,10 @@
 // and rebuilds the free list, release_layer zeroes and frees one layer.
 //
 // Device page storage keeps the quants and the f16 scales of each token row in
-// two planes ("split planes"): row r of an arena has W int8 quants at
-// q + r*W and W/32 scales at d + r*(W/32). A row is one (token, stream) slot:
+// separate planes ("split planes"): row r of an arena has qrow quant bytes at
+// q + r*qrow (Q8_0: W int8; Q4_0 and Q5_0: W/2 bytes of pair-packed low
+// nibbles; FP32: 4W bytes of values), for Q5_0 W/8 bytes of 5th bits at
+// h + r*(W/8), and W/32 f16 scales at d + r*(W/32). A row is one (token, stream) slot:
 // REFERENCE layout rows are ((page*bs + offset)*n_stream + stream); SEQUENCE
 // layout rows are (layer*n_pages + page)*bs + offset. vkb_kv_read_page
 // reassembles the reference's 34-byte on-wire blocks from the two planes.
@@ -27,11 +29,13 @@ struct vkb_kv_pool {
     vkb_context* ctx = nullptr;
     vkb_kv_pool_desc d{};
     int W = 0, row_blocks = 0, ppl = 0, ppseq = 0, rpp = 0, n_arena = 1;
+    int qrow = 0, hrow = 0;          // bytes per row of the quant plane and of the Q5_0 high-bit plane
     int64_t n_pages = 0, table_len = 0;
     std::vector<int32_t> table;      // host mirror (-1 = empty)
     std::vector<int32_t> free_list;  // LIFO
     // device
-    DevBuf kq, kd, vq, vd;           // arena planes
+    DevBuf kq, kd, vq, vd;           // arena planes: quants (or f32 values), f16 scales
+    DevBuf kh, vh;                   // Q5_0 5th-bit planes
     DevBuf table_dev;
     DevBuf rows_dev;                 // int64 [n_layer][max_step]: row of each step token per layer
     DevBuf groups_dev;               // AttnGroup [max_groups]
@@ -48,6 +52,11 @@ struct vkb_kv_pool {
     int n_tok = 0, n_groups = 0, maxq = 1, splits = 1, max_keys = 0;
     std::vector<int32_t> step_seq, step_pos;
     int64_t rows_in_arena() const { return n_pages * rpp; }
+    int srow_bytes() const { return d.mode == VKB_KV_FP32 ? 0 : row_blocks * 2; }
+    // on-wire bytes of one token row (the reference's block encoding; f32 values for FP32)
+    int wire_row_bytes() const {
+        return d.mode == VKB_KV_FP32 ? 4 * W : row_blocks * (d.mode == VKB_KV_Q8_0 ? 34 : d.mode == VKB_KV_Q5_0 ? 22 : 18);
+    }
 };
 
 namespace vkb {
@@ -58,9 +67,10 @@ namespace vkb {
 // NaN rules (max ignores NaN, clamp keeps NaN, NaN casts to 0).
 // ---------------------------------------------------------------------------
 
+template <int MODE>
 __global__ void kv_append_kernel(const float* __restrict__ k, const float* __restrict__ v, int64_t ld,
-                                 const int64_t* __restrict__ rows, int n_tok, int W, int8_t* kq, __half* kd,
-                                 int8_t* vq, __half* vd) {
+                                 const int64_t* __restrict__ rows, int n_tok, int W, int qrow, int hrow, uint8_t* kq,
+                                 __half* kd, uint8_t* kh, uint8_t* vq, __half* vd, uint8_t* vh) {
     pdl_entry();
     const int nb = W / 32;
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -69,11 +79,19 @@ __global__ void kv_append_kernel(const float* __restrict__ k, const float* __res
     const int is_v = (int)(gw / ((int64_t)n_tok * nb));
     const int64_t rem = gw % ((int64_t)n_tok * nb);
     const int tok = (int)(rem / nb), b = (int)(rem % nb);
-    const float* src = (is_v ? v : k) + (int64_t)tok * ld + b * 32;
+    const float x = ((is_v ? v : k) + (int64_t)tok * ld + b * 32)[lane];
     const int64_t row = rows[tok];
-    int8_t* q = (is_v ? vq : kq) + row * W + b * 32;
+    uint8_t* q = (is_v ? vq : kq) + row * qrow;
     __half* d = (is_v ? vd : kd) + row * nb + b;
-    q8_0_block_warp(src[lane], lane, q, d);
+    if constexpr (MODE == VKB_KV_Q8_0) {
+        q8_0_block_warp(x, lane, reinterpret_cast<int8_t*>(q) + b * 32, d);
+    } else if constexpr (MODE == VKB_KV_Q4_0) {
+        q4_0_block_warp(x, lane, q + b * 16, d);
+    } else if constexpr (MODE == VKB_KV_Q5_0) {
+        q5_0_block_warp(x, lane, q + b * 16, (is_v ? vh : kh) + row * hrow + b * 4, d);
+    } else {
+        reinterpret_cast<float*>(q)[b * 32 + lane] = x;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -266,8 +284,8 @@ __global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t ld, in
 // ---------------------------------------------------------------------------
 // Key splits are fixed per launch (n_splits); each CTA derives its key range
 // from its group's key count, so the launch shape does not depend on the step.
-template <int MAXQ>
-__global__ void __launch_bounds__(ATTN_MAX_THREADS, MAXQ > 1 ? 1 : 2) paged_attn_kernel(FetchPagedQ8 f, const float* __restrict__ q, int64_t q_ld, const AttnGroup* __restrict__ groups,
+template <class FP, int MAXQ>
+__global__ void __launch_bounds__(ATTN_MAX_THREADS, MAXQ > 1 ? 1 : 2) paged_attn_kernel(FP f, const float* __restrict__ q, int64_t q_ld, const AttnGroup* __restrict__ groups,
                                   int n_head, int d_head, int n_splits, void* ctx_out,
                                   int out_fmt, float* ws, int per_seq_base, int ppseq, int64_t out_plane) {
     pdl_entry();
@@ -277,10 +295,10 @@ __global__ void __launch_bounds__(ATTN_MAX_THREADS, MAXQ > 1 ? 1 : 2) paged_attn
     const int kps = (n_keys + n_splits - 1) / n_splits;
     const int kb = min(n_keys, split * kps);
     const int ke = min(n_keys, kb + kps);
-    FetchPagedQ8 ff = f;
+    FP ff = f;
     if (per_seq_base) ff.table_base = g.seq * ppseq;
     else ff.slot = g.seq;
-    attn_body<FetchPagedQ8, MAXQ>(ff, q, q_ld, g, n_head, d_head, f.W, kb, ke, split, n_splits, ctx_out,
+    attn_body<FP, MAXQ>(ff, q, q_ld, g, n_head, d_head, f.W, kb, ke, split, n_splits, ctx_out,
                                   out_fmt, out_plane, ws);
 }
 
@@ -431,10 +449,13 @@ void run_quantize_rows(vkb_context* ctx, const float* x, int64_t ld, int64_t n_r
 vkb_kv_pool* kv_pool_create(vkb_context* ctx, const vkb_kv_pool_desc* desc) {
     if (!ctx || !desc) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: null argument");
     const vkb_kv_pool_desc& d = *desc;
-    if (d.mode == VKB_KV_FP32)
+    // The reference's QuantizedPagedKvCache takes the quantized modes only;
+    // FP32 pages exist here in the SEQUENCE layout, as the dense f32 cache the
+    // reference's Whisper decoder keeps (whisper/decoder.rs:183-200).
+    if (d.mode == VKB_KV_FP32 && d.layout != VKB_KV_LAYOUT_SEQUENCE)
         fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: mode=Fp32 — the paged quant cache needs a quantized mode");
-    if (d.mode != VKB_KV_Q8_0)
-        fail(VKB_ERROR_UNSUPPORTED_OP, "kv_pool_create: the device kernels implement Q8_0 pages only");
+    if (d.mode != VKB_KV_FP32 && d.mode != VKB_KV_Q4_0 && d.mode != VKB_KV_Q5_0 && d.mode != VKB_KV_Q8_0)
+        fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: unknown mode " + std::to_string(d.mode));
     if (d.n_layer <= 0 || d.n_head <= 0 || d.d_head <= 0 || d.n_stream <= 0 || d.n_codebook <= 0 || d.max_time <= 0)
         fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: every axis must be > 0");
     if ((d.n_head * d.d_head) % 32) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_pool_create: n_head*d_head not a multiple of 32");
@@ -450,6 +471,8 @@ vkb_kv_pool* kv_pool_create(vkb_context* ctx, const vkb_kv_pool_desc* desc) {
         p->d = d;
         p->W = d.n_head * d.d_head;
         p->row_blocks = p->W / 32;
+        p->qrow = d.mode == VKB_KV_Q8_0 ? p->W : d.mode == VKB_KV_FP32 ? 4 * p->W : p->W / 2;
+        p->hrow = d.mode == VKB_KV_Q5_0 ? p->W / 8 : 0;
         if (d.layout == VKB_KV_LAYOUT_REFERENCE) {
             p->ppl = (d.max_time + d.page_tokens - 1) / d.page_tokens;
             p->n_pages = (int64_t)p->ppl * d.n_layer;  // paged_quant.rs:300 total_pages
@@ -469,16 +492,14 @@ vkb_kv_pool* kv_pool_create(vkb_context* ctx, const vkb_kv_pool_desc* desc) {
         for (int64_t i = p->n_pages - 1; i >= 0; --i) p->free_list.push_back((int32_t)i);
         const int64_t rows = (int64_t)p->n_arena * p->n_pages * p->rpp;
         VKB_CUDA(cudaSetDevice(ctx->device));
-        p->kq.alloc((size_t)rows * p->W);
-        p->vq.alloc((size_t)rows * p->W);
-        p->kd.alloc((size_t)rows * p->row_blocks * 2);
-        p->vd.alloc((size_t)rows * p->row_blocks * 2);
-        VKB_CUDA(cudaMemsetAsync(p->kq.p, 0, p->kq.n, ctx->stream));
-        VKB_CUDA(cudaMemsetAsync(p->vq.p, 0, p->vq.n, ctx->stream));
-        VKB_CUDA(cudaMemsetAsync(p->kd.p, 0, p->kd.n, ctx->stream));
-        VKB_CUDA(cudaMemsetAsync(p->vd.p, 0, p->vd.n, ctx->stream));
+        const size_t sbytes = d.mode == VKB_KV_FP32 ? 0 : (size_t)p->row_blocks * 2;
+        for (DevBuf* b : {&p->kq, &p->vq}) b->alloc((size_t)rows * p->qrow);
+        for (DevBuf* b : {&p->kd, &p->vd}) b->alloc((size_t)rows * sbytes);
+        for (DevBuf* b : {&p->kh, &p->vh}) b->alloc((size_t)rows * p->hrow);
+        for (DevBuf* b : {&p->kq, &p->vq, &p->kd, &p->vd, &p->kh, &p->vh})
+            if (b->n) VKB_CUDA(cudaMemsetAsync(b->p, 0, b->n, ctx->stream));
         p->table_dev.alloc((size_t)p->table_len * 4);
-        p->max_step = std::max(64, d.n_stream * 8);
+        p->max_step = std::max(2048, d.n_stream * 8);  // tokens per step (prefills)
         p->rows_dev.alloc((size_t)d.n_layer * p->max_step * 8);
         p->groups_dev.alloc((size_t)p->max_step * sizeof(AttnGroup));
         // Partials: up to 4096 CTAs x 4 queries of (W + 2H) floats.
@@ -635,8 +656,11 @@ void kv_append_ex(vkb_kv_pool* p, int layer, const float* k, const float* v, int
     }
     const int64_t warps = (int64_t)p->n_tok * p->row_blocks * 2;
     const int64_t* rows = p->rows_dev.as<int64_t>() + (size_t)layer * p->n_tok;
-    launch_pdl(p->ctx, kv_append_kernel, (unsigned)((warps * 32 + 255) / 256), 256, 0, 
-        k, v, ld, rows, p->n_tok, p->W, p->kq.as<int8_t>(), p->kd.as<__half>(), p->vq.as<int8_t>(), p->vd.as<__half>());
+    with_kv_mode(p->d.mode, [&](auto M) {
+        launch_pdl(p->ctx, kv_append_kernel<decltype(M)::value>, (unsigned)((warps * 32 + 255) / 256), 256, 0, k, v,
+                   ld, rows, p->n_tok, p->W, p->qrow, p->hrow, p->kq.as<uint8_t>(), p->kd.as<__half>(),
+                   p->kh.as<uint8_t>(), p->vq.as<uint8_t>(), p->vd.as<__half>(), p->vh.as<uint8_t>());
+    });
     VKB_CUDA(cudaGetLastError());
     p->ctx->count();
 }
@@ -647,8 +671,8 @@ void kv_append_ex(vkb_kv_pool* p, int layer, const float* k, const float* v, int
 bool kv_decode_fused(const vkb_kv_pool* p) {
     static const bool off = std::getenv("VKB_DECODE_ATTN_SPLIT") != nullptr;
     const auto& d = p->d;
-    return !off && p->n_tok > 0 && d.layout == VKB_KV_LAYOUT_SEQUENCE && p->maxq == 1 && p->n_groups == p->n_tok &&
-           d.d_head == 64 && d.n_head % 4 == 0;
+    return !off && p->n_tok > 0 && d.mode == VKB_KV_Q8_0 && d.layout == VKB_KV_LAYOUT_SEQUENCE && p->maxq == 1 &&
+           p->n_groups == p->n_tok && d.d_head == 64 && d.n_head % 4 == 0;
 }
 
 // Append + attention of one decode step for one layer: the fused kernel when
@@ -690,45 +714,52 @@ void kv_attention_ex(vkb_kv_pool* p, int layer, const float* q, int64_t q_ld, vo
     const auto& d = p->d;
     const int W = p->W;
     const int R = attn_rowgroups(W, p->maxq);
-    FetchPagedQ8 f;
-    f.kq = p->kq.as<int8_t>();
-    f.kd = p->kd.as<__half>();
-    f.vq = p->vq.as<int8_t>();
-    f.vd = p->vd.as<__half>();
-    f.table = p->table_dev.as<int32_t>();
-    f.W = W;
-    f.layout = d.layout;
-    f.bs = d.page_tokens;
-    int per_seq_base;
-    if (d.layout == VKB_KV_LAYOUT_REFERENCE) {
-        f.table_base = layer * p->ppl;
-        f.n_sc = d.n_stream;
-        f.slot = 0;
-        f.arena_row0 = 0;
-        per_seq_base = 0;
-    } else {
-        f.table_base = 0;
-        f.n_sc = 1;
-        f.slot = 0;
-        f.arena_row0 = (int64_t)layer * p->n_pages * p->rpp;
-        per_seq_base = 1;
-    }
-    dim3 grid((unsigned)p->n_groups, (unsigned)p->splits);
-    const int threads = R * (W / 16);
     float* ws = p->part_dev.as<float>();
+    with_kv_mode(d.mode, [&](auto M) {
+        using FP = FetchPaged<decltype(M)::value>;
+        FP f;
+        f.kq = p->kq.as<uint8_t>();
+        f.kd = p->kd.as<__half>();
+        f.kh = p->kh.as<uint8_t>();
+        f.vq = p->vq.as<uint8_t>();
+        f.vd = p->vd.as<__half>();
+        f.vh = p->vh.as<uint8_t>();
+        f.table = p->table_dev.as<int32_t>();
+        f.W = W;
+        f.qrow = p->qrow;
+        f.hrow = p->hrow;
+        f.layout = d.layout;
+        f.bs = d.page_tokens;
+        int per_seq_base;
+        if (d.layout == VKB_KV_LAYOUT_REFERENCE) {
+            f.table_base = layer * p->ppl;
+            f.n_sc = d.n_stream;
+            f.slot = 0;
+            f.arena_row0 = 0;
+            per_seq_base = 0;
+        } else {
+            f.table_base = 0;
+            f.n_sc = 1;
+            f.slot = 0;
+            f.arena_row0 = (int64_t)layer * p->n_pages * p->rpp;
+            per_seq_base = 1;
+        }
+        dim3 grid((unsigned)p->n_groups, (unsigned)p->splits);
+        const int threads = R * (W / 16);
+        const int64_t oplane = (int64_t)p->n_tok * W;
+        if (p->maxq == 1) {
+            smem_optin(paged_attn_kernel<FP, 1>, 200 * 1024);
+            launch_pdl(p->ctx, paged_attn_kernel<FP, 1>, grid, threads, attn_smem_bytes(R, 1, W, d.n_head), f, q, q_ld,
+                       p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->splits, out, out_dtype, ws, per_seq_base,
+                       p->ppseq, oplane);
+        } else {
+            smem_optin(paged_attn_kernel<FP, 4>, 200 * 1024);
+            launch_pdl(p->ctx, paged_attn_kernel<FP, 4>, grid, threads, attn_smem_bytes(R, 4, W, d.n_head), f, q, q_ld,
+                       p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->splits, out, out_dtype, ws, per_seq_base,
+                       p->ppseq, oplane);
+        }
+    });
     const int of16 = out_dtype;  // 0 f32, 1 f16, 2 f16 hi+lo planes
-    const int64_t oplane = (int64_t)p->n_tok * W;
-    if (p->maxq == 1) {
-        smem_optin(paged_attn_kernel<1>, 200 * 1024);
-        launch_pdl(p->ctx, paged_attn_kernel<1>, grid, threads, attn_smem_bytes(R, 1, W, d.n_head), 
-            f, q, q_ld, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->splits, out, of16, ws,
-            per_seq_base, p->ppseq, oplane);
-    } else {
-        smem_optin(paged_attn_kernel<4>, 200 * 1024);
-        launch_pdl(p->ctx, paged_attn_kernel<4>, grid, threads, attn_smem_bytes(R, 4, W, d.n_head), 
-            f, q, q_ld, p->groups_dev.as<AttnGroup>(), d.n_head, d.d_head, p->splits, out, of16, ws,
-            per_seq_base, p->ppseq, oplane);
-    }
     VKB_CUDA(cudaGetLastError());
     p->ctx->count();
     if (p->splits > 1) {
@@ -744,30 +775,26 @@ void kv_attention_ex(vkb_kv_pool* p, int layer, const float* q, int64_t q_ld, vo
 // Copies whole pages of every layer (SEQUENCE layout): pair i = (source page,
 // destination page); one CTA per (pair, layer), 16-byte moves of the K and V
 // quants and scales of the page's rows.
-__global__ void kv_copy_pages_kernel(const int2* __restrict__ pairs, int64_t n_pages, int bs, int W, int8_t* kq,
-                                     __half* kd, int8_t* vq, __half* vd) {
+__global__ void kv_copy_pages_kernel(const int2* __restrict__ pairs, int64_t n_pages, int bs, int qrow, int hrow,
+                                     int srow, uint8_t* kq, uint8_t* kd, uint8_t* kh, uint8_t* vq, uint8_t* vd,
+                                     uint8_t* vh) {
     pdl_entry();
     const int2 pr = pairs[blockIdx.x];
     const int64_t layer = blockIdx.y;
-    const int nb = W / 32;
     const int64_t src = (layer * n_pages + pr.x) * bs, dst = (layer * n_pages + pr.y) * bs;
-    const int qn = bs * W / 16, sn = bs * nb * 2 / 16;
-    const uint4* ks = reinterpret_cast<const uint4*>(kq + src * W);
-    const uint4* vs = reinterpret_cast<const uint4*>(vq + src * W);
-    uint4* kdst = reinterpret_cast<uint4*>(kq + dst * W);
-    uint4* vdst = reinterpret_cast<uint4*>(vq + dst * W);
-    for (int i = threadIdx.x; i < qn; i += blockDim.x) {
-        kdst[i] = ks[i];
-        vdst[i] = vs[i];
-    }
-    const uint4* kss = reinterpret_cast<const uint4*>(kd + src * nb);
-    const uint4* vss = reinterpret_cast<const uint4*>(vd + src * nb);
-    uint4* ksd = reinterpret_cast<uint4*>(kd + dst * nb);
-    uint4* vsd = reinterpret_cast<uint4*>(vd + dst * nb);
-    for (int i = threadIdx.x; i < sn; i += blockDim.x) {
-        ksd[i] = kss[i];
-        vsd[i] = vss[i];
-    }
+    auto move = [&](uint8_t* plane, int row_bytes) {
+        if (!row_bytes) return;
+        const uint4* from = reinterpret_cast<const uint4*>(plane + src * row_bytes);
+        uint4* to = reinterpret_cast<uint4*>(plane + dst * row_bytes);
+        const int n = bs * row_bytes / 16;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) to[i] = from[i];
+    };
+    move(kq, qrow);
+    move(vq, qrow);
+    move(kd, srow);
+    move(vd, srow);
+    move(kh, hrow);
+    move(vh, hrow);
 }
 
 // Makes stream dst a copy of the first n_pos positions of stream src (the
@@ -782,7 +809,8 @@ void kv_copy_stream(vkb_kv_pool* p, int src, int dst, int n_pos) {
         fail(VKB_ERROR_INVALID_ARGUMENT, "copy_stream: bad stream");
     if (n_pos < 0 || n_pos > d.max_time) fail(VKB_ERROR_INVALID_ARGUMENT, "copy_stream: bad position count");
     if (src == dst) return;
-    if (d.page_tokens * (p->W / 32) * 2 % 16) fail(VKB_ERROR_UNSUPPORTED_OP, "copy_stream: page scales not 16-byte sized");
+    if (d.page_tokens * p->srow_bytes() % 16 || d.page_tokens * p->hrow % 16 || d.page_tokens * p->qrow % 16)
+        fail(VKB_ERROR_UNSUPPORTED_OP, "copy_stream: page planes not 16-byte sized");
     const int n_pg = (n_pos + d.page_tokens - 1) / d.page_tokens;
     // Validate everything before touching dst, so a failed call leaves both
     // streams and the device page table as they were.
@@ -819,22 +847,26 @@ void kv_copy_stream(vkb_kv_pool* p, int src, int dst, int n_pos) {
     VKB_CUDA(cudaMemcpyAsync(p->pairs_dev.p, pairs.data(), pairs.size() * sizeof(int2), cudaMemcpyHostToDevice,
                              p->ctx->stream));
     dim3 grid((unsigned)pairs.size(), (unsigned)d.n_layer);
-    launch_pdl(p->ctx, kv_copy_pages_kernel, grid, 256, 0, p->pairs_dev.as<int2>(), p->n_pages, d.page_tokens, p->W,
-               p->kq.as<int8_t>(), p->kd.as<__half>(), p->vq.as<int8_t>(), p->vd.as<__half>());
+    launch_pdl(p->ctx, kv_copy_pages_kernel, grid, 256, 0, p->pairs_dev.as<int2>(), p->n_pages, d.page_tokens, p->qrow,
+               p->hrow, p->srow_bytes(), p->kq.as<uint8_t>(), p->kd.as<uint8_t>(), p->kh.as<uint8_t>(),
+               p->vq.as<uint8_t>(), p->vd.as<uint8_t>(), p->vh.as<uint8_t>());
     VKB_CUDA(cudaGetLastError());
     p->ctx->count();
 }
 
 static void zero_page(vkb_kv_pool* p, int32_t pid, int layer_for_seq) {
     cudaStream_t st = p->ctx->stream;
-    auto z = [&](int64_t row0, int64_t nrows) {
-        VKB_CUDA(cudaMemsetAsync(p->kq.as<int8_t>() + row0 * p->W, 0, (size_t)nrows * p->W, st));
-        VKB_CUDA(cudaMemsetAsync(p->vq.as<int8_t>() + row0 * p->W, 0, (size_t)nrows * p->W, st));
-        VKB_CUDA(cudaMemsetAsync(p->kd.as<uint8_t>() + row0 * p->row_blocks * 2, 0, (size_t)nrows * p->row_blocks * 2, st));
-        VKB_CUDA(cudaMemsetAsync(p->vd.as<uint8_t>() + row0 * p->row_blocks * 2, 0, (size_t)nrows * p->row_blocks * 2, st));
-    };
-    if (p->d.layout == VKB_KV_LAYOUT_REFERENCE) z((int64_t)pid * p->rpp, p->rpp);
-    else z(((int64_t)layer_for_seq * p->n_pages + pid) * p->rpp, p->rpp);
+    const int64_t row0 = p->d.layout == VKB_KV_LAYOUT_REFERENCE ? (int64_t)pid * p->rpp
+                                                                 : ((int64_t)layer_for_seq * p->n_pages + pid) * p->rpp;
+    const int64_t nrows = p->rpp;
+    for (int side = 0; side < 2; ++side) {
+        VKB_CUDA(cudaMemsetAsync((side ? p->vq : p->kq).as<uint8_t>() + row0 * p->qrow, 0, (size_t)nrows * p->qrow, st));
+        if (p->srow_bytes())
+            VKB_CUDA(cudaMemsetAsync((side ? p->vd : p->kd).as<uint8_t>() + row0 * p->srow_bytes(), 0,
+                                     (size_t)nrows * p->srow_bytes(), st));
+        if (p->hrow)
+            VKB_CUDA(cudaMemsetAsync((side ? p->vh : p->kh).as<uint8_t>() + row0 * p->hrow, 0, (size_t)nrows * p->hrow, st));
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1001,10 +1033,8 @@ vkb_status vkb_kv_reset(vkb_kv_pool* pool) {
         if (!pool) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_reset: null pool");
         std::fill(pool->table.begin(), pool->table.end(), -1);
         cudaStream_t st = pool->ctx->stream;
-        VKB_CUDA(cudaMemsetAsync(pool->kq.p, 0, pool->kq.n, st));
-        VKB_CUDA(cudaMemsetAsync(pool->vq.p, 0, pool->vq.n, st));
-        VKB_CUDA(cudaMemsetAsync(pool->kd.p, 0, pool->kd.n, st));
-        VKB_CUDA(cudaMemsetAsync(pool->vd.p, 0, pool->vd.n, st));
+        for (DevBuf* b : {&pool->kq, &pool->vq, &pool->kd, &pool->vd, &pool->kh, &pool->vh})
+            if (b->n) VKB_CUDA(cudaMemsetAsync(b->p, 0, b->n, st));
         pool->free_list.clear();
         for (int64_t i = pool->n_pages - 1; i >= 0; --i) pool->free_list.push_back((int32_t)i);
         pool->n_tok = 0;
@@ -1050,12 +1080,46 @@ int32_t vkb_kv_pages_in_use(const vkb_kv_pool* pool) {
 }
 
 size_t vkb_kv_page_bytes(const vkb_kv_pool* pool) {
-    return pool ? (size_t)pool->rpp * pool->row_blocks * 34 : 0;
+    return pool ? (size_t)pool->rpp * pool->wire_row_bytes() : 0;
 }
 
 size_t vkb_kv_on_wire_bytes(const vkb_kv_pool* pool) {
     return pool ? (size_t)pool->n_arena * pool->n_pages * 2 * vkb_kv_page_bytes(pool) : 0;
 }
+
+namespace vkb {
+// Host copy of rows [row0, row0 + n) of one side (K or V) in the reference's
+// on-wire block encoding: Q8_0 34-byte blocks (d, 32 quants), Q4_0 18-byte
+// blocks (d, 16 nibble bytes), Q5_0 22-byte blocks (d, 4 qh bytes, 16 nibble
+// bytes), FP32 the plain values.
+static std::vector<uint8_t> wire_rows(const vkb_kv_pool* p, int side, int64_t row0, int64_t n) {
+    const int nb = p->row_blocks, sb = p->srow_bytes();
+    std::vector<uint8_t> q((size_t)n * p->qrow), d((size_t)n * sb), h((size_t)n * p->hrow);
+    cudaStream_t st = p->ctx->stream;
+    VKB_CUDA(cudaMemcpyAsync(q.data(), (side ? p->vq : p->kq).as<uint8_t>() + row0 * p->qrow, q.size(),
+                             cudaMemcpyDeviceToHost, st));
+    if (sb) VKB_CUDA(cudaMemcpyAsync(d.data(), (side ? p->vd : p->kd).as<uint8_t>() + row0 * sb, d.size(),
+                                     cudaMemcpyDeviceToHost, st));
+    if (p->hrow) VKB_CUDA(cudaMemcpyAsync(h.data(), (side ? p->vh : p->kh).as<uint8_t>() + row0 * p->hrow, h.size(),
+                                          cudaMemcpyDeviceToHost, st));
+    VKB_CUDA(cudaStreamSynchronize(st));
+    if (p->d.mode == VKB_KV_FP32) return q;
+    const int bb = p->wire_row_bytes() / nb, qb = p->qrow / nb;
+    std::vector<uint8_t> o((size_t)n * nb * bb);
+    for (int64_t r = 0; r < n; ++r)
+        for (int b = 0; b < nb; ++b) {
+            uint8_t* blk = o.data() + ((size_t)r * nb + b) * bb;
+            memcpy(blk, &d[((size_t)r * nb + b) * 2], 2);
+            int off = 2;
+            if (p->hrow) {
+                memcpy(blk + 2, &h[(size_t)r * p->hrow + b * 4], 4);
+                off = 6;
+            }
+            memcpy(blk + off, &q[(size_t)r * p->qrow + b * qb], qb);
+        }
+    return o;
+}
+}  // namespace vkb
 
 vkb_status vkb_kv_read_page(const vkb_kv_pool* pool, int32_t layer, int32_t page, void* k_host, void* v_host) {
     return guard([&] {
@@ -1064,25 +1128,9 @@ vkb_status vkb_kv_read_page(const vkb_kv_pool* pool, int32_t layer, int32_t page
         int arena = pool->d.layout == VKB_KV_LAYOUT_SEQUENCE ? layer : 0;
         if (arena < 0 || arena >= pool->n_arena) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_read_page: layer out of range");
         const int64_t row0 = ((int64_t)arena * pool->n_pages + page) * pool->rpp;
-        const int W = pool->W, nb = pool->row_blocks;
-        std::vector<int8_t> q((size_t)pool->rpp * W);
-        std::vector<uint16_t> d((size_t)pool->rpp * nb);
-        cudaStream_t st = pool->ctx->stream;
         for (int side = 0; side < 2; ++side) {
-            const DevBuf& qb = side ? pool->vq : pool->kq;
-            const DevBuf& db = side ? pool->vd : pool->kd;
-            VKB_CUDA(cudaMemcpyAsync(q.data(), qb.as<int8_t>() + row0 * W, q.size(), cudaMemcpyDeviceToHost, st));
-            VKB_CUDA(cudaMemcpyAsync(d.data(), db.as<uint16_t>() + row0 * nb, d.size() * 2, cudaMemcpyDeviceToHost, st));
-            VKB_CUDA(cudaStreamSynchronize(st));
-            uint8_t* o = reinterpret_cast<uint8_t*>(side ? v_host : k_host);
-            for (int64_t r = 0; r < pool->rpp; ++r)
-                for (int b = 0; b < nb; ++b) {
-                    uint8_t* blk = o + ((size_t)r * nb + b) * 34;
-                    uint16_t h = d[(size_t)r * nb + b];
-                    blk[0] = (uint8_t)(h & 0xff);
-                    blk[1] = (uint8_t)(h >> 8);
-                    memcpy(blk + 2, &q[(size_t)r * W + b * 32], 32);
-                }
+            std::vector<uint8_t> o = wire_rows(pool, side, row0, pool->rpp);
+            memcpy(side ? v_host : k_host, o.data(), o.size());
         }
     });
 }
@@ -1097,21 +1145,30 @@ vkb_status vkb_kv_read_step(const vkb_kv_pool* pool, int32_t layer, int32_t t, i
         int64_t row = row_of(pool, layer, t, s);
         if (row < 0) fail(VKB_ERROR_OTHER, "kv_read_step: slot was never written");
         const int W = pool->W, nb = pool->row_blocks;
-        std::vector<int8_t> q(W);
-        std::vector<uint16_t> sc(nb);
-        cudaStream_t st = pool->ctx->stream;
         for (int side = 0; side < 2; ++side) {
-            const DevBuf& qb = side ? pool->vq : pool->kq;
-            const DevBuf& db = side ? pool->vd : pool->kd;
-            VKB_CUDA(cudaMemcpyAsync(q.data(), qb.as<int8_t>() + row * W, W, cudaMemcpyDeviceToHost, st));
-            VKB_CUDA(cudaMemcpyAsync(sc.data(), db.as<uint16_t>() + row * nb, nb * 2, cudaMemcpyDeviceToHost, st));
-            VKB_CUDA(cudaStreamSynchronize(st));
-            float* o = side ? v_host : k_host;
-            for (int i = 0; i < W; ++i) {
-                // BlockQ8_0::unpack (q8_0.rs:69): q as f32 times the f16 scale
-                uint16_t h = sc[i / 32];
-                __half hh = __ushort_as_half(h);
-                o[i] = (float)q[i] * __half2float(hh);
+            std::vector<uint8_t> o = wire_rows(pool, side, row, 1);
+            float* out = side ? v_host : k_host;
+            if (d.mode == VKB_KV_FP32) {
+                memcpy(out, o.data(), (size_t)W * 4);
+                continue;
+            }
+            // BlockQ8_0 / BlockQ4_0 / BlockQ5_0 ::unpack (q8_0.rs:69, q4_0.rs:73, q5_0.rs:84)
+            const int bb = pool->wire_row_bytes() / nb;
+            for (int b = 0; b < nb; ++b) {
+                const uint8_t* blk = o.data() + (size_t)b * bb;
+                const float sc = f16_bits_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+                for (int i = 0; i < 32; ++i) {
+                    int q;
+                    if (d.mode == VKB_KV_Q8_0) {
+                        q = (int8_t)blk[2 + i];
+                    } else if (d.mode == VKB_KV_Q4_0) {
+                        q = (int)((blk[2 + i / 2] >> (4 * (i & 1))) & 0xf) - 8;
+                    } else {
+                        const int lo = (blk[6 + i / 2] >> (4 * (i & 1))) & 0xf, hi = (blk[2 + i / 8] >> (i % 8)) & 1;
+                        q = (lo | (hi << 4)) - 16;
+                    }
+                    out[b * 32 + i] = (float)q * sc;
+                }
             }
         }
     });

@@ -48,27 +48,92 @@ static void repack_host(int fmt, const uint8_t* src, int64_t n, int64_t k, int64
                     memcpy(&qs[(size_t)((t * KC + sb * 4 + c) * TILE_N + r) * 32], blkp + 16 + 32 * c, 32);
             }
         }
+    } else if (fmt == W_Q5_K) {
+        // per 64-chunk c of a 176-byte block (q5_k.rs): qs nibbles, the qh bits
+        // 2c / 2c+1 as two masks, d, dmin and the chunk's decoded sub-scales
+        const int64_t KC = k / 64, KSB = k / 256;
+        qs.assign((size_t)T * KC * TILE_N * 48, 0);
+        for (int64_t row = 0; row < n; ++row) {
+            const int64_t t = row / TILE_N, r = row % TILE_N;
+            for (int64_t sb = 0; sb < KSB; ++sb) {
+                const uint8_t* b = src + (size_t)(row * KSB + sb) * 176;
+                for (int c = 0; c < 4; ++c) {
+                    uint8_t* dst = &qs[(size_t)((t * KC + sb * 4 + c) * TILE_N + r) * 48];
+                    memcpy(dst, b + 48 + 32 * c, 32);
+                    uint32_t mlo = 0, mhi = 0;
+                    for (int l = 0; l < 32; ++l) {
+                        mlo |= (uint32_t)((b[16 + l] >> (2 * c)) & 1) << l;
+                        mhi |= (uint32_t)((b[16 + l] >> (2 * c + 1)) & 1) << l;
+                    }
+                    memcpy(dst + 32, &mlo, 4);
+                    memcpy(dst + 36, &mhi, 4);
+                    memcpy(dst + 40, b, 4);  // d, dmin
+                    const uint8_t* sc6 = b + 4;
+                    for (int h = 0; h < 2; ++h) {
+                        const int j = 2 * c + h;  // get_scale_min_k4 (gguf/quant/mod.rs:140)
+                        uint8_t scv, mv;
+                        if (j < 4) { scv = sc6[j] & 63; mv = sc6[j + 4] & 63; }
+                        else { scv = (sc6[j + 4] & 0xf) | ((sc6[j - 4] >> 6) << 4); mv = (sc6[j + 4] >> 4) | ((sc6[j] >> 6) << 4); }
+                        dst[44 + 2 * h] = scv;
+                        dst[45 + 2 * h] = mv;
+                    }
+                }
+            }
+        }
+    } else if (fmt == W_Q6_K) {
+        // per 64-chunk c of a 210-byte block (q6_k.rs): chunk element e is
+        // n = 64c + e at (half, quarter, l) = (n/128, n%128/32, n%32)
+        const int64_t KC = k / 64, KSB = k / 256;
+        qs.assign((size_t)T * KC * TILE_N * 64, 0);
+        for (int64_t row = 0; row < n; ++row) {
+            const int64_t t = row / TILE_N, r = row % TILE_N;
+            for (int64_t sb = 0; sb < KSB; ++sb) {
+                const uint8_t* b = src + (size_t)(row * KSB + sb) * 210;
+                for (int c = 0; c < 4; ++c) {
+                    uint8_t* dst = &qs[(size_t)((t * KC + sb * 4 + c) * TILE_N + r) * 64];
+                    const int half = c / 2;
+                    for (int e = 0; e < 64; ++e) {
+                        const int o = 64 * (c % 2) + e, quarter = o / 32, l = o % 32;
+                        const uint8_t low4 = (b[64 * half + (quarter & 1) * 32 + l] >> (4 * (quarter >> 1))) & 0xf;
+                        const uint8_t hi2 = (b[128 + 32 * half + l] >> (2 * quarter)) & 3;
+                        dst[e % 32] |= (uint8_t)(low4 << (4 * (e / 32)));
+                        dst[32 + e / 4] |= (uint8_t)(hi2 << (2 * (e % 4)));
+                    }
+                    // sub-scales of the chunk's 16-element groups: is = l/16 + 2*quarter
+                    for (int j = 0; j < 4; ++j) {
+                        const int o = 64 * (c % 2) + 16 * j, quarter = o / 32, l = o % 32;
+                        dst[48 + j] = b[192 + 8 * half + l / 16 + 2 * quarter];
+                    }
+                    memcpy(dst + 52, b + 208, 2);
+                }
+            }
+        }
     } else {
+        // dense: F16 kept as one plane; F32 / BF16 as hi = f16(w), lo = f16(w - hi)
+        const bool two = fmt == W_F16X2;
+        const int rb = two ? 256 : 128;
         int64_t KC = k / 64;
-        qs.assign((size_t)T * KC * TILE_N * 128, 0);
+        qs.assign((size_t)T * KC * TILE_N * rb, 0);
         for (int64_t row = 0; row < n; ++row) {
             int64_t t = row / TILE_N, r = row % TILE_N;
             for (int64_t c = 0; c < KC; ++c) {
-                uint16_t* dst = reinterpret_cast<uint16_t*>(&qs[(size_t)((t * KC + c) * TILE_N + r) * 128]);
+                uint16_t* dst = reinterpret_cast<uint16_t*>(&qs[(size_t)((t * KC + c) * TILE_N + r) * rb]);
                 for (int e = 0; e < 64; ++e) {
                     int64_t idx = row * k + c * 64 + e;
                     if (tag == VKB_GGML_F16) {
                         memcpy(&dst[e], src + idx * 2, 2);
-                    } else if (tag == VKB_GGML_BF16) {
-                        uint32_t b = (uint32_t)(src[idx * 2] | (src[idx * 2 + 1] << 8)) << 16;
-                        float f;
-                        memcpy(&f, &b, 4);
-                        dst[e] = f32_to_f16_bits(f);
-                    } else {
-                        float f;
-                        memcpy(&f, src + idx * 4, 4);
-                        dst[e] = f32_to_f16_bits(f);
+                        continue;
                     }
+                    float f;
+                    if (tag == VKB_GGML_BF16) {
+                        uint32_t b = (uint32_t)(src[idx * 2] | (src[idx * 2 + 1] << 8)) << 16;
+                        memcpy(&f, &b, 4);
+                    } else {
+                        memcpy(&f, src + idx * 4, 4);
+                    }
+                    const uint16_t h = f32_to_f16_bits(f);
+                    dst[e] = h;
+                    if (two) dst[64 + e] = f32_to_f16_bits(f - f16_bits_to_f32(h));
                 }
             }
         }
@@ -83,6 +148,8 @@ static int64_t payload_bytes(uint32_t tag, int64_t n, int64_t k) {
         case VKB_GGML_Q4_0: return e / 32 * 18;
         case VKB_GGML_Q8_0: return e / 32 * 34;
         case VKB_GGML_Q4_K: return e / 256 * 144;
+        case VKB_GGML_Q5_K: return e / 256 * 176;
+        case VKB_GGML_Q6_K: return e / 256 * 210;
         default: return -1;
     }
 }
@@ -96,12 +163,16 @@ vkb_weight* upload_weight(vkb_context* ctx, uint32_t tag, int64_t n, int64_t k, 
         case VKB_GGML_Q4_0: fmt = W_Q4_0; break;
         case VKB_GGML_Q8_0: fmt = W_Q8_0; break;
         case VKB_GGML_Q4_K: fmt = W_Q4_K; break;
-        case VKB_GGML_F32: case VKB_GGML_F16: case VKB_GGML_BF16: fmt = W_F16; break;
+        case VKB_GGML_Q5_K: fmt = W_Q5_K; break;
+        case VKB_GGML_Q6_K: fmt = W_Q6_K; break;
+        case VKB_GGML_F16: fmt = W_F16; break;
+        case VKB_GGML_F32: case VKB_GGML_BF16: fmt = W_F16X2; break;
         default:
             fail(VKB_ERROR_UNSUPPORTED_OP, "weight_upload: ggml type " + std::to_string(tag) +
-                                               " has no B200 kernel (supported: Q4_0, Q8_0, Q4_K, F16, BF16, F32)");
+                                               " has no B200 kernel (supported: Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, F16, "
+                                               "BF16, F32)");
     }
-    int64_t kmul = fmt == W_Q4_K ? 256 : 64;
+    int64_t kmul = (fmt == W_Q4_K || fmt == W_Q5_K || fmt == W_Q6_K) ? 256 : 64;
     if (k % kmul)
         fail(VKB_ERROR_UNSUPPORTED_OP, "weight_upload: k=" + std::to_string(k) + " must be a multiple of " +
                                            std::to_string(kmul) + " for this dtype");
@@ -756,12 +827,7 @@ static void dispatch_tc(vkb_context* ctx, const vkb_weight* w, int64_t m, const 
 template <bool SPLIT>
 static void dispatch_fmt(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const Epi& e, float* ws,
                          const LinearPlan& p) {
-    switch (w->fmt) {
-        case W_Q4_0: dispatch_tc<W_Q4_0, SPLIT>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
-        case W_Q8_0: dispatch_tc<W_Q8_0, SPLIT>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
-        case W_Q4_K: dispatch_tc<W_Q4_K, SPLIT>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
-        default: dispatch_tc<W_F16, SPLIT>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); break;
-    }
+    with_fmt(w->fmt, [&](auto F) { dispatch_tc<decltype(F)::value, SPLIT>(ctx, w, m, a16, e, ws, p.bn, p.sps, p.splits, p.m_tiles); });
 }
 
 LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m, bool split) {
@@ -843,12 +909,7 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
     uint8_t* wsb = ctx->workspace.as<uint8_t>();
     float* ws = ws_override ? ws_override : reinterpret_cast<float*>(wsb + a16_bytes);
     if (!p.tc) {
-        switch (w->fmt) {
-            case W_Q4_0: launch_gemv<W_Q4_0>(ctx, w, m, a, a_dtype, e, ws, p.sps, p.splits); break;
-            case W_Q8_0: launch_gemv<W_Q8_0>(ctx, w, m, a, a_dtype, e, ws, p.sps, p.splits); break;
-            case W_Q4_K: launch_gemv<W_Q4_K>(ctx, w, m, a, a_dtype, e, ws, p.sps, p.splits); break;
-            default: launch_gemv<W_F16>(ctx, w, m, a, a_dtype, e, ws, p.sps, p.splits); break;
-        }
+        with_fmt(w->fmt, [&](auto F) { launch_gemv<decltype(F)::value>(ctx, w, m, a, a_dtype, e, ws, p.sps, p.splits); });
     } else {
         const __half* a16;
         if (a_dtype != VKB_DT_F32) {

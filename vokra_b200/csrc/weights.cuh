@@ -9,6 +9,17 @@
 //   Q4_K: qs  [t][K/64][128][32 B] (the 32 qs bytes of the 64-chunk),
 //         hdr [t][K/256][128][16 B] (f16 d, f16 dmin, 12 scale bytes, verbatim)
 //   F16 : val [t][K/64][128][128 B] (64 halves)
+//   Q5_K: qs  [t][K/64][128][48 B]: the chunk's 32 nibble bytes (element l in
+//         the low nibble of byte l, element 32+l in the high one), a 32-bit
+//         mask of the low half's 5th bits, one of the high half's, f16 d,
+//         f16 dmin, then sc, m of the low half and sc, m of the high half
+//         (the 6-bit values get_scale_min_k4 decodes, stored as bytes)
+//   Q6_K: qs  [t][K/64][128][64 B]: 32 nibble bytes (low 4 bits of element e
+//         in byte e%32, nibble e/32), 16 bytes of high 2-bit pairs (element e
+//         at bits 2*(e%4) of byte e/4), 4 int8 sub-scales (16 elements each),
+//         f16 d, 10 bytes of padding
+//   F16X2: val [t][K/64][128][256 B]: 64 halves hi = f16(w), then 64 halves
+//         lo = f16(w - hi) (dense f32 / bf16 weights at about fp32 precision)
 // so that one stage of one tile is a few contiguous, 16-byte-aligned runs
 // (one bulk copy each) and a warp's 32 rows read 512+ contiguous bytes.
 #pragma once
@@ -16,14 +27,30 @@
 
 namespace vkb {
 
-enum WFmt : int { W_Q4_0 = 0, W_Q8_0 = 1, W_Q4_K = 2, W_F16 = 3 };
+enum WFmt : int { W_Q4_0 = 0, W_Q8_0 = 1, W_Q4_K = 2, W_F16 = 3, W_Q5_K = 4, W_Q6_K = 5, W_F16X2 = 6 };
+
+// Calls f(std::integral_constant<int, FMT>{}) for the runtime format.
+template <class F>
+inline void with_fmt(int fmt, F&& f) {
+    switch (fmt) {
+        case W_Q4_0: f(std::integral_constant<int, W_Q4_0>{}); break;
+        case W_Q8_0: f(std::integral_constant<int, W_Q8_0>{}); break;
+        case W_Q4_K: f(std::integral_constant<int, W_Q4_K>{}); break;
+        case W_F16: f(std::integral_constant<int, W_F16>{}); break;
+        case W_Q5_K: f(std::integral_constant<int, W_Q5_K>{}); break;
+        case W_Q6_K: f(std::integral_constant<int, W_Q6_K>{}); break;
+        case W_F16X2: f(std::integral_constant<int, W_F16X2>{}); break;
+        default: fail(VKB_ERROR_OTHER, "weight: unknown device format " + std::to_string(fmt));
+    }
+}
 
 constexpr int TILE_N = 128;   // weight rows per tile (= tcgen05 MMA M)
 constexpr int STAGE_K = 64;   // K elements per pipeline stage
 
 // Bytes per row per stage in the quant plane and in the scale/header plane.
 __host__ __device__ constexpr int qs_bytes_per_row_stage(int fmt) {
-    return fmt == W_Q4_0 ? 32 : fmt == W_Q8_0 ? 64 : fmt == W_Q4_K ? 32 : 128;
+    return fmt == W_Q4_0 ? 32 : fmt == W_Q8_0 ? 64 : fmt == W_Q4_K ? 32 : fmt == W_Q5_K ? 48 : fmt == W_Q6_K ? 64
+           : fmt == W_F16X2 ? 256 : 128;
 }
 
 
@@ -60,7 +87,7 @@ __host__ __device__ __forceinline__ StagePtrs stage_ptrs(int fmt, const uint8_t*
         p.sc = sc + ((tile * KSB + stage / 4) * TILE_N) * 16;
     } else {
         int64_t KC = K / 64;
-        p.qs = qs + ((tile * KC + stage) * TILE_N) * 128;
+        p.qs = qs + ((tile * KC + stage) * TILE_N) * qs_bytes_per_row_stage(fmt);
         p.sc = nullptr;
     }
     return p;
@@ -128,8 +155,55 @@ __device__ __forceinline__ void dequant_row_stage(const uint8_t* qs, const uint8
 #pragma unroll
         for (int l = 0; l < 32; ++l) {
             uint32_t byte = (qq[l >> 2] >> (8 * (l & 3))) & 0xffu;
-            w[l] = d1 * (float)(byte & 0xfu) - mm1;
-            w[32 + l] = d2 * (float)(byte >> 4) - mm2;
+            // two roundings, as the reference (no contraction into an FMA)
+            w[l] = __fsub_rn(__fmul_rn(d1, (float)(byte & 0xfu)), mm1);
+            w[32 + l] = __fsub_rn(__fmul_rn(d2, (float)(byte >> 4)), mm2);
+        }
+    } else if constexpr (FMT == W_Q5_K) {
+        // q5_k.rs:36-80: y = (d*sc)*q - dmin*m, q = nibble + 16*(5th bit)
+        const uint4* p = reinterpret_cast<const uint4*>(qs + r * 48);
+        const uint4 q0 = p[0], q1 = p[1], t = p[2];
+        const float d = h2f((uint16_t)(t.z & 0xffffu)), dmin = h2f((uint16_t)(t.z >> 16));
+        const float d1 = __fmul_rn(d, (float)(t.w & 0xffu)), m1 = __fmul_rn(dmin, (float)((t.w >> 8) & 0xffu));
+        const float d2 = __fmul_rn(d, (float)((t.w >> 16) & 0xffu)), m2 = __fmul_rn(dmin, (float)(t.w >> 24));
+        const uint32_t qq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int l = 0; l < 32; ++l) {
+            const uint32_t byte = (qq[l >> 2] >> (8 * (l & 3))) & 0xffu;
+            const uint32_t lo = (byte & 0xfu) | (((t.x >> l) & 1u) << 4), hi = (byte >> 4) | (((t.y >> l) & 1u) << 4);
+            w[l] = __fsub_rn(__fmul_rn(d1, (float)lo), m1);
+            w[32 + l] = __fsub_rn(__fmul_rn(d2, (float)hi), m2);
+        }
+    } else if constexpr (FMT == W_Q6_K) {
+        // q6_k.rs:36-70: y = (d*sc)*(q - 32), q = low nibble | high pair << 4
+        const uint4* p = reinterpret_cast<const uint4*>(qs + r * 64);
+        const uint4 q0 = p[0], q1 = p[1], h = p[2], t = p[3];
+        const float d = h2f((uint16_t)(t.y & 0xffffu));
+        const uint32_t qq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const uint32_t hh[4] = {h.x, h.y, h.z, h.w};
+        float ds[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ds[j] = __fmul_rn(d, (float)(int8_t)((t.x >> (8 * j)) & 0xffu));
+#pragma unroll
+        for (int e = 0; e < 64; ++e) {
+            const uint32_t byte = (qq[(e & 31) >> 2] >> (8 * (e & 3))) & 0xffu;
+            const uint32_t low4 = e < 32 ? (byte & 0xfu) : (byte >> 4);
+            const uint32_t hi2 = (hh[e >> 4] >> (2 * (e & 15))) & 3u;
+            w[e] = __fmul_rn(ds[e >> 4], (float)((int)(low4 | (hi2 << 4)) - 32));
+        }
+    } else if constexpr (FMT == W_F16X2) {
+        const uint4* p = reinterpret_cast<const uint4*>(qs + r * 256);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint4 v = p[i], u = p[8 + i];
+            const uint32_t vv[4] = {v.x, v.y, v.z, v.w}, uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&vv[e]));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&uu[e]));
+                w[8 * i + 2 * e] = a.x + b.x;
+                w[8 * i + 2 * e + 1] = a.y + b.y;
+            }
         }
     } else {
         const uint4* p = reinterpret_cast<const uint4*>(qs + r * 128);
@@ -208,6 +282,17 @@ __device__ __forceinline__ void dequant_row_stage_h(const uint8_t* qs, const uin
                 q_pair_to_f16<SPLIT>(__byte_perm(u, 0x64u, 0x4140), bias, d2, hi[16 * j + 2 * wi], lo[16 * j + 2 * wi]);
                 q_pair_to_f16<SPLIT>(__byte_perm(u, 0x64u, 0x4342), bias, d2, hi[16 * j + 2 * wi + 1],
                                      lo[16 * j + 2 * wi + 1]);
+            }
+        }
+    } else if constexpr (FMT == W_F16X2) {
+        const uint4* p = reinterpret_cast<const uint4*>(qs + r * 256);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            uint4 v = p[i];
+            hi[4 * i] = v.x; hi[4 * i + 1] = v.y; hi[4 * i + 2] = v.z; hi[4 * i + 3] = v.w;
+            if (SPLIT) {
+                uint4 u = p[8 + i];
+                lo[4 * i] = u.x; lo[4 * i + 1] = u.y; lo[4 * i + 2] = u.z; lo[4 * i + 3] = u.w;
             }
         }
     } else if constexpr (FMT == W_F16) {

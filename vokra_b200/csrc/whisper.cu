@@ -287,7 +287,13 @@ vkb_session* create_session(vkb_whisper* m, const vkb_session_options* o) {
     kd.n_codebook = 1;
     kd.max_time = D.n_text_ctx;
     kd.page_tokens = o->kv_page_tokens ? o->kv_page_tokens : 16;
-    kd.mode = VKB_KV_Q8_0;
+    switch (o->self_kv_mode) {
+        case VKB_SELF_KV_Q8_0: kd.mode = VKB_KV_Q8_0; break;
+        case VKB_SELF_KV_F32: kd.mode = VKB_KV_FP32; break;
+        case VKB_SELF_KV_Q4_0: kd.mode = VKB_KV_Q4_0; break;
+        case VKB_SELF_KV_Q5_0: kd.mode = VKB_KV_Q5_0; break;
+        default: fail(VKB_ERROR_INVALID_ARGUMENT, "session_create: bad self_kv_mode");
+    }
     kd.layout = VKB_KV_LAYOUT_SEQUENCE;
     kd.n_pages = 0;
     s->pool = kv_pool_create(s->ctx, &kd);

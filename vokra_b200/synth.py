@@ -42,6 +42,12 @@ def payload_size(tag: int, n: int) -> int:
     if tag == Q4_K:
         assert n % 256 == 0
         return n // 256 * 144
+    if tag == Q5_K:
+        assert n % 256 == 0
+        return n // 256 * 176
+    if tag == Q6_K:
+        assert n % 256 == 0
+        return n // 256 * 210
     raise ValueError(f"unsupported tag {tag}")
 
 
@@ -118,6 +124,81 @@ def quantize_q4_k(x: np.ndarray) -> bytes:
     return out.tobytes()
 
 
+def _affine_quants(x: np.ndarray, max_q: int):
+    """Per 256-block affine map y = step*q + base with uniform sub-scales
+    (affine_quants, crates/vokra-convert/src/quantize.rs:99-121)."""
+    lo = x.min(axis=1)
+    hi = x.max(axis=1)
+    base = np.minimum(lo, np.float32(0))
+    step = ((hi - base).astype(np.float32) / np.float32(max_q)).astype(np.float32)
+    d = np.where(step > 0, step / np.float32(63), np.float32(0)).astype(np.float32)
+    dmin = np.where(base < 0, -base / np.float32(63), np.float32(0)).astype(np.float32)
+    safe = np.where(step > 0, step, np.float32(1)).astype(np.float32)
+    qf = round_half_away(((x - base[:, None]).astype(np.float32) / safe[:, None]).astype(np.float32))
+    q = np.where(step[:, None] > 0, np.clip(qf, 0, max_q), 0).astype(np.uint8)
+    return q, d, dmin
+
+
+def quantize_q5_k(x: np.ndarray) -> bytes:
+    """vokra-convert's Q5_K encoder (crates/vokra-convert/src/quantize.rs:144-170)."""
+    x = np.asarray(x, dtype=np.float32).reshape(-1, 256)
+    q, d, dmin = _affine_quants(x, 31)
+    out = np.empty((x.shape[0], 176), dtype=np.uint8)
+    out[:, 0:2] = f32_to_f16_bits(d).reshape(-1, 1).view(np.uint8)
+    out[:, 2:4] = f32_to_f16_bits(dmin).reshape(-1, 1).view(np.uint8)
+    out[:, 4:16] = 0xFF
+    qq = q.reshape(-1, 4, 64)
+    lo, hi = qq[:, :, :32], qq[:, :, 32:]
+    qh = np.zeros((x.shape[0], 32), np.uint8)
+    for k in range(4):
+        qh |= ((lo[:, k] >> 4) & 1) << (2 * k)
+        qh |= ((hi[:, k] >> 4) & 1) << (2 * k + 1)
+    out[:, 16:48] = qh
+    out[:, 48:] = ((lo & 0xF) | ((hi & 0xF) << 4)).reshape(-1, 128)
+    return out.tobytes()
+
+
+def quantize_q6_k(x: np.ndarray) -> bytes:
+    """vokra-convert's Q6_K encoder (crates/vokra-convert/src/quantize.rs:176-230):
+    one symmetric scale per block, uniform int8 sub-scales 31."""
+    x = np.asarray(x, dtype=np.float32).reshape(-1, 256)
+    amax = np.abs(x).max(axis=1)
+    step = (amax / np.float32(31)).astype(np.float32)
+    d = np.where(step > 0, step / np.float32(31), np.float32(0)).astype(np.float32)
+    safe = np.where(step > 0, step, np.float32(1)).astype(np.float32)
+    q = np.where(step[:, None] > 0, np.clip(round_half_away((x / safe[:, None]).astype(np.float32)), -32, 31), 0)
+    st = (q.astype(np.int32) + 32).astype(np.uint8).reshape(-1, 2, 4, 32)  # [block][half][quarter][l]
+    low4, hi2 = st & 0xF, (st >> 4) & 3
+    ql = np.concatenate([low4[:, :, 0] | (low4[:, :, 2] << 4), low4[:, :, 1] | (low4[:, :, 3] << 4)], axis=2)
+    qh = hi2[:, :, 0] | (hi2[:, :, 1] << 2) | (hi2[:, :, 2] << 4) | (hi2[:, :, 3] << 6)
+    out = np.empty((x.shape[0], 210), dtype=np.uint8)
+    out[:, 0:128] = ql.reshape(-1, 128)
+    out[:, 128:192] = qh.reshape(-1, 64)
+    out[:, 192:208] = 31
+    out[:, 208:210] = f32_to_f16_bits(d).reshape(-1, 1).view(np.uint8)
+    return out.tobytes()
+
+
+def random_kquant_blocks(tag: int, n: int, rng, scale: float = 0.02) -> bytes:
+    """Valid Q5_K / Q6_K blocks with every field random (sub-scales, mins, high
+    bits), the f16 super-scales sized so values come out around `scale`: covers
+    the decode paths the uniform-scale encoders above never reach."""
+    nb = n // 256
+    if tag == Q5_K:
+        out = rng.integers(0, 256, (nb, 176), dtype=np.uint8)
+        out[:, 0:2] = f32_to_f16_bits(rng.uniform(0.2, 1.0, nb).astype(np.float32) * np.float32(scale / 500)
+                                      ).reshape(-1, 1).view(np.uint8)
+        out[:, 2:4] = f32_to_f16_bits(rng.uniform(0.2, 1.0, nb).astype(np.float32) * np.float32(scale / 30)
+                                      ).reshape(-1, 1).view(np.uint8)
+        return out.tobytes()
+    if tag == Q6_K:
+        out = rng.integers(0, 256, (nb, 210), dtype=np.uint8)
+        out[:, 208:210] = f32_to_f16_bits(rng.uniform(0.2, 1.0, nb).astype(np.float32) * np.float32(scale / 1000)
+                                          ).reshape(-1, 1).view(np.uint8)
+        return out.tobytes()
+    raise ValueError(f"no random blocks for tag {tag}")
+
+
 def quantize(tag: int, x: np.ndarray) -> bytes:
     if tag == Q8_0:
         return quantize_q8_0(x)
@@ -125,6 +206,14 @@ def quantize(tag: int, x: np.ndarray) -> bytes:
         return quantize_q4_0(x)
     if tag == Q4_K:
         return quantize_q4_k(x)
+    if tag == Q5_K:
+        return quantize_q5_k(x)
+    if tag == Q6_K:
+        return quantize_q6_k(x)
+    if tag == BF16:
+        b = np.asarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+        rne = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)  # round to nearest even
+        return rne.tobytes()
     if tag == F32:
         return np.asarray(x, dtype=np.float32).tobytes()
     if tag == F16:

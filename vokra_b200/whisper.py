@@ -40,12 +40,15 @@ class WhisperModel:
 
 
 class Session:
-    """A batched decoding session (paged Q8_0 self-attention KV + cross-attention store)."""
+    """A batched decoding session (paged self-attention KV + cross-attention store)."""
 
     def __init__(self, model: WhisperModel, max_streams: int, max_step_tokens: int | None = None,
-                 max_clips: int = 0, cross_kv_q8: bool = True, kv_page_tokens: int = 16):
+                 max_clips: int = 0, cross_kv_q8: bool = True, kv_page_tokens: int = 16,
+                 self_kv: int = _lib.SELF_KV_Q8_0):
+        """self_kv: SELF_KV_Q8_0 (int8 pages, default), SELF_KV_F32 (the reference
+        decoder's dense f32 cache numerics), SELF_KV_Q4_0 or SELF_KV_Q5_0."""
         o = _lib.SessionOptions(max_streams, max_step_tokens or 4 * max_streams, max_clips, int(cross_kv_q8),
-                                kv_page_tokens)
+                                kv_page_tokens, self_kv)
         h = C.c_void_p()
         check(_L.vkb_session_create(model.h, C.byref(o), C.byref(h)))
         self.h, self.model, self.ctx = h, model, model.ctx
