@@ -381,6 +381,88 @@ def run_paged_decode(ctx, args):
                                    "frac": round(gbs / hbm, 4), "peak_kind": peak_kind}}), flush=True)
 
 
+SWEEP_SHAPES = [(1280, 1280), (1280, 5120), (5120, 1280), (1280, 51866)]  # (K, N)
+SWEEP_M = [1, 8, 64, 256, 1500, 12000]
+
+
+def run_sweep(args):
+    """the quantized Linear alone over K x N in SWEEP_SHAPES, Q8_0 / Q4_0 /
+    Q4_K weights (seeded N(0, 0.02), quantized by the GGUF quantizers), M tokens in SWEEP_M.
+
+    Timing: C copies of the weight (C x bytes > 300 MB, so no launch finds its weight in the
+    126 MB L2) are launched back to back through vkb_linear, the C launches recorded once as a
+    CUDA graph; the graph is replayed and timed with CUDA events, per launch = time / C. This
+    is the steady state a decode step sees (launch latencies overlap through programmatic
+    dependent launch). f32 activations for M <= 8, f16 hi+lo planes above (what the producing
+    kernels hand the tensor-core GEMM), f32 output. One JSON line per point with the achieved
+    HBM GB/s (algorithmic bytes: N*K*b_w + M*K*4 + M*N*4) and tensor TFLOP/s (2*M*N*K)."""
+    import ctypes as C
+    import torch
+    from vokra_b200 import _lib, ops, synth
+    ctx = ops.Context(0)
+    L = _lib.load()
+    hbm, bf16, _, peak_kind = _peaks()
+    fmts = {"q8_0": (synth.Q8_0, 34 / 32), "q4_0": (synth.Q4_0, 18 / 32), "q4_k": (synth.Q4_K, 144 / 256)}
+    only = set(args.sweep_formats.split(",")) if args.sweep_formats else set(fmts)
+    ms_list = [int(x) for x in args.sweep_m.split(",")] if args.sweep_m else SWEEP_M
+    for fname, (tag, bw) in fmts.items():
+        if fname not in only:
+            continue
+        for (K, N) in SWEEP_SHAPES:
+            if args.sweep_shapes and f"{K}x{N}" not in args.sweep_shapes.split(","):
+                continue
+            rng = np.random.default_rng(K * 7 + N)
+            wq = synth.quantize(tag, rng.standard_normal(N * K, dtype=np.float32) * np.float32(0.02))
+            copies = int(min(200, max(2, np.ceil(300e6 / (N * K * bw)))))
+            ws = [ops.Weight(ctx, tag, N, K, wq) for _ in range(copies)]
+            for M in ms_list:
+                if M <= 8:
+                    a = torch.randn((M, K), device="cuda")
+                    a_dt = _lib.DT_F32
+                else:
+                    a = (torch.randn((2 * M, K), device="cuda") * 0.5).half()
+                    a_dt = _lib.DT_F16X2
+                out = torch.empty((M, N), device="cuda")
+
+                def launch(w):
+                    _lib.check(L.vkb_linear(ctx.h, w.h, M, C.c_void_p(a.data_ptr()), a_dt, None,
+                                            C.c_void_p(out.data_ptr()), _lib.DT_F32, _lib.EPI_NONE, None,
+                                            C.c_float(1.0)))
+                for w in ws[:3]:
+                    launch(w)  # plans, workspace, attributes
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                side = torch.cuda.Stream()
+                with torch.cuda.stream(side):
+                    ctx.set_stream(side.cuda_stream)
+                    with torch.cuda.graph(g, stream=side):
+                        for w in ws:
+                            launch(w)
+                ctx.set_stream(torch.cuda.current_stream().cuda_stream or 1)
+                g.replay()
+                torch.cuda.synchronize()
+                times = []
+                for _ in range(3):
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    g.replay()
+                    e1.record()
+                    torch.cuda.synchronize()
+                    times.append(e0.elapsed_time(e1) / copies)
+                ms = float(np.median(times))
+                alg = N * K * bw + M * K * 4 + M * N * 4
+                gbs = alg / (ms / 1e3) / 1e9
+                tfl = 2.0 * M * N * K / (ms / 1e3) / 1e12
+                print(json.dumps({"sweep": "configs[1]", "format": fname, "K": K, "N": N, "M": M,
+                                  "us": round(ms * 1e3, 2), "algorithmic_bytes": int(alg), "GB_s": round(gbs, 1),
+                                  "hbm_frac": round(gbs / hbm, 4), "TFLOP_s": round(tfl, 2),
+                                  "tensor_frac": round(tfl / bf16, 4), "peak_kind": peak_kind,
+                                  "launches_per_graph": copies}), flush=True)
+                del g
+            for w in ws:
+                w.close()
+
+
 def throughput_utterances(n: int, rank: int, pool: int):
     """configs[4] workload of one rank: clip lengths U[5, 30] s (padded to 30 s by the
     frontend), decode lengths U[32, 224]; clip i reads row i % pool of the PCM pool."""
@@ -468,9 +550,13 @@ def main():
                          "1500), the decode cross-attention over the Q8_0 store (clips streams x 1500 keys), or "
                          "the encoder of a one-layer model with large-v3's dimensions on 8 clips, or the fused decode "
                          "self-attention over configs[2] (prints its own JSON line with the HBM roofline)")
-    ap.add_argument("--config", default="batch", choices=["batch", "throughput"],
+    ap.add_argument("--sweep-formats", default="", help="sweep: comma-separated subset of q8_0,q4_0,q4_k")
+    ap.add_argument("--sweep-m", default="", help="sweep: comma-separated M values")
+    ap.add_argument("--sweep-shapes", default="", help="sweep: comma-separated KxN shapes, e.g. 1280x51866")
+    ap.add_argument("--config", default="batch", choices=["batch", "throughput", "sweep"],
                     help="batch: configs[3] (the default bench line); throughput: configs[4], continuous batching "
-                         "of --utterances utterances per job (an extra measurement, not the driver's line)")
+                         "of --utterances utterances per job; sweep: configs[1], the quantized Linear alone (extra "
+                         "measurements, not the driver's line)")
     ap.add_argument("--utterances", type=int, default=2048)
     args = ap.parse_args()
 
@@ -486,6 +572,9 @@ def main():
         return
     if args.config == "throughput":
         run_throughput(args, world, rank, local_rank)
+        return
+    if args.config == "sweep":
+        run_sweep(args)
         return
 
     import torch

@@ -384,6 +384,16 @@ VKB_API vkb_status vkb_session_cross_kv(const vkb_session* s, int32_t layer, con
 VKB_API vkb_status vkb_session_step(vkb_session* s, int32_t n_tok, const int32_t* streams_host,
                                     const int32_t* positions_host, const int32_t* tokens_host,
                                     float* logits_dev, int32_t* ids_dev);
+/* vkb_session_step whose tokens may come from the device: where
+ * feed_rows_host[i] >= 0, token i is feed_ids_dev[feed_rows_host[i]] (e.g.
+ * the greedy id a previous step wrote for that stream into its ids_dev),
+ * read on the device when the step runs; elsewhere tokens_host[i] is used.
+ * A greedy loop can so launch step t+1 before reading step t's ids back
+ * (the reference's loop reads each id on the host first, whisper/greedy.rs:32). */
+VKB_API vkb_status vkb_session_step_feed(vkb_session* s, int32_t n_tok, const int32_t* streams_host,
+                                         const int32_t* positions_host, const int32_t* tokens_host,
+                                         const int32_t* feed_rows_host, const int32_t* feed_ids_dev,
+                                         float* logits_dev, int32_t* ids_dev);
 VKB_API const float* vkb_session_logits(const vkb_session* s);
 VKB_API const int32_t* vkb_session_ids(const vkb_session* s);
 /* Returns a finished stream's KV pages to the pool (continuous batching). */

@@ -42,6 +42,10 @@ class FakeSession:
             out.append((sum(h) * 31 + len(h)) % 997)
         ids_dev[:len(out)] = torch.tensor(out, dtype=torch.int32)
 
+    def step_feed(self, streams, positions, tokens, feed_rows, feed_ids, ids_dev=None):
+        toks = [int(feed_ids[f]) if f >= 0 else t for t, f in zip(tokens, feed_rows)]
+        self.step(streams, positions, toks, ids_dev=ids_dev)
+
     def release(self, slot):
         del self.hist[slot]
         self.encoded.pop(slot)

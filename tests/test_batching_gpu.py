@@ -35,3 +35,49 @@ def test_continuous_batching_matches_one_at_a_time(ctx, tmp_path):
     assert b.tokens == sum(news)
     assert all(len(i) == n for i, n in zip(batched, news))
     assert batched == alone
+
+
+def test_continuous_batching_matches_oracle_greedy(ctx, tmp_path):
+    """Each utterance's greedy ids under continuous batching (4 slots, clips
+    encoded 2 at a time, streams joining and leaving between steps) against
+    the oracle decoding that utterance alone from its own log-mel: the oracle
+    restates the reference's greedy loop (whisper/greedy.rs:32; argmax of the
+    last logits row, fed back), with the same Q8_0 self-KV and cross store.
+    The ids agree up to the first step where the oracle's own top-2 gap is
+    below 1e-3 (a near-tie the two may break differently); the test prints
+    how many utterances stopped early for that reason."""
+    import torch
+    from oracle import py as o, whisper_ref
+    from vokra_b200 import whisper
+    from vokra_b200.batching import ContinuousBatcher, Utterance
+    arch = synth.WhisperArch(80, 1500, 512, 8, 1, 64, 8, 1, 1000, 2048, 999, (1, 2, 3, 4))
+    path = str(tmp_path / "cb_oracle.gguf")
+    synth.write_synthetic_whisper(path, arch, synth.Q8_0, seed=9)
+    rng = np.random.default_rng(5)
+    pcm_host = np.stack([synth.synthetic_audio(60 + i) for i in range(4)])
+    pcm = torch.from_numpy(pcm_host).cuda()
+    n_utt = 7
+    lengths = [int(x) for x in rng.integers(16000, 480000, n_utt)]
+    news = [int(x) for x in rng.integers(3, 12, n_utt)]
+    model = whisper.WhisperModel(ctx, path)
+    sess = whisper.Session(model, max_streams=4, max_step_tokens=32, max_clips=2)
+    utts = [Utterance(i % 4, lengths[i], news[i]) for i in range(n_utt)]
+    ContinuousBatcher(ctx, sess, 4, 2, arch.start_ids, arch.n_mels).run(utts, pcm)
+    sess.close()
+    assert all(len(u.ids) == u.n_new_tokens for u in utts)
+    ref = whisper_ref.RefWhisper(path)
+    near_ties = 0
+    for u in utts:
+        dec = ref.decoder(ref.encode(o.log_mel(pcm_host[u.pcm_index][:u.n_samples], arch.n_mels)),
+                          kv_mode="q8", cross_mode="q8")
+        logits = dec.step(list(arch.start_ids))[-1]
+        for t in range(u.n_new_tokens):
+            top2 = np.sort(logits)[-2:]
+            if top2[1] - top2[0] < 1e-3:
+                near_ties += 1
+                break
+            want = int(np.argmax(logits))
+            assert u.ids[t] == want, (u, t)
+            logits = dec.step([want])[-1]
+    print(f"continuous batching vs oracle greedy: {n_utt} utterances, {near_ties} stopped at a near-tie")
+    assert near_ties < n_utt

@@ -57,10 +57,15 @@ def _run(ctx, tag, n, k, m, seed=0, bias=True, a_f16=False, out_f16=False, epi=_
 
 
 @pytest.mark.parametrize("tag", TAGS)
-@pytest.mark.parametrize("m", [1, 2, 3, 4])
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8])
 def test_gemv_path_matches_oracle(ctx, tag, m):
+    # m <= 8 with Q4_0 / Q8_0 / Q4_K: the streaming GEMV with its in-kernel split-K
+    # reduction; other formats m <= 4: the row-per-thread GEMV; fp32 arithmetic either way
     for i, (k, n) in enumerate([(256, 128), (512, 300), (1280, 1280)]):
         got, ref = _run(ctx, tag, n, k, m, seed=k + n, rnd=i % 2 == 1)
+        if m > 4 and tag not in (synth.Q4_0, synth.Q8_0, synth.Q4_K):  # the tensor-core GEMM takes these
+            assert _rel_rms(got, ref) <= 1e-3
+            continue
         assert np.max(np.abs(got - ref)) <= 1e-4 * max(1.0, np.max(np.abs(ref)))
         assert _rel_rms(got, ref) <= 1e-5
 
@@ -82,11 +87,11 @@ def test_tensor_core_large_k_and_ragged_n(ctx, tag):
     assert np.max(np.abs(got - ref)) <= 2e-2
 
 
-@pytest.mark.parametrize("m", [2, 64])
+@pytest.mark.parametrize("m", [2, 7, 64])
 @pytest.mark.parametrize("epi", [_lib.EPI_GELU, _lib.EPI_SCALE, _lib.EPI_RESIDUAL])
 def test_epilogues(ctx, m, epi):
     got, ref = _run(ctx, synth.Q4_0, 256, 512, m, epi=epi, scale=0.125)
-    tol = 1e-3 if m > 4 else 1e-5
+    tol = 1e-3 if m > 8 else 1e-5
     assert _rel_rms(got, ref) <= tol
 
 

@@ -91,14 +91,17 @@ def test_tiny_whisper_self_kv_modes(ctx, tiny, self_kv):
     The packs themselves are bit-exact (test_kv_gpu); end to end, the device's
     K/V rows differ from the oracle's in their last bits (split-precision
     GEMMs), and a 4- or 5-bit pack turns a value that sits on a rounding
-    boundary into a whole quantum (1/7 or 1/15 of the block's amax), so the
-    relative-RMS bar for those two modes is 5e-3; f32 pages keep 1e-3."""
+    boundary into a whole quantum (1/7 or 1/15 of the block's amax). For
+    those two modes the bars are 1e-2 relative RMS and 5e-2 max-abs (a wrong
+    page or a wrong block decode moves logits by O(1)); f32 pages keep the
+    1e-3 / 1e-2 budget and identical argmax ids."""
     enc, ref_enc, results = _run(ctx, tiny, n_streams=2, n_steps=5, self_kv=self_kv)
-    tol = 1e-3 if self_kv == "f32" else 5e-3
+    rms_tol, abs_tol = (1e-3, 1e-2) if self_kv == "f32" else (1e-2, 5e-2)
     for got, ref in results:
-        assert np.max(np.abs(got - ref)) <= 1e-2
-        assert _rel_rms(got, ref) <= tol
-        assert np.array_equal(np.argmax(got, axis=-1), np.argmax(ref, axis=-1)) or self_kv != "f32"
+        assert np.max(np.abs(got - ref)) <= abs_tol
+        assert _rel_rms(got, ref) <= rms_tol
+        if self_kv == "f32":
+            assert np.array_equal(np.argmax(got, axis=-1), np.argmax(ref, axis=-1))
 
 
 def test_tiny_whisper_f16_cross_store(ctx, tiny):

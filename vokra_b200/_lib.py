@@ -132,6 +132,7 @@ SIGNATURES = {
     "vkb_session_encoder_output": (P, [P]),
     "vkb_session_read_encoder_output": (C.c_int, [P, P, SZ]),
     "vkb_session_step": (C.c_int, [P, I32, P, P, P, P, P]),
+    "vkb_session_step_feed": (C.c_int, [P, I32, P, P, P, P, P, P, P]),
     "vkb_session_logits": (P, [P]),
     "vkb_session_ids": (P, [P]),
     "vkb_session_release": (C.c_int, [P, I32]),

@@ -109,6 +109,7 @@ struct vkb_context {
     int precision = VKB_PREC_SPLIT;  // tensor-core operand precision (vkb_context_set_precision)
     vkb::DevBuf workspace;
     vkb::DevBuf err_flag;  // int set by a kernel whose bounded wait gave up
+    vkb::DevBuf tile_ctr;  // per-tile arrival counters of in-kernel split-K reductions (each returns to 0)
     vkb::DevBuf frontend;  // log-mel tables (window, twiddles, mel bank) + per-clip maxima
     int frontend_mels = 0; // mel count the tables were built for
     // Programmatic dependent launch: each kernel may start while the previous
@@ -125,6 +126,8 @@ struct vkb_context {
 };
 
 namespace vkb {
+
+constexpr int kTileCounters = 1 << 16;  // weight tiles a split-K GEMV launch may count (N <= 8M rows)
 
 // Launch with programmatic stream serialization (see vkb_context::pdl). Every
 // kernel launched this way calls pdl_wait() before reading or writing memory

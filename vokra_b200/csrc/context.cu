@@ -38,6 +38,8 @@ vkb_status vkb_context_create(int device, vkb_context** out) {
             VKB_CUDA(cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking));
             c->stream = c->own_stream;
             c->err_flag.alloc(sizeof(int));
+            c->tile_ctr.alloc(vkb::kTileCounters * sizeof(unsigned));
+            VKB_CUDA(cudaMemset(c->tile_ctr.p, 0, c->tile_ctr.n));
             const char* pdl = getenv("VKB_PDL");
             c->pdl = !(pdl && pdl[0] == '0');
             VKB_CUDA(cudaMemset(c->err_flag.p, 0, sizeof(int)));

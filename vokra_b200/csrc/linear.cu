@@ -319,6 +319,300 @@ __global__ void __launch_bounds__(128) gemv_kernel(const uint8_t* __restrict__ q
     }
 }
 
+// ---------------------------------------------------------------------------
+// Small-m streaming GEMV (m <= 8) for Q4_0, Q8_0 and Q4_K: one CTA = one
+// 128-row weight tile x one K range of units (32-blocks; 64-chunks for Q4_K);
+// thread = row. In the tile layout the CTA's weights are a few contiguous
+// runs (quants, scales or super-block headers), so thread 0 requests them
+// with bulk copies into shared memory, in two halves on two mbarriers, before
+// waiting on the previous kernel (weights are never written by one); the
+// threads then stage the activations (f32; hi + lo summed for F16X2) and
+// decode from shared memory while the second half lands. The quants enter the
+// dot product as exact small-integer floats (packed f32x2 subtract and FMA):
+// acc += d * sum(q * x) per block; Q4_K: d1 * sum(q x) - m1 * sum(x) per half
+// chunk. Split-K partials go to ws[split][m][n]; the last CTA of a tile to
+// arrive (a counter that resets itself) sums them in split order and applies
+// the epilogue, so the result does not depend on arrival order and no reduce
+// kernel runs. Every mbarrier wait is bounded: on timeout the CTA sets the
+// error flag, waits (bounded) for its copies in flight and skips its work.
+// ---------------------------------------------------------------------------
+template <int FMT>
+struct GvUnit {
+    static constexpr int K = FMT == W_Q4_K ? 64 : 32;  // K elements per unit
+};
+
+// Bytes of one unit for the whole 128-row tile in the quant plane and in the
+// scale plane (Q4_K: a 16-byte header per row per super-block of 4 units).
+template <int FMT>
+struct GvBytes {
+    static constexpr int Q = TILE_N * (FMT == W_Q4_0 ? 16 : 32);
+    static constexpr int S = FMT == W_Q4_K ? 0 : TILE_N * 2;
+    static constexpr int HDR = TILE_N * 16;
+};
+
+template <int FMT>
+struct GvRaw {
+    uint4 q0, q1;  // Q4_0: q0; Q8_0 and Q4_K: q0, q1
+    uint4 h;       // Q4_K: the super-block header (d, dmin, 12 scale bytes)
+    uint32_t d;    // Q4_0 / Q8_0: f16 scale bits
+};
+
+template <int FMT>
+__device__ __forceinline__ void gv_read(const uint8_t* q_s, const uint8_t* s_s, int i, int64_t unit, int64_t sb0,
+                                        int r, GvRaw<FMT>& o) {
+    constexpr int QB = GvBytes<FMT>::Q;
+    if constexpr (FMT == W_Q4_0) {
+        o.q0 = *reinterpret_cast<const uint4*>(q_s + i * QB + r * 16);
+        o.d = *reinterpret_cast<const unsigned short*>(s_s + i * GvBytes<FMT>::S + r * 2);
+    } else if constexpr (FMT == W_Q8_0) {
+        const uint4* q = reinterpret_cast<const uint4*>(q_s + i * QB + r * 32);
+        o.q0 = q[0];
+        o.q1 = q[1];
+        o.d = *reinterpret_cast<const unsigned short*>(s_s + i * GvBytes<FMT>::S + r * 2);
+    } else {
+        const uint4* q = reinterpret_cast<const uint4*>(q_s + i * QB + r * 32);
+        o.q0 = q[0];
+        o.q1 = q[1];
+        o.h = *reinterpret_cast<const uint4*>(s_s + (unit / 4 - sb0) * GvBytes<FMT>::HDR + r * 16);
+    }
+}
+
+// Byte b of w as the float 2^23 + byte (exact).
+__device__ __forceinline__ float gv_magic(uint32_t w, int b) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u + b));
+}
+
+// 16 quants of four words as 8 exact float pairs q - bias (packed f32x2 subtraction).
+__device__ __forceinline__ void gv_pairs(const uint32_t (&w)[4], float bias, float2 (&q)[8]) {
+    const float2 c = make_float2(-(8388608.0f + bias), -(8388608.0f + bias));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        q[2 * i] = __fadd2_rn(make_float2(gv_magic(w[i], 0), gv_magic(w[i], 1)), c);
+        q[2 * i + 1] = __fadd2_rn(make_float2(gv_magic(w[i], 2), gv_magic(w[i], 3)), c);
+    }
+}
+
+// acc + q * x over 16 elements (x: 16 consecutive floats in shared memory), as a float2
+__device__ __forceinline__ float2 gv_dot16(const float2 (&q)[8], const float* x, float2 acc) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 v = x4[i];
+        acc = __ffma2_rn(q[2 * i], make_float2(v.x, v.y), acc);
+        acc = __ffma2_rn(q[2 * i + 1], make_float2(v.z, v.w), acc);
+    }
+    return acc;
+}
+
+__device__ __forceinline__ void gv_nibbles(const uint4& v, uint32_t (&lo)[4], uint32_t (&hi)[4]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        lo[i] = w[i] & 0x0F0F0F0Fu;
+        hi[i] = (w[i] >> 4) & 0x0F0F0F0Fu;
+    }
+}
+
+template <int FMT, int MM>
+__device__ __forceinline__ void gv_unit(const GvRaw<FMT>& u, int64_t unit, const float* __restrict__ xs, int ks,
+                                        const float* __restrict__ xsum, int ns, float (&acc)[MM]) {
+    if constexpr (FMT == W_Q4_0 || FMT == W_Q8_0) {
+        float2 qa[8], qb[8];  // elements 0..15 and 16..31 of the block
+        if constexpr (FMT == W_Q4_0) {
+            // ggml order: element j in the low nibble of byte j, j + 16 in the high one
+            uint32_t lo[4], hi[4];
+            gv_nibbles(u.q0, lo, hi);
+            gv_pairs(lo, 8.0f, qa);
+            gv_pairs(hi, 8.0f, qb);
+        } else {
+            const uint32_t a[4] = {u.q0.x ^ 0x80808080u, u.q0.y ^ 0x80808080u, u.q0.z ^ 0x80808080u,
+                                   u.q0.w ^ 0x80808080u};
+            const uint32_t b[4] = {u.q1.x ^ 0x80808080u, u.q1.y ^ 0x80808080u, u.q1.z ^ 0x80808080u,
+                                   u.q1.w ^ 0x80808080u};
+            gv_pairs(a, 128.0f, qa);
+            gv_pairs(b, 128.0f, qb);
+        }
+        const float d = __half2float(__ushort_as_half((unsigned short)u.d));
+#pragma unroll
+        for (int m = 0; m < MM; ++m) {
+            float2 sacc = gv_dot16(qa, xs + m * ks, make_float2(0.0f, 0.0f));
+            sacc = gv_dot16(qb, xs + m * ks + 16, sacc);
+            acc[m] = fmaf(d, sacc.x + sacc.y, acc[m]);
+        }
+    } else {
+        // Q4_K chunk c of its super-block: element l in the low nibble of byte
+        // l, 32 + l in the high one; w = d1*q - m1 (low half), d2*q - m2 (high)
+        const uint32_t hh[4] = {u.h.x, u.h.y, u.h.z, u.h.w};
+        const float d = __half2float(__ushort_as_half((unsigned short)(hh[0] & 0xffffu)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(hh[0] >> 16)));
+        const int c = (int)(unit & 3), j0 = 2 * c, j1 = 2 * c + 1;
+        auto byte6 = [&](int k) { return (hh[1 + (k >> 2)] >> (8 * (k & 3))) & 0xffu; };  // scale byte k
+        uint32_t sc0, m0, sc1, m1;  // get_scale_min_k4 (crates/vokra-core/src/gguf/quant/mod.rs:140)
+        if (j0 < 4) { sc0 = byte6(j0) & 63; m0 = byte6(j0 + 4) & 63; }
+        else { sc0 = (byte6(j0 + 4) & 0xf) | ((byte6(j0 - 4) >> 6) << 4); m0 = (byte6(j0 + 4) >> 4) | ((byte6(j0) >> 6) << 4); }
+        if (j1 < 4) { sc1 = byte6(j1) & 63; m1 = byte6(j1 + 4) & 63; }
+        else { sc1 = (byte6(j1 + 4) & 0xf) | ((byte6(j1 - 4) >> 6) << 4); m1 = (byte6(j1 + 4) >> 4) | ((byte6(j1) >> 6) << 4); }
+        const float d1 = __fmul_rn(d, (float)sc0), mm1 = __fmul_rn(dmin, (float)m0);
+        const float d2 = __fmul_rn(d, (float)sc1), mm2 = __fmul_rn(dmin, (float)m1);
+        float2 la[8], lb[8], ha[8], hb[8];
+        {
+            uint32_t l0[4], h0[4], l1[4], h1[4];
+            gv_nibbles(u.q0, l0, h0);
+            gv_nibbles(u.q1, l1, h1);
+            gv_pairs(l0, 0.0f, la);
+            gv_pairs(l1, 0.0f, lb);
+            gv_pairs(h0, 0.0f, ha);
+            gv_pairs(h1, 0.0f, hb);
+        }
+#pragma unroll
+        for (int m = 0; m < MM; ++m) {
+            const float* x = xs + m * ks;
+            float2 s1 = gv_dot16(la, x, make_float2(0.0f, 0.0f));
+            s1 = gv_dot16(lb, x + 16, s1);
+            float2 s2 = gv_dot16(ha, x + 32, make_float2(0.0f, 0.0f));
+            s2 = gv_dot16(hb, x + 48, s2);
+            const float t1 = xsum[m * ns], t2 = xsum[m * ns + 1];
+            acc[m] = fmaf(d1, s1.x + s1.y, acc[m]);
+            acc[m] = fmaf(-mm1, t1, acc[m]);
+            acc[m] = fmaf(d2, s2.x + s2.y, acc[m]);
+            acc[m] = fmaf(-mm2, t2, acc[m]);
+        }
+    }
+}
+
+template <int FMT, int MM>
+__global__ void __launch_bounds__(128) gemv2_kernel(const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc,
+                                                    int64_t K, int64_t N, int64_t M, const void* __restrict__ a,
+                                                    int a_fmt, int units_per_split, int n_splits, float* ws,
+                                                    unsigned* ctr, int* err, Epi e) {
+    constexpr int UK = GvUnit<FMT>::K;
+    constexpr int QB = GvBytes<FMT>::Q, SB = GvBytes<FMT>::S, HB = GvBytes<FMT>::HDR;
+    extern __shared__ __align__(128) uint8_t gv_smem[];
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ unsigned last;
+    const int tile = blockIdx.x, split = blockIdx.y, r = threadIdx.x;
+    const int64_t total = K / UK;
+    const int64_t u0 = (int64_t)split * units_per_split;
+    const int64_t u1 = min(total, u0 + units_per_split);
+    const int nu = (int)(u1 - u0);
+    const int ks = units_per_split * UK;
+    const int ns = ks / 32;
+    // shared memory: quants [ups][QB] | scales [ups][SB] or headers | x [MM][ks] | sums [MM][ns]
+    const int64_t sb0 = u0 / 4, n_sb = FMT == W_Q4_K ? (u1 - 1) / 4 - sb0 + 1 : 0;
+    uint8_t* q_s = gv_smem;
+    uint8_t* s_s = q_s + (size_t)units_per_split * QB;
+    const size_t s_bytes = FMT == W_Q4_K ? (size_t)((units_per_split + 6) / 4) * HB : (size_t)units_per_split * SB;
+    float* xs = reinterpret_cast<float*>(s_s + s_bytes);
+    float* xsum = xs + MM * ks;
+    const int h0 = (nu + 1) / 2;  // units in the first half
+    pdl_launch();
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(&bars[0], 1);
+        ptx::mbar_init(&bars[1], 1);
+        ptx::fence_mbar_init();
+        const uint8_t* qsrc = qs + ((int64_t)tile * total + u0) * QB;
+        if constexpr (FMT == W_Q4_K) {
+            const uint8_t* hsrc = sc + ((int64_t)tile * (K / 256) + sb0) * HB;
+            ptx::mbar_expect_tx(&bars[0], (uint32_t)(h0 * QB + n_sb * HB));
+            ptx::bulk_load(s_s, hsrc, (uint32_t)(n_sb * HB), &bars[0]);
+            if (nu > h0) ptx::mbar_expect_tx(&bars[1], (uint32_t)((nu - h0) * QB));
+        } else {
+            const uint8_t* ssrc = sc + ((int64_t)tile * total + u0) * SB;
+            ptx::mbar_expect_tx(&bars[0], (uint32_t)(h0 * (QB + SB)));
+            ptx::bulk_load(s_s, ssrc, (uint32_t)(h0 * SB), &bars[0]);
+            if (nu > h0) {
+                ptx::mbar_expect_tx(&bars[1], (uint32_t)((nu - h0) * (QB + SB)));
+                ptx::bulk_load(s_s + h0 * SB, ssrc + (size_t)h0 * SB, (uint32_t)((nu - h0) * SB), &bars[1]);
+            }
+        }
+        ptx::bulk_load(q_s, qsrc, (uint32_t)(h0 * QB), &bars[0]);
+        if (nu > h0)
+            ptx::bulk_load(q_s + (size_t)h0 * QB, qsrc + (size_t)h0 * QB, (uint32_t)((nu - h0) * QB), &bars[1]);
+    }
+    pdl_wait();
+    // this K range of the activations (rows >= M are zero)
+    const int kspan = nu * UK;
+    for (int i = threadIdx.x; i < MM * ks / 4; i += blockDim.x) {
+        const int m = i / (ks / 4), kk = 4 * (i % (ks / 4));
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (m < M && kk < kspan) {
+            const int64_t g = (int64_t)m * K + u0 * UK + kk;
+            if (a_fmt == VKB_DT_F32) {
+                v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a) + g);
+            } else {
+                const __half* ah = reinterpret_cast<const __half*>(a);
+                const float2 p0 = __half22float2(*reinterpret_cast<const __half2*>(ah + g));
+                const float2 p1 = __half22float2(*reinterpret_cast<const __half2*>(ah + g + 2));
+                v = make_float4(p0.x, p0.y, p1.x, p1.y);
+                if (a_fmt == VKB_DT_F16X2) {
+                    const float2 l0 = __half22float2(*reinterpret_cast<const __half2*>(ah + M * K + g));
+                    const float2 l1 = __half22float2(*reinterpret_cast<const __half2*>(ah + M * K + g + 2));
+                    v.x += l0.x; v.y += l0.y; v.z += l1.x; v.w += l1.y;
+                }
+            }
+        }
+        *reinterpret_cast<float4*>(xs + m * ks + kk) = v;
+    }
+    __syncthreads();
+    if constexpr (FMT == W_Q4_K) {  // sum of each 32 activations (the min terms)
+        for (int i = threadIdx.x; i < MM * ns; i += blockDim.x) {
+            const float* x = xs + (i / ns) * ks + (i % ns) * 32;
+            float t = 0.0f;
+            for (int j = 0; j < 32; ++j) t += x[j];
+            xsum[i] = t;
+        }
+        __syncthreads();
+    }
+    float acc[MM];
+#pragma unroll
+    for (int m = 0; m < MM; ++m) acc[m] = 0.0f;
+    bool ok = ptx::mbar_wait(&bars[0], 0);
+    for (int i = 0; i < nu && ok; ++i) {
+        if (i == h0) ok = ptx::mbar_wait(&bars[1], 0);
+        if (!ok) break;
+        GvRaw<FMT> cur;
+        gv_read<FMT>(q_s, s_s, i, u0 + i, sb0, r, cur);
+        gv_unit<FMT, MM>(cur, u0 + i, xs + i * UK, ks, xsum + i * (UK / 32), ns, acc);
+    }
+    if (!ok) {
+        if (threadIdx.x == 0) atomicExch(err, 1);
+        // let copies still in flight land before the CTA's shared memory goes away
+        ptx::mbar_wait(&bars[0], 0);
+        if (nu > h0) ptx::mbar_wait(&bars[1], 0);
+    }
+    const int64_t n = (int64_t)tile * TILE_N + r;
+    if (n_splits == 1) {
+        if (n < N && ok) {
+            const float b = e.bias ? e.bias[n] : 0.0f;
+#pragma unroll
+            for (int m = 0; m < MM; ++m)
+                if (m < M) epi_store(e, m, n, acc[m], b);
+        }
+        return;
+    }
+    if (n < N) {
+#pragma unroll
+        for (int m = 0; m < MM; ++m)
+            if (m < M) ws[((int64_t)split * M + m) * N + n] = acc[m];
+    }
+    // the last CTA of this tile sums the partials in split order
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(ctr + tile, 1u) == (unsigned)(n_splits - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (n < N) {
+        const float b = e.bias ? e.bias[n] : 0.0f;
+        for (int m = 0; m < (int)M && m < MM; ++m) {
+            float t = 0.0f;
+            for (int sp = 0; sp < n_splits; ++sp) t += __ldcg(ws + ((int64_t)sp * M + m) * N + n);
+            epi_store(e, m, n, t, b);
+        }
+    }
+    if (threadIdx.x == 0) ctr[tile] = 0;
+}
+
 // Sums split-K partials ws[split][m][n] in split order and applies the epilogue.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int n_splits, int64_t M, int64_t N, Epi e) {
     pdl_entry();
@@ -753,7 +1047,47 @@ void make_tmap_3d_f32(CUtensorMap* map, const void* base, int64_t planes, int64_
 
 static int* device_err_flag(vkb_context* ctx) { return ctx->err_flag.as<int>(); }
 
-int gemv_max_m() { return 4; }
+// Largest m the streaming GEMVs take (VKB_GEMV_MAX_M overrides, for measurements).
+int gemv_max_m() {
+    static const int v = [] { const char* e = std::getenv("VKB_GEMV_MAX_M"); return e ? std::atoi(e) : 8; }();
+    return v;
+}
+
+static bool gemv2_fmt(int fmt) { return fmt == W_Q4_0 || fmt == W_Q8_0 || fmt == W_Q4_K; }
+
+// Shared memory of one gemv2 CTA (see the kernel's layout).
+static size_t gemv2_smem(int fmt, int mm, int ups) {
+    const int uk = fmt == W_Q4_K ? 64 : 32;
+    const size_t qb = (size_t)TILE_N * (fmt == W_Q4_0 ? 16 : 32);
+    const size_t sbytes = fmt == W_Q4_K ? (size_t)((ups + 6) / 4) * TILE_N * 16 : (size_t)ups * TILE_N * 2;
+    const size_t ks = (size_t)ups * uk;
+    return (size_t)ups * qb + sbytes + (size_t)mm * ks * 4 + (size_t)mm * (ks / 32) * 4;
+}
+
+
+template <int FMT>
+static void launch_gemv2(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_fmt, const Epi& e,
+                         float* ws, int units_per_split, int splits) {
+    const int n_tiles = (int)(w->n_pad / TILE_N);
+    if (splits > 1 && n_tiles > kTileCounters) fail(VKB_ERROR_UNSUPPORTED_OP, "linear: too many weight tiles");
+    dim3 grid((unsigned)n_tiles, (unsigned)splits);
+    const uint8_t* qs = w->qs.as<uint8_t>();
+    const uint8_t* sc = w->sc.as<uint8_t>();
+    unsigned* ctr = ctx->tile_ctr.as<unsigned>();
+    auto go = [&](auto MMc) {
+        constexpr int MMv = decltype(MMc)::value;
+        const size_t sm = gemv2_smem(FMT, MMv, units_per_split);
+        smem_optin(gemv2_kernel<FMT, MMv>, 200 * 1024);
+        launch_pdl(ctx, gemv2_kernel<FMT, MMv>, grid, 128, sm, qs, sc, w->k, w->n, m, a, a_fmt, units_per_split,
+                   splits, ws, ctr, device_err_flag(ctx), e);
+    };
+    if (m <= 1) go(std::integral_constant<int, 1>{});
+    else if (m <= 2) go(std::integral_constant<int, 2>{});
+    else if (m <= 4) go(std::integral_constant<int, 4>{});
+    else go(std::integral_constant<int, 8>{});
+    VKB_CUDA(cudaGetLastError());
+    ctx->count();
+}
 
 template <int FMT>
 static void launch_gemv(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_fmt, const Epi& e,
@@ -835,7 +1169,22 @@ LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m, b
     const int64_t total = w->k / STAGE_K;
     const int n_tiles = (int)(w->n_pad / TILE_N);
     const int sms = ctx->sm_count;
-    if (m <= gemv_max_m()) {
+    static const bool gv2_off = [] { const char* v = std::getenv("VKB_GEMV2"); return v && v[0] == '0'; }();
+    if (m <= gemv_max_m() && gemv2_fmt(w->fmt) && !gv2_off) {
+        // the streaming GEMV: about 8 CTAs per SM, at least 2 units each, at
+        // most ~28 KB of shared memory per CTA
+        p.tc = false;
+        p.gv2 = true;
+        const int uk = w->fmt == W_Q4_K ? 64 : 32;
+        const int64_t units = w->k / uk;
+        const int mm = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8;
+        int splits = (int)std::max<int64_t>(1, std::min<int64_t>(units / 2, (8LL * sms + n_tiles - 1) / n_tiles));
+        int ups = (int)((units + splits - 1) / splits);
+        while (ups > 2 && gemv2_smem(w->fmt, mm, ups) > 28 * 1024) --ups;
+        splits = (int)((units + ups - 1) / ups);
+        p.splits = splits;
+        p.sps = ups;
+    } else if (m <= std::min(4, gemv_max_m())) {
         p.tc = false;
         // Enough CTAs to cover the SMs several times; at least 2 stages each.
         int splits = std::max(1, std::min<int>((int)(total / 2), (4 * sms + n_tiles - 1) / n_tiles));
@@ -909,7 +1258,13 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
     uint8_t* wsb = ctx->workspace.as<uint8_t>();
     float* ws = ws_override ? ws_override : reinterpret_cast<float*>(wsb + a16_bytes);
     if (!p.tc) {
-        with_fmt(w->fmt, [&](auto F) { launch_gemv<decltype(F)::value>(ctx, w, m, a, a_dtype, e, ws, p.sps, p.splits); });
+        if (p.gv2) {
+            if (w->fmt == W_Q4_0) launch_gemv2<W_Q4_0>(ctx, w, m, a, a_dtype, e, ws, p.sps, p.splits);
+            else if (w->fmt == W_Q8_0) launch_gemv2<W_Q8_0>(ctx, w, m, a, a_dtype, e, ws, p.sps, p.splits);
+            else launch_gemv2<W_Q4_K>(ctx, w, m, a, a_dtype, e, ws, p.sps, p.splits);
+        } else {
+            with_fmt(w->fmt, [&](auto F) { launch_gemv<decltype(F)::value>(ctx, w, m, a, a_dtype, e, ws, p.sps, p.splits); });
+        }
     } else {
         const __half* a16;
         if (a_dtype != VKB_DT_F32) {
@@ -948,7 +1303,8 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
         }
     }
     if (x.splits_out) *x.splits_out = p.splits;
-    if (p.splits > 1 && !x.splits_out) {
+    if (p.gv2 && x.splits_out) *x.splits_out = 1;  // reduced in the kernel
+    if (p.splits > 1 && !x.splits_out && !p.gv2) {
         int64_t tot = m * w->n;
         launch_pdl(ctx, splitk_reduce_kernel, (unsigned)((tot + 255) / 256), 256, 0, ws, p.splits, m, w->n, e);
         VKB_CUDA(cudaGetLastError());

@@ -8,6 +8,7 @@ namespace vkb {
 
 struct LinearPlan {
     bool tc = false;     // tcgen05 GEMM (else the streaming GEMV)
+    bool gv2 = false;    // the small-m GEMV with the in-kernel split-K reduction (Q4_0, Q8_0, Q4_K)
     int bn = 0;          // token tile of the GEMM
     int m_tiles = 0;
     int splits = 1;      // K splits (partials reduced by splitk_reduce_kernel)

@@ -92,8 +92,8 @@ struct vkb_session {
     vkb_kv_pool* pool = nullptr;
     int max_tok = 0;
     // decoder step buffers
-    DevBuf h, xln, qkv, ctxb, qc, ffn, logits, ids, tok, pos, seq, ws;
-    int32_t* h_tok = nullptr;  // pinned staging: tokens | positions | streams
+    DevBuf h, xln, qkv, ctxb, qc, ffn, logits, ids, tok, pos, seq, ws, feed;
+    int32_t* h_tok = nullptr;  // pinned staging: tokens | positions | streams | feed rows
     cudaEvent_t staged = nullptr;
     bool staged_pending = false;
     // cross-attention store: per layer K and V planes for n_stream * n_audio_ctx rows
@@ -311,7 +311,8 @@ vkb_session* create_session(vkb_whisper* m, const vkb_session_options* o) {
     s->tok.alloc(mt * 4);
     s->pos.alloc(mt * 4);
     s->seq.alloc(mt * 4);
-    VKB_CUDA(cudaMallocHost(&s->h_tok, (size_t)mt * 3 * 4));
+    VKB_CUDA(cudaMallocHost(&s->h_tok, (size_t)mt * 4 * 4));
+    s->feed.alloc(mt * 4);
     VKB_CUDA(cudaEventCreateWithFlags(&s->staged, cudaEventDisableTiming));
     // cross store
     const int64_t rows = S * T;
@@ -454,14 +455,34 @@ void session_encode(vkb_session* s, int n, const float* logmel, const int32_t* s
     s->last_clips = n;
 }
 
+// Tokens fed from the device: token i = feed_ids[rows[i]] where rows[i] >= 0
+// (a previous step's greedy ids, never seen by the host); elsewhere the host
+// value already copied stays.
+__global__ void feed_tokens_kernel(int32_t* tok, const int32_t* __restrict__ rows, const int32_t* __restrict__ feed_ids,
+                                   int n_tok) {
+    pdl_entry();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n_tok && rows[i] >= 0) tok[i] = feed_ids[rows[i]];
+}
+
 void session_step(vkb_session* s, int n_tok, const int32_t* streams, const int32_t* positions, const int32_t* tokens,
-                  float* logits_out, int32_t* ids_out) {
+                  float* logits_out, int32_t* ids_out, const int32_t* feed_rows = nullptr,
+                  const int32_t* feed_ids = nullptr) {
     vkb_whisper* m = s->m;
     vkb_context* ctx = s->ctx;
     const auto& D = m->dims;
     if (n_tok <= 0 || n_tok > s->max_tok) fail(VKB_ERROR_INVALID_ARGUMENT, "session_step: n_tok out of range");
     if (!streams || !positions || !tokens) fail(VKB_ERROR_INVALID_ARGUMENT, "session_step: null argument");
+    if ((feed_rows == nullptr) != (feed_ids == nullptr))
+        fail(VKB_ERROR_INVALID_ARGUMENT, "session_step: feed rows and feed ids go together");
     for (int i = 0; i < n_tok; ++i) {
+        if (feed_rows && feed_rows[i] >= 0) {
+            if (feed_rows[i] >= s->max_tok) fail(VKB_ERROR_INVALID_ARGUMENT, "session_step: feed row out of range");
+            if (positions[i] < 0 || positions[i] >= D.n_text_ctx)
+                fail(VKB_ERROR_INVALID_ARGUMENT, "whisper decoder: position " + std::to_string(positions[i] + 1) +
+                                                     " exceeds n_text_ctx " + std::to_string(D.n_text_ctx));
+            continue;
+        }
         if (tokens[i] < 0 || tokens[i] >= D.n_vocab)
             fail(VKB_ERROR_INVALID_ARGUMENT, "whisper decoder: token id " + std::to_string(tokens[i]) + " >= n_vocab " +
                                                  std::to_string(D.n_vocab));
@@ -478,6 +499,15 @@ void session_step(vkb_session* s, int n_tok, const int32_t* streams, const int32
     VKB_CUDA(cudaMemcpyAsync(s->tok.p, s->h_tok, (size_t)n_tok * 4, cudaMemcpyHostToDevice, ctx->stream));
     VKB_CUDA(cudaMemcpyAsync(s->pos.p, s->h_tok + n_tok, (size_t)n_tok * 4, cudaMemcpyHostToDevice, ctx->stream));
     VKB_CUDA(cudaMemcpyAsync(s->seq.p, s->h_tok + 2 * n_tok, (size_t)n_tok * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (feed_rows) {
+        int32_t* hf = s->h_tok + 3 * n_tok;
+        for (int i = 0; i < n_tok; ++i) hf[i] = feed_rows[i] >= 0 ? feed_rows[i] : -1;
+        VKB_CUDA(cudaMemcpyAsync(s->feed.p, hf, (size_t)n_tok * 4, cudaMemcpyHostToDevice, ctx->stream));
+        launch_pdl(ctx, feed_tokens_kernel, (unsigned)((n_tok + 127) / 128), 128, 0, s->tok.as<int32_t>(),
+                   s->feed.as<int32_t>(), feed_ids, n_tok);
+        VKB_CUDA(cudaGetLastError());
+        ctx->count();
+    }
     VKB_CUDA(cudaEventRecord(s->staged, ctx->stream));
     s->staged_pending = true;
 
@@ -681,6 +711,18 @@ vkb_status vkb_session_step(vkb_session* s, int32_t n_tok, const int32_t* stream
     return guard([&] {
         if (!s) fail(VKB_ERROR_INVALID_ARGUMENT, "session_step: null session");
         session_step(s, n_tok, streams_host, positions_host, tokens_host, logits_dev, ids_dev);
+    });
+}
+
+vkb_status vkb_session_step_feed(vkb_session* s, int32_t n_tok, const int32_t* streams_host,
+                                 const int32_t* positions_host, const int32_t* tokens_host,
+                                 const int32_t* feed_rows_host, const int32_t* feed_ids_dev, float* logits_dev,
+                                 int32_t* ids_dev) {
+    return guard([&] {
+        if (!s) fail(VKB_ERROR_INVALID_ARGUMENT, "session_step: null session");
+        if (!feed_rows_host || !feed_ids_dev) fail(VKB_ERROR_INVALID_ARGUMENT, "session_step_feed: null feed");
+        session_step(s, n_tok, streams_host, positions_host, tokens_host, logits_dev, ids_dev, feed_rows_host,
+                     feed_ids_dev);
     });
 }
 

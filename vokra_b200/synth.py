@@ -418,19 +418,35 @@ def whisper_metadata(a: WhisperArch) -> dict:
     }
 
 
-def write_synthetic_whisper(path: str, a: WhisperArch, qtag: int, seed: int = 0) -> None:
-    """Seeded N(0, 0.02) weights (layer norms 1/0), Linear + embed_tokens in `qtag`."""
-    rng = np.random.default_rng(seed)
+def _synthetic_tensor(args):
+    seed, i, name, tag, dims = args
+    n = int(np.prod(dims))
+    if "layer_norm" in name:
+        v = np.ones(n, np.float32) if name.endswith(".weight") else np.zeros(n, np.float32)
+    else:
+        v = np.random.default_rng([seed, i]).standard_normal(n, dtype=np.float32) * np.float32(0.02)
+    return quantize(tag, v)
+
+
+def write_synthetic_whisper(path: str, a: WhisperArch, qtag: int, seed: int = 0, workers: int | None = None) -> None:
+    """Seeded N(0, 0.02) weights (layer norms 1/0), Linear + embed_tokens in `qtag`.
+    Tensor i draws from rng([seed, i]), so the file does not depend on how many
+    worker processes quantize the tensors."""
+    import os
     decls = whisper_tensor_decls(a, qtag)
     w = GgufStreamWriter(path, whisper_metadata(a), [TensorDecl(n, t, dims) for n, t, dims in decls])
     w.begin()
-    for name, tag, dims in decls:
-        n = int(np.prod(dims))
-        if "layer_norm" in name:
-            v = np.ones(n, np.float32) if name.endswith(".weight") else np.zeros(n, np.float32)
-        else:
-            v = rng.standard_normal(n, dtype=np.float32) * np.float32(0.02)
-        w.write(quantize(tag, v))
+    jobs = [(seed, i, name, tag, dims) for i, (name, tag, dims) in enumerate(decls)]
+    n_workers = workers if workers is not None else min(16, os.cpu_count() or 1)
+    big = sum(int(np.prod(d)) for _, _, _, _, d in jobs) > (64 << 20)
+    if n_workers > 1 and big:
+        import multiprocessing as mp
+        with mp.get_context("fork").Pool(n_workers) as pool:
+            for data in pool.imap(_synthetic_tensor, jobs, chunksize=1):
+                w.write(data)
+    else:
+        for j in jobs:
+            w.write(_synthetic_tensor(j))
     w.finish()
 
 

@@ -74,6 +74,18 @@ class Session:
                                   C.c_void_p(logits_dev.data_ptr() if logits_dev is not None else None),
                                   C.c_void_p(ids_dev.data_ptr() if ids_dev is not None else None)))
 
+    def step_feed(self, streams, positions, tokens, feed_rows, feed_ids_dev, logits_dev=None, ids_dev=None):
+        """step() where token i is feed_ids_dev[feed_rows[i]] wherever feed_rows[i] >= 0 (read on the device)."""
+        s = np.ascontiguousarray(streams, dtype=np.int32)
+        p = np.ascontiguousarray(positions, dtype=np.int32)
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        f = np.ascontiguousarray(feed_rows, dtype=np.int32)
+        check(_L.vkb_session_step_feed(self.h, s.size, s.ctypes.data_as(C.c_void_p), p.ctypes.data_as(C.c_void_p),
+                                       t.ctypes.data_as(C.c_void_p), f.ctypes.data_as(C.c_void_p),
+                                       C.c_void_p(feed_ids_dev.data_ptr()),
+                                       C.c_void_p(logits_dev.data_ptr() if logits_dev is not None else None),
+                                       C.c_void_p(ids_dev.data_ptr() if ids_dev is not None else None)))
+
     def release(self, stream: int):
         check(_L.vkb_session_release(self.h, stream))
 
