@@ -605,8 +605,17 @@ __global__ void __launch_bounds__(128) gemv2_kernel(const uint8_t* __restrict__ 
     if (n < N) {
         const float b = e.bias ? e.bias[n] : 0.0f;
         for (int m = 0; m < (int)M && m < MM; ++m) {
+            // loads issued 8 at a time, added in split order
             float t = 0.0f;
-            for (int sp = 0; sp < n_splits; ++sp) t += __ldcg(ws + ((int64_t)sp * M + m) * N + n);
+            for (int sp0 = 0; sp0 < n_splits; sp0 += 8) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    v[j] = sp0 + j < n_splits ? __ldcg(ws + ((int64_t)(sp0 + j) * M + m) * N + n) : 0.0f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if (sp0 + j < n_splits) t += v[j];
+            }
             epi_store(e, m, n, t, b);
         }
     }
@@ -1053,6 +1062,12 @@ int gemv_max_m() {
     return v;
 }
 
+// Most K splits of one streaming-GEMV tile (the last CTA sums them all).
+static int gv2_max_splits() {
+    static const int v = [] { const char* e = std::getenv("VKB_GV2_MAX_SPLITS"); return e ? std::atoi(e) : 16; }();
+    return v;
+}
+
 static bool gemv2_fmt(int fmt) { return fmt == W_Q4_0 || fmt == W_Q8_0 || fmt == W_Q4_K; }
 
 // Shared memory of one gemv2 CTA (see the kernel's layout).
@@ -1170,7 +1185,10 @@ LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m, b
     const int n_tiles = (int)(w->n_pad / TILE_N);
     const int sms = ctx->sm_count;
     static const bool gv2_off = [] { const char* v = std::getenv("VKB_GEMV2"); return v && v[0] == '0'; }();
-    if (m <= gemv_max_m() && gemv2_fmt(w->fmt) && !gv2_off) {
+    // the streaming GEMV wins at m = 1, and up to m = 4 for wide weights (the
+    // logits head); the tensor-core GEMM's fixed cost is lower elsewhere
+    // (configs[1] sweep, CUDA-graph timing)
+    if (m <= gemv_max_m() && gemv2_fmt(w->fmt) && !gv2_off && (m == 1 || (m <= 4 && w->n >= 16384))) {
         // the streaming GEMV: about 8 CTAs per SM, at least 2 units each, at
         // most ~28 KB of shared memory per CTA
         p.tc = false;
@@ -1178,13 +1196,18 @@ LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m, b
         const int uk = w->fmt == W_Q4_K ? 64 : 32;
         const int64_t units = w->k / uk;
         const int mm = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8;
-        int splits = (int)std::max<int64_t>(1, std::min<int64_t>(units / 2, (8LL * sms + n_tiles - 1) / n_tiles));
+        int splits = (int)std::max<int64_t>(
+            1, std::min<int64_t>({units / 2, (8LL * sms + n_tiles - 1) / n_tiles, (int64_t)gv2_max_splits()}));
         int ups = (int)((units + splits - 1) / splits);
-        while (ups > 2 && gemv2_smem(w->fmt, mm, ups) > 28 * 1024) --ups;
+        static const size_t cap = [] {
+            const char* v = std::getenv("VKB_GV2_SMEM_KB");
+            return (size_t)(v ? std::atoi(v) : 28) * 1024;
+        }();
+        while (ups > 2 && gemv2_smem(w->fmt, mm, ups) > cap) --ups;
         splits = (int)((units + ups - 1) / ups);
         p.splits = splits;
         p.sps = ups;
-    } else if (m <= std::min(4, gemv_max_m())) {
+    } else if (m <= std::min(4, gemv_max_m()) && !gemv2_fmt(w->fmt)) {
         p.tc = false;
         // Enough CTAs to cover the SMs several times; at least 2 stages each.
         int splits = std::max(1, std::min<int>((int)(total / 2), (4 * sms + n_tiles - 1) / n_tiles));
