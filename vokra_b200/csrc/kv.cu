@@ -144,31 +144,54 @@ __global__ void __launch_bounds__(256) paged_decode_kernel(
         }
     }
     __syncthreads();
-    // phase 1: scores
+    // The V bytes of every key (this group's 256 channels and their scales) are
+    // requested into L2 now, so that phase 3 reads them at L2 latency; they do
+    // not depend on the scores.
+    for (int i = t; i < 3 * n_keys; i += 256) {
+        const int64_t row = rows_s[i / 3];
+        const int part = i % 3;
+        const void* p = part < 2 ? static_cast<const void*>(vq + row * W + c0 + 128 * part)
+                                 : static_cast<const void*>(vd + row * nb + b0);
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+    }
+    // phase 1: scores, two keys per iteration (their 8 loads issued together)
     {
         const int hl = t >> 6, slot = t & 63;
         const float* qh = qs + hl * 64;
-        for (int k = slot; k < n_keys; k += 64) {
-            const int64_t row = rows_s[k];
-            const uint4* kp = reinterpret_cast<const uint4*>(kq + row * W + c0 + hl * 64);
-            uint4 kv4[4];
+        for (int k0 = slot; k0 < n_keys; k0 += 128) {
+            uint4 kv4[2][4];
+            __half2 s2[2];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) kv4[i] = __ldcg(kp + i);
-            const __half2 s2 = __ldcg(reinterpret_cast<const __half2*>(kd + row * nb + b0 + hl * 2));
-            float part[2] = {0.0f, 0.0f};
+            for (int u = 0; u < 2; ++u) {
+                const int k = k0 + 64 * u;
+                if (k < n_keys) {
+                    const int64_t row = rows_s[k];
+                    const uint4* kp = reinterpret_cast<const uint4*>(kq + row * W + c0 + hl * 64);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t w4[4] = {kv4[i].x ^ 0x80808080u, kv4[i].y ^ 0x80808080u, kv4[i].z ^ 0x80808080u,
-                                        kv4[i].w ^ 0x80808080u};
-#pragma unroll
-                for (int wd = 0; wd < 4; ++wd)
-#pragma unroll
-                    for (int b = 0; b < 4; ++b) {
-                        const float kf = __uint_as_float(__byte_perm(w4[wd], 0x4B000000u, 0x7440u + b)) - 8388736.0f;
-                        part[i >> 1] = fmaf(qh[16 * i + 4 * wd + b], kf, part[i >> 1]);
-                    }
+                    for (int i = 0; i < 4; ++i) kv4[u][i] = __ldcg(kp + i);
+                    s2[u] = __ldcg(reinterpret_cast<const __half2*>(kd + row * nb + b0 + hl * 2));
+                }
             }
-            sc[hl * max_keys + k] = part[0] * __low2float(s2) + part[1] * __high2float(s2);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int k = k0 + 64 * u;
+                if (k >= n_keys) break;
+                float part[2] = {0.0f, 0.0f};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t w4[4] = {kv4[u][i].x ^ 0x80808080u, kv4[u][i].y ^ 0x80808080u,
+                                            kv4[u][i].z ^ 0x80808080u, kv4[u][i].w ^ 0x80808080u};
+#pragma unroll
+                    for (int wd = 0; wd < 4; ++wd)
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            const float kf =
+                                __uint_as_float(__byte_perm(w4[wd], 0x4B000000u, 0x7440u + b)) - 8388736.0f;
+                            part[i >> 1] = fmaf(qh[16 * i + 4 * wd + b], kf, part[i >> 1]);
+                        }
+                }
+                sc[hl * max_keys + k] = part[0] * __low2float(s2[u]) + part[1] * __high2float(s2[u]);
+            }
         }
     }
     __syncthreads();
@@ -200,7 +223,7 @@ __global__ void __launch_bounds__(256) paged_decode_kernel(
         float a[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) a[i] = 0.0f;
-#pragma unroll 2
+#pragma unroll 4
         for (int k = kg; k < n_keys; k += 16) {
             const int64_t row = rows_s[k];
             const uint4 v4 = __ldcg(reinterpret_cast<const uint4*>(vcol + row * W));
