@@ -463,6 +463,80 @@ def run_sweep(args):
                 w.close()
 
 
+def run_base(args):
+    """Whisper-base (6+6 layers, d 512, 51865-token vocabulary) in Q8_0,
+    one 30 s clip at batch 1: log-mel frontend, encoder, the 4-token prefix and 64
+    teacher-forced tokens, every kernel on the device (the decode steps replay CUDA graphs).
+    Timed over --steps passes with CUDA events after --warmup passes (the clip's PCM is
+    resident; e2e adds its H2D copy and the ids' D2H read). cpu_baseline: the same pass
+    through the oracle (the reference CPU algorithm, f32 caches) on the host cores."""
+    import torch
+    from vokra_b200 import ops, synth, whisper
+    arch = synth.WHISPER_BASE
+    path = ensure_model(model_path("base_q8_0"), arch, synth.Q8_0)
+    ctx = ops.Context(0)
+    model = whisper.WhisperModel(ctx, path)
+    sess = whisper.Session(model, max_streams=1, max_step_tokens=8, max_clips=1, cross_kv_q8=True)
+    NT = 64
+    pcm_host = torch.from_numpy(synthetic_pcm(1, 7)).pin_memory()
+    pcm_dev = pcm_host.cuda()
+    lm = torch.empty((1, arch.n_mels, 3000), device="cuda")
+    toks = np.random.default_rng(3).integers(0, arch.n_vocab, NT).astype(np.int32)
+    ids_dev = torch.zeros(NT, dtype=torch.int32, device="cuda")
+    ids_host = torch.zeros(NT, dtype=torch.int32).pin_memory()
+    pre = list(arch.start_ids[:PREFIX])
+    stream = torch.cuda.current_stream()
+
+    def one(e2e):
+        if e2e:
+            pcm_dev.copy_(pcm_host, non_blocking=True)
+        ops.log_mel(ctx, pcm_dev, arch.n_mels, out=lm)
+        sess.encode(lm, [0])
+        sess.step([0] * PREFIX, list(range(PREFIX)), pre)
+        for t in range(NT):
+            sess.step([0], [PREFIX + t], [int(toks[t])], ids_dev=ids_dev[t:t + 1])
+        if e2e:
+            ids_host.copy_(ids_dev, non_blocking=True)
+        sess.release(0)
+
+    for _ in range(max(3, args.warmup)):
+        one(False)
+    torch.cuda.synchronize()
+    res = {}
+    for e2e in (False, True):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            one(e2e)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        res[e2e] = e0.elapsed_time(e1) / args.steps
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import py as o, whisper_ref
+        threads = os.cpu_count() or 1
+        o.lib().orc_set_threads(threads)
+        ref = whisper_ref.RefWhisper(path)
+        t0 = time.perf_counter()
+        dec = ref.decoder(ref.encode(o.log_mel(pcm_host.numpy()[0], arch.n_mels)), "f32", "f32")
+        dec.step(pre)
+        for t in range(NT):
+            dec.step([int(toks[t])])
+        cpu_s = time.perf_counter() - t0
+        cpu = {"value": round(CLIP_SECONDS / cpu_s, 3), "unit": "audio-s/s", "cores": threads, "kind": "port",
+               "sample": "the whole configs[0] pass (1 clip, 64 tokens) through the oracle, f32 self-KV and cross K/V"}
+    print(json.dumps({
+        "metric": "audio-s/s, Whisper-base Q8_0 batch 1 (configs[0])", "value": round(CLIP_SECONDS / (res[False] / 1e3), 2),
+        "unit": "audio-s/s", "decode_tok_s": None, "ms_per_step": round(res[False], 3), "n_gpus": 1,
+        "steps": args.steps, "warmup": max(3, args.warmup), "higher_is_better": True,
+        "dtype": "f16 hi+lo tensor-core operands / fp32 GEMV (Q8_0 weights, Q8_0 KV)", "data": "synthetic",
+        "config": {"workload": "configs[0]: whisper-base q8_0, 1 clip x 30 s, log-mel + encoder + 4-token prefix + 64 "
+                               "teacher-forced tokens, batch 1"},
+        "e2e": {"value": round(CLIP_SECONDS / (res[True] / 1e3), 2), "unit": "audio-s/s",
+                "h2d_bytes_per_step": int(pcm_host.numel() * 4), "d2h_bytes_per_step": NT * 4},
+        "cpu_baseline": cpu}), flush=True)
+
+
 def throughput_utterances(n: int, rank: int, pool: int):
     """configs[4] workload of one rank: clip lengths U[5, 30] s (padded to 30 s by the
     frontend), decode lengths U[32, 224]; clip i reads row i % pool of the PCM pool."""
@@ -553,9 +627,9 @@ def main():
     ap.add_argument("--sweep-formats", default="", help="sweep: comma-separated subset of q8_0,q4_0,q4_k")
     ap.add_argument("--sweep-m", default="", help="sweep: comma-separated M values")
     ap.add_argument("--sweep-shapes", default="", help="sweep: comma-separated KxN shapes, e.g. 1280x51866")
-    ap.add_argument("--config", default="batch", choices=["batch", "throughput", "sweep"],
+    ap.add_argument("--config", default="batch", choices=["batch", "throughput", "sweep", "base"],
                     help="batch: configs[3] (the default bench line); throughput: configs[4], continuous batching "
-                         "of --utterances utterances per job; sweep: configs[1], the quantized Linear alone (extra "
+                         "of --utterances utterances per job; sweep: configs[1], the quantized Linear alone; base: configs[0] (extra "
                          "measurements, not the driver's line)")
     ap.add_argument("--utterances", type=int, default=2048)
     args = ap.parse_args()
@@ -572,6 +646,9 @@ def main():
         return
     if args.config == "throughput":
         run_throughput(args, world, rank, local_rank)
+        return
+    if args.config == "base":
+        run_base(args)
         return
     if args.config == "sweep":
         run_sweep(args)
@@ -613,14 +690,22 @@ def main():
     ids_host = torch.zeros((NT, B), dtype=torch.int32).pin_memory()
     stream = torch.cuda.current_stream()
 
-    def one_step(e2e: bool):
+    dec_events = []  # (start, end) of the decode loop of each timed device-resident step
+
+    def one_step(e2e: bool, mark: bool = False):
         if e2e:
             pcm_dev.copy_(pcm_host, non_blocking=True)
         ops.log_mel(ctx, pcm_dev, arch.n_mels, out=logmel_dev)
         sess.encode(logmel_dev, streams)
         sess.step(pre_streams, pre_pos, pre_tok)
+        if mark:
+            d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            d0.record(stream)
         for t in range(NT):
             sess.step(streams, positions[t], toks[t], ids_dev=ids_dev[t])
+        if mark:
+            d1.record(stream)
+            dec_events.append((d0, d1))
         if e2e:
             ids_host.copy_(ids_dev, non_blocking=True)
         for s in range(B):
@@ -638,7 +723,7 @@ def main():
         ev1 = torch.cuda.Event(enable_timing=True)
         ev0.record(stream)
         for _ in range(args.steps):
-            one_step(e2e)
+            one_step(e2e, mark=not e2e)
         ev1.record(stream)
         torch.cuda.synchronize()
         barrier()
@@ -702,6 +787,26 @@ def main():
         except Exception:
             pass
 
+    # The decode loop (128 one-token steps of 64 streams, events inside the timed steps):
+    # algorithmic bytes per token step = the decoder's Q4_0 Linear weights incl. the
+    # embedding-tied logits head, the Q8_0 cross K/V store of every stream and layer,
+    # the Q8_0 self-KV of every key each stream attends to (34/32 bytes per element).
+    dec_ms = float(np.mean([a.elapsed_time(b) for a, b in dec_events])) / NT
+    d_, f_, Ld, V_, T_ = arch.d_model, arch.ffn_dim, arch.n_text_layer, arch.n_vocab, arch.n_audio_ctx
+    w_bytes = (Ld * (4 * d_ * d_ + 2 * d_ * d_ + 2 * d_ * f_) + V_ * d_) * 18 / 32
+    cross_bytes = Ld * B * T_ * 2 * d_ * 34 / 32
+    self_bytes = np.mean([Ld * B * (PREFIX + t + 1) * 2 * d_ * 34 / 32 for t in range(NT)])
+    dec_alg = w_bytes + cross_bytes + self_bytes
+    dec_gbs = dec_alg / (dec_ms / 1e3) / 1e9
+    roofline_decode = {"bound": "hbm", "achieved": round(dec_gbs, 1), "peak": hbm, "unit": "GB/s",
+                       "frac": round(dec_gbs / hbm, 4), "traffic": None,
+                       "kernel": "whole decode step (64 streams, 32 layers, CUDA-graph replay), mean over 128 "
+                                 "token steps",
+                       "ms_per_token_step": round(dec_ms, 4), "algorithmic_bytes_per_step": int(dec_alg),
+                       "bytes_split": {"weights": int(w_bytes), "cross_kv": int(cross_bytes),
+                                       "self_kv_mean": int(self_bytes)},
+                       "peak_kind": f"{peak_kind} HBM copy"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -735,6 +840,7 @@ def main():
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches),
             "roofline": roofline,
+            "roofline_decode": roofline_decode,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
         }

@@ -1227,7 +1227,10 @@ LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m, b
         }
         int ctas = n_tiles * m_tiles;
         int splits = 1;
-        if (ctas < sms) splits = std::max(1, std::min<int>((int)(total / 2), sms / ctas));
+        // K splits to fill the SMs (VKB_TC_CTA_TARGET scales the CTA target, for measurements)
+        static const int target = [] { const char* v = std::getenv("VKB_TC_CTA_TARGET"); return v ? std::atoi(v) : 100; }();
+        const int want = std::max(1, sms * target / 100);
+        if (ctas < want) splits = std::max(1, std::min<int>((int)(total / 2), want / ctas));
         int sps = (int)((total + splits - 1) / splits);
         splits = (int)((total + sps - 1) / sps);
         p.bn = bn;
