@@ -229,7 +229,16 @@ VKB_API vkb_status vkb_kv_append_attention(vkb_kv_pool* pool, int32_t layer, con
                                            void* ctx_out_dev, int out_dtype);
 /* 1 when the step begun last runs vkb_kv_append_attention as the fused kernel. */
 VKB_API int32_t vkb_kv_decode_fused(const vkb_kv_pool* pool);
-/* Frees every page of one stream (SEQUENCE layout). */
+/* Branches a stream (SEQUENCE layout): dst becomes the first n_pos positions
+ * of src. dst's pages are let go; src's completely filled pages are shared by
+ * reference count (no copy), a partly filled last page is copied on the
+ * device. A later step that writes into a shared page gives the writing
+ * stream its own copy first (copy on write, in vkb_kv_begin_step). The
+ * reference deep-copies its host cache per beam (selfkv_snapshot /
+ * selfkv_restore, whisper/decoder.rs:343-368). */
+VKB_API vkb_status vkb_kv_copy_stream(vkb_kv_pool* pool, int32_t src, int32_t dst, int32_t n_pos);
+/* Frees every page of one stream (SEQUENCE layout); a page shared with other
+ * streams stays in use until its last holder lets go. */
 VKB_API vkb_status vkb_kv_release_seq(vkb_kv_pool* pool, int32_t seq_id);
 /* release_layer (paged_quant.rs:500): REFERENCE layout only. */
 VKB_API vkb_status vkb_kv_release_layer(vkb_kv_pool* pool, int32_t layer);
@@ -405,8 +414,9 @@ VKB_API vkb_status vkb_session_release(vkb_session* s, int32_t stream);
  * src (once per clip: beams of one clip share them afterwards). This is the
  * per-beam branch of beam search: the reference deep-copies the host cache
  * (selfkv_snapshot / selfkv_restore, whisper/decoder.rs:343-368); here the
- * pages are copied on the device in one launch. Asynchronous on the context's
- * stream. */
+ * filled pages are shared (copy on write, as vkb_kv_copy_stream) and at most
+ * one partly filled page is copied on the device. Asynchronous on the
+ * context's stream. */
 VKB_API vkb_status vkb_session_copy_stream(vkb_session* s, int32_t src, int32_t dst, int32_t n_pos,
                                            int32_t copy_cross);
 

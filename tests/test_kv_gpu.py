@@ -412,3 +412,62 @@ def test_fused_decode_matches_unfused_route(ctx):
         outs.append(out.cpu().numpy())
         pool.close()
     assert np.max(np.abs(outs[0] - outs[1])) <= 1e-5
+
+
+def test_copy_stream_shares_pages_copy_on_write(ctx):
+    """Beam branching on the pool: vkb_kv_copy_stream shares the source's
+    filled pages (only a partly filled last page is copied), and a later write
+    into a shared page copies it first, so no stream sees another's K/V."""
+    import torch
+    from vokra_b200 import ops
+    rng = np.random.default_rng(31)
+    n_head, d_head, bs = 4, 64, 16
+    w = n_head * d_head
+    pool = ops.QuantizedPagedKvCache(ctx, ops.KvDims(1, n_head, d_head, 4, 1, 128), bs, _lib.KV_Q8_0,
+                                     _lib.KV_LAYOUT_SEQUENCE)
+    K = rng.standard_normal((40, w)).astype(np.float32)
+    V = rng.standard_normal((40, w)).astype(np.float32)
+    pool.begin_step([0] * 37, list(range(37)))
+    pool.append(0, _dev(K[:37]), _dev(V[:37]))
+    assert pool.pages_in_use() == 3
+    pool.copy_stream(0, 1, 37)  # two full pages shared, the third copied
+    assert pool.pages_in_use() == 4
+    pool.copy_stream(0, 2, 32)  # two full pages shared, nothing copied
+    assert pool.pages_in_use() == 4
+    table = pool.page_table().reshape(4, -1)
+    assert table[1, 0] == table[0, 0] and table[1, 1] == table[0, 1] and table[1, 2] != table[0, 2]
+    assert table[2, 0] == table[0, 0] and table[2, 2] == -1
+    # stream 2 overwrites position 20 (inside a shared page): it gets its own copy
+    K2 = rng.standard_normal((1, w)).astype(np.float32)
+    pool.begin_step([2], [20])
+    pool.append(0, _dev(K2), _dev(K2))
+    assert pool.pages_in_use() == 5
+    table = pool.page_table().reshape(4, -1)
+    assert table[2, 1] != table[0, 1] and table[2, 0] == table[0, 0]
+    # every stream still reads its own history
+    got0, _ = pool.read_step(0, 20, 0)
+    got2, _ = pool.read_step(0, 20, 2)
+    got2b, _ = pool.read_step(0, 21, 2)
+    ref = lambda x: o.kv_unpack(3, o.kv_pack(3, x)).reshape(-1, w)
+    assert np.array_equal(got0, ref(K[20:21])[0])
+    assert np.array_equal(got2, ref(K2)[0])
+    assert np.array_equal(got2b, ref(K[21:22])[0])  # the rest of the copied page came along
+    # the branches attend over their own keys
+    pool.begin_step([0, 1], [37, 37])
+    kn = rng.standard_normal((2, w)).astype(np.float32)
+    pool.append(0, _dev(kn), _dev(kn))
+    q = rng.standard_normal((2, w)).astype(np.float32) * np.float32(0.125)
+    out = torch.zeros((2, w), dtype=torch.float32, device="cuda:0")
+    pool.attention(0, _dev(q), out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for s in range(2):
+        kd = ref(np.concatenate([K[:37], kn[s:s + 1]]))
+        vd = ref(np.concatenate([V[:37], kn[s:s + 1]]))
+        assert np.max(np.abs(got[s] - o.attention(q[s:s + 1], kd, vd, n_head)[0])) <= 1e-4
+    # releasing the source keeps the shared pages for the branches
+    pool.release_seq(0)
+    assert pool.pages_in_use() == 4  # page 0 (streams 1, 2), page 1 (stream 1), stream 1's page 2, stream 2's page 1
+    pool.release_seq(1)
+    pool.release_seq(2)
+    assert pool.pages_in_use() == 0

@@ -106,6 +106,7 @@ SIGNATURES = {
     "vkb_kv_append_attention": (C.c_int, [P, I32, P, I64, P, C.c_int]),
     "vkb_kv_decode_fused": (I32, [P]),
     "vkb_gguf_inspect": (C.c_int, [P, SZ, P, P]),
+    "vkb_kv_copy_stream": (C.c_int, [P, I32, I32, I32]),
     "vkb_kv_release_seq": (C.c_int, [P, I32]),
     "vkb_kv_release_layer": (C.c_int, [P, I32]),
     "vkb_kv_reset": (C.c_int, [P]),

@@ -33,6 +33,7 @@ struct vkb_kv_pool {
     int64_t n_pages = 0, table_len = 0;
     std::vector<int32_t> table;      // host mirror (-1 = empty)
     std::vector<int32_t> free_list;  // LIFO
+    std::vector<int32_t> refs;       // SEQUENCE layout: streams whose table holds each page (beams share pages)
     // device
     DevBuf kq, kd, vq, vd;           // arena planes: quants (or f32 values), f16 scales
     DevBuf kh, vh;                   // Q5_0 5th-bit planes
@@ -513,6 +514,7 @@ vkb_kv_pool* kv_pool_create(vkb_context* ctx, const vkb_kv_pool_desc* desc) {
         }
         p->table.assign(p->table_len, -1);
         for (int64_t i = p->n_pages - 1; i >= 0; --i) p->free_list.push_back((int32_t)i);
+        p->refs.assign(p->n_pages, 0);
         const int64_t rows = (int64_t)p->n_arena * p->n_pages * p->rpp;
         VKB_CUDA(cudaSetDevice(ctx->device));
         const size_t sbytes = d.mode == VKB_KV_FP32 ? 0 : (size_t)p->row_blocks * 2;
@@ -522,6 +524,8 @@ vkb_kv_pool* kv_pool_create(vkb_context* ctx, const vkb_kv_pool_desc* desc) {
         for (DevBuf* b : {&p->kq, &p->vq, &p->kd, &p->vd, &p->kh, &p->vh})
             if (b->n) VKB_CUDA(cudaMemsetAsync(b->p, 0, b->n, ctx->stream));
         p->table_dev.alloc((size_t)p->table_len * 4);
+        // page copies of one call: a stream's pages (copy_stream) or one per step token (copy-on-write)
+        p->pairs_dev.alloc((size_t)std::max<int64_t>(p->ppseq, std::max(2048, d.n_stream * 8)) * sizeof(int2));
         p->max_step = std::max(2048, d.n_stream * 8);  // tokens per step (prefills)
         p->rows_dev.alloc((size_t)d.n_layer * p->max_step * 8);
         p->groups_dev.alloc((size_t)p->max_step * sizeof(AttnGroup));
@@ -557,8 +561,20 @@ static int32_t acquire(vkb_kv_pool* p) {
                                                " pages, " + std::to_string(p->n_pages) + " in use");
     int32_t id = p->free_list.back();
     p->free_list.pop_back();
+    p->refs[id] = 1;
     return id;
 }
+
+// One table entry lets go of its page; the page returns to the free list when
+// no stream holds it any more.
+static void drop(vkb_kv_pool* p, int32_t id) {
+    if (--p->refs[id] <= 0) {
+        p->refs[id] = 0;
+        p->free_list.push_back(id);
+    }
+}
+
+static void copy_pages(vkb_kv_pool* p, const std::vector<int2>& pairs);
 
 static int64_t row_of(const vkb_kv_pool* p, int layer, int t, int s) {
     const int bs = p->d.page_tokens;
@@ -607,10 +623,21 @@ void kv_begin_step(vkb_kv_pool* p, int n_tok, const int32_t* seq, const int32_t*
     // vkb_kv_append, in the order the reference's append_step would
     // (paged_quant.rs:396-420).
     if (d.layout == VKB_KV_LAYOUT_SEQUENCE) {
+        std::vector<int2> cow;
         for (int i = 0; i < n_tok; ++i) {
             int64_t idx = (int64_t)seq[i] * p->ppseq + pos[i] / d.page_tokens;
-            if (p->table[idx] < 0) p->table[idx] = acquire(p);
+            if (p->table[idx] < 0) {
+                p->table[idx] = acquire(p);
+            } else if (p->refs[p->table[idx]] > 1) {
+                // a page shared with another stream (a beam branch) is written:
+                // this stream gets its own copy first (copy on write)
+                const int32_t old = p->table[idx];
+                p->table[idx] = acquire(p);
+                cow.push_back(make_int2(old, p->table[idx]));
+                drop(p, old);
+            }
         }
+        if (!cow.empty()) copy_pages(p, cow);
         memcpy(p->h_table, p->table.data(), (size_t)p->table_len * 4);
         for (int layer = 0; layer < d.n_layer; ++layer)
             for (int i = 0; i < n_tok; ++i) p->h_rows[(size_t)layer * n_tok + i] = row_of(p, layer, pos[i], seq[i]);
@@ -820,11 +847,29 @@ __global__ void kv_copy_pages_kernel(const int2* __restrict__ pairs, int64_t n_p
     move(vh, hrow);
 }
 
+// Copies whole pages of every layer on the device: pair i = (source page,
+// destination page), one launch of kv_copy_pages_kernel.
+static void copy_pages(vkb_kv_pool* p, const std::vector<int2>& pairs) {
+    if (pairs.empty()) return;
+    if (p->pairs_dev.n < pairs.size() * sizeof(int2)) fail(VKB_ERROR_OTHER, "kv: too many page copies in one call");
+    // pageable source: the copy is staged before cudaMemcpyAsync returns
+    VKB_CUDA(cudaMemcpyAsync(p->pairs_dev.p, pairs.data(), pairs.size() * sizeof(int2), cudaMemcpyHostToDevice,
+                             p->ctx->stream));
+    dim3 grid((unsigned)pairs.size(), (unsigned)p->d.n_layer);
+    launch_pdl(p->ctx, kv_copy_pages_kernel, grid, 256, 0, p->pairs_dev.as<int2>(), p->n_pages, p->d.page_tokens,
+               p->qrow, p->hrow, p->srow_bytes(), p->kq.as<uint8_t>(), p->kd.as<uint8_t>(), p->kh.as<uint8_t>(),
+               p->vq.as<uint8_t>(), p->vd.as<uint8_t>(), p->vh.as<uint8_t>());
+    VKB_CUDA(cudaGetLastError());
+    p->ctx->count();
+}
+
 // Makes stream dst a copy of the first n_pos positions of stream src (the
 // per-beam branch of the self-attention cache; the reference deep-copies the
-// host cache, whisper/decoder.rs:343-368): dst's pages are released, fresh
-// pages are acquired for src's first ceil(n_pos / page_tokens) pages and
-// filled on the device in one launch.
+// host cache, whisper/decoder.rs:343-368). dst's own pages are let go; the
+// pages src has filled completely are shared (reference counts, nothing is
+// copied), only a partly filled last page is copied, in one launch. A later
+// write into a shared page (a step at a position it holds) copies it first
+// (kv_begin_step).
 void kv_copy_stream(vkb_kv_pool* p, int src, int dst, int n_pos) {
     const auto& d = p->d;
     if (d.layout != VKB_KV_LAYOUT_SEQUENCE) fail(VKB_ERROR_INVALID_ARGUMENT, "copy_stream: sequence layout only");
@@ -834,47 +879,41 @@ void kv_copy_stream(vkb_kv_pool* p, int src, int dst, int n_pos) {
     if (src == dst) return;
     if (d.page_tokens * p->srow_bytes() % 16 || d.page_tokens * p->hrow % 16 || d.page_tokens * p->qrow % 16)
         fail(VKB_ERROR_UNSUPPORTED_OP, "copy_stream: page planes not 16-byte sized");
-    const int n_pg = (n_pos + d.page_tokens - 1) / d.page_tokens;
+    const int full = n_pos / d.page_tokens, n_pg = (n_pos + d.page_tokens - 1) / d.page_tokens;
+    const int copied = n_pg - full;  // 0 or 1
     // Validate everything before touching dst, so a failed call leaves both
     // streams and the device page table as they were.
-    size_t dst_held = 0;
-    for (int i = 0; i < p->ppseq; ++i) dst_held += p->table[(int64_t)dst * p->ppseq + i] >= 0;
+    size_t dst_freed = 0;
+    for (int i = 0; i < p->ppseq; ++i) {
+        const int32_t e = p->table[(int64_t)dst * p->ppseq + i];
+        dst_freed += e >= 0 && p->refs[e] == 1;
+    }
     for (int i = 0; i < n_pg; ++i)
         if (p->table[(int64_t)src * p->ppseq + i] < 0)
             fail(VKB_ERROR_INVALID_ARGUMENT, "copy_stream: source stream has no page for position " +
                                                  std::to_string(i * d.page_tokens));
-    if (p->free_list.size() + dst_held < (size_t)n_pg)
-        fail(VKB_ERROR_KV_CACHE_EXHAUSTED, "copy_stream: " + std::to_string(n_pg) + " pages needed, " +
-                                               std::to_string(p->free_list.size() + dst_held) + " free");
+    if (p->free_list.size() + dst_freed < (size_t)copied)
+        fail(VKB_ERROR_KV_CACHE_EXHAUSTED, "copy_stream: " + std::to_string(copied) + " page needed, " +
+                                               std::to_string(p->free_list.size() + dst_freed) + " free");
+    // take src's pages first: dst may already share some of them
+    for (int i = 0; i < full; ++i) ++p->refs[p->table[(int64_t)src * p->ppseq + i]];
     for (int i = 0; i < p->ppseq; ++i) {
         int32_t& e = p->table[(int64_t)dst * p->ppseq + i];
         if (e >= 0) {
-            p->free_list.push_back(e);
+            drop(p, e);
             e = -1;
         }
     }
+    for (int i = 0; i < full; ++i) p->table[(int64_t)dst * p->ppseq + i] = p->table[(int64_t)src * p->ppseq + i];
     std::vector<int2> pairs;
-    for (int i = 0; i < n_pg; ++i) {
-        const int32_t sp = p->table[(int64_t)src * p->ppseq + i];
+    if (copied) {
+        const int32_t sp = p->table[(int64_t)src * p->ppseq + full];
         const int32_t dp = acquire(p);
-        p->table[(int64_t)dst * p->ppseq + i] = dp;
+        p->table[(int64_t)dst * p->ppseq + full] = dp;
         pairs.push_back(make_int2(sp, dp));
     }
     upload_table(p);
-    if (pairs.empty()) return;
-    if (p->pairs_dev.n < pairs.size() * sizeof(int2)) {
-        VKB_CUDA(cudaStreamSynchronize(p->ctx->stream));
-        p->pairs_dev.alloc((size_t)p->ppseq * sizeof(int2));
-    }
-    // pageable source: the copy is staged before cudaMemcpyAsync returns
-    VKB_CUDA(cudaMemcpyAsync(p->pairs_dev.p, pairs.data(), pairs.size() * sizeof(int2), cudaMemcpyHostToDevice,
-                             p->ctx->stream));
-    dim3 grid((unsigned)pairs.size(), (unsigned)d.n_layer);
-    launch_pdl(p->ctx, kv_copy_pages_kernel, grid, 256, 0, p->pairs_dev.as<int2>(), p->n_pages, d.page_tokens, p->qrow,
-               p->hrow, p->srow_bytes(), p->kq.as<uint8_t>(), p->kd.as<uint8_t>(), p->kh.as<uint8_t>(),
-               p->vq.as<uint8_t>(), p->vd.as<uint8_t>(), p->vh.as<uint8_t>());
-    VKB_CUDA(cudaGetLastError());
-    p->ctx->count();
+    copy_pages(p, pairs);
 }
 
 static void zero_page(vkb_kv_pool* p, int32_t pid, int layer_for_seq) {
@@ -1012,6 +1051,13 @@ vkb_status vkb_kv_append_attention(vkb_kv_pool* pool, int32_t layer, const float
     });
 }
 
+vkb_status vkb_kv_copy_stream(vkb_kv_pool* pool, int32_t src, int32_t dst, int32_t n_pos) {
+    return guard([&] {
+        if (!pool) fail(VKB_ERROR_INVALID_ARGUMENT, "kv_copy_stream: null pool");
+        kv_copy_stream(pool, src, dst, n_pos);
+    });
+}
+
 int32_t vkb_kv_decode_fused(const vkb_kv_pool* pool) { return pool && kv_decode_fused(pool) ? 1 : 0; }
 
 vkb_status vkb_kv_release_seq(vkb_kv_pool* pool, int32_t seq_id) {
@@ -1023,7 +1069,7 @@ vkb_status vkb_kv_release_seq(vkb_kv_pool* pool, int32_t seq_id) {
         for (int i = 0; i < pool->ppseq; ++i) {
             int32_t& e = pool->table[(int64_t)seq_id * pool->ppseq + i];
             if (e >= 0) {
-                pool->free_list.push_back(e);
+                drop(pool, e);
                 e = -1;
             }
         }
@@ -1043,7 +1089,8 @@ vkb_status vkb_kv_release_layer(vkb_kv_pool* pool, int32_t layer) {
             int32_t& e = pool->table[(int64_t)layer * pool->ppl + i];
             if (e >= 0) {
                 zero_page(pool, e, 0);
-                pool->free_list.push_back(e);
+                pool->refs[e] = 1;
+                drop(pool, e);
                 e = -1;
             }
         }
@@ -1060,6 +1107,7 @@ vkb_status vkb_kv_reset(vkb_kv_pool* pool) {
             if (b->n) VKB_CUDA(cudaMemsetAsync(b->p, 0, b->n, st));
         pool->free_list.clear();
         for (int64_t i = pool->n_pages - 1; i >= 0; --i) pool->free_list.push_back((int32_t)i);
+        std::fill(pool->refs.begin(), pool->refs.end(), 0);
         pool->n_tok = 0;
         upload_table(pool);
     });
@@ -1082,8 +1130,10 @@ vkb_status vkb_kv_set_page_table(vkb_kv_pool* pool, const int32_t* table_host, s
         }
         pool->table.assign(table_host, table_host + len);
         pool->free_list.clear();
-        for (int64_t i = pool->n_pages - 1; i >= 0; --i)
+        for (int64_t i = pool->n_pages - 1; i >= 0; --i) {
+            pool->refs[i] = used[i] ? 1 : 0;
             if (!used[i]) pool->free_list.push_back((int32_t)i);
+        }
         upload_table(pool);
     });
 }

@@ -239,6 +239,10 @@ class QuantizedPagedKvCache:
     def release_layer(self, layer: int):
         check(_L.vkb_kv_release_layer(self.h, layer))
 
+    def copy_stream(self, src: int, dst: int, n_pos: int):
+        """dst := the first n_pos positions of src (filled pages shared, copy on write)."""
+        check(_L.vkb_kv_copy_stream(self.h, src, dst, n_pos))
+
     def release_seq(self, seq: int):
         check(_L.vkb_kv_release_seq(self.h, seq))
 
