@@ -305,6 +305,32 @@ def run_kernel_only(args):
     if args.kernel == "paged_decode":
         run_paged_decode(ctx, args)
         return
+    if args.kernel == "decode_step":
+        # one 64-stream decode step of the bench model at position ~100, alone between
+        # cudaProfilerStart/Stop (for ncu --profile-from-start off)
+        import torch
+        from vokra_b200 import whisper
+        arch = synth.WHISPER_LARGE_V3
+        path = ensure_model(model_path("large_v3_q4_0"), arch, synth.Q4_0)
+        model = whisper.WhisperModel(ctx, path)
+        B = args.clips
+        sess = whisper.Session(model, max_streams=B, max_step_tokens=B * PREFIX, max_clips=B, cross_kv_q8=True)
+        st = np.arange(B, dtype=np.int32)
+        sess.encode(torch.from_numpy(synthetic_logmels(B, arch.n_mels, 2 * arch.n_audio_ctx, 5)).cuda(), st)
+        sess.step(np.repeat(st, PREFIX), np.tile(np.arange(PREFIX, dtype=np.int32), B),
+                  np.tile(np.array(arch.start_ids[:PREFIX], np.int32), B))
+        ids = torch.zeros(B, dtype=torch.int32, device="cuda")
+        pos = PREFIX
+        for _ in range(96):
+            sess.step(st, np.full(B, pos, np.int32), np.full(B, 7, np.int32), ids_dev=ids)
+            pos += 1
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        sess.step(st, np.full(B, pos, np.int32), np.full(B, 7, np.int32), ids_dev=ids)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"kernel": args.kernel, "streams": B, "position": pos, "ok": True}))
+        return
     if args.precision == "f16":
         _lib.check(_lib.load().vkb_context_set_precision(ctx.h, _lib.PREC_F16))
     M = 1500 if args.kernel == "fc1_m1500" else args.clips * 1500
@@ -619,11 +645,12 @@ def main():
     ap.add_argument("--tokens", type=int, default=128)
     ap.add_argument("--precision", default="split", choices=["split", "f16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", default=None, choices=["fc1", "fc1_m1500", "xattn", "encoder", "paged_decode"],
+    ap.add_argument("--kernel", default=None, choices=["fc1", "fc1_m1500", "xattn", "encoder", "paged_decode", "decode_step"],
                     help="run only one kernel three times, for ncu: the encoder fc1 GEMM (M = clips x 1500, or "
                          "1500), the decode cross-attention over the Q8_0 store (clips streams x 1500 keys), or "
                          "the encoder of a one-layer model with large-v3's dimensions on 8 clips, or the fused decode "
-                         "self-attention over configs[2] (prints its own JSON line with the HBM roofline)")
+                         "self-attention over configs[2] (prints its own JSON line with the HBM roofline), or one "
+                         "64-stream decode step at position 100 between profiler start/stop")
     ap.add_argument("--sweep-formats", default="", help="sweep: comma-separated subset of q8_0,q4_0,q4_k")
     ap.add_argument("--sweep-m", default="", help="sweep: comma-separated M values")
     ap.add_argument("--sweep-shapes", default="", help="sweep: comma-separated KxN shapes, e.g. 1280x51866")
