@@ -143,17 +143,20 @@ def rank_input_seed(rank: int) -> int:
     return 1000 + rank
 
 
-def init_process_group(world: int, local_rank: int, backend: str):
-    """Joins the job's process group (torchrun's env:// rendezvous on 127.0.0.1)."""
+def init_process_group(world: int, local_rank: int, backend: str, timeout_s: float | None = None):
+    """Joins the job's process group (torchrun's env:// rendezvous on 127.0.0.1). With
+    timeout_s, a collective that a dead rank never joins fails after that long."""
+    import datetime
     import torch
     import torch.distributed as dist
     if world <= 1:
         return None
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    kw = {"timeout": datetime.timedelta(seconds=timeout_s)} if timeout_s else {}
     if backend == "nccl":
-        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"), **kw)
     else:
-        dist.init_process_group(backend)
+        dist.init_process_group(backend, **kw)
     return dist
 
 

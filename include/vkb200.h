@@ -118,6 +118,14 @@ VKB_API vkb_status vkb_context_set_precision(vkb_context* ctx, int precision);
  * crates/vokra-backend-cuda/src/context.rs:3152). */
 VKB_API uint64_t vkb_context_launch_count(const vkb_context* ctx);
 
+/* Failure-path self-test (no counterpart in the reference): launches one
+ * kernel whose mbarrier wait can never complete, bounded by `polls` polls
+ * (1..2^20), the same bounded wait every tensor-core pipeline stage of this
+ * library uses. The wait gives up, the kernel records the device error flag
+ * and returns; the call then reports VKB_ERROR_OTHER and clears the flag, and
+ * the context remains usable. No GPU fault, trap or hang is involved. */
+VKB_API vkb_status vkb_context_selftest_bounded_wait(vkb_context* ctx, uint32_t polls);
+
 /* ---- quantized Linear: Compute::gemm_q_f32 (compute.rs:943) ---------------- */
 
 /* Uploads an untransposed [n][k] GGUF weight payload (`bytes`, `len` host

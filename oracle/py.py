@@ -7,7 +7,7 @@ import os
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB = os.path.join(_HERE, "libvkb_oracle.so")
+LIB = os.environ.get("VKB_ORACLE_LIB") or os.path.join(_HERE, "libvkb_oracle.so")
 _l = None
 
 

@@ -77,3 +77,48 @@ def test_throughput_workload_shards():
     assert all(5 * 16000 <= u.n_samples <= 30 * 16000 and 32 <= u.n_new_tokens <= 224 for u in a)
     assert all(u.pcm_index == i % 64 for i, u in enumerate(a))
     assert abs(sa - sum(u.n_samples for u in a) / 16000) < 256 / 16000 + 1e-6
+
+
+def _dying_rank_main(rank, world, port, out_dir):
+    import sys
+    import time
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import bench
+    dist = bench.init_process_group(world, rank, "gloo", timeout_s=3.0)
+    dist.barrier()  # both ranks took part in the first step
+    if rank == 1:
+        os._exit(0)  # the shard dies between steps, with nothing in flight
+    t0 = time.time()
+    err = ""
+    try:
+        bench.max_over_ranks(10.0, dist, "cpu")  # the next step's max-over-ranks time
+    except Exception as e:  # the collective fails instead of waiting forever
+        err = type(e).__name__
+    waited = time.time() - t0
+    # the dead rank's utterances are a pure function of its rank: a surviving rank re-queues them
+    utts, _ = bench.throughput_utterances(64, 1, 16)
+    np.savez(os.path.join(out_dir, "survivor.npz"), err=err, waited=waited,
+             requeued=np.array([(u.n_samples, u.n_new_tokens) for u in utts]))
+    os._exit(0)
+
+
+def test_rank_death_is_detected_and_its_shard_requeued(tmp_path):
+    """A rank that leaves between steps (no kernel or collective in flight):
+    the survivor's next collective raises within the process-group timeout
+    instead of hanging, and the dead rank's share of utterances, seeded by its
+    rank, is rebuilt on the survivor unchanged."""
+    import torch.multiprocessing as mp
+    import bench
+    port = _free_port()
+    ctx = mp.start_processes(_dying_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=False,
+                             start_method="spawn")
+    for p in ctx.processes:
+        p.join(60)
+        assert not p.is_alive()
+    r = np.load(tmp_path / "survivor.npz")
+    assert str(r["err"]) != ""
+    assert float(r["waited"]) < 30.0
+    want, _ = bench.throughput_utterances(64, 1, 16)
+    assert np.array_equal(r["requeued"], np.array([(u.n_samples, u.n_new_tokens) for u in want]))

@@ -10,7 +10,8 @@ import ctypes as C
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libvkb200.so")
+# VKB_LIB_PATH selects another build of the same library (the sanitizer build)
+LIB_PATH = os.environ.get("VKB_LIB_PATH") or os.path.join(_HERE, "libvkb200.so")
 
 # Status codes (vkb_status == vokra_status_t numbering, include/vokra.h:58-78).
 OK = 0
@@ -107,6 +108,7 @@ SIGNATURES = {
     "vkb_kv_decode_fused": (I32, [P]),
     "vkb_gguf_inspect": (C.c_int, [P, SZ, P, P]),
     "vkb_kv_copy_stream": (C.c_int, [P, I32, I32, I32]),
+    "vkb_context_selftest_bounded_wait": (C.c_int, [P, U32]),
     "vkb_kv_release_seq": (C.c_int, [P, I32]),
     "vkb_kv_release_layer": (C.c_int, [P, I32]),
     "vkb_kv_reset": (C.c_int, [P]),

@@ -1369,6 +1369,19 @@ bool run_linear_q8_pair(vkb_context* ctx, const vkb_weight* w, int64_t m, const 
     return true;
 }
 
+// A wait that can never complete (an mbarrier nothing arrives at), bounded by
+// `polls` polls, exactly as every pipeline wait of the library is bounded: on
+// giving up it records the error flag and returns, and the context stays usable.
+__global__ void bounded_wait_selftest_kernel(int* err, uint32_t polls) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(&bar, 1);
+        ptx::fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && !ptx::mbar_wait(&bar, 0, polls)) atomicExch(err, 1);
+}
+
 int read_and_clear_err_flag(vkb_context* ctx) {
     int* f = device_err_flag(ctx);
     int h = 0;
@@ -1424,6 +1437,20 @@ vkb_status vkb_gemm_q_f32(vkb_context* ctx, int64_t m, int64_t n, int64_t k, con
         VKB_CUDA(cudaMemcpyAsync(out_host, o.p, o.n, cudaMemcpyDeviceToHost, ctx->stream));
         VKB_CUDA(cudaStreamSynchronize(ctx->stream));
         if (read_and_clear_err_flag(ctx)) fail(VKB_ERROR_OTHER, "gemm_q_f32: a pipeline wait timed out on the device");
+    });
+}
+
+vkb_status vkb_context_selftest_bounded_wait(vkb_context* ctx, uint32_t polls) {
+    return guard([&] {
+        if (!ctx) fail(VKB_ERROR_INVALID_ARGUMENT, "selftest_bounded_wait: null context");
+        if (polls == 0 || polls > (1u << 20)) fail(VKB_ERROR_INVALID_ARGUMENT, "selftest_bounded_wait: polls in 1..2^20");
+        VKB_CUDA(cudaSetDevice(ctx->device));
+        if (read_and_clear_err_flag(ctx)) fail(VKB_ERROR_OTHER, "selftest_bounded_wait: the error flag was already set");
+        bounded_wait_selftest_kernel<<<1, 32, 0, ctx->stream>>>(device_err_flag(ctx), polls);
+        VKB_CUDA(cudaGetLastError());
+        ctx->count();
+        if (read_and_clear_err_flag(ctx)) fail(VKB_ERROR_OTHER, "selftest_bounded_wait: the wait gave up after " +
+                                                                    std::to_string(polls) + " polls");
     });
 }
 
