@@ -646,7 +646,9 @@ def main():
     ap.add_argument("--impl", default="vkb", choices=["vkb", "reference"])
     ap.add_argument("--clips", type=int, default=64)
     ap.add_argument("--tokens", type=int, default=128)
-    ap.add_argument("--precision", default="split", choices=["split", "f16"])
+    ap.add_argument("--precision", default="enc_f16", choices=["split", "f16", "enc_f16"],
+                    help="split: hi+lo f16 operands everywhere; enc_f16: single-f16 operands in the encoder "
+                         "(VKB_PREC_ENCODER_F16), split in the decoder; f16: single f16 everywhere")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", default=None, choices=["fc1", "fc1_m1500", "xattn", "encoder", "paged_decode", "decode_step"],
                     help="run only one kernel three times, for ncu: the encoder fc1 GEMM (M = clips x 1500, or "
@@ -700,8 +702,8 @@ def main():
     barrier()
 
     ctx = ops.Context(local_rank)
-    if args.precision == "f16":
-        _lib.check(_lib.load().vkb_context_set_precision(ctx.h, _lib.PREC_F16))
+    prec = {"split": _lib.PREC_SPLIT, "f16": _lib.PREC_F16, "enc_f16": _lib.PREC_ENCODER_F16}[args.precision]
+    _lib.check(_lib.load().vkb_context_set_precision(ctx.h, prec))
     model = whisper.WhisperModel(ctx, path)
     B, NT = args.clips, args.tokens
     sess = whisper.Session(model, max_streams=B, max_step_tokens=B * PREFIX, max_clips=B, cross_kv_q8=True)
@@ -813,7 +815,8 @@ def main():
     prof = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(prof):
         try:
-            roofline["traffic"] = json.load(open(prof)).get("tc_gemm_fc1_bytes_per_launch")
+            key = "tc_gemm_fc1_bytes_per_launch" if planes == 2 else "tc_gemm_fc1_f16_bytes_per_launch"
+            roofline["traffic"] = json.load(open(prof)).get(key)
         except Exception:
             pass
 
@@ -855,8 +858,10 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "f16 hi+lo tensor-core operands, fp32 accumulate (Q4_0 weights, Q8_0 KV)"
-            if planes == 2 else "f16 (Q4_0 weights, Q8_0 KV)",
+            "dtype": {"split": "f16 hi+lo tensor-core operands, fp32 accumulate (Q4_0 weights, Q8_0 KV)",
+                      "enc_f16": "encoder: f16 tensor-core operands, fp32 accumulate; decoder: f16 hi+lo "
+                                 "operands, fp32 accumulate (Q4_0 weights, Q8_0 KV)",
+                      "f16": "f16 (Q4_0 weights, Q8_0 KV)"}[args.precision],
             "data": "synthetic",
             "config": {"workload": "configs[3]: whisper-large-v3 q4_0, 64 clips x 30 s per GPU, log-mel frontend + "
                                    "encoder + 4-token "

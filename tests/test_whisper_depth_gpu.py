@@ -265,3 +265,48 @@ def test_fused_decode_attention_long_contexts(ctx, tmp_path):
     fused.check()
     sess.close()
     model.close()
+
+
+def test_large_v3_full_depth_q4_0(ctx, tmp_path):
+    """Whisper-large-v3 at full depth (32 encoder + 32 decoder layers, 20 heads,
+    51866-token vocabulary) in Q4_0, one 30 s clip through the frontend, 12
+    teacher-forced tokens, f32 self-KV and the Q8_0 cross store, against the
+    reference decoder's f32 caches: the full budget in the default split
+    precision and with the encoder on single-f16 operands
+    (VKB_PREC_ENCODER_F16, the bench's mode)."""
+    import torch
+    from vokra_b200 import _lib, ops, whisper
+    L = _lib.load()
+    arch = synth.WHISPER_LARGE_V3
+    path = str(tmp_path / "large_v3_q4_0.gguf")
+    synth.write_synthetic_whisper(path, arch, synth.Q4_0, seed=12)
+    ref = whisper_ref.RefWhisper(path)
+    pcm = synth.synthetic_audio(40)
+    ref_enc = ref.encode(o.log_mel(pcm, arch.n_mels))
+    toks = [int(t) for t in np.random.default_rng(40).integers(0, arch.n_vocab, 12)]
+    dec = ref.decoder(ref_enc, "f32", "f32")
+    refs = [dec.step(list(arch.start_ids))] + [dec.step([t]) for t in toks]
+    del ref, dec
+    model = whisper.WhisperModel(ctx, path)
+    try:
+        for prec, name in ((_lib.PREC_SPLIT, "split"), (_lib.PREC_ENCODER_F16, "encoder f16")):
+            _lib.check(L.vkb_context_set_precision(ctx.h, prec))
+            sess = whisper.Session(model, max_streams=1, max_clips=1, self_kv=_lib.SELF_KV_F32)
+            sess.encode(ops.log_mel(ctx, torch.from_numpy(pcm[None]).cuda(), arch.n_mels), [0])
+            enc = sess.encoder_output(1)[0]
+            b = Budget()
+            P = len(arch.start_ids)
+            out = torch.zeros((P, arch.n_vocab), device="cuda")
+            sess.step([0] * P, list(range(P)), list(arch.start_ids), logits_dev=out)
+            b.add(out.cpu().numpy(), refs[0])
+            out1 = torch.zeros((1, arch.n_vocab), device="cuda")
+            for i, t in enumerate(toks):
+                sess.step([0], [P + i], [t], logits_dev=out1)
+                b.add(out1.cpu().numpy(), refs[i + 1])
+            print(f"large-v3 32+32 q4_0, {name}: encoder output rel-rms {_rel_rms(enc, ref_enc):.2e}")
+            b.report(f"large-v3 32+32 q4_0, {name}, f32 self-KV")
+            b.check()
+            sess.close()
+    finally:
+        _lib.check(L.vkb_context_set_precision(ctx.h, _lib.PREC_SPLIT))
+        model.close()

@@ -37,7 +37,7 @@ GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0, GGML_Q4_K, GGML_Q5_K, GGML_Q6_K, GGML_
 # KvQuant
 KV_FP32, KV_Q4_0, KV_Q5_0, KV_Q8_0 = 0, 1, 2, 3
 DT_F32, DT_F16, DT_F16X2 = 0, 1, 2
-PREC_SPLIT, PREC_F16 = 0, 1
+PREC_SPLIT, PREC_F16, PREC_ENCODER_F16 = 0, 1, 2
 EPI_NONE, EPI_GELU, EPI_RESIDUAL, EPI_SCALE = 0, 1, 2, 3
 KV_LAYOUT_REFERENCE, KV_LAYOUT_SEQUENCE = 0, 1
 

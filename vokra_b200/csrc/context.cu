@@ -79,7 +79,7 @@ vkb_status vkb_context_synchronize(vkb_context* ctx) {
 vkb_status vkb_context_set_precision(vkb_context* ctx, int precision) {
     return guard([&] {
         if (!ctx) fail(VKB_ERROR_INVALID_ARGUMENT, "set_precision: null context");
-        if (precision != VKB_PREC_SPLIT && precision != VKB_PREC_F16)
+        if (precision != VKB_PREC_SPLIT && precision != VKB_PREC_F16 && precision != VKB_PREC_ENCODER_F16)
             fail(VKB_ERROR_INVALID_ARGUMENT, "set_precision: unknown precision");
         ctx->precision = precision;
     });

@@ -1243,7 +1243,7 @@ LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m, b
 }
 
 LinearPlan plan_linear(const vkb_context* ctx, const vkb_weight* w, int64_t m) {
-    return plan_linear(ctx, w, m, ctx->precision == VKB_PREC_SPLIT);
+    return plan_linear(ctx, w, m, ctx->precision != VKB_PREC_F16);
 }
 
 void run_linear(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_dtype, const float* bias,
@@ -1268,7 +1268,7 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
     if (x.col_block > 0 && out_dtype == VKB_DT_F16X2)
         fail(VKB_ERROR_INVALID_ARGUMENT, "linear: a column-block layout needs an f32 or f16 output");
     // A single f16 activation plane carries no low part: the GEMM then runs unsplit.
-    const bool split = ctx->precision == VKB_PREC_SPLIT && a_dtype != VKB_DT_F16;
+    const bool split = ctx->precision != VKB_PREC_F16 && a_dtype != VKB_DT_F16;
     LinearPlan p = plan_linear(ctx, w, m, split);
     const int64_t out_rows = x.out_rows > 0 ? x.out_rows : m;
     Epi e{bias, residual, out, out_dtype, epilogue, scale, w->n,
@@ -1345,7 +1345,7 @@ bool run_linear_q8_pair(vkb_context* ctx, const vkb_weight* w, int64_t m, const 
     if (pv && pv[0] == '0') return false;
     const char* fq = std::getenv("VKB_FUSED_CROSS_Q8");
     if (fq && fq[0] == '0') return false;
-    if (ctx->precision != VKB_PREC_SPLIT || m <= 0 || w->n != 2 * width || width % TILE_N || w->n_pad != w->n)
+    if (ctx->precision == VKB_PREC_F16 || m <= 0 || w->n != 2 * width || width % TILE_N || w->n_pad != w->n)
         return false;
     if (plan_linear(ctx, w, m, true).splits != 1) return false;
     PEpi pe;

@@ -381,6 +381,14 @@ void session_encode(vkb_session* s, int n, const float* logmel, const int32_t* s
         if (streams[i] < 0 || streams[i] >= s->opt.max_streams)
             fail(VKB_ERROR_INVALID_ARGUMENT, "session_encode: stream id out of range");
     const int64_t d = D.d_model, f = D.ffn_dim, T = D.n_audio_ctx, Tin = 2 * T, M = (int64_t)n * T;
+    // VKB_PREC_ENCODER_F16: the whole encode (conv stem, encoder, cross K/V
+    // projections) runs single-f16 operands; the context's mode comes back after
+    struct PrecisionScope {
+        vkb_context* c;
+        int saved;
+        ~PrecisionScope() { c->precision = saved; }
+    } scope{ctx, ctx->precision};
+    if (ctx->precision == VKB_PREC_ENCODER_F16) ctx->precision = VKB_PREC_F16;
     float* ws = s->ws.as<float>();
     __half* bufA = s->bufA.as<__half>();
     __half* bufB = s->bufB.as<__half>();
@@ -527,7 +535,7 @@ void session_step(vkb_session* s, int n_tok, const int32_t* streams, const int32
         float* qc = s->qc.as<float>();
         __half* ffn = s->ffn.as<__half>();
         float* ws = s->ws.as<float>();
-        const int AF = ctx->precision == VKB_PREC_SPLIT ? VKB_DT_F16X2 : VKB_DT_F16;
+        const int AF = ctx->precision != VKB_PREC_F16 ? VKB_DT_F16X2 : VKB_DT_F16;
         run_embed(ctx, m->tok_emb.get(), s->tok.as<int32_t>(), s->pos.as<int32_t>(), n_tok, m->dec_pos.as<float>(), h);
         const float scale = 1.0f / sqrtf((float)(d / D.n_text_head));
         const int64_t rows = (int64_t)s->opt.max_streams * T;
