@@ -163,3 +163,13 @@ def test_streaming_gemv_wide_weight(ctx, tag, m):
     got, ref = _run(ctx, tag, 16500, 512, m, seed=21 + m)
     assert _rel_rms(got, ref) <= 1e-5
     assert np.max(np.abs(got - ref)) <= 1e-4 * max(1.0, np.max(np.abs(ref)))
+
+
+@pytest.mark.parametrize("tag", [synth.Q4_0, synth.Q8_0, synth.Q4_K])
+def test_persistent_gemm_single_f16(ctx, tag):
+    """Large M with a single f16 activation plane (the encoder in
+    VKB_PREC_ENCODER_F16): the persistent kernel at one MMA per K step;
+    weights rounded to f16 once, so 2e-3 relative RMS like the other f16 path."""
+    got, ref = _run(ctx, tag, 1300, 1280, 12000, seed=13, a_f16=True)
+    assert _rel_rms(got, ref) <= 2e-3
+    assert np.max(np.abs(got - ref)) <= 3e-2

@@ -1,5 +1,6 @@
 // gemm_persist.cu — persistent tcgen05 GEMM for the large-M Linear layers of
-// the encoder (M = clips x 1500 tokens), split precision (W_hi/W_lo x X_hi/X_lo).
+// the encoder (M = clips x 1500 tokens), split precision (W_hi/W_lo x X_hi/X_lo)
+// or, with SPLIT = false, single f16 operands (one MMA per K=16 step).
 //
 // Same product as tc_gemm_kernel's non-stacked split mode (three MMAs per
 // K=16 step: W_hi.X_hi + W_hi.X_lo + W_lo.X_hi, weights dequantized into
@@ -29,16 +30,18 @@
 
 namespace vkb {
 
-template <int FMT>
+template <int FMT, bool SPLIT = true>
 struct PCfg {
     static constexpr int BN = 192;                          // tokens per tile
+    static constexpr int NP = SPLIT ? 2 : 1;                // activation planes (hi, lo)
     static constexpr int B_BYTES = BN * 128;                // one activation plane per stage
     static constexpr int RAW_Q = stage_qs_bytes(FMT);
     static constexpr int RAW_S = stage_sc_bytes(FMT);
     static constexpr int RAW_BYTES = ((RAW_Q + RAW_S) + 1023) / 1024 * 1024;
-    static constexpr int STAGE_BYTES = 2 * B_BYTES + RAW_BYTES;
+    static constexpr int STAGE_BYTES = NP * B_BYTES + RAW_BYTES;
     static constexpr int S0 = (225 * 1024 - 2048) / STAGE_BYTES;
-    static constexpr int S = S0 > 4 ? 4 : S0;
+    static constexpr int SMAX = SPLIT ? 4 : 6;
+    static constexpr int S = S0 > SMAX ? SMAX : S0;
     static constexpr int SMEM = 1024 + S * STAGE_BYTES + 1024;
     static constexpr int AS = 2;
     static constexpr int A_COL0 = 2 * BN;
@@ -110,12 +113,12 @@ __device__ __forceinline__ int64_t q8_row(const PEpi& e, int64_t m) {
     return (int64_t)e.row_map[g] * e.row_group + ((unsigned)m - g * (unsigned)e.row_group);
 }
 
-template <int FMT>
-__global__ void __launch_bounds__(PCfg<FMT>::THREADS, 1)
+template <int FMT, bool SPLIT>
+__global__ void __launch_bounds__(PCfg<FMT, SPLIT>::THREADS, 1)
     tc_gemm_persist_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_lo,
                            const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc, int64_t K, int64_t N,
                            int64_t M, int n_tiles, int total_tiles, PEpi e, int* err) {
-    using C = PCfg<FMT>;
+    using C = PCfg<FMT, SPLIT>;
     constexpr int BN = C::BN, S = C::S, AS = C::AS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -163,9 +166,9 @@ __global__ void __launch_bounds__(PCfg<FMT>::THREADS, 1)
     if (warp == 0) {
         if (lane == 0) {
             auto load_weights = [&](int s, int n_tile, int i) {
-                uint8_t* raw_dst = ring + s * C::STAGE_BYTES + 2 * C::B_BYTES;
+                uint8_t* raw_dst = ring + s * C::STAGE_BYTES + C::NP * C::B_BYTES;
                 StagePtrs p = stage_ptrs(FMT, qs, sc, K, n_tile, i);
-                ptx::mbar_expect_tx(&full[s], 2 * C::B_BYTES + C::RAW_Q + C::RAW_S);
+                ptx::mbar_expect_tx(&full[s], C::NP * C::B_BYTES + C::RAW_Q + C::RAW_S);
                 ptx::bulk_load(raw_dst, p.qs, C::RAW_Q, &full[s]);
                 if (C::RAW_S) ptx::bulk_load(raw_dst + C::RAW_Q, p.sc, C::RAW_S, &full[s]);
             };
@@ -186,7 +189,7 @@ __global__ void __launch_bounds__(PCfg<FMT>::THREADS, 1)
                     }
                     uint8_t* b_dst = ring + s * C::STAGE_BYTES;
                     ptx::tma_load_2d(b_dst, &xmap, &full[s], i * STAGE_K, m_tile * BN);
-                    ptx::tma_load_2d(b_dst + C::B_BYTES, &xmap_lo, &full[s], i * STAGE_K, m_tile * BN);
+                    if (SPLIT) ptx::tma_load_2d(b_dst + C::B_BYTES, &xmap_lo, &full[s], i * STAGE_K, m_tile * BN);
                 }
             }
         }
@@ -214,10 +217,12 @@ __global__ void __launch_bounds__(PCfg<FMT>::THREADS, 1)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint64_t bd = ptx::sdesc_sw128(b_addr + kk * 32);
-                        const uint64_t bd_lo = ptx::sdesc_sw128(b_addr + C::B_BYTES + kk * 32);
                         ptx::mma_f16_ts(d_t, a_t + kk * 8, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-                        ptx::mma_f16_ts(d_t, a_t + kk * 8, bd_lo, idesc, 1u);
-                        ptx::mma_f16_ts(d_t, a_t + 32 + kk * 8, bd, idesc, 1u);
+                        if (SPLIT) {
+                            const uint64_t bd_lo = ptx::sdesc_sw128(b_addr + C::B_BYTES + kk * 32);
+                            ptx::mma_f16_ts(d_t, a_t + kk * 8, bd_lo, idesc, 1u);
+                            ptx::mma_f16_ts(d_t, a_t + 32 + kk * 8, bd, idesc, 1u);
+                        }
                     }
                     ptx::mma_commit(&empty[s]);
                     ptx::mma_commit(&a_empty[a]);
@@ -238,13 +243,13 @@ __global__ void __launch_bounds__(PCfg<FMT>::THREADS, 1)
                     ok = false;
                     break;
                 }
-                const uint8_t* raw = ring + s * C::STAGE_BYTES + 2 * C::B_BYTES;
+                const uint8_t* raw = ring + s * C::STAGE_BYTES + C::NP * C::B_BYTES;
                 const uint32_t a_t = tmem + ((uint32_t)(quarter * 32) << 16) + C::A_COL0 + a * 64;
                 uint32_t hi[32], lo[32];
-                dequant_row_stage_h<FMT, true>(raw, raw + C::RAW_Q, r, i, hi, lo);
+                dequant_row_stage_h<FMT, SPLIT>(raw, raw + C::RAW_Q, r, i, hi, lo);
                 ptx::tc_fence_after();
                 ptx::tmem_st32(a_t, hi);
-                ptx::tmem_st32(a_t + 32, lo);
+                if (SPLIT) ptx::tmem_st32(a_t + 32, lo);
                 ptx::tmem_st_wait();
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(&a_full[a]);
@@ -358,26 +363,31 @@ __global__ void __launch_bounds__(PCfg<FMT>::THREADS, 1)
 
 int persist_bn() { return PCfg<W_Q4_0>::BN; }
 
-template <int FMT>
+template <int FMT, bool SPLIT>
 static void launch_persist(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e,
                            int* err) {
-    using C = PCfg<FMT>;
-    smem_optin(tc_gemm_persist_kernel<FMT>, C::SMEM);
+    using C = PCfg<FMT, SPLIT>;
+    smem_optin(tc_gemm_persist_kernel<FMT, SPLIT>, C::SMEM);
     CUtensorMap map, map_lo;
     make_tmap_f16(&map, a16, m, w->k, C::BN);
-    make_tmap_f16(&map_lo, a16 + m * w->k, m, w->k, C::BN);
+    if (SPLIT) make_tmap_f16(&map_lo, a16 + m * w->k, m, w->k, C::BN);
+    else map_lo = map;
     const int n_tiles = (int)(w->n_pad / TILE_N);
     const int m_tiles = (int)((m + C::BN - 1) / C::BN);
     const int total = n_tiles * m_tiles;
     const int grid = std::min(total, ctx->sm_count);
-    launch_pdl(ctx, tc_gemm_persist_kernel<FMT>, grid, C::THREADS, C::SMEM, map, map_lo, w->qs.as<uint8_t>(),
+    launch_pdl(ctx, tc_gemm_persist_kernel<FMT, SPLIT>, grid, C::THREADS, C::SMEM, map, map_lo, w->qs.as<uint8_t>(),
                w->sc.as<uint8_t>(), w->k, w->n, m, n_tiles, total, e, err);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
 }
 
-void run_tc_persistent(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e, int* err) {
-    with_fmt(w->fmt, [&](auto F) { launch_persist<decltype(F)::value>(ctx, w, m, a16, e, err); });
+void run_tc_persistent(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e, int* err,
+                       bool split) {
+    with_fmt(w->fmt, [&](auto F) {
+        if (split) launch_persist<decltype(F)::value, true>(ctx, w, m, a16, e, err);
+        else launch_persist<decltype(F)::value, false>(ctx, w, m, a16, e, err);
+    });
 }
 
 }  // namespace vkb

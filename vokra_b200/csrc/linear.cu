@@ -1309,7 +1309,8 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
         const char* pv = std::getenv("VKB_GEMM_PERSIST");
         const bool p_off = pv && pv[0] == '0', p_force = pv && pv[0] == 'f';
         const int64_t p_tiles = (w->n_pad / TILE_N) * ((m + persist_bn() - 1) / persist_bn());
-        if (!p_off && p.split && p.splits == 1 && x.col_block == 0 && !x.row_map &&
+        // (single-f16 operands: not for the residual projections, measured faster on the classic kernel)
+        if (!p_off && p.splits == 1 && x.col_block == 0 && !x.row_map && (p.split || epilogue != VKB_EPI_RESIDUAL) &&
             (p_force || (p_tiles >= 4 * (int64_t)ctx->sm_count && w->k <= 20 * STAGE_K))) {
             PEpi pe;
             pe.bias = bias;
@@ -1321,7 +1322,7 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
             pe.ldo = w->n;
             pe.n_scaled = e.n_scaled;
             pe.plane = e.plane;
-            run_tc_persistent(ctx, w, m, a16, pe, device_err_flag(ctx));
+            run_tc_persistent(ctx, w, m, a16, pe, device_err_flag(ctx), p.split);
         } else if (p.split) {
             dispatch_fmt<true>(ctx, w, m, a16, e, ws, p);
         } else {

@@ -72,7 +72,8 @@ struct PEpi {
 };
 // Split-precision (hi+lo) GEMM over f16 activation planes a16 [2][m][k], one
 // CTA per SM over a static tile list; token tile persist_bn().
-void run_tc_persistent(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e, int* err);
+void run_tc_persistent(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e, int* err,
+                       bool split = true);
 int persist_bn();
 // out = Q8_0(a . W^T + bias) split into a K and a V store (see PEpi::q8_width)
 // on the persistent kernel; false (nothing launched) when the shape or
