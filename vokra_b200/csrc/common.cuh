@@ -15,6 +15,7 @@
 #include <stdexcept>
 
 #include "../../include/vkb200.h"
+#include <nvtx3/nvToolsExt.h>
 
 namespace vkb {
 
@@ -126,6 +127,16 @@ struct vkb_context {
 };
 
 namespace vkb {
+
+// NVTX range for the duration of a scope (header-only NVTX 3: a no-op unless a
+// profiler attaches): one per kernel family at the entry points, so a timeline
+// shows the log-mel frontend, the encoder, the decode step and each Linear.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 constexpr int kTileCounters = 1 << 16;  // weight tiles a split-K GEMV launch may count (N <= 8M rows)
 

@@ -245,6 +245,7 @@ extern "C" {
 vkb_status vkb_log_mel(vkb_context* ctx, const float* pcm_dev, int64_t n_clips, int64_t stride,
                        const int32_t* lengths_dev, int32_t n_mels, float* out_dev) {
     return guard([&] {
+        NvtxRange nvtx_range("vkb.log_mel");
         if (!ctx || !out_dev) fail(VKB_ERROR_INVALID_ARGUMENT, "log_mel: null context or output");
         if (n_clips <= 0 || n_clips > 65535) fail(VKB_ERROR_INVALID_ARGUMENT, "log_mel: n_clips must be in 1..65535");
         if (stride < 0) fail(VKB_ERROR_INVALID_ARGUMENT, "log_mel: negative stride");

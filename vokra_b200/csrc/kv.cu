@@ -731,6 +731,7 @@ bool kv_decode_fused(const vkb_kv_pool* p) {
 // the projection's split-K partials with its bias and q scale.
 void kv_append_attention_ex(vkb_kv_pool* p, int layer, const float* qkv, int64_t ld, void* out, int out_dtype,
                             const float* part, int splits, const float* bias, float qscale) {
+    NvtxRange nvtx_range("vkb.kv.append_attention");
     const auto& d = p->d;
     if (layer < 0 || layer >= d.n_layer) fail(VKB_ERROR_INVALID_ARGUMENT, "decode attention: layer out of range");
     if (out_dtype != VKB_DT_F32 && out_dtype != VKB_DT_F16 && out_dtype != VKB_DT_F16X2)

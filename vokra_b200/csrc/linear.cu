@@ -1256,6 +1256,7 @@ void run_linear(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a,
 void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void* a, int a_dtype, const float* bias,
                    void* out, int out_dtype, int epilogue, const float* residual, float scale, float* ws_override,
                    __half* a16_override, const LinearExtra& x) {
+    NvtxRange nvtx_range(m <= gemv_max_m() ? "vkb.linear.small_m" : "vkb.linear.gemm");
     if (m <= 0) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: m must be positive");
     if (!a || !out) fail(VKB_ERROR_INVALID_ARGUMENT, "linear: null activation or output pointer");
     if (a_dtype != VKB_DT_F32 && a_dtype != VKB_DT_F16 && a_dtype != VKB_DT_F16X2)

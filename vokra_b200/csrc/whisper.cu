@@ -372,6 +372,7 @@ vkb_session* create_session(vkb_whisper* m, const vkb_session_options* o) {
 
 // Encoder forward of n clips plus the cross K/V projection into stream slots.
 void session_encode(vkb_session* s, int n, const float* logmel, const int32_t* streams) {
+    NvtxRange nvtx_range("vkb.session_encode");
     vkb_whisper* m = s->m;
     vkb_context* ctx = s->ctx;
     const auto& D = m->dims;
@@ -476,6 +477,7 @@ __global__ void feed_tokens_kernel(int32_t* tok, const int32_t* __restrict__ row
 void session_step(vkb_session* s, int n_tok, const int32_t* streams, const int32_t* positions, const int32_t* tokens,
                   float* logits_out, int32_t* ids_out, const int32_t* feed_rows = nullptr,
                   const int32_t* feed_ids = nullptr) {
+    NvtxRange nvtx_range("vkb.session_step");
     vkb_whisper* m = s->m;
     vkb_context* ctx = s->ctx;
     const auto& D = m->dims;
