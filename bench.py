@@ -437,9 +437,9 @@ def run_sweep(args):
     for fname, (tag, bw) in fmts.items():
         if fname not in only:
             continue
-        for (K, N) in SWEEP_SHAPES:
-            if args.sweep_shapes and f"{K}x{N}" not in args.sweep_shapes.split(","):
-                continue
+        shapes = ([tuple(int(v) for v in x.split("x")) for x in args.sweep_shapes.split(",")]
+                  if args.sweep_shapes else SWEEP_SHAPES)
+        for (K, N) in shapes:
             rng = np.random.default_rng(K * 7 + N)
             wq = synth.quantize(tag, rng.standard_normal(N * K, dtype=np.float32) * np.float32(0.02))
             copies = int(min(200, max(2, np.ceil(300e6 / (N * K * bw)))))

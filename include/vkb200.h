@@ -122,6 +122,10 @@ VKB_API vkb_status vkb_context_set_precision(vkb_context* ctx, int precision);
 /* Number of kernels this context has launched (CudaContext::submission_count,
  * crates/vokra-backend-cuda/src/context.rs:3152). */
 VKB_API uint64_t vkb_context_launch_count(const vkb_context* ctx);
+/* Bytes of device scratch the context holds for calls that size their own
+ * workspace (it only grows); vkb_attention_dense_noalloc never touches it.
+ * No counterpart in the reference (a diagnostics accessor). */
+VKB_API size_t vkb_context_workspace_bytes(const vkb_context* ctx);
 
 /* Failure-path self-test (no counterpart in the reference): launches one
  * kernel whose mbarrier wait can never complete, bounded by `polls` polls

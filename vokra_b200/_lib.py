@@ -91,6 +91,7 @@ SIGNATURES = {
     "vkb_context_set_stream": (C.c_int, [P, P]),
     "vkb_context_synchronize": (C.c_int, [P]),
     "vkb_context_launch_count": (U64, [P]),
+    "vkb_context_workspace_bytes": (SZ, [P]),
     "vkb_context_set_precision": (C.c_int, [P, C.c_int]),
     "vkb_weight_upload": (C.c_int, [P, U32, I64, I64, P, SZ, PP]),
     "vkb_weight_destroy": (C.c_int, [P]),

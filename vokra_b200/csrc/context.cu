@@ -86,5 +86,6 @@ vkb_status vkb_context_set_precision(vkb_context* ctx, int precision) {
 }
 
 uint64_t vkb_context_launch_count(const vkb_context* ctx) { return ctx ? ctx->launches : 0; }
+size_t vkb_context_workspace_bytes(const vkb_context* ctx) { return ctx ? ctx->workspace.n : 0; }
 
 }  // extern "C"

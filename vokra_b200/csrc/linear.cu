@@ -790,6 +790,9 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
     if (warp == 0) {
         if (lane == 0) {
             // weights of the first ring stages, then wait for the previous kernel
+            ptx::prefetch_tmap(&xmap);
+            if (SPLIT) ptx::prefetch_tmap(&xmap_lo);
+            if (tma_epi) ptx::prefetch_tmap(&omap);
             const int pre = nst < C::S ? nst : C::S;
             for (int i = 0; i < pre; ++i) {
                 uint8_t* raw_dst = st_ring + i * C::STAGE_BYTES + C::NP * C::B_BYTES;
