@@ -408,6 +408,50 @@ def run_paged_decode(ctx, args):
                       "keys": keys, "algorithmic_bytes": alg, "us_per_launch": round(ms * 1e3, 2),
                       "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
                                    "frac": round(gbs / hbm, 4), "peak_kind": peak_kind}}), flush=True)
+    # the cross-attention half of configs[2]: one query per sequence over its dense 1500 x 1280 K/V,
+    # in the Q8_0 store the session keeps (the bench default) and in the f16 store
+    del pool, flush
+    n_ctx = 1500
+    seq = torch.arange(n_seq, dtype=torch.int32, device="cuda")
+    q = torch.randn((n_seq, W), device="cuda", generator=g) * D ** -0.5
+    for store in ("q8_0", "f16"):
+        if store == "q8_0":
+            kq = torch.empty((n_seq * n_ctx, W), dtype=torch.int8, device="cuda")
+            vq = torch.empty_like(kq)
+            kd = torch.empty((n_seq * n_ctx, W // 32), dtype=torch.float16, device="cuda")
+            vd = torch.empty_like(kd)
+            for q8, dd in ((kq, kd), (vq, vd)):
+                for r0 in range(0, n_seq * n_ctx, 96000):
+                    r1 = min(n_seq * n_ctx, r0 + 96000)
+                    ops.quantize_rows_q8_0(ctx, torch.randn((r1 - r0, W), device="cuda", generator=g), q8[r0:r1],
+                                           dd[r0:r1])
+            call = lambda: ops.attention_dense(ctx, q, seq, kq, vq, n_ctx, H, D, out, k_scale=kd, v_scale=vd)
+            kv_bytes = n_seq * n_ctx * 2 * (W + W // 16)
+        else:
+            kq = torch.randn((n_seq * n_ctx, W), device="cuda", generator=g).half()
+            vq = torch.randn((n_seq * n_ctx, W), device="cuda", generator=g).half()
+            call = lambda: ops.attention_dense(ctx, q, seq, kq, vq, n_ctx, H, D, out)
+            kv_bytes = n_seq * n_ctx * 2 * W * 2
+        for _ in range(3):
+            call()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        e0.record(stream)
+        for _ in range(reps):
+            call()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_x = e0.elapsed_time(e1) / reps
+        alg_x = kv_bytes + 2 * n_seq * W * 4
+        gbs_x = alg_x / (ms_x / 1e3) / 1e9
+        print(json.dumps({"kernel": f"cross-attention over the dense {store} store (vkb_attention_dense)",
+                          "workload": f"configs[2] cross half: 256 sequences x 1500 keys, 20 heads x 64, {store} "
+                                      "K/V (> L2, read once per launch)",
+                          "algorithmic_bytes": alg_x, "us_per_launch": round(ms_x * 1e3, 2),
+                          "roofline": {"bound": "hbm", "achieved": round(gbs_x, 1), "peak": hbm, "unit": "GB/s",
+                                       "frac": round(gbs_x / hbm, 4), "peak_kind": peak_kind}}), flush=True)
+        del kq, vq
 
 
 SWEEP_SHAPES = [(1280, 1280), (1280, 5120), (5120, 1280), (1280, 51866)]  # (K, N)

@@ -396,7 +396,8 @@ static void check_heads(int n_head, int d_head) {
 // Dense attention (cross-attention): launch helper shared with the session.
 void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, const float* q, const int32_t* seq_of_tok,
                          const void* k, const void* v, const void* k_scale, const void* v_scale, int n_ctx,
-                         int kv_fmt, void* out, int out_dtype, float* ws_override, size_t ws_cap_floats) {
+                         int kv_fmt, void* out, int out_dtype, float* ws_override, size_t ws_cap_floats,
+                         bool kv_ready) {
     check_heads(n_head, d_head);
     const int W = n_head * d_head;
     if (kv_fmt != VKB_DT_F16) {
@@ -409,7 +410,8 @@ void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, co
                 ctx->ensure_workspace(xp.ws_floats * sizeof(float));
                 ws = ctx->workspace.as<float>();
             }
-            run_xattn_q8(ctx, xp, n_tok, n_head, n_ctx, q, seq_of_tok, k, v, k_scale, v_scale, out, out_dtype, ws);
+            run_xattn_q8(ctx, xp, n_tok, n_head, n_ctx, q, seq_of_tok, k, v, k_scale, v_scale, out, out_dtype, ws,
+                         kv_ready);
             return;
         }
     }

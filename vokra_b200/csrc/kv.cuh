@@ -21,7 +21,8 @@ void kv_copy_stream(vkb_kv_pool* p, int src, int dst, int n_pos);
 void kv_attention_ex(vkb_kv_pool* p, int layer, const float* q, int64_t q_ld, void* out, int out_dtype);
 void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, const float* q, const int32_t* seq_of_tok,
                          const void* k, const void* v, const void* k_scale, const void* v_scale, int n_ctx,
-                         int kv_fmt, void* out, int out_dtype, float* ws_override, size_t ws_cap_floats = 0);
+                         int kv_fmt, void* out, int out_dtype, float* ws_override, size_t ws_cap_floats = 0,
+                         bool kv_ready = false);
 void run_quantize_rows(vkb_context* ctx, const float* x, int64_t ld, int64_t n_rows, int W, int8_t* q, __half* d,
                        const int32_t* map, int group);
 }  // namespace vkb

@@ -555,6 +555,9 @@ void session_step(vkb_session* s, int n_tok, const int32_t* streams, const int32
         };
         run_layer_norm(ctx, h, n_tok, (int)d, m->dec[0].ln1g.as<float>(), m->dec[0].ln1b.as<float>(), LN_EPS, xln,
                        AF);
+        // the cross store is written by the encoder and the step starts with host copies (a full
+        // barrier), so the cross-attention may fill its ring before the query projection ends
+        static const bool xa_early = [] { const char* v = std::getenv("VKB_XA_EARLY"); return !v || v[0] != '0'; }();
         for (int l = 0; l < D.n_text_layer; ++l) {
             const DecLayer& L = m->dec[l];
             LinearExtra x;
@@ -577,7 +580,7 @@ void session_step(vkb_session* s, int n_tok, const int32_t* streams, const int32
                                     s->ck.as<int8_t>() + (size_t)l * rows * d, s->cv.as<int8_t>() + (size_t)l * rows * d,
                                     s->cks.as<__half>() + (size_t)l * rows * (d / 32),
                                     s->cvs.as<__half>() + (size_t)l * rows * (d / 32), (int)T, VKB_KV_Q8_0, ctxb,
-                                    AF, s->xws.as<float>(), s->xws_floats);
+                                    AF, s->xws.as<float>(), s->xws_floats, xa_early);
             } else {
                 run_dense_attention(ctx, n_tok, D.n_text_head, 64, qc, s->seq.as<int32_t>(),
                                     s->ck.as<__half>() + (size_t)l * rows * d, s->cv.as<__half>() + (size_t)l * rows * d,

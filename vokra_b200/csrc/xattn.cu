@@ -55,6 +55,11 @@ struct XaArgs {
     int total;
     float* ws;                      // partials [G][max_seg][W + 2H]
     int* err;
+    // 1: no kernel still in flight writes K/V or seq_of_tok (the decode step:
+    // the store is written by the encoder and the step starts with host
+    // copies, a full barrier), so the ring is filled before the wait for the
+    // previous kernel (the query projection) and overlaps its tail
+    int kv_ready;
 };
 
 // First chunk of CTA c (the host guarantees total * G < 2^31, so 32-bit math is exact).
@@ -119,7 +124,7 @@ __device__ __forceinline__ void xa_load_q(const float* __restrict__ qrow, int ro
 }
 
 __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
-    pdl_entry();
+    pdl_launch();
     extern __shared__ __align__(128) uint8_t xa_smem[];
     const int W = a.W, H = a.H, S = a.S;
     const int nb = W / 32;
@@ -151,6 +156,7 @@ __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
     if (warp == n_cw) {
         // ---- producer warp: one lane streams the CTA's chunks through the ring ----
         if (lane == 0) {
+            if (!a.kv_ready) pdl_wait();
             int tok = (int)(x0 / a.chunks), j = (int)(x0 % a.chunks);
             for (int i = 0; i < n_my; ++i, ++j) {
                 if (j == a.chunks) {
@@ -176,6 +182,7 @@ __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
         }
     } else {
         // ---- compute warps: heads 2*warp, 2*warp+1 ----
+        pdl_wait();  // q and the partial slots belong to earlier kernels
         const int h = tid >> 4;     // head of this thread (both roles)
         const int kk = tid & 15;    // key of this thread in the Q.K role
         XaQ Q;
@@ -413,9 +420,10 @@ XaPlan xattn_q8_plan(const vkb_context* ctx, int n_tok, int n_head, int d_head, 
 
 void run_xattn_q8(vkb_context* ctx, const XaPlan& plan, int n_tok, int n_head, int n_ctx, const float* q,
                   const int32_t* seq_of_tok, const void* k, const void* v, const void* ks, const void* vs, void* out,
-                  int out_fmt, float* ws) {
+                  int out_fmt, float* ws, bool kv_ready) {
     const int W = n_head * XA_DH;
     XaArgs a;
+    a.kv_ready = kv_ready ? 1 : 0;
     a.q = q;
     a.seq_of_tok = seq_of_tok;
     a.kq = reinterpret_cast<const int8_t*>(k);

@@ -13,5 +13,5 @@ XaPlan xattn_q8_plan(const vkb_context* ctx, int n_tok, int n_head, int d_head, 
                      const void* k, const void* v, const void* ks, const void* vs, size_t ws_cap_floats);
 void run_xattn_q8(vkb_context* ctx, const XaPlan& plan, int n_tok, int n_head, int n_ctx, const float* q,
                   const int32_t* seq_of_tok, const void* k, const void* v, const void* ks, const void* vs, void* out,
-                  int out_fmt, float* ws);
+                  int out_fmt, float* ws, bool kv_ready = false);
 }  // namespace vkb
