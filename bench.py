@@ -278,9 +278,11 @@ def run_kernel_only(args):
         arch = dataclasses.replace(big, n_audio_layer=1, n_text_layer=1, n_vocab=1000, eot=999,
                                    start_ids=(1, 2, 3, 4))
         path = ensure_model(model_path("large_v3_dims_e1d1_q4_0"), arch, synth.Q4_0)
+        prec = {"split": _lib.PREC_SPLIT, "f16": _lib.PREC_F16, "enc_f16": _lib.PREC_ENCODER_F16}[args.precision]
+        _lib.check(_lib.load().vkb_context_set_precision(ctx.h, prec))
         model = whisper.WhisperModel(ctx, path)
-        B = 8
-        sess = whisper.Session(model, max_streams=B, max_clips=B)
+        B = args.clips
+        sess = whisper.Session(model, max_streams=B, max_clips=B, cross_kv_q8=True)
         lm = torch.from_numpy(synthetic_logmels(B, arch.n_mels, 2 * arch.n_audio_ctx, 5)).cuda()
         for _ in range(3):
             sess.encode(lm, list(range(B)))

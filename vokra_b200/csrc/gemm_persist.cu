@@ -16,10 +16,11 @@
 // kernel pays CTA setup, pipeline fill and the epilogue with the tensor pipe
 // idle, once per tile.
 //
-// Warp roles (448 threads): warp 0 producer (one lane: weight bulk copies +
+// Warp roles (448 or 576 threads): warp 0 producer (one lane: weight bulk copies +
 // activation TMA), warp 1 MMA issuer (one lane), warps 2-5 dequantization
-// (thread = weight row = tensor-memory lane), warps 6-13 epilogue (two groups
-// of four warps; a group covers the 128 lanes and half of the 192 columns).
+// (thread = weight row = tensor-memory lane), then the epilogue: EG groups of
+// four warps (two in split mode, three with single-f16 operands); a group
+// covers the 128 lanes and 192 / EG of the columns.
 // The epilogue needs both groups to stay shorter than a tile's MMAs at K = 1280
 // (measured: one group of four made fc1's GELU epilogue the bottleneck).
 // Every mbarrier wait is bounded; a timeout flags the context error.
@@ -30,7 +31,7 @@
 
 namespace vkb {
 
-template <int FMT, bool SPLIT = true>
+template <int FMT, bool SPLIT = true, int EG = 2>
 struct PCfg {
     static constexpr int BN = 192;                          // tokens per tile
     static constexpr int NP = SPLIT ? 2 : 1;                // activation planes (hi, lo)
@@ -46,7 +47,8 @@ struct PCfg {
     static constexpr int AS = 2;
     static constexpr int A_COL0 = 2 * BN;
     static constexpr int DEQ_WARPS = 4;
-    static constexpr int EPI_WARPS = 8;
+    static constexpr int EPI_WARPS = 4 * EG;  // EG groups of four warps, BN / EG columns each
+    static_assert((BN / EG) % 32 == 0, "epilogue column share");
     static constexpr int THREADS = 32 * (2 + DEQ_WARPS + EPI_WARPS);
     static_assert(A_COL0 + AS * 64 <= 512, "tensor memory budget");
     static_assert(S >= 2, "pipeline needs at least two stages");
@@ -113,13 +115,14 @@ __device__ __forceinline__ int64_t q8_row(const PEpi& e, int64_t m) {
     return (int64_t)e.row_map[g] * e.row_group + ((unsigned)m - g * (unsigned)e.row_group);
 }
 
-template <int FMT, bool SPLIT>
-__global__ void __launch_bounds__(PCfg<FMT, SPLIT>::THREADS, 1)
+template <int FMT, bool SPLIT, int EG>
+__global__ void __launch_bounds__(PCfg<FMT, SPLIT, EG>::THREADS, 1)
     tc_gemm_persist_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_lo,
                            const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc, int64_t K, int64_t N,
                            int64_t M, int n_tiles, int total_tiles, PEpi e, int* err) {
-    using C = PCfg<FMT, SPLIT>;
+    using C = PCfg<FMT, SPLIT, EG>;
     constexpr int BN = C::BN, S = C::S, AS = C::AS;
+    constexpr int CG = BN / EG;  // columns per epilogue group
     extern __shared__ uint8_t smem_raw[];
     uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(ring + S * C::STAGE_BYTES);
@@ -259,7 +262,7 @@ __global__ void __launch_bounds__(PCfg<FMT, SPLIT>::THREADS, 1)
         // epilogue: warp w reads lane quarter w % 4; group (w - 6) / 4 takes half the columns
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
-        const int cb = ((warp - 2 - C::DEQ_WARPS) >> 2) * (BN / 2);
+        const int cb = ((warp - 2 - C::DEQ_WARPS) >> 2) * CG;
         const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
         pdl_wait();
         int tt = 0;
@@ -283,7 +286,7 @@ __global__ void __launch_bounds__(PCfg<FMT, SPLIT>::THREADS, 1)
                 __half* db = half ? e.q8d[1] : e.q8d[0];
                 const float bias_q = e.bias ? e.bias[n] : 0.0f;
 #pragma unroll 1
-                for (int c0 = cb; c0 < cb + BN / 2; c0 += 32) {
+                for (int c0 = cb; c0 < cb + CG; c0 += 32) {
                     uint32_t v[32];
                     ptx::tmem_ld32(lane_base + b * BN + c0, v);
                     ptx::tmem_ld_wait();
@@ -315,7 +318,7 @@ __global__ void __launch_bounds__(PCfg<FMT, SPLIT>::THREADS, 1)
             const float bias_n = (nv && e.bias) ? e.bias[n] : 0.0f;
             const float scl = (e.kind == VKB_EPI_SCALE && n < e.n_scaled) ? e.scale : 1.0f;
 #pragma unroll 1
-            for (int c0 = cb; c0 < cb + BN / 2; c0 += 32) {
+            for (int c0 = cb; c0 < cb + CG; c0 += 32) {
                 uint32_t v[32];
                 ptx::tmem_ld32(lane_base + b * BN + c0, v);
                 ptx::tmem_ld_wait();
@@ -363,11 +366,11 @@ __global__ void __launch_bounds__(PCfg<FMT, SPLIT>::THREADS, 1)
 
 int persist_bn() { return PCfg<W_Q4_0>::BN; }
 
-template <int FMT, bool SPLIT>
+template <int FMT, bool SPLIT, int EG>
 static void launch_persist(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e,
                            int* err) {
-    using C = PCfg<FMT, SPLIT>;
-    smem_optin(tc_gemm_persist_kernel<FMT, SPLIT>, C::SMEM);
+    using C = PCfg<FMT, SPLIT, EG>;
+    smem_optin(tc_gemm_persist_kernel<FMT, SPLIT, EG>, C::SMEM);
     CUtensorMap map, map_lo;
     make_tmap_f16(&map, a16, m, w->k, C::BN);
     if (SPLIT) make_tmap_f16(&map_lo, a16 + m * w->k, m, w->k, C::BN);
@@ -376,7 +379,7 @@ static void launch_persist(vkb_context* ctx, const vkb_weight* w, int64_t m, con
     const int m_tiles = (int)((m + C::BN - 1) / C::BN);
     const int total = n_tiles * m_tiles;
     const int grid = std::min(total, ctx->sm_count);
-    launch_pdl(ctx, tc_gemm_persist_kernel<FMT, SPLIT>, grid, C::THREADS, C::SMEM, map, map_lo, w->qs.as<uint8_t>(),
+    launch_pdl(ctx, tc_gemm_persist_kernel<FMT, SPLIT, EG>, grid, C::THREADS, C::SMEM, map, map_lo, w->qs.as<uint8_t>(),
                w->sc.as<uint8_t>(), w->k, w->n, m, n_tiles, total, e, err);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
@@ -384,9 +387,15 @@ static void launch_persist(vkb_context* ctx, const vkb_weight* w, int64_t m, con
 
 void run_tc_persistent(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e, int* err,
                        bool split) {
+    // single-f16 operands: three epilogue groups (the MMAs of a tile are a third of the split
+    // mode's, so fc1's GELU epilogue is the longer phase with two; measured 812 vs 819 ms per
+    // bench step); VKB_PERSIST_EPI_GROUPS=2 selects two
+    static const int groups = [] { const char* v = std::getenv("VKB_PERSIST_EPI_GROUPS"); return v ? std::atoi(v) : 3; }();
     with_fmt(w->fmt, [&](auto F) {
-        if (split) launch_persist<decltype(F)::value, true>(ctx, w, m, a16, e, err);
-        else launch_persist<decltype(F)::value, false>(ctx, w, m, a16, e, err);
+        constexpr int FM = decltype(F)::value;
+        if (split) launch_persist<FM, true, 2>(ctx, w, m, a16, e, err);
+        else if (groups == 3) launch_persist<FM, false, 3>(ctx, w, m, a16, e, err);
+        else launch_persist<FM, false, 2>(ctx, w, m, a16, e, err);
     });
 }
 
