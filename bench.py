@@ -853,8 +853,8 @@ def main():
     tflops = 2.0 * M * N * K / (k_ms / 1e3) / 1e12
     roofline = {"bound": "tensor", "achieved": round(tflops, 1), "peak": bf16, "unit": "TFLOP/s",
                 "frac": round(tflops / bf16, 4), "traffic": None,
-                "kernel": ("tc_gemm_persist_kernel (persistent, double-buffered accumulator)" if planes == 2
-                           else "tc_gemm_kernel") + f" Q4_0 encoder fc1 M={M} N={N} K={K}, "
+                "kernel": "tc_gemm_persist_kernel (persistent, double-buffered accumulator)"
+                          + f" Q4_0 encoder fc1 M={M} N={N} K={K}, "
                           f"{'split f16 (3 MMAs per step)' if planes == 2 else 'f16'}",
                 "algorithmic_flops": 2 * M * N * K, "mma_flops_issued": 2 * M * N * K * mma_factor,
                 "ms_per_launch": round(k_ms, 4), "peak_kind": f"{peak_kind} bf16 dense burst"}
