@@ -400,10 +400,12 @@ void run_dense_attention(vkb_context* ctx, int n_tok, int n_head, int d_head, co
                          bool kv_ready) {
     check_heads(n_head, d_head);
     const int W = n_head * d_head;
-    if (kv_fmt != VKB_DT_F16) {
+    {
+        // the streaming kernel for both stores (Q8_0 rows + scales, or f16 rows);
+        // VKB_XATTN_ROWGROUPS selects the row-group kernel below instead
         static const bool old_path = std::getenv("VKB_XATTN_ROWGROUPS") != nullptr;
         XaPlan xp = old_path ? XaPlan{} : xattn_q8_plan(ctx, n_tok, n_head, d_head, n_ctx, q, k, v, k_scale, v_scale,
-                                                        ws_cap_floats);
+                                                        ws_cap_floats, kv_fmt == VKB_DT_F16);
         if (xp.ok) {
             float* ws = ws_override;
             if (!ws) {

@@ -1,4 +1,4 @@
-// xattn.cu — decode cross-attention over a dense Q8_0 K/V store, built to
+// xattn.cu — decode cross-attention over a dense Q8_0 (or f16) K/V store, built to
 // stream the store at HBM bandwidth.
 //
 // Semantics are those of dense_attn_kernel (the softmax attention of
@@ -38,8 +38,8 @@
 
 namespace vkb {
 
-constexpr int XA_T = 32;        // keys per stage
-constexpr int XA_KPL = XA_T / 16;  // keys per lane in the Q.K role
+constexpr int XA_T = 32;        // keys per stage (Q8_0 store)
+constexpr int XA_T16 = 16;      // keys per stage (f16 store: the same bytes per stage)
 constexpr int XA_DH = 64;       // head width this kernel handles
 constexpr int XA_MAX_STAGES = 6;
 constexpr int XA_SMEM_BUDGET = 200 * 1024;
@@ -123,17 +123,23 @@ __device__ __forceinline__ void xa_load_q(const float* __restrict__ qrow, int ro
     }
 }
 
+// F16 = true: the store holds K and V as f16 rows (no scales); XT = 16 keys
+// per stage, q held as 64 fp32 registers per thread (rotated like the int8
+// planes), Q.K and P.V in fp32 with packed f32x2 FMAs.
+template <bool F16>
 __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
+    constexpr int XT = F16 ? XA_T16 : XA_T;  // keys per stage
+    constexpr int KPL = XT / 16;               // keys per lane in the Q.K role
     pdl_launch();
     extern __shared__ __align__(128) uint8_t xa_smem[];
     const int W = a.W, H = a.H, S = a.S;
     const int nb = W / 32;
-    const int kq_bytes = XA_T * W, kd_bytes = XA_T * nb * 2;
+    const int kq_bytes = F16 ? XT * W * 2 : XT * W, kd_bytes = F16 ? 0 : XT * nb * 2;
     const int stage_bytes = 2 * (kq_bytes + kd_bytes);
     const int n_cw = H / 2;  // compute warps: two heads each
     uint8_t* ring = xa_smem;
-    float* wt = reinterpret_cast<float*>(ring + (size_t)S * stage_bytes);  // [XA_T][nb]
-    uint64_t* full = reinterpret_cast<uint64_t*>(wt + XA_T * nb);
+    float* wt = reinterpret_cast<float*>(ring + (size_t)S * stage_bytes);  // [XT][nb]
+    uint64_t* full = reinterpret_cast<uint64_t*>(wt + XT * nb);
     uint64_t* empty = full + S;
 
     const int tid = threadIdx.x;
@@ -168,15 +174,22 @@ __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
                     failed = true;
                     break;
                 }
-                const int nk = min(XA_T, a.n_ctx - j * XA_T);
-                const int64_t row = (int64_t)a.seq_of_tok[tok] * a.n_ctx + (int64_t)j * XA_T;
+                const int nk = min(XT, a.n_ctx - j * XT);
+                const int64_t row = (int64_t)a.seq_of_tok[tok] * a.n_ctx + (int64_t)j * XT;
                 uint8_t* st = ring + (size_t)s * stage_bytes;
                 uint64_t* bar = &full[s];
-                ptx::mbar_expect_tx(bar, (uint32_t)(2 * nk * (W + nb * 2)));
-                ptx::bulk_load(st, a.kq + row * W, (uint32_t)(nk * W), bar);
-                ptx::bulk_load(st + kq_bytes, a.kd + row * nb, (uint32_t)(nk * nb * 2), bar);
-                ptx::bulk_load(st + kq_bytes + kd_bytes, a.vq + row * W, (uint32_t)(nk * W), bar);
-                ptx::bulk_load(st + 2 * kq_bytes + kd_bytes, a.vd + row * nb, (uint32_t)(nk * nb * 2), bar);
+                if constexpr (F16) {
+                    // K and V rows as f16: W * 2 bytes per key
+                    ptx::mbar_expect_tx(bar, (uint32_t)(4 * nk * W));
+                    ptx::bulk_load(st, a.kq + row * W * 2, (uint32_t)(nk * W * 2), bar);
+                    ptx::bulk_load(st + kq_bytes, a.vq + row * W * 2, (uint32_t)(nk * W * 2), bar);
+                } else {
+                    ptx::mbar_expect_tx(bar, (uint32_t)(2 * nk * (W + nb * 2)));
+                    ptx::bulk_load(st, a.kq + row * W, (uint32_t)(nk * W), bar);
+                    ptx::bulk_load(st + kq_bytes, a.kd + row * nb, (uint32_t)(nk * nb * 2), bar);
+                    ptx::bulk_load(st + kq_bytes + kd_bytes, a.vq + row * W, (uint32_t)(nk * W), bar);
+                    ptx::bulk_load(st + 2 * kq_bytes + kd_bytes, a.vd + row * nb, (uint32_t)(nk * nb * 2), bar);
+                }
                 issued = i + 1;
             }
         }
@@ -186,6 +199,7 @@ __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
         const int h = tid >> 4;     // head of this thread (both roles)
         const int kk = tid & 15;    // key of this thread in the Q.K role
         XaQ Q;
+        float qf[F16 ? XA_DH : 1];  // f16 store: q of the head, chunk cc = channels 8*((cc + kk) & 7) ..
         float m = -INFINITY, l = 0.0f;
         float2 acc01 = make_float2(0.0f, 0.0f), acc23 = make_float2(0.0f, 0.0f);
         int cur_tok = -1, seg = 0;
@@ -213,9 +227,21 @@ __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
                 l = 0.0f;
                 acc01 = make_float2(0.0f, 0.0f);
                 acc23 = acc01;
-                xa_load_q(a.q + (int64_t)tok * W + h * XA_DH, kk, Q);
+                if constexpr (F16) {
+                    const float* qrow = a.q + (int64_t)tok * W + h * XA_DH;
+#pragma unroll
+                    for (int cc = 0; cc < 8; ++cc) {
+                        const int pc = (cc + kk) & 7;
+                        const float4 v0 = *reinterpret_cast<const float4*>(qrow + 8 * pc);
+                        const float4 v1 = *reinterpret_cast<const float4*>(qrow + 8 * pc + 4);
+                        qf[8 * cc + 0] = v0.x; qf[8 * cc + 1] = v0.y; qf[8 * cc + 2] = v0.z; qf[8 * cc + 3] = v0.w;
+                        qf[8 * cc + 4] = v1.x; qf[8 * cc + 5] = v1.y; qf[8 * cc + 6] = v1.z; qf[8 * cc + 7] = v1.w;
+                    }
+                } else {
+                    xa_load_q(a.q + (int64_t)tok * W + h * XA_DH, kk, Q);
+                }
             }
-            const int nk = min(XA_T, a.n_ctx - j * XA_T);
+            const int nk = min(XT, a.n_ctx - j * XT);
             const int s = i % S;
             if (!ptx::mbar_wait(&full[s], (uint32_t)((i / S) & 1))) {
                 failed = true;
@@ -227,13 +253,29 @@ __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
             const int8_t* Vs = reinterpret_cast<const int8_t*>(st + kq_bytes + kd_bytes);
             const __half* Vd = reinterpret_cast<const __half*>(st + 2 * kq_bytes + kd_bytes);
 
-            // ---- Q.K and the online softmax (16 lanes per head, XA_KPL keys per lane) ----
-            float score[XA_KPL];
+            // ---- Q.K and the online softmax (16 lanes per head, KPL keys per lane) ----
+            float score[KPL];
 #pragma unroll
-            for (int u = 0; u < XA_KPL; ++u) {
+            for (int u = 0; u < KPL; ++u) {
                 const int key = kk + 16 * u;
                 score[u] = -INFINITY;
-                if (key < nk) {
+                if (F16 && key < nk) {
+                    // 8 chunks of 8 channels in the rotated order of qf (16-byte loads on distinct banks)
+                    const __half* krow = reinterpret_cast<const __half*>(st) + (size_t)key * W + h * XA_DH;
+                    float2 acc2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+                    for (int cc = 0; cc < 8; ++cc) {
+                        const int pc = (cc + kk) & 7;
+                        const uint4 kv = *reinterpret_cast<const uint4*>(krow + 8 * pc);
+                        const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) {
+                            const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&kw[w]));
+                            acc2 = __ffma2_rn(kf, make_float2(qf[8 * cc + 2 * w], qf[8 * cc + 2 * w + 1]), acc2);
+                        }
+                    }
+                    score[u] = acc2.x + acc2.y;
+                } else if (!F16 && key < nk) {
                     const uint8_t* krow = reinterpret_cast<const uint8_t*>(Ks + key * W + h * XA_DH);
                     const __half2 kd2 = *reinterpret_cast<const __half2*>(Kd + key * nb + 2 * h);
                     const float ks0 = __low2float(kd2), ks1 = __high2float(kd2);
@@ -260,19 +302,21 @@ __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
             }
             float mx = score[0];
 #pragma unroll
-            for (int u = 1; u < XA_KPL; ++u) mx = fmaxf(mx, score[u]);
+            for (int u = 1; u < KPL; ++u) mx = fmaxf(mx, score[u]);
 #pragma unroll
             for (int o = 8; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
             const float mn = fmaxf(m, mx);
             const float corr = (m == -INFINITY) ? 0.0f : __expf(m - mn);
             float ps = 0.0f;
 #pragma unroll
-            for (int u = 0; u < XA_KPL; ++u) {
+            for (int u = 0; u < KPL; ++u) {
                 const int key = kk + 16 * u;
                 const float p = (key < nk && mn != -INFINITY) ? __expf(score[u] - mn) : 0.0f;
                 ps += p;
                 float w0 = 0.0f, w1 = 0.0f;
-                if (key < nk) {
+                if (F16) {
+                    w0 = w1 = p;
+                } else if (key < nk) {
                     const __half2 vd2 = *reinterpret_cast<const __half2*>(Vd + key * nb + 2 * h);
                     w0 = p * __low2float(vd2);
                     w1 = p * __high2float(vd2);
@@ -292,6 +336,19 @@ __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
                 const float2 bias = make_float2(-8388736.0f, -8388736.0f);
                 acc01 = __fmul2_rn(acc01, cr);
                 acc23 = __fmul2_rn(acc23, cr);
+                if constexpr (F16) {
+                    const __half* Vh = reinterpret_cast<const __half*>(Vs);
+#pragma unroll 4
+                    for (int t = 0; t < nk; ++t) {
+                        const float wv = wt[t * nb + b];
+                        const uint2 v = *reinterpret_cast<const uint2*>(Vh + (size_t)t * W + 4 * tid);
+                        const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+                        const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+                        const float2 w2 = make_float2(wv, wv);
+                        acc01 = __ffma2_rn(w2, f01, acc01);
+                        acc23 = __ffma2_rn(w2, f23, acc23);
+                    }
+                } else {
 #pragma unroll 4
                 for (int t = 0; t < nk; ++t) {
                     const float wv = wt[t * nb + b];
@@ -305,6 +362,7 @@ __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
                     const float2 w2 = make_float2(wv, wv);
                     acc01 = __ffma2_rn(w2, f01, acc01);
                     acc23 = __ffma2_rn(w2, f23, acc23);
+                }
                 }
             }
             __syncwarp();
@@ -382,20 +440,21 @@ __global__ void xattn_combine_kernel(XaArgs a, void* out, int out_fmt) {
     }
 }
 
-static int xa_stages(int W) {
-    const int stage = 2 * XA_T * (W + W / 16);
-    const int extra = XA_T * (W / 32) * 4 + 2 * XA_MAX_STAGES * 8;
-    return std::min(XA_MAX_STAGES, (XA_SMEM_BUDGET - extra) / stage);
+static int xa_keys(bool f16) { return f16 ? XA_T16 : XA_T; }
+static int xa_stage_bytes(int W, bool f16) { return f16 ? 2 * XA_T16 * W * 2 : 2 * XA_T * (W + W / 16); }
+static int xa_stages(int W, bool f16) {
+    const int extra = xa_keys(f16) * (W / 32) * 4 + 2 * XA_MAX_STAGES * 8;
+    return std::min(XA_MAX_STAGES, (XA_SMEM_BUDGET - extra) / xa_stage_bytes(W, f16));
 }
 
 XaPlan xattn_q8_plan(const vkb_context* ctx, int n_tok, int n_head, int d_head, int n_ctx, const float* q,
-                     const void* k, const void* v, const void* ks, const void* vs, size_t ws_cap_floats) {
+                     const void* k, const void* v, const void* ks, const void* vs, size_t ws_cap_floats, bool f16) {
     XaPlan p;
     const int W = n_head * d_head;
     if (d_head != XA_DH || W % 256 || (W + 2 * n_head) % 4 || 16 * n_head + 32 > 512 || n_tok <= 0 || n_ctx <= 0) return p;
     if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)ks | (uintptr_t)vs) & 15) return p;
-    if (xa_stages(W) < 2) return p;
-    const int chunks = (n_ctx + XA_T - 1) / XA_T;
+    if (xa_stages(W, f16) < 2) return p;
+    const int chunks = (n_ctx + xa_keys(f16) - 1) / xa_keys(f16);
     const int64_t total = (int64_t)n_tok * chunks;
     if (total * ctx->sm_count >= (int64_t(1) << 31)) return p;
     int G = (int)std::min<int64_t>(ctx->sm_count, total);
@@ -412,6 +471,7 @@ XaPlan xattn_q8_plan(const vkb_context* ctx, int n_tok, int n_head, int d_head, 
     }
     if (ws_cap_floats && need > ws_cap_floats) return p;
     p.ok = true;
+    p.f16 = f16;
     p.G = G;
     p.max_seg = max_seg;
     p.ws_floats = need;
@@ -434,17 +494,24 @@ void run_xattn_q8(vkb_context* ctx, const XaPlan& plan, int n_tok, int n_head, i
     a.n_ctx = n_ctx;
     a.H = n_head;
     a.W = W;
-    a.chunks = (n_ctx + XA_T - 1) / XA_T;
+    const bool f16 = plan.f16;
+    a.chunks = (n_ctx + xa_keys(f16) - 1) / xa_keys(f16);
     a.total = n_tok * a.chunks;
     a.G = plan.G;
     a.max_seg = plan.max_seg;
-    a.S = xa_stages(W);
+    a.S = xa_stages(W, f16);
     a.ws = ws;
 
     a.err = ctx->err_flag.as<int>();
-    const size_t smem = (size_t)a.S * 2 * XA_T * (W + W / 16) + (size_t)XA_T * (W / 32) * 4 + (size_t)a.S * 16;
-    smem_optin(xattn_q8_kernel, XA_SMEM_BUDGET);
-    launch_pdl(ctx, xattn_q8_kernel, plan.G, 16 * n_head + 32, smem, a);
+    const size_t smem =
+        (size_t)a.S * xa_stage_bytes(W, f16) + (size_t)xa_keys(f16) * (W / 32) * 4 + (size_t)a.S * 16;
+    if (f16) {
+        smem_optin(xattn_q8_kernel<true>, XA_SMEM_BUDGET);
+        launch_pdl(ctx, xattn_q8_kernel<true>, plan.G, 16 * n_head + 32, smem, a);
+    } else {
+        smem_optin(xattn_q8_kernel<false>, XA_SMEM_BUDGET);
+        launch_pdl(ctx, xattn_q8_kernel<false>, plan.G, 16 * n_head + 32, smem, a);
+    }
     VKB_CUDA(cudaGetLastError());
     ctx->count();
     launch_pdl(ctx, xattn_combine_kernel, (unsigned)n_tok, std::min(256, W / 4), (size_t)plan.G * sizeof(int), a, out, out_fmt);
