@@ -9,7 +9,8 @@
 // and the accumulator is double-buffered in tensor memory:
 //   columns [0, 192)    accumulator 0      (128 weight rows x 192 tokens, f32)
 //   columns [192, 384)  accumulator 1
-//   columns [384, 512)  two A stages of W_hi | W_lo (64 K each)
+//   columns [384, 512)  two A stages of W_hi | W_lo (64 K each), or four of a
+//                       single f16 W plane
 // so the epilogue of tile i (its own 8 warps: tensor-memory load, bias, GELU /
 // scale / residual, stores) runs while the MMAs of tile i+1 fill the other
 // buffer, and the TMA ring never drains between tiles. The non-persistent
@@ -44,13 +45,17 @@ struct PCfg {
     static constexpr int SMAX = SPLIT ? 4 : 6;
     static constexpr int S = S0 > SMAX ? SMAX : S0;
     static constexpr int SMEM = 1024 + S * STAGE_BYTES + 1024;
-    static constexpr int AS = 2;
+    // A stages in tensor memory: W_hi | W_lo take 64 columns, a single f16 plane
+    // 32, so the single-f16 kernel keeps four stages in the same 128 columns
+    // (the dequant warps run two stages further ahead of the MMAs)
+    static constexpr int A_STRIDE = SPLIT ? 64 : 32;
+    static constexpr int AS = SPLIT ? 2 : 4;
     static constexpr int A_COL0 = 2 * BN;
     static constexpr int DEQ_WARPS = 4;
     static constexpr int EPI_WARPS = 4 * EG;  // EG groups of four warps, BN / EG columns each
     static_assert((BN / EG) % 32 == 0, "epilogue column share");
     static constexpr int THREADS = 32 * (2 + DEQ_WARPS + EPI_WARPS);
-    static_assert(A_COL0 + AS * 64 <= 512, "tensor memory budget");
+    static_assert(A_COL0 + AS * A_STRIDE <= 512, "tensor memory budget");
     static_assert(S >= 2, "pipeline needs at least two stages");
     static_assert(B_BYTES % 1024 == 0, "128-byte swizzle atoms");
 };
@@ -215,7 +220,7 @@ __global__ void __launch_bounds__(PCfg<FMT, SPLIT, EG>::THREADS, 1)
                         break;
                     }
                     ptx::tc_fence_after();
-                    const uint32_t a_t = tmem + C::A_COL0 + a * 64;
+                    const uint32_t a_t = tmem + C::A_COL0 + a * C::A_STRIDE;
                     const uint32_t b_addr = ptx::smem_u32(ring + s * C::STAGE_BYTES);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
@@ -247,7 +252,7 @@ __global__ void __launch_bounds__(PCfg<FMT, SPLIT, EG>::THREADS, 1)
                     break;
                 }
                 const uint8_t* raw = ring + s * C::STAGE_BYTES + C::NP * C::B_BYTES;
-                const uint32_t a_t = tmem + ((uint32_t)(quarter * 32) << 16) + C::A_COL0 + a * 64;
+                const uint32_t a_t = tmem + ((uint32_t)(quarter * 32) << 16) + C::A_COL0 + a * C::A_STRIDE;
                 uint32_t hi[32], lo[32];
                 dequant_row_stage_h<FMT, SPLIT>(raw, raw + C::RAW_Q, r, i, hi, lo);
                 ptx::tc_fence_after();
