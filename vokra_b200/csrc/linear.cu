@@ -680,7 +680,11 @@ void run_split_f16(vkb_context* ctx, const float* x, int64_t n, __half* y, bool 
 //   warps 6..   : epilogue only (up to 3 more groups of 4 warps), on the same
 //                 TMEM lanes as warps 2..5 and their share of the token columns
 // Rings: S stages of (X tile(s) + raw weights) in shared memory, AS stages of
-// A tiles in tensor memory.
+// A tiles in tensor memory. A stage's raw weights and its X tiles complete on
+// separate mbarriers (w_full, full): weights are never written by a kernel,
+// so they are fetched and the first stages dequantized before the wait for
+// the previous kernel; after it only the X loads, the MMAs and the epilogue
+// remain (the latency a decode-step GEMM is made of).
 // Every mbarrier wait is bounded; on timeout the kernel records an error flag
 // and returns without hanging.
 // ---------------------------------------------------------------------------
@@ -746,7 +750,8 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
     uint64_t* a_empty = a_full + C::AS;
     uint64_t* acc_full = a_empty + C::AS;
     uint64_t* res_full = acc_full + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 1);
+    uint64_t* w_full = res_full + 1;  // [S] the raw weights of a stage (full[] counts the activations)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(w_full + C::S);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int bid = blockIdx.x;
@@ -763,6 +768,7 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
         for (int i = 0; i < C::S; ++i) {
             ptx::mbar_init(&full[i], 1);
             ptx::mbar_init(&empty[i], 1);
+            ptx::mbar_init(&w_full[i], 1);
         }
         for (int i = 0; i < C::AS; ++i) {
             ptx::mbar_init(&a_full[i], 128);
@@ -797,9 +803,9 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
             for (int i = 0; i < pre; ++i) {
                 uint8_t* raw_dst = st_ring + i * C::STAGE_BYTES + C::NP * C::B_BYTES;
                 StagePtrs p = stage_ptrs(FMT, qs, sc, K, n_tile, s0 + i);
-                ptx::mbar_expect_tx(&full[i], C::NP * C::B_BYTES + C::RAW_Q + C::RAW_S);
-                ptx::bulk_load(raw_dst, p.qs, C::RAW_Q, &full[i]);
-                if (C::RAW_S) ptx::bulk_load(raw_dst + C::RAW_Q, p.sc, C::RAW_S, &full[i]);
+                ptx::mbar_expect_tx(&w_full[i], C::RAW_Q + C::RAW_S);
+                ptx::bulk_load(raw_dst, p.qs, C::RAW_Q, &w_full[i]);
+                if (C::RAW_S) ptx::bulk_load(raw_dst + C::RAW_Q, p.sc, C::RAW_S, &w_full[i]);
             }
             pdl_wait();
             for (int i = 0; i < nst && ok; ++i) {
@@ -810,10 +816,11 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
                     if (!ptx::mbar_wait(&empty[s], ((i / C::S) & 1) ^ 1)) { ok = false; break; }
                     uint8_t* raw_dst = b_dst + C::NP * C::B_BYTES;
                     StagePtrs p = stage_ptrs(FMT, qs, sc, K, n_tile, stage);
-                    ptx::mbar_expect_tx(&full[s], C::NP * C::B_BYTES + C::RAW_Q + C::RAW_S);
-                    ptx::bulk_load(raw_dst, p.qs, C::RAW_Q, &full[s]);
-                    if (C::RAW_S) ptx::bulk_load(raw_dst + C::RAW_Q, p.sc, C::RAW_S, &full[s]);
+                    ptx::mbar_expect_tx(&w_full[s], C::RAW_Q + C::RAW_S);
+                    ptx::bulk_load(raw_dst, p.qs, C::RAW_Q, &w_full[s]);
+                    if (C::RAW_S) ptx::bulk_load(raw_dst + C::RAW_Q, p.sc, C::RAW_S, &w_full[s]);
                 }
+                ptx::mbar_expect_tx(&full[s], C::NP * C::B_BYTES);
                 ptx::tma_load_2d(b_dst, &xmap, &full[s], (int32_t)(stage * STAGE_K), m_tile * BN);
                 if (SPLIT)
                     ptx::tma_load_2d(b_dst + C::B_BYTES, &xmap_lo, &full[s], (int32_t)(stage * STAGE_K), m_tile * BN);
@@ -852,7 +859,8 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
         const int r = quarter * 32 + lane;
         for (int i = 0; i < nst && ok; ++i) {
             int s = i % C::S, a = i % C::AS;
-            if (!ptx::mbar_wait(&full[s], (i / C::S) & 1)) { ok = false; break; }
+            // only the weights: the first stages dequantize before the previous kernel ends
+            if (!ptx::mbar_wait(&w_full[s], (i / C::S) & 1)) { ok = false; break; }
             if (!ptx::mbar_wait(&a_empty[a], ((i / C::AS) & 1) ^ 1)) { ok = false; break; }
             const uint8_t* raw = st_ring + s * C::STAGE_BYTES + C::NP * C::B_BYTES;
             uint32_t hi[32], lo[32];
