@@ -98,13 +98,15 @@ __global__ void kv_append_kernel(const float* __restrict__ k, const float* __res
 // ---------------------------------------------------------------------------
 // Fused decode self-attention (one query per stream, SEQUENCE layout, d_head
 // 64): one CTA of 256 threads per (stream, group of 4 heads = 256 channels).
-// It appends the step's K/V for its channels (the bit-exact BlockQ8_0::pack of
-// kv_append_kernel), then attends over every key of the stream without key
-// splits, so no partials and no combine launch:
+// Before waiting for the QKV projection it looks up the key rows and requests
+// their K and V bytes into L2; then it appends the step's K/V for its channels
+// (the bit-exact BlockQ8_0::pack of kv_append_kernel) and attends over every
+// key of the stream without key splits, so no partials and no combine launch:
 //   scores  thread (head h = t/64, key slot t%64): 64 int8 K of the key
 //           converted exactly, dotted with q (shared memory), x block scales
 //   softmax one warp per head over the scores in shared memory
-//   P.V     thread = channel; per key one byte of V, its block scale, p
+//   P.V     thread = (16 channels, key group); 16 bytes of V per key, its
+//           block scale, p; the 16 key groups summed in shared memory
 // ---------------------------------------------------------------------------
 // With splits > 0 the q|k|v row is read from the QKV projection's split-K
 // partials [splits][n_tok][ld] instead: value = (sum of partials in split
@@ -115,15 +117,35 @@ __global__ void __launch_bounds__(256) paged_decode_kernel(
     const AttnGroup* __restrict__ groups, const int64_t* __restrict__ new_rows, const int32_t* __restrict__ table,
     int ppseq, int64_t arena_row0, int bs, int8_t* kq, __half* kd, int8_t* vq, __half* vd, int W, int max_keys,
     void* out, int out_fmt, int64_t out_plane) {
-    pdl_entry();
+    pdl_launch();
     extern __shared__ __align__(16) float pd_smem[];
     float* sc = pd_smem;                               // [4][max_keys]; later the [16][256] P.V sums
     float* qs = sc + (4 * max_keys > 4096 ? 4 * max_keys : 4096);  // [256]
     int64_t* rows_s = reinterpret_cast<int64_t*>(qs + 256);               // [max_keys]
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    // The query groups, the rows of the new keys and the page table come from
+    // host copies that precede the step, so the key rows are looked up, and
+    // the K and V bytes of every key (this group's 256 channels and their
+    // scales) requested into L2, while the QKV projection still runs; an L2
+    // prefetch is correct whatever writes those bytes.
     const AttnGroup g = groups[blockIdx.x];
     const int tok = g.first_tok, n_keys = g.pos0 + 1;
     const int c0 = blockIdx.y * 256, nb = W / 32, b0 = c0 / 32;
+    for (int k = t; k < n_keys; k += 256) {
+        const int pid = table[g.seq * ppseq + k / bs];
+        rows_s[k] = arena_row0 + (int64_t)pid * bs + k % bs;
+    }
+    __syncthreads();
+    for (int i = t; i < 6 * n_keys; i += 256) {
+        const int64_t row = rows_s[i / 6];
+        const int pt = i % 6;
+        const void* pp = pt < 2   ? static_cast<const void*>(kq + row * W + c0 + 128 * pt)
+                         : pt == 2 ? static_cast<const void*>(kd + row * nb + b0)
+                         : pt < 5  ? static_cast<const void*>(vq + row * W + c0 + 128 * (pt - 3))
+                                   : static_cast<const void*>(vd + row * nb + b0);
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(pp));
+    }
+    pdl_wait();
     auto val = [&](int col) {
         const int64_t i = (int64_t)tok * ld + col;
         if (splits == 0) return qkv[i];
@@ -139,22 +161,8 @@ __global__ void __launch_bounds__(256) paged_decode_kernel(
         q8_0_block_warp(val(2 * W + c0 + warp * 32 + lane), lane, vq + row * W + c0 + warp * 32,
                         vd + row * nb + b0 + warp);
         qs[t] = val(c0 + t);
-        for (int k = t; k < n_keys; k += 256) {
-            const int pid = table[g.seq * ppseq + k / bs];
-            rows_s[k] = arena_row0 + (int64_t)pid * bs + k % bs;
-        }
     }
     __syncthreads();
-    // The V bytes of every key (this group's 256 channels and their scales) are
-    // requested into L2 now, so that phase 3 reads them at L2 latency; they do
-    // not depend on the scores.
-    for (int i = t; i < 3 * n_keys; i += 256) {
-        const int64_t row = rows_s[i / 3];
-        const int part = i % 3;
-        const void* p = part < 2 ? static_cast<const void*>(vq + row * W + c0 + 128 * part)
-                                 : static_cast<const void*>(vd + row * nb + b0);
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-    }
     // phase 1: scores, two keys per iteration (their 8 loads issued together)
     {
         const int hl = t >> 6, slot = t & 63;
