@@ -88,15 +88,17 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 __global__ void layer_norm_row_kernel(const float* __restrict__ x, int64_t rows, int cols, const float* __restrict__ g,
                                       const float* __restrict__ b, float eps, void* out, int out_fmt) {
-    pdl_entry();
+    pdl_launch();
     __shared__ float red[32];
     const int64_t row = blockIdx.x;
     const int c = threadIdx.x, n4 = cols >> 2;
     const bool on = c < n4;
     const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    const float4 v = on ? __ldg(reinterpret_cast<const float4*>(x + row * cols) + c) : z;
+    // LayerNorm parameters are model weights: read before the wait, x after it
     const float4 gg = on ? __ldg(reinterpret_cast<const float4*>(g) + c) : z;
     const float4 bb = on ? __ldg(reinterpret_cast<const float4*>(b) + c) : z;
+    pdl_wait();
+    const float4 v = on ? __ldg(reinterpret_cast<const float4*>(x + row * cols) + c) : z;
     const float inv_cols = 1.0f / (float)cols;
     const float mean = block_sum((v.x + v.y) + (v.z + v.w), red) * inv_cols;
     const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
@@ -135,16 +137,23 @@ __global__ void reduce_residual_ln_kernel(const float* __restrict__ part, int sp
                                           const float* __restrict__ bias, float* __restrict__ h,
                                           const float* __restrict__ g, const float* __restrict__ b, float eps,
                                           void* out, int out_fmt) {
-    pdl_entry();
+    pdl_launch();
     __shared__ float red[32];
     const int64_t row = blockIdx.x;
     const int c = threadIdx.x, n4 = cols >> 2;
     const bool on = c < n4;
     const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    float4 v = z, gg = z, bb = z;
+    float4 v = z, gg = z, bb = z, bi = z;
+    // the layer's bias and LayerNorm parameters are model weights (no kernel
+    // writes them): loaded while the projection that produced the partials ends
+    if (on) {
+        if (bias) bi = __ldg(reinterpret_cast<const float4*>(bias) + c);
+        gg = __ldg(reinterpret_cast<const float4*>(g) + c);
+        bb = __ldg(reinterpret_cast<const float4*>(b) + c);
+    }
+    pdl_wait();
     if (on) {
         const int64_t o4 = row * n4 + c;
-        const float4 bi = bias ? __ldg(reinterpret_cast<const float4*>(bias) + c) : z;
         float4 acc = z;
         constexpr int U = 8;
         for (int s0 = 0; s0 < splits; s0 += U) {
@@ -161,8 +170,6 @@ __global__ void reduce_residual_ln_kernel(const float* __restrict__ part, int sp
         const float4 r = reinterpret_cast<const float4*>(h)[o4];
         v = make_float4(r.x + (acc.x + bi.x), r.y + (acc.y + bi.y), r.z + (acc.z + bi.z), r.w + (acc.w + bi.w));
         reinterpret_cast<float4*>(h)[o4] = v;
-        gg = __ldg(reinterpret_cast<const float4*>(g) + c);
-        bb = __ldg(reinterpret_cast<const float4*>(b) + c);
     }
     const float inv_cols = 1.0f / (float)cols;
     const float mean = block_sum((v.x + v.y) + (v.z + v.w), red) * inv_cols;

@@ -624,7 +624,7 @@ __global__ void __launch_bounds__(128) gemv2_kernel(const uint8_t* __restrict__ 
 
 // Sums split-K partials ws[split][m][n] in split order and applies the epilogue.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int n_splits, int64_t M, int64_t N, Epi e) {
-    pdl_entry();
+    pdl_launch();
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= M * N) return;
     int64_t m, n;
@@ -635,9 +635,19 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int n_splits,
         m = i / N;
         n = i % N;
     }
+    const float bias_n = e.bias ? __ldg(e.bias + n) : 0.0f;  // a model weight: read before the wait
+    pdl_wait();
+    // partials in split order, up to 8 loads in flight
     float acc = 0.0f;
-    for (int s = 0; s < n_splits; ++s) acc += __ldg(ws + (int64_t)s * M * N + i);
-    epi_store(e, m, n, acc, e.bias ? e.bias[n] : 0.0f);
+    for (int s0 = 0; s0 < n_splits; s0 += 8) {
+        float t[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) t[u] = s0 + u < n_splits ? __ldcg(ws + (int64_t)(s0 + u) * M * N + i) : 0.0f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (s0 + u < n_splits) acc += t[u];
+    }
+    epi_store(e, m, n, acc, bias_n);
 }
 
 // x (f32) -> f16 plane, or hi / lo f16 planes (x = hi + lo to ~2^-22) when split.
@@ -883,11 +893,11 @@ __global__ void __launch_bounds__(TcCfg<FMT, BN, SPLIT>::THREADS, TcCfg<FMT, BN,
         const int r = quarter * 32 + lane;
         constexpr int HALF = BN / C::EG;  // columns per group
         const int cb = ((warp - 2) >> 2) * HALF;
+        const int64_t n = (int64_t)n_tile * TILE_N + r;
+        const float bias_n = (e.bias && n < N) ? __ldg(e.bias + n) : 0.0f;  // a model weight: before the wait
         pdl_wait();
         const bool go = ok && ptx::mbar_wait(acc_full, 0);
         ptx::tc_fence_after();
-        const int64_t n = (int64_t)n_tile * TILE_N + r;
-        const float bias_n = (go && e.bias && n < N) ? e.bias[n] : 0.0f;
         const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
         // 32 accumulator columns per tcgen05.ld (16 for narrow tiles)
         constexpr int CW = HALF >= 32 ? 32 : 16;

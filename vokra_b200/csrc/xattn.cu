@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(512, 1) xattn_q8_kernel(XaArgs a) {
 // One CTA per query row: thread 0 lists the partial slots of the CTAs whose
 // range covers the row (in shared memory), then each thread merges 4 channels.
 __global__ void xattn_combine_kernel(XaArgs a, void* out, int out_fmt) {
-    pdl_entry();
+    pdl_launch();  // the slot list below is plan arithmetic: it runs before the wait
     extern __shared__ int s_slot[];  // [G]
     __shared__ int s_n;
     const int W = a.W, H = a.H;
@@ -404,6 +404,7 @@ __global__ void xattn_combine_kernel(XaArgs a, void* out, int out_fmt) {
         s_n = n;
     }
     __syncthreads();
+    pdl_wait();
     const int n = s_n;
     const size_t stride = (size_t)(W + 2 * H);
     for (int ch = 4 * threadIdx.x; ch < W; ch += 4 * blockDim.x) {
