@@ -173,3 +173,26 @@ def test_persistent_gemm_single_f16(ctx, tag):
     got, ref = _run(ctx, tag, 1300, 1280, 12000, seed=13, a_f16=True)
     assert _rel_rms(got, ref) <= 2e-3
     assert np.max(np.abs(got - ref)) <= 3e-2
+
+
+@pytest.mark.parametrize("tag,n,k,epi,out_f16", [
+    (synth.Q4_0, 1300, 1280, _lib.EPI_GELU, True),
+    (synth.Q8_0, 1280, 1280, _lib.EPI_SCALE, False),
+    (synth.Q4_K, 1280, 1280, _lib.EPI_NONE, True),
+    (synth.Q4_0, 1280, 5120, _lib.EPI_RESIDUAL, False),
+])
+def test_persistent_gemm_shared_operands_match_tmem_path(ctx, monkeypatch, tag, n, k, epi, out_f16):
+    """Single-f16 large-M GEMM on the kernel whose weight tile arrives by TMA
+    from an f16 plane dequantized once per call (both MMA operands in shared
+    memory, 256-token tiles) against the kernel that dequantizes into tensor
+    memory per tile: the same f16 weights and the same K order, so the same
+    values; and both against the oracle. M = 12001 leaves a ragged last tile."""
+    import torch
+    outs = []
+    for ss in ("1", "0"):
+        monkeypatch.setenv("VKB_GEMM_SS", ss)
+        monkeypatch.setenv("VKB_GEMM_PERSIST", "force")
+        got, ref = _run(ctx, tag, n, k, 12001, seed=31, a_f16=True, out_f16=out_f16, epi=epi, scale=0.125)
+        outs.append(got)
+        assert _rel_rms(got, ref) <= 2e-3
+    assert np.max(np.abs(outs[0] - outs[1])) <= 1e-5 * max(1.0, float(np.max(np.abs(outs[1]))))

@@ -113,6 +113,7 @@ struct vkb_context {
     vkb::DevBuf tile_ctr;  // per-tile arrival counters of in-kernel split-K reductions (each returns to 0)
     vkb::DevBuf frontend;  // log-mel tables (window, twiddles, mel bank) + per-clip maxima
     int frontend_mels = 0; // mel count the tables were built for
+    vkb::DevBuf wplane;    // f16 weight plane of the SS encoder GEMM (n_pad x k halves, grown on first use)
     // Programmatic dependent launch: each kernel may start while the previous
     // one in the stream drains; it waits (griddepcontrol.wait) before touching
     // anything that kernel wrote (VKB_PDL=0 turns it off).

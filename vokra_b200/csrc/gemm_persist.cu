@@ -32,30 +32,35 @@
 
 namespace vkb {
 
-template <int FMT, bool SPLIT = true, int EG = 2>
+// SS = true: the weight tile arrives by TMA as f16 from a plane that
+// dequant_plane_kernel wrote just before (single-f16 operands only); both MMA
+// operands come from shared memory, there are no dequantization warps, and
+// tensor memory holds two 256-token accumulators.
+template <int FMT, bool SPLIT = true, int EG = 2, bool SS = false>
 struct PCfg {
-    static constexpr int BN = 192;                          // tokens per tile
+    static_assert(!(SS && SPLIT), "the f16 weight plane carries no low part");
+    static constexpr int BN = SS ? 256 : 192;               // tokens per tile
     static constexpr int NP = SPLIT ? 2 : 1;                // activation planes (hi, lo)
     static constexpr int B_BYTES = BN * 128;                // one activation plane per stage
-    static constexpr int RAW_Q = stage_qs_bytes(FMT);
-    static constexpr int RAW_S = stage_sc_bytes(FMT);
+    static constexpr int RAW_Q = SS ? TILE_N * 128 : stage_qs_bytes(FMT);
+    static constexpr int RAW_S = SS ? 0 : stage_sc_bytes(FMT);
     static constexpr int RAW_BYTES = ((RAW_Q + RAW_S) + 1023) / 1024 * 1024;
     static constexpr int STAGE_BYTES = NP * B_BYTES + RAW_BYTES;
     static constexpr int S0 = (225 * 1024 - 2048) / STAGE_BYTES;
-    static constexpr int SMAX = SPLIT ? 4 : 6;
+    static constexpr int SMAX = SPLIT ? 4 : (SS ? 4 : 6);
     static constexpr int S = S0 > SMAX ? SMAX : S0;
     static constexpr int SMEM = 1024 + S * STAGE_BYTES + 1024;
     // A stages in tensor memory: W_hi | W_lo take 64 columns, a single f16 plane
     // 32, so the single-f16 kernel keeps four stages in the same 128 columns
     // (the dequant warps run two stages further ahead of the MMAs)
     static constexpr int A_STRIDE = SPLIT ? 64 : 32;
-    static constexpr int AS = SPLIT ? 2 : 4;
+    static constexpr int AS = SS ? 1 : (SPLIT ? 2 : 4);  // (unused with SS)
     static constexpr int A_COL0 = 2 * BN;
-    static constexpr int DEQ_WARPS = 4;
+    static constexpr int DEQ_WARPS = SS ? 0 : 4;
     static constexpr int EPI_WARPS = 4 * EG;  // EG groups of four warps, BN / EG columns each
     static_assert((BN / EG) % 32 == 0, "epilogue column share");
     static constexpr int THREADS = 32 * (2 + DEQ_WARPS + EPI_WARPS);
-    static_assert(A_COL0 + AS * A_STRIDE <= 512, "tensor memory budget");
+    static_assert(SS ? 2 * BN <= 512 : A_COL0 + AS * A_STRIDE <= 512, "tensor memory budget");
     static_assert(S >= 2, "pipeline needs at least two stages");
     static_assert(B_BYTES % 1024 == 0, "128-byte swizzle atoms");
 };
@@ -120,12 +125,13 @@ __device__ __forceinline__ int64_t q8_row(const PEpi& e, int64_t m) {
     return (int64_t)e.row_map[g] * e.row_group + ((unsigned)m - g * (unsigned)e.row_group);
 }
 
-template <int FMT, bool SPLIT, int EG>
-__global__ void __launch_bounds__(PCfg<FMT, SPLIT, EG>::THREADS, 1)
+template <int FMT, bool SPLIT, int EG, bool SS>
+__global__ void __launch_bounds__(PCfg<FMT, SPLIT, EG, SS>::THREADS, 1)
     tc_gemm_persist_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_lo,
-                           const uint8_t* __restrict__ qs, const uint8_t* __restrict__ sc, int64_t K, int64_t N,
-                           int64_t M, int n_tiles, int total_tiles, PEpi e, int* err) {
-    using C = PCfg<FMT, SPLIT, EG>;
+                           const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ qs,
+                           const uint8_t* __restrict__ sc, int64_t K, int64_t N, int64_t M, int n_tiles,
+                           int total_tiles, PEpi e, int* err) {
+    using C = PCfg<FMT, SPLIT, EG, SS>;
     constexpr int BN = C::BN, S = C::S, AS = C::AS;
     constexpr int CG = BN / EG;  // columns per epilogue group
     extern __shared__ uint8_t smem_raw[];
@@ -175,14 +181,21 @@ __global__ void __launch_bounds__(PCfg<FMT, SPLIT, EG>::THREADS, 1)
         if (lane == 0) {
             auto load_weights = [&](int s, int n_tile, int i) {
                 uint8_t* raw_dst = ring + s * C::STAGE_BYTES + C::NP * C::B_BYTES;
+                if constexpr (SS) {
+                    ptx::mbar_expect_tx(&full[s], C::NP * C::B_BYTES + C::RAW_Q);
+                    ptx::tma_load_2d(raw_dst, &wmap, &full[s], i * STAGE_K, n_tile * TILE_N);
+                    return;
+                }
                 StagePtrs p = stage_ptrs(FMT, qs, sc, K, n_tile, i);
                 ptx::mbar_expect_tx(&full[s], C::NP * C::B_BYTES + C::RAW_Q + C::RAW_S);
                 ptx::bulk_load(raw_dst, p.qs, C::RAW_Q, &full[s]);
                 if (C::RAW_S) ptx::bulk_load(raw_dst + C::RAW_Q, p.sc, C::RAW_S, &full[s]);
             };
             const int pre = nst < S ? nst : S;
+            // the f16 weight plane is written by the kernel before this one
+            if (SS) pdl_wait();
             for (int i = 0; i < pre; ++i) load_weights(i, first % n_tiles, i);
-            pdl_wait();
+            if (!SS) pdl_wait();
             int g = 0;
             for (int t = first; t < total_tiles && ok; t += stride) {
                 const int n_tile = t % n_tiles, m_tile = t / n_tiles;
@@ -214,7 +227,23 @@ __global__ void __launch_bounds__(PCfg<FMT, SPLIT, EG>::THREADS, 1)
                 ptx::tc_fence_after();
                 const uint32_t d_t = tmem + b * BN;
                 for (int i = 0; i < nst; ++i, ++g) {
-                    const int s = g % S, a = g % AS;
+                    const int s = g % S;
+                    if constexpr (SS) {
+                        if (!ptx::mbar_wait(&full[s], (g / S) & 1)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+                        const uint32_t b_addr = ptx::smem_u32(ring + s * C::STAGE_BYTES);
+                        const uint32_t w_addr = b_addr + C::NP * C::B_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            ptx::mma_f16_ss(d_t, ptx::sdesc_sw128(w_addr + kk * 32), ptx::sdesc_sw128(b_addr + kk * 32),
+                                            idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                        ptx::mma_commit(&empty[s]);
+                        continue;
+                    }
+                    const int a = g % AS;
                     if (!ptx::mbar_wait(&full[s], (g / S) & 1) || !ptx::mbar_wait(&a_full[a], (g / AS) & 1)) {
                         ok = false;
                         break;
@@ -239,7 +268,7 @@ __global__ void __launch_bounds__(PCfg<FMT, SPLIT, EG>::THREADS, 1)
                 ptx::mma_commit(&acc_full[b]);
             }
         }
-    } else if (warp < 2 + C::DEQ_WARPS) {
+    } else if (!SS && warp < 2 + C::DEQ_WARPS) {
         // dequantization: row r of the 128-row weight tile = tensor-memory lane r
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
@@ -371,23 +400,64 @@ __global__ void __launch_bounds__(PCfg<FMT, SPLIT, EG>::THREADS, 1)
 
 int persist_bn() { return PCfg<W_Q4_0>::BN; }
 
-template <int FMT, bool SPLIT, int EG>
+// The f16 weight plane of the SS kernel: row n of the (padded) weight, K
+// halves, row-major, each value the f16 the TMEM path's dequantization warps
+// would produce (dequant_row_stage_h, single f16). One CTA per (stage, tile),
+// thread = weight row: 64 halves = 128 contiguous bytes per thread.
+template <int FMT>
+__global__ void __launch_bounds__(TILE_N) dequant_plane_kernel(const uint8_t* __restrict__ qs,
+                                                               const uint8_t* __restrict__ sc, int64_t K,
+                                                               __half* __restrict__ plane) {
+    // the plane may still be read by the GEMM launched before this kernel
+    pdl_entry();
+    const int i = blockIdx.x, n_tile = blockIdx.y, r = threadIdx.x;
+    const StagePtrs p = stage_ptrs(FMT, qs, sc, K, n_tile, i);
+    uint32_t hi[32], lo[32];
+    dequant_row_stage_h<FMT, false>(p.qs, p.sc, r, i, hi, lo);
+    uint4* dst = reinterpret_cast<uint4*>(plane + ((int64_t)n_tile * TILE_N + r) * K + (int64_t)i * STAGE_K);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dst[j] = make_uint4(hi[4 * j], hi[4 * j + 1], hi[4 * j + 2], hi[4 * j + 3]);
+}
+
+template <int FMT, bool SPLIT, int EG, bool SS>
 static void launch_persist(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e,
                            int* err) {
-    using C = PCfg<FMT, SPLIT, EG>;
-    smem_optin(tc_gemm_persist_kernel<FMT, SPLIT, EG>, C::SMEM);
-    CUtensorMap map, map_lo;
+    using C = PCfg<FMT, SPLIT, EG, SS>;
+    smem_optin(tc_gemm_persist_kernel<FMT, SPLIT, EG, SS>, C::SMEM);
+    CUtensorMap map, map_lo, wmap;
     make_tmap_f16(&map, a16, m, w->k, C::BN);
     if (SPLIT) make_tmap_f16(&map_lo, a16 + m * w->k, m, w->k, C::BN);
     else map_lo = map;
     const int n_tiles = (int)(w->n_pad / TILE_N);
+    if (SS) {
+        const size_t bytes = (size_t)w->n_pad * w->k * sizeof(__half);
+        if (ctx->wplane.n < bytes) {
+            VKB_CUDA(cudaStreamSynchronize(ctx->stream));
+            ctx->wplane.alloc(bytes);
+        }
+        launch_pdl(ctx, dequant_plane_kernel<FMT>, dim3((unsigned)(w->k / STAGE_K), (unsigned)n_tiles), TILE_N, 0,
+                   w->qs.as<uint8_t>(), w->sc.as<uint8_t>(), w->k, ctx->wplane.as<__half>());
+        VKB_CUDA(cudaGetLastError());
+        ctx->count();
+        make_tmap_f16(&wmap, ctx->wplane.p, w->n_pad, w->k, TILE_N);
+    } else {
+        wmap = map;
+    }
     const int m_tiles = (int)((m + C::BN - 1) / C::BN);
     const int total = n_tiles * m_tiles;
     const int grid = std::min(total, ctx->sm_count);
-    launch_pdl(ctx, tc_gemm_persist_kernel<FMT, SPLIT, EG>, grid, C::THREADS, C::SMEM, map, map_lo, w->qs.as<uint8_t>(),
-               w->sc.as<uint8_t>(), w->k, w->n, m, n_tiles, total, e, err);
+    launch_pdl(ctx, tc_gemm_persist_kernel<FMT, SPLIT, EG, SS>, grid, C::THREADS, C::SMEM, map, map_lo, wmap,
+               w->qs.as<uint8_t>(), w->sc.as<uint8_t>(), w->k, w->n, m, n_tiles, total, e, err);
     VKB_CUDA(cudaGetLastError());
     ctx->count();
+}
+
+// Whether single-f16 GEMMs of large M run on the SS kernel (VKB_GEMM_SS=0: the
+// TMEM-operand kernel with in-kernel dequantization).
+// Read at every call (a host-side getenv per large GEMM), so one process can compare both kernels.
+bool persist_ss_enabled() {
+    const char* v = std::getenv("VKB_GEMM_SS");
+    return !v || v[0] != '0';
 }
 
 void run_tc_persistent(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e, int* err,
@@ -396,11 +466,14 @@ void run_tc_persistent(vkb_context* ctx, const vkb_weight* w, int64_t m, const _
     // mode's, so fc1's GELU epilogue is the longer phase with two; measured 812 vs 819 ms per
     // bench step); VKB_PERSIST_EPI_GROUPS=2 selects two
     static const int groups = [] { const char* v = std::getenv("VKB_PERSIST_EPI_GROUPS"); return v ? std::atoi(v) : 3; }();
+    static const int ss_groups = [] { const char* v = std::getenv("VKB_SS_EPI_GROUPS"); return v ? std::atoi(v) : 2; }();
     with_fmt(w->fmt, [&](auto F) {
         constexpr int FM = decltype(F)::value;
-        if (split) launch_persist<FM, true, 2>(ctx, w, m, a16, e, err);
-        else if (groups == 3) launch_persist<FM, false, 3>(ctx, w, m, a16, e, err);
-        else launch_persist<FM, false, 2>(ctx, w, m, a16, e, err);
+        if (split) launch_persist<FM, true, 2, false>(ctx, w, m, a16, e, err);
+        else if (persist_ss_enabled() && ss_groups == 4) launch_persist<FM, false, 4, true>(ctx, w, m, a16, e, err);
+        else if (persist_ss_enabled()) launch_persist<FM, false, 2, true>(ctx, w, m, a16, e, err);
+        else if (groups == 3) launch_persist<FM, false, 3, false>(ctx, w, m, a16, e, err);
+        else launch_persist<FM, false, 2, false>(ctx, w, m, a16, e, err);
     });
 }
 

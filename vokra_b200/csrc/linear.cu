@@ -1332,8 +1332,12 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
         const bool p_off = pv && pv[0] == '0', p_force = pv && pv[0] == 'f';
         const int64_t p_tiles = (w->n_pad / TILE_N) * ((m + persist_bn() - 1) / persist_bn());
         // (single-f16 operands: not for the residual projections, measured faster on the classic kernel)
-        if (!p_off && p.splits == 1 && x.col_block == 0 && !x.row_map && (p.split || epilogue != VKB_EPI_RESIDUAL) &&
-            (p_force || (p_tiles >= 4 * (int64_t)ctx->sm_count && w->k <= 20 * STAGE_K))) {
+        // The SS kernel (single f16: weights dequantized once per call into an f16 plane, both operands
+        // by TMA) takes every such GEMM, residual projections and K = 5120 included.
+        const bool ss = !p.split && persist_ss_enabled();
+        if (!p_off && p.splits == 1 && x.col_block == 0 && !x.row_map &&
+            (p.split || ss || epilogue != VKB_EPI_RESIDUAL) &&
+            (p_force || (p_tiles >= 4 * (int64_t)ctx->sm_count && (ss || w->k <= 20 * STAGE_K)))) {
             PEpi pe;
             pe.bias = bias;
             pe.residual = residual;

@@ -72,6 +72,8 @@ struct PEpi {
 };
 // Split-precision (hi+lo) GEMM over f16 activation planes a16 [2][m][k], one
 // CTA per SM over a static tile list; token tile persist_bn().
+// Whether single-f16 large-M GEMMs take the shared-memory-operand (SS) persistent kernel.
+bool persist_ss_enabled();
 void run_tc_persistent(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e, int* err,
                        bool split = true);
 int persist_bn();
