@@ -345,13 +345,27 @@ def run_kernel_only(args):
     planes = 2 if args.precision == "split" else 1
     a = (torch.randn((planes * M, K), device="cuda") * 0.5).half()
     out = torch.empty((M, N), device="cuda", dtype=torch.float16)
-    for _ in range(3):
+    def fc1():
         _lib.check(_lib.load().vkb_linear(ctx.h, w.h, M, C.c_void_p(a.data_ptr()),
                                           _lib.DT_F16X2 if planes == 2 else _lib.DT_F16, None,
                                           C.c_void_p(out.data_ptr()), _lib.DT_F16, _lib.EPI_NONE, None,
                                           C.c_float(1.0)))
+    for _ in range(3):
+        fc1()
     torch.cuda.synchronize()
-    print(json.dumps({"kernel": args.kernel, "M": M, "N": N, "K": K, "ok": True}))
+    # under a profiler only the three launches above run (ncu -s 2 -c 1 takes the last one)
+    ms = None
+    if not os.environ.get("VKB_BENCH_NO_TIMING"):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        e0.record()
+        for _ in range(reps):
+            fc1()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+    print(json.dumps({"kernel": args.kernel, "M": M, "N": N, "K": K, "ok": True,
+                      "ms_per_launch": ms, "tflops": None if ms is None else 2.0 * M * N * K / ms / 1e9}))
 
 
 def run_paged_decode(ctx, args):

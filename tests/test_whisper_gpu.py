@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 
 from oracle import whisper_ref
-from vokra_b200 import synth
+from vokra_b200 import _lib, synth
 
 pytestmark = pytest.mark.gpu
 
@@ -200,13 +200,27 @@ def _cross_store(sess, layer, rows, d):
     return out
 
 
-def test_fused_cross_kv_q8_bytes(ctx, tmp_path, monkeypatch):
+@pytest.mark.parametrize("prec", ["split", "encoder_f16"])
+def test_fused_cross_kv_q8_bytes(ctx, tmp_path, monkeypatch, prec):
     """The cross K/V projection with Q8_0 packing in the persistent GEMM's
     epilogue writes the same store bytes as the f32 projection followed by
-    the quantize kernel (BlockQ8_0::pack), clips remapped to stream slots."""
+    the quantize kernel (BlockQ8_0::pack), clips remapped to stream slots.
+    Split precision: the TMEM-operand kernel; encoder-f16: tc_gemm_ss_kernel,
+    whose epilogue thread holds one 32-channel block of one token."""
     import torch
     from vokra_b200 import whisper
     monkeypatch.setenv("VKB_GEMM_PERSIST", "force")
+    if prec == "encoder_f16":
+        _lib.check(_lib.load().vkb_context_set_precision(ctx.h, _lib.PREC_ENCODER_F16))
+    try:
+        _fused_cross_kv_q8_bytes(ctx, tmp_path, monkeypatch)
+    finally:
+        _lib.check(_lib.load().vkb_context_set_precision(ctx.h, _lib.PREC_SPLIT))
+
+
+def _fused_cross_kv_q8_bytes(ctx, tmp_path, monkeypatch):
+    import torch
+    from vokra_b200 import whisper
     arch = synth.WhisperArch(80, 1500, 512, 8, 1, 64, 8, 2, 1000, 2048, 999, (1, 2, 3, 4))
     path = str(tmp_path / "xq.gguf")
     synth.write_synthetic_whisper(path, arch, synth.Q4_0, seed=6)

@@ -1367,14 +1367,15 @@ void run_linear_ex(vkb_context* ctx, const vkb_weight* w, int64_t m, const void*
 
 bool run_linear_q8_pair(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const float* bias,
                         int64_t width, int8_t* kq, __half* kd, int8_t* vq, __half* vd, const int32_t* row_map,
-                        int row_group) {
+                        int row_group, bool split) {
     const char* pv = std::getenv("VKB_GEMM_PERSIST");
     if (pv && pv[0] == '0') return false;
     const char* fq = std::getenv("VKB_FUSED_CROSS_Q8");
     if (fq && fq[0] == '0') return false;
-    if (ctx->precision == VKB_PREC_F16 || m <= 0 || w->n != 2 * width || width % TILE_N || w->n_pad != w->n)
-        return false;
-    if (plan_linear(ctx, w, m, true).splits != 1) return false;
+    // split: hi + lo activation planes (TMEM-operand kernel); single f16: tc_gemm_ss_kernel only
+    if (split ? ctx->precision == VKB_PREC_F16 : !persist_ss_enabled()) return false;
+    if (m <= 0 || w->n != 2 * width || width % TILE_N || w->n_pad != w->n) return false;
+    if (plan_linear(ctx, w, m, split).splits != 1) return false;
     PEpi pe;
     pe.bias = bias;
     pe.residual = nullptr;
@@ -1392,7 +1393,7 @@ bool run_linear_q8_pair(vkb_context* ctx, const vkb_weight* w, int64_t m, const 
     pe.q8d[1] = vd;
     pe.row_map = row_map;
     pe.row_group = row_group > 0 ? row_group : 1;
-    run_tc_persistent(ctx, w, m, a16, pe, device_err_flag(ctx));
+    run_tc_persistent(ctx, w, m, a16, pe, device_err_flag(ctx), split);
     return true;
 }
 

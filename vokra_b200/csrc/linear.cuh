@@ -72,7 +72,7 @@ struct PEpi {
 };
 // Split-precision (hi+lo) GEMM over f16 activation planes a16 [2][m][k], one
 // CTA per SM over a static tile list; token tile persist_bn().
-// Whether single-f16 large-M GEMMs take the shared-memory-operand (SS) persistent kernel.
+// Whether single-f16 large-M GEMMs take tc_gemm_ss_kernel (both operands in shared memory).
 bool persist_ss_enabled();
 void run_tc_persistent(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e, int* err,
                        bool split = true);
@@ -82,7 +82,7 @@ int persist_bn();
 // precision does not take it.
 bool run_linear_q8_pair(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const float* bias,
                         int64_t width, int8_t* kq, __half* kd, int8_t* vq, __half* vd, const int32_t* row_map,
-                        int row_group);
+                        int row_group, bool split = true);
 int gemv_max_m();
 
 }  // namespace vkb

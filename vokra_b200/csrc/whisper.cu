@@ -445,8 +445,8 @@ void session_encode(vkb_session* s, int n, const float* logmel, const int32_t* s
             __half* ks = s->cks.as<__half>() + (size_t)l * rows * (d / 32);
             __half* vs = s->cvs.as<__half>() + (size_t)l * rows * (d / 32);
             // the projection's epilogue packs Q8_0 rows straight into the store (no f32 round trip)
-            if (split && run_linear_q8_pair(ctx, L.ckv.get(), M, xln, L.ckv_b.as<float>(), d, kq, ks, vq, vs, map,
-                                            (int)T))
+            if (run_linear_q8_pair(ctx, L.ckv.get(), M, xln, L.ckv_b.as<float>(), d, kq, ks, vq, vs, map, (int)T,
+                                   split))
                 continue;
             float* tmp = reinterpret_cast<float*>(bufA);  // [M][2d] f32
             run_linear(ctx, L.ckv.get(), M, xln, AF, L.ckv_b.as<float>(), tmp, VKB_DT_F32, VKB_EPI_NONE,
