@@ -867,7 +867,10 @@ def main():
     tflops = 2.0 * M * N * K / (k_ms / 1e3) / 1e12
     roofline = {"bound": "tensor", "achieved": round(tflops, 1), "peak": bf16, "unit": "TFLOP/s",
                 "frac": round(tflops / bf16, 4), "traffic": None,
-                "kernel": "tc_gemm_persist_kernel (persistent, double-buffered accumulator)"
+                "kernel": ("tc_gemm_persist_kernel (persistent, double-buffered accumulator, weights dequantized "
+                           "into tensor memory)" if planes == 2 else
+                           "tc_gemm_persist_kernel<SS> (persistent, both operands by TMA from shared memory; the "
+                           "time includes dequant_plane_kernel, the once-per-call f16 weight plane)")
                           + f" Q4_0 encoder fc1 M={M} N={N} K={K}, "
                           f"{'split f16 (3 MMAs per step)' if planes == 2 else 'f16'}",
                 "algorithmic_flops": 2 * M * N * K, "mma_flops_issued": 2 * M * N * K * mma_factor,
