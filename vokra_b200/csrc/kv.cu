@@ -145,22 +145,45 @@ __global__ void __launch_bounds__(256) paged_decode_kernel(
                                    : static_cast<const void*>(vd + row * nb + b0);
         asm volatile("prefetch.global.L2 [%0];" ::"l"(pp));
     }
+    // the projection's bias (model weights) before the wait as well
+    const int ck = W + c0 + warp * 32 + lane, cv = 2 * W + c0 + warp * 32 + lane, cq = c0 + t;
+    float bk = 0.0f, bv = 0.0f, bq = 0.0f;
+    if (splits > 0 && bias) {
+        bk = bias[ck];
+        bv = bias[cv];
+        bq = bias[cq];
+    }
     pdl_wait();
-    auto val = [&](int col) {
-        const int64_t i = (int64_t)tok * ld + col;
-        if (splits == 0) return qkv[i];
-        float acc = 0.0f;
-        for (int sp = 0; sp < splits; ++sp) acc += __ldcg(part + sp * plane + i);
-        const float x = acc + (bias ? bias[col] : 0.0f);
-        return col < W ? x * qscale : x;
-    };
-    // phase 0: append this token's K and V blocks of the group (warp w: block w)
+    // phase 0: this token's K, V (warp w: block w of the group) and q columns; from split-K
+    // partials the three sums' loads are issued together, each summed in split order
+    float xk, xv, xq;
+    {
+        const int64_t r0 = (int64_t)tok * ld;
+        if (splits == 0) {
+            xk = qkv[r0 + ck];
+            xv = qkv[r0 + cv];
+            xq = qkv[r0 + cq];
+        } else {
+            float ak = 0.0f, av = 0.0f, aq = 0.0f;
+#pragma unroll 4
+            for (int sp = 0; sp < splits; ++sp) {
+                const float* pp = part + sp * plane + r0;
+                const float a = __ldcg(pp + ck), b = __ldcg(pp + cv), c = __ldcg(pp + cq);
+                ak += a;
+                av += b;
+                aq += c;
+            }
+            xk = ak + bk;
+            xv = av + bv;
+            xq = (aq + bq) * qscale;
+        }
+    }
+    // append this token's K and V blocks of the group
     {
         const int64_t row = new_rows[tok];
-        q8_0_block_warp(val(W + c0 + warp * 32 + lane), lane, kq + row * W + c0 + warp * 32, kd + row * nb + b0 + warp);
-        q8_0_block_warp(val(2 * W + c0 + warp * 32 + lane), lane, vq + row * W + c0 + warp * 32,
-                        vd + row * nb + b0 + warp);
-        qs[t] = val(c0 + t);
+        q8_0_block_warp(xk, lane, kq + row * W + c0 + warp * 32, kd + row * nb + b0 + warp);
+        q8_0_block_warp(xv, lane, vq + row * W + c0 + warp * 32, vd + row * nb + b0 + warp);
+        qs[t] = xq;
     }
     __syncthreads();
     // phase 1: scores, two keys per iteration (their 8 loads issued together)
