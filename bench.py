@@ -29,6 +29,12 @@ import time
 
 import numpy as np
 
+# The arithmetic of each --precision mode, as the JSON lines' "dtype" states it.
+PREC_DTYPE = {"split": "f16 hi+lo tensor-core operands, fp32 accumulate (Q4_0 weights, Q8_0 KV)",
+              "enc_f16": "encoder: f16 tensor-core operands, fp32 accumulate; decoder: f16 hi+lo "
+                         "operands, fp32 accumulate (Q4_0 weights, Q8_0 KV)",
+              "f16": "f16 (Q4_0 weights, Q8_0 KV)"}
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
@@ -651,6 +657,9 @@ def run_throughput(args, world, rank, local_rank):
     if dist is not None:
         dist.barrier()
     ctx = ops.Context(local_rank)
+    from vokra_b200 import _lib
+    prec = {"split": _lib.PREC_SPLIT, "f16": _lib.PREC_F16, "enc_f16": _lib.PREC_ENCODER_F16}[args.precision]
+    _lib.check(_lib.load().vkb_context_set_precision(ctx.h, prec))
     model = whisper.WhisperModel(ctx, path)
     SLOTS, ENC, POOL = 128, 32, 64
     sess = whisper.Session(model, max_streams=SLOTS, max_step_tokens=4 * SLOTS, max_clips=ENC, cross_kv_q8=True)
@@ -682,7 +691,7 @@ def run_throughput(args, world, rank, local_rank):
             "metric": METRIC, "value": round(audio / (ms / 1e3), 2), "unit": "audio-s/s",
             "decode_tok_s": round(tokens / (ms / 1e3), 1), "n_gpus": world, "steps": 1, "warmup": 1,
             "ms_per_step": round(ms, 1), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16 hi+lo tensor-core operands, fp32 accumulate (Q4_0 weights, Q8_0 KV)", "data": "synthetic",
+            "dtype": PREC_DTYPE[args.precision], "data": "synthetic",
             "config": {"workload": f"configs[4]: {n_rank * world} utterances of whisper-large-v3 q4_0 ({n_rank} per "
                                    f"GPU), clip lengths U[5, 30] s padded to 30 s, greedy decode lengths U[32, 224]; "
                                    f"continuous batching of up to {SLOTS} streams per GPU, clips encoded {ENC} at a "
@@ -921,10 +930,7 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None,
-            "dtype": {"split": "f16 hi+lo tensor-core operands, fp32 accumulate (Q4_0 weights, Q8_0 KV)",
-                      "enc_f16": "encoder: f16 tensor-core operands, fp32 accumulate; decoder: f16 hi+lo "
-                                 "operands, fp32 accumulate (Q4_0 weights, Q8_0 KV)",
-                      "f16": "f16 (Q4_0 weights, Q8_0 KV)"}[args.precision],
+            "dtype": PREC_DTYPE[args.precision],
             "data": "synthetic",
             "config": {"workload": "configs[3]: whisper-large-v3 q4_0, 64 clips x 30 s per GPU, log-mel frontend + "
                                    "encoder + 4-token "
