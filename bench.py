@@ -878,8 +878,9 @@ def main():
                 "frac": round(tflops / bf16, 4), "traffic": None,
                 "kernel": ("tc_gemm_persist_kernel (persistent, double-buffered accumulator, weights dequantized "
                            "into tensor memory)" if planes == 2 else
-                           "tc_gemm_persist_kernel<SS> (persistent, both operands by TMA from shared memory; the "
-                           "time includes dequant_plane_kernel, the once-per-call f16 weight plane)")
+                           "tc_gemm_pair_kernel (persistent, CTA pairs with one cta_group::2 MMA per 256x256 tile, "
+                           "both operands by TMA from shared memory; the time includes dequant_plane_kernel, the "
+                           "once-per-call f16 weight plane)")
                           + f" Q4_0 encoder fc1 M={M} N={N} K={K}, "
                           f"{'split f16 (3 MMAs per step)' if planes == 2 else 'f16'}",
                 "algorithmic_flops": 2 * M * N * K, "mma_flops_issued": 2 * M * N * K * mma_factor,

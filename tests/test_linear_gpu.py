@@ -189,10 +189,13 @@ def test_persistent_gemm_shared_operands_match_tmem_path(ctx, monkeypatch, tag, 
     values; and both against the oracle. M = 12001 leaves a ragged last tile."""
     import torch
     outs = []
-    for ss in ("1", "0"):
+    # shared operands on CTA pairs (cta_group::2), on one CTA, then the TMEM-operand kernel
+    for ss, pair in (("1", "1"), ("1", "0"), ("0", "0")):
         monkeypatch.setenv("VKB_GEMM_SS", ss)
+        monkeypatch.setenv("VKB_GEMM_PAIR", pair)
         monkeypatch.setenv("VKB_GEMM_PERSIST", "force")
         got, ref = _run(ctx, tag, n, k, 12001, seed=31, a_f16=True, out_f16=out_f16, epi=epi, scale=0.125)
         outs.append(got)
         assert _rel_rms(got, ref) <= 2e-3
-    assert np.max(np.abs(outs[0] - outs[1])) <= 1e-5 * max(1.0, float(np.max(np.abs(outs[1]))))
+    for o in outs[:2]:
+        assert np.max(np.abs(o - outs[2])) <= 1e-5 * max(1.0, float(np.max(np.abs(outs[2]))))
