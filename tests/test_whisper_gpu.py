@@ -205,8 +205,8 @@ def test_fused_cross_kv_q8_bytes(ctx, tmp_path, monkeypatch, prec):
     """The cross K/V projection with Q8_0 packing in the persistent GEMM's
     epilogue writes the same store bytes as the f32 projection followed by
     the quantize kernel (BlockQ8_0::pack), clips remapped to stream slots.
-    Split precision: the TMEM-operand kernel; encoder-f16: tc_gemm_ss_kernel,
-    whose epilogue thread holds one 32-channel block of one token."""
+    Split precision: the TMEM-operand kernel; encoder-f16: the shared-operand
+    kernel on CTA pairs (weights as a once-per-call f16 plane)."""
     import torch
     from vokra_b200 import whisper
     monkeypatch.setenv("VKB_GEMM_PERSIST", "force")

@@ -154,6 +154,8 @@ __global__ void reduce_residual_ln_kernel(const float* __restrict__ part, int sp
     pdl_wait();
     if (on) {
         const int64_t o4 = row * n4 + c;
+        // the residual row with the first partials: one round of loads
+        const float4 r = reinterpret_cast<const float4*>(h)[o4];
         float4 acc = z;
         constexpr int U = 8;
         for (int s0 = 0; s0 < splits; s0 += U) {
@@ -167,7 +169,6 @@ __global__ void reduce_residual_ln_kernel(const float* __restrict__ part, int sp
                     acc.x += t[u].x; acc.y += t[u].y; acc.z += t[u].z; acc.w += t[u].w;
                 }
         }
-        const float4 r = reinterpret_cast<const float4*>(h)[o4];
         v = make_float4(r.x + (acc.x + bi.x), r.y + (acc.y + bi.y), r.z + (acc.z + bi.z), r.w + (acc.w + bi.w));
         reinterpret_cast<float4*>(h)[o4] = v;
     }

@@ -1372,7 +1372,7 @@ bool run_linear_q8_pair(vkb_context* ctx, const vkb_weight* w, int64_t m, const 
     if (pv && pv[0] == '0') return false;
     const char* fq = std::getenv("VKB_FUSED_CROSS_Q8");
     if (fq && fq[0] == '0') return false;
-    // split: hi + lo activation planes (TMEM-operand kernel); single f16: tc_gemm_ss_kernel only
+    // split: hi + lo activation planes (TMEM-operand kernel); single f16: the shared-operand kernels only
     if (split ? ctx->precision == VKB_PREC_F16 : !persist_ss_enabled()) return false;
     if (m <= 0 || w->n != 2 * width || width % TILE_N || w->n_pad != w->n) return false;
     if (plan_linear(ctx, w, m, split).splits != 1) return false;

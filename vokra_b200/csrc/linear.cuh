@@ -72,7 +72,8 @@ struct PEpi {
 };
 // Split-precision (hi+lo) GEMM over f16 activation planes a16 [2][m][k], one
 // CTA per SM over a static tile list; token tile persist_bn().
-// Whether single-f16 large-M GEMMs take tc_gemm_ss_kernel (both operands in shared memory).
+// Whether single-f16 large-M GEMMs take the shared-operand kernels (tc_gemm_pair_kernel, or
+// tc_gemm_persist_kernel with SS; weights as a once-per-call f16 plane, both operands in shared memory).
 bool persist_ss_enabled();
 void run_tc_persistent(vkb_context* ctx, const vkb_weight* w, int64_t m, const __half* a16, const PEpi& e, int* err,
                        bool split = true);
