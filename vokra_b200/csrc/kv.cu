@@ -97,7 +97,7 @@ __global__ void kv_append_kernel(const float* __restrict__ k, const float* __res
 
 // ---------------------------------------------------------------------------
 // Fused decode self-attention (one query per stream, SEQUENCE layout, d_head
-// 64): one CTA of 256 threads per (stream, group of 4 heads = 256 channels).
+// 64): one CTA of 64 x HG threads per (stream, group of HG heads = 64 x HG channels; HG = 2 or 4).
 // Before waiting for the QKV projection it looks up the key rows and requests
 // their K and V bytes into L2; then it appends the step's K/V for its channels
 // (the bit-exact BlockQ8_0::pack of kv_append_kernel) and attends over every
@@ -111,38 +111,42 @@ __global__ void kv_append_kernel(const float* __restrict__ k, const float* __res
 // With splits > 0 the q|k|v row is read from the QKV projection's split-K
 // partials [splits][n_tok][ld] instead: value = (sum of partials in split
 // order + bias) x (qscale for the q columns), the reduce kernel's epilogue.
-__global__ void __launch_bounds__(256) paged_decode_kernel(
+template <int HG>
+__global__ void __launch_bounds__(64 * HG) paged_decode_kernel(
     const float* __restrict__ qkv, int64_t ld, const float* __restrict__ part, int splits, int64_t plane,
     const float* __restrict__ bias, float qscale,
     const AttnGroup* __restrict__ groups, const int64_t* __restrict__ new_rows, const int32_t* __restrict__ table,
     int ppseq, int64_t arena_row0, int bs, int8_t* kq, __half* kd, int8_t* vq, __half* vd, int W, int max_keys,
     void* out, int out_fmt, int64_t out_plane) {
     pdl_launch();
+    constexpr int NT = 64 * HG;  // threads = channels of the group
+    constexpr int KP = NT / 128; // 128-byte pieces of a key's K (or V) row in the group
     extern __shared__ __align__(16) float pd_smem[];
-    float* sc = pd_smem;                               // [4][max_keys]; later the [16][256] P.V sums
-    float* qs = sc + (4 * max_keys > 4096 ? 4 * max_keys : 4096);  // [256]
-    int64_t* rows_s = reinterpret_cast<int64_t*>(qs + 256);               // [max_keys]
+    float* sc = pd_smem;                               // [HG][max_keys]; later the [16][NT] P.V sums
+    float* qs = sc + (HG * max_keys > 16 * NT ? HG * max_keys : 16 * NT);  // [NT]
+    int64_t* rows_s = reinterpret_cast<int64_t*>(qs + NT);                // [max_keys]
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     // The query groups, the rows of the new keys and the page table come from
     // host copies that precede the step, so the key rows are looked up, and
-    // the K and V bytes of every key (this group's 256 channels and their
+    // the K and V bytes of every key (this group's 64 * HG channels and their
     // scales) requested into L2, while the QKV projection still runs; an L2
     // prefetch is correct whatever writes those bytes.
     const AttnGroup g = groups[blockIdx.x];
     const int tok = g.first_tok, n_keys = g.pos0 + 1;
-    const int c0 = blockIdx.y * 256, nb = W / 32, b0 = c0 / 32;
-    for (int k = t; k < n_keys; k += 256) {
+    const int c0 = blockIdx.y * NT, nb = W / 32, b0 = c0 / 32;
+    for (int k = t; k < n_keys; k += NT) {
         const int pid = table[g.seq * ppseq + k / bs];
         rows_s[k] = arena_row0 + (int64_t)pid * bs + k % bs;
     }
     __syncthreads();
-    for (int i = t; i < 6 * n_keys; i += 256) {
-        const int64_t row = rows_s[i / 6];
-        const int pt = i % 6;
-        const void* pp = pt < 2   ? static_cast<const void*>(kq + row * W + c0 + 128 * pt)
-                         : pt == 2 ? static_cast<const void*>(kd + row * nb + b0)
-                         : pt < 5  ? static_cast<const void*>(vq + row * W + c0 + 128 * (pt - 3))
-                                   : static_cast<const void*>(vd + row * nb + b0);
+    constexpr int PP = 2 * KP + 2;  // L2 lines requested per key
+    for (int i = t; i < PP * n_keys; i += NT) {
+        const int64_t row = rows_s[i / PP];
+        const int pt = i % PP;
+        const void* pp = pt < KP           ? static_cast<const void*>(kq + row * W + c0 + 128 * pt)
+                         : pt == KP        ? static_cast<const void*>(kd + row * nb + b0)
+                         : pt < 2 * KP + 1 ? static_cast<const void*>(vq + row * W + c0 + 128 * (pt - KP - 1))
+                                           : static_cast<const void*>(vd + row * nb + b0);
         asm volatile("prefetch.global.L2 [%0];" ::"l"(pp));
     }
     // the projection's bias (model weights) before the wait as well
@@ -227,8 +231,8 @@ __global__ void __launch_bounds__(256) paged_decode_kernel(
         }
     }
     __syncthreads();
-    // phase 2: softmax per head (warps 0..3), p normalised in place
-    if (warp < 4) {
+    // phase 2: softmax per head (warps 0 .. HG - 1), p normalised in place
+    if (warp < HG) {
         float* s = sc + warp * max_keys;
         float m = -INFINITY;
         for (int k = lane; k < n_keys; k += 32) m = fmaxf(m, s[k]);
@@ -248,7 +252,7 @@ __global__ void __launch_bounds__(256) paged_decode_kernel(
     // 16-byte load of V per key over every 16th key (16 loads in flight per
     // 16 keys), the 16 key groups summed in shared memory
     {
-        const int cg = t & 15, kg = t >> 4;
+        const int cg = t % (4 * HG), kg = t / (4 * HG);  // 16 key groups
         const float* p = sc + (cg >> 2) * max_keys;
         const int8_t* vcol = vq + c0 + 16 * cg;
         const __half* vdc = vd + b0 + (cg >> 1);
@@ -269,15 +273,15 @@ __global__ void __launch_bounds__(256) paged_decode_kernel(
                                           a[4 * wd + bb]);
         }
         __syncthreads();  // the score rows are no longer read: reuse them for the key-group sums
-        float* red = sc;  // [16][256]
+        float* red = sc;  // [16][NT]
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-            *reinterpret_cast<float4*>(red + kg * 256 + 16 * cg + 4 * i) =
+            *reinterpret_cast<float4*>(red + kg * NT + 16 * cg + 4 * i) =
                 make_float4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]);
         __syncthreads();
         float acc = 0.0f;
 #pragma unroll
-        for (int g2 = 0; g2 < 16; ++g2) acc += red[g2 * 256 + t];
+        for (int g2 = 0; g2 < 16; ++g2) acc += red[g2 * NT + t];
         const int64_t o = (int64_t)tok * W + c0 + t;
         if (out_fmt == 0) {
             reinterpret_cast<float*>(out)[o] = acc;
@@ -778,11 +782,16 @@ void kv_append_attention_ex(vkb_kv_pool* p, int layer, const float* qkv, int64_t
         return;
     }
     const int max_keys = d.max_time;
-    const size_t smem = (size_t)(std::max(4 * max_keys, 4096) + 256) * sizeof(float) + (size_t)max_keys * sizeof(int64_t);
-    smem_optin(paged_decode_kernel, 200 * 1024);
+    // heads per CTA: 2 (default: twice the CTAs of 4, half the channels each; decode step 4.080 vs
+    // 4.097 ms at 64 streams, configs[2] 80.5 vs 82.4 us) or 4 (VKB_DECODE_HEADS=4)
+    static const int hg = [] { const char* v = std::getenv("VKB_DECODE_HEADS"); return v && v[0] == '4' ? 4 : 2; }();
+    const int nt = 64 * hg;
+    const size_t smem = (size_t)(std::max(hg * max_keys, 16 * nt) + nt) * sizeof(float) + (size_t)max_keys * sizeof(int64_t);
     if (smem > 200 * 1024) fail(VKB_ERROR_UNSUPPORTED_OP, "decode attention: max_time too large");
-    dim3 grid((unsigned)p->n_tok, (unsigned)(d.n_head / 4));
-    launch_pdl(p->ctx, paged_decode_kernel, grid, 256, smem, qkv, ld, part, splits, (int64_t)p->n_tok * ld, bias,
+    dim3 grid((unsigned)p->n_tok, (unsigned)(d.n_head / hg));
+    auto kern = hg == 2 ? paged_decode_kernel<2> : paged_decode_kernel<4>;
+    smem_optin(kern, 200 * 1024);
+    launch_pdl(p->ctx, kern, grid, nt, smem, qkv, ld, part, splits, (int64_t)p->n_tok * ld, bias,
                qscale, p->groups_dev.as<AttnGroup>(), p->rows_dev.as<int64_t>() + (size_t)layer * p->n_tok,
                p->table_dev.as<int32_t>(), p->ppseq, (int64_t)layer * p->n_pages * p->rpp, d.page_tokens,
                p->kq.as<int8_t>(), p->kd.as<__half>(), p->vq.as<int8_t>(), p->vd.as<__half>(), p->W, max_keys, out,
